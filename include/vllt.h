@@ -1,0 +1,267 @@
+/*
+ * vllt.h -- C ABI of the B200 (sm_100a) forward hot path for vllm-lite.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, sizes and a CUDA stream passed as `void*`
+ *     (a cudaStream_t; NULL = the legacy default stream);
+ *   - is stream-ordered and asynchronous: it validates its arguments on the
+ *     host, enqueues kernels and returns;
+ *   - returns an int status (VLLT_OK = 0). On failure the thread-local
+ *     message is available from vllt_last_error().
+ *   - allocates no device memory: callers pass every buffer, including
+ *     workspaces sized by the *_bytes() helpers.
+ *
+ * KV cache layout (one layer): [num_blocks][n_kv_heads][block_size][head_dim],
+ * i.e. one block of one KV head is a contiguous block_size x head_dim tile.
+ * A "slot" is the reference's flat cache index block_id * block_size + offset
+ * (vllmlite/attention.py:40-44, vllmlite/block.py:154-156). With block_size 1
+ * the layout equals the reference's per-layer cache [slots][n_kv][head_dim]
+ * (vllmlite/runner.py:41-44).
+ *
+ * Weights use the reference's row-major [in][out] orientation
+ * (vllmlite/model.py:34-43); the fused matrices are documented at
+ * vllt_model_desc.
+ */
+#ifndef VLLT_H_
+#define VLLT_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  VLLT_OK = 0,
+  VLLT_ERR_ARG = 1,         /* bad pointer / size / unsupported shape */
+  VLLT_ERR_CUDA = 2,        /* a CUDA call or launch failed */
+  VLLT_ERR_TIMEOUT = 3,     /* a bounded device-side wait expired */
+  VLLT_ERR_UNSUPPORTED = 4, /* valid request this build does not implement */
+  VLLT_ERR_DATA = 5         /* device-side validation flagged bad metadata */
+};
+
+enum { VLLT_F32 = 0, VLLT_BF16 = 1 };
+
+/* Last error message of the calling thread ("" when none). */
+const char* vllt_last_error(void);
+/* Library version, major*10000 + minor*100 + patch. */
+int vllt_version(void);
+/* Kernels this library has launched in the process so far (all threads). */
+int64_t vllt_kernel_launches(void);
+
+/* ------------------------------------------------------------------------ */
+/* KV cache                                                                 */
+/* ------------------------------------------------------------------------ */
+
+/* Scatter new K/V rows into the paged cache through a slot mapping.
+ * Replaces write_kv (vllmlite/attention.py:47-49):
+ *   cache[slot_mapping[t]] = k[t], v[t]   for t < num_tokens.
+ * k, v: [num_tokens][n_kv][head_dim] of `dtype`. Slots outside
+ * [0, num_blocks*block_size) are skipped by the kernel (never written). */
+int vllt_reshape_and_cache(const void* k, const void* v, void* k_cache, void* v_cache,
+                           const int32_t* slot_mapping, int32_t num_tokens, int32_t n_kv,
+                           int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                           int32_t dtype, void* stream);
+
+/* Copy whole blocks src -> dst in every layer, K and V, before any KV write of
+ * the step. Replaces NumpyRunner._do_cow (vllmlite/runner.py:54-60).
+ * pairs: device int32 [n_pairs][2] = (src_block, dst_block).
+ * k_cache/v_cache: base of [n_layers][num_blocks][n_kv][block_size][head_dim]. */
+int vllt_copy_blocks(void* k_cache, void* v_cache, const int32_t* pairs, int32_t n_pairs,
+                     int32_t n_layers, int32_t num_blocks, int32_t n_kv, int32_t block_size,
+                     int32_t head_dim, int32_t dtype, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Batch flatten (ModelRunner.execute, vllmlite/runner.py:66-90)            */
+/* ------------------------------------------------------------------------ */
+
+/* A packed step record (device int32), written by the host once per pass:
+ *   [0]=num_seqs S  [1]=num_tokens T  [2]=num_rows R  [3]=table width W
+ *   seq_start[S]   position of the first token pushed this pass (num_computed)
+ *   seq_qlen[S]    tokens pushed this pass (ScheduledSeq.num_tokens)
+ *   seq_count[S]   logit rows wanted: min(1 + num_drafts, qlen) (runner.py:88)
+ *   token_ids[T]   the pushed tokens, sequence after sequence
+ *   block_tables[S][W]  physical block ids (BlockTable.block_ids), padded
+ * Its length is 4 + 3*S + T + S*W int32 words. */
+
+/* Capacities of the buffers one runner allocates once. */
+typedef struct vllt_caps {
+  int32_t max_seqs;        /* S <= max_seqs */
+  int32_t max_tokens;      /* T <= max_tokens */
+  int32_t max_rows;        /* R <= max_rows */
+  int32_t max_table_width; /* W <= max_table_width (= ceil(max_seq_len / block_size)) */
+} vllt_caps;
+
+/* Bytes of the opaque batch-metadata buffer for the given capacities. */
+int64_t vllt_meta_bytes(const vllt_caps* caps);
+
+/* Build, on the device, everything the forward pass indexes by:
+ * cu_seqlens, per-token positions / flat slots / sequence ids, logit-row
+ * token indices, context lengths and the attention work lists.
+ * Positions follow runner.py:75 (start..start+qlen-1), slots follow
+ * gather_slots (attention.py:40-44), rows follow runner.py:86-90.
+ * A block id outside [0, num_blocks) or a context beyond the table marks the
+ * slot -1 and sets the device error flag (counter 7, below). */
+int vllt_build_batch_meta(const int32_t* step_record, const vllt_caps* caps, int32_t block_size,
+                          int32_t num_blocks, int32_t n_rep, void* meta, void* stream);
+
+/* Device pointers into the meta buffer (for callers that launch their own
+ * kernels on it): which = 0 counters[16], 1 cu_seqlens_q[S+1], 2 cu_rows[S+1],
+ * 3 ctx_lens[S], 4 positions[T], 5 slot_mapping[T], 6 logit-row token
+ * indices[R], 7 block tables [max_seqs][max_table_width]. NULL if unknown. */
+int32_t* vllt_meta_field(void* meta, const vllt_caps* caps, int32_t which);
+
+/* Counters: 0 S, 1 T, 2 R, 3 W, 4 single-query sequences, 5 query tiles,
+ * 6 max context, 7 error flags (bit 0 capacity, bit 1 block table / range). */
+
+/* ------------------------------------------------------------------------ */
+/* Attention                                                                */
+/* ------------------------------------------------------------------------ */
+
+/* Workspace bytes for vllt_paged_attention_varlen's split-K partials
+ * (0 when max_ctx is short enough that single-query sequences are not split). */
+int64_t vllt_attention_workspace_bytes(int32_t num_tokens, int32_t n_heads, int32_t head_dim,
+                                       int32_t max_ctx);
+
+/* Varlen causal paged attention over a ragged batch (decode, chunked
+ * prefill and speculative-verify rows mixed). Replaces paged_attention
+ * (vllmlite/attention.py:59-98) applied per sequence by the loop at
+ * vllmlite/model.py:105-112.
+ *   q    [num_tokens][n_heads][head_dim]   (dtype)
+ *   out  [num_tokens][n_heads][head_dim]   (dtype)
+ *   caches: one layer, layout in the file header (dtype)
+ *   block_tables [num_seqs][table_width], cu_seqlens_q [num_seqs+1],
+ *   ctx_lens [num_seqs] (tokens in the cache including this pass's).
+ * Query j of sequence s sits at position ctx_lens[s] - qlen_s + j and sees
+ * keys 0..that position; head h reads KV head h / (n_heads / n_kv).
+ * max_qlen and max_ctx bound the work launched. With a NULL or short
+ * workspace, long single-query contexts are walked by one CTA (no split-K). */
+int vllt_paged_attention_varlen(const void* q, const void* k_cache, const void* v_cache,
+                                const int32_t* block_tables, int32_t table_width,
+                                const int32_t* cu_seqlens_q, const int32_t* ctx_lens,
+                                int32_t num_seqs, int32_t num_tokens, int32_t max_qlen,
+                                int32_t max_ctx, int32_t n_heads, int32_t n_kv,
+                                int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                                float scale, int32_t dtype, void* out, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Layer pieces                                                             */
+/* ------------------------------------------------------------------------ */
+
+/* out[r] = x[idx[r]] / sqrt(mean(x[idx[r]]^2) + eps) * w; idx may be NULL
+ * (identity). fp32. Replaces rms_norm (vllmlite/model.py:17-19). */
+int vllt_rmsnorm(const float* x, const int32_t* idx, const float* w, float* out,
+                 int32_t rows, int32_t dim, float eps, void* stream);
+
+/* Interleaved-pair rotary embedding in place on x [T][heads][head_dim] (fp32)
+ * with tables cos/sin [max_pos][head_dim/2]. Replaces apply_rope
+ * (vllmlite/attention.py:28-37). */
+int vllt_rope(float* x, const int32_t* positions, const float* cos_t, const float* sin_t,
+              int32_t num_tokens, int32_t heads, int32_t head_dim, int32_t max_pos,
+              void* stream);
+
+/* C[M][N] = A[M][K] @ B[K][N] (fp32, row-major, CUDA-core FFMA, no TF32).
+ * The parity-mode GEMM behind every projection of vllmlite/model.py:98-120. */
+int vllt_sgemm(const float* A, const float* B, float* C, int32_t M, int32_t N, int32_t K,
+               void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Sampling (vllmlite/sampling.py:41-64, vllmlite/speculative.py:86-100)    */
+/* ------------------------------------------------------------------------ */
+
+/* Greedy pick per row with the reference's pre-steps: EOS masked to -inf in
+ * rows whose eos_mask[r] != 0 (min_tokens, sampling.py:51-52), repetition
+ * penalty on the tokens seen by the row (sampling.py:54, seen_bits[r] is a
+ * bitmap of ceil(vocab/32) words, may be NULL when penalty[r] == 1), then the
+ * first index of the maximum (np.argmax). logits [rows][ld] fp32. */
+int vllt_sample_greedy(const float* logits, int32_t rows, int32_t vocab, int32_t ld,
+                       const uint8_t* eos_mask, int32_t eos_id, const float* penalty,
+                       const uint32_t* seen_bits, int32_t* out_tokens, void* stream);
+
+/* Temperature / top-k / top-p sampling per row with a caller-provided uniform
+ * u[r] in [0,1): the kept nucleus follows sampling.py:23-33 (descending
+ * order, keep while the mass before a token is < p) and the token is the
+ * inverse-CDF pick of u over the renormalised kept probabilities. */
+int vllt_sample_top_p(const float* logits, int32_t rows, int32_t vocab, int32_t ld,
+                      const float* temperature, const int32_t* top_k, const float* top_p,
+                      const float* u, int32_t* out_tokens, void* stream);
+
+/* Speculative accept/reject for a batch of sequences. Sequence s owns logit
+ * rows [cu_rows[s], cu_rows[s+1]) = n_drafts[s] + 1 rows (total_rows =
+ * cu_rows[num_seqs], passed from the host); drafts are packed at
+ * draft_offsets[s]. Writes out_tokens[cu_rows[s] + i] (the emitted tokens)
+ * and n_accepted[s]; the number of emitted tokens is n_accepted[s] + 1.
+ * Follows verify (vllmlite/speculative.py:86-100). */
+int vllt_spec_verify(const float* logits, int32_t ld, int32_t vocab, const int32_t* cu_rows,
+                     int32_t total_rows, const int32_t* drafts, const int32_t* draft_offsets,
+                     int32_t num_seqs, int32_t* out_tokens, int32_t* n_accepted, void* stream);
+
+/* The accept rule alone over tokens already picked per row (e.g. by
+ * vllt_sample_greedy with its EOS mask / penalty): n_accepted[s] = length of
+ * the longest prefix where picks[cu_rows[s] + i] == drafts[draft_offsets[s] + i]
+ * (speculative.py:92-98). */
+int vllt_spec_accept(const int32_t* cu_rows, const int32_t* drafts, const int32_t* draft_offsets,
+                     int32_t num_seqs, const int32_t* picks, int32_t* n_accepted, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Whole forward pass (TinyLlama.forward, vllmlite/model.py:80-120)         */
+/* ------------------------------------------------------------------------ */
+
+typedef struct vllt_model_desc {
+  /* shape */
+  int32_t n_layers, n_heads, n_kv_heads, head_dim, d_model, d_ff, vocab, vocab_padded;
+  int32_t max_seq_len, block_size, num_blocks;
+  float rms_eps;
+  int32_t dtype; /* VLLT_F32 (parity mode) */
+  /* weights (device, fp32). Per-layer arrays hold n_layers host-side pointers:
+   *   wqkv[l]   [d_model][(n_heads + 2*n_kv_heads)*head_dim]  = [wq | wk | wv]
+   *   wo[l]     [n_heads*head_dim][d_model]
+   *   w_gu[l]   [d_model][2*d_ff], column 2j = w_gate[:, j], 2j+1 = w_up[:, j]
+   *   w_down[l] [d_ff][d_model]
+   *   lm_head   [d_model][vocab_padded] (zero columns past vocab)          */
+  const float* tok_emb;
+  const float* final_norm;
+  const float* lm_head;
+  const float* rope_cos; /* [max_seq_len][head_dim/2] */
+  const float* rope_sin;
+  const float* const* attn_norm;
+  const float* const* wqkv;
+  const float* const* wo;
+  const float* const* ffn_norm;
+  const float* const* w_gu;
+  const float* const* w_down;
+  /* KV cache base: [n_layers][num_blocks][n_kv][block_size][head_dim] */
+  void* k_cache;
+  void* v_cache;
+} vllt_model_desc;
+
+/* Upper bounds of one step, used to size grids (exact counts are read on the
+ * device). For eager calls pass the step's own values; a CUDA graph captured
+ * with some bounds replays correctly for every step within them. */
+typedef struct vllt_step_bounds {
+  int32_t tokens;      /* >= T */
+  int32_t rows;        /* >= R */
+  int32_t decode_seqs; /* >= sequences with a single query token */
+  int32_t tiles;       /* >= multi-token query tiles (16 (position, head) rows each) */
+  int32_t max_ctx;     /* >= longest context (start + qlen) */
+} vllt_step_bounds;
+
+/* Activation workspace bytes for the given capacities. */
+int64_t vllt_forward_workspace_bytes(const vllt_model_desc* m, const vllt_caps* caps);
+
+/* One batched forward pass over a packed step record already on the device:
+ * builds the batch metadata into `meta` (see vllt_build_batch_meta), embeds,
+ * runs every layer (RMSNorm -> QKV GEMM with RoPE and the K/V cache write
+ * fused in its epilogue -> paged attention -> o_proj + residual -> RMSNorm ->
+ * gate/up GEMM with SwiGLU -> down + residual), then the final RMSNorm and
+ * lm_head on the logit rows only. logits: [max_rows][vocab_padded] fp32;
+ * rows >= R are left untouched. */
+int vllt_forward(const vllt_model_desc* m, const int32_t* step_record, const vllt_caps* caps,
+                 const vllt_step_bounds* bounds, void* meta, void* workspace,
+                 int64_t workspace_bytes, float* logits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VLLT_H_ */

@@ -1,0 +1,306 @@
+"""GPU: every kernel through the C ABI against the oracle / golden vectors.
+
+Tolerances: fp32 kernels use the reference's own attention tolerance
+(rtol 1e-4, atol 1e-5, tests/test_attention.py:57 of the reference) or tighter;
+bf16 attention (fp32 accumulate, bf16 output) is checked against a float64
+oracle on the same bf16 inputs within rtol 2e-2, atol 2e-2. Integer and index
+work (slots, block copies, token picks) must be bit-exact.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import attention as A
+from oracle import model as OM
+from oracle import runner as OR
+from oracle import sampling as SP
+from tests import fixtures as F
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    return torch.device("cuda", 0)
+
+
+def to_lib_layout(cache, bs):
+    """Reference cache [slots, n_kv, D] -> library [NB, n_kv, bs, D]."""
+    slots, n_kv, D = cache.shape
+    return np.ascontiguousarray(cache.reshape(slots // bs, bs, n_kv, D).transpose(0, 2, 1, 3))
+
+
+def test_attention_golden_cases_dropin(dev):
+    """The NumPy drop-in paged_attention on every reference test case."""
+    from vllt.ops import paged_attention
+
+    for i, inp, want in F.attention_cases():
+        slots = A.table_slots(inp["block_ids"], inp["block_size"], inp["ctx"])
+        got = paged_attention(inp["q"], inp["cache_k"], inp["cache_v"], slots, inp["n_kv"], inp["scale"])
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-5, err_msg=f"case {i}")
+
+
+def test_attention_golden_cases_paged_layout(dev):
+    """Same cases through block tables in the library's paged layout."""
+    from vllt.ops import paged_attention_varlen
+
+    for i, inp, want in F.attention_cases():
+        bs = inp["block_size"]
+        ck = torch.from_numpy(to_lib_layout(inp["cache_k"], bs)).to(dev)
+        cv = torch.from_numpy(to_lib_layout(inp["cache_v"], bs)).to(dev)
+        q = torch.from_numpy(inp["q"]).to(dev)
+        got = paged_attention_varlen(q, ck, cv, np.asarray([inp["block_ids"]]), [0, q.shape[0]],
+                                     [inp["ctx"]], inp["scale"]).cpu().numpy()
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-5, err_msg=f"case {i}")
+
+
+def ragged_batch(rng, H, KV, D, bs, qlens, ctxs, dtype=np.float32):
+    nb_need = [(c + bs - 1) // bs for c in ctxs]
+    total = sum(nb_need) + 7
+    perm = rng.permutation(total)
+    tables, o = [], 0
+    for n in nb_need:
+        tables.append(perm[o:o + n].tolist())
+        o += n
+    W = max(nb_need)
+    tab = np.zeros((len(ctxs), W), np.int32)
+    for i, t in enumerate(tables):
+        tab[i, :len(t)] = t
+    ck = rng.standard_normal((total * bs, KV, D)).astype(np.float32)
+    cv = rng.standard_normal((total * bs, KV, D)).astype(np.float32)
+    q = rng.standard_normal((sum(qlens), H, D)).astype(np.float32)
+    if dtype != np.float32:  # round inputs to bf16 so both sides see the same values
+        r = lambda a: torch.from_numpy(a).bfloat16().float().numpy()
+        ck, cv, q = r(ck), r(cv), r(q)
+    return q, ck, cv, tables, tab
+
+
+@pytest.mark.parametrize("H,KV,D,bs,dtype", [
+    (8, 4, 48, 16, "f32"), (4, 2, 16, 4, "f32"), (6, 1, 8, 1, "f32"), (8, 8, 64, 16, "f32"),
+    (32, 8, 128, 16, "f32"), (32, 8, 128, 16, "bf16"), (8, 4, 48, 16, "bf16")])
+def test_attention_varlen_mixed_batch(dev, H, KV, D, bs, dtype):
+    """Decode, chunked-prefill and verify rows in one launch, including a
+    context long enough to take the split-K path."""
+    from vllt.ops import paged_attention_varlen
+
+    rng = np.random.default_rng(H * 100 + D + bs)
+    qlens = [1, 1, 7, 1, 33, 5, 1, 64, 2]
+    ctxs = [1, 300, 40, 1500, 33, 700, 17, 1100, 16]
+    npdt = np.float32 if dtype == "f32" else "bf16"
+    q, ck, cv, tables, tab = ragged_batch(rng, H, KV, D, bs, qlens, ctxs, npdt)
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    tq = torch.from_numpy(q).to(dev, tdt)
+    tk = torch.from_numpy(to_lib_layout(ck, bs)).to(dev, tdt)
+    tv = torch.from_numpy(to_lib_layout(cv, bs)).to(dev, tdt)
+    cu = np.concatenate([[0], np.cumsum(qlens)])
+    scale = 1.0 / np.sqrt(D)
+    got = paged_attention_varlen(tq, tk, tv, tab, cu, ctxs, scale).float().cpu().numpy()
+    for i, (ql, c) in enumerate(zip(qlens, ctxs)):
+        slots = A.table_slots(tables[i], bs, c)
+        if dtype == "f32":
+            want = A.paged_attention(q[cu[i]:cu[i + 1]], ck, cv, slots, KV, scale)
+            np.testing.assert_allclose(got[cu[i]:cu[i + 1]], want, rtol=1e-4, atol=1e-5, err_msg=f"seq {i}")
+        else:
+            want = A.dense_attention(q[cu[i]:cu[i + 1]], ck[slots], cv[slots], KV, scale)
+            np.testing.assert_allclose(got[cu[i]:cu[i + 1]], want, rtol=2e-2, atol=2e-2, err_msg=f"seq {i}")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_reshape_and_cache_is_exact(dev, dtype):
+    from vllt.ops import write_kv
+
+    rng = np.random.default_rng(1)
+    nb, KV, bs, D, T = 40, 4, 16, 48, 77
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    ref_k = rng.standard_normal((nb * bs, KV, D)).astype(np.float32)
+    ref_v = rng.standard_normal((nb * bs, KV, D)).astype(np.float32)
+    ref_k = torch.from_numpy(ref_k).to(tdt).float().numpy()
+    ref_v = torch.from_numpy(ref_v).to(tdt).float().numpy()
+    k = torch.from_numpy(rng.standard_normal((T, KV, D)).astype(np.float32)).to(tdt)
+    v = torch.from_numpy(rng.standard_normal((T, KV, D)).astype(np.float32)).to(tdt)
+    slots = rng.permutation(nb * bs)[:T]
+    slots[5] = -1  # skipped
+    ck = torch.from_numpy(to_lib_layout(ref_k, bs)).to(dev, tdt)
+    cv = torch.from_numpy(to_lib_layout(ref_v, bs)).to(dev, tdt)
+    write_kv(ck, cv, k.to(dev), v.to(dev), slots)
+    keep = slots >= 0
+    A.scatter_kv(ref_k, ref_v, k.float().numpy()[keep], v.float().numpy()[keep], slots[keep])
+    np.testing.assert_array_equal(ck.float().cpu().numpy(), to_lib_layout(ref_k, bs))
+    np.testing.assert_array_equal(cv.float().cpu().numpy(), to_lib_layout(ref_v, bs))
+
+
+def test_copy_blocks_is_exact(dev):
+    from vllt.ops import copy_blocks
+
+    rng = np.random.default_rng(2)
+    L, nb, KV, bs, D = 3, 20, 4, 16, 48
+    rk = rng.standard_normal((L, nb * bs, KV, D)).astype(np.float32)
+    rv = rng.standard_normal((L, nb * bs, KV, D)).astype(np.float32)
+    tk = torch.from_numpy(np.stack([to_lib_layout(rk[l], bs) for l in range(L)])).to(dev)
+    tv = torch.from_numpy(np.stack([to_lib_layout(rv[l], bs) for l in range(L)])).to(dev)
+    pairs = [(3, 7), (0, 19), (12, 4)]
+    copy_blocks(tk, tv, pairs)
+    OR.copy_blocks(rk, rv, pairs, bs)
+    np.testing.assert_array_equal(tk.cpu().numpy(), np.stack([to_lib_layout(rk[l], bs) for l in range(L)]))
+    np.testing.assert_array_equal(tv.cpu().numpy(), np.stack([to_lib_layout(rv[l], bs) for l in range(L)]))
+
+
+def test_rmsnorm_rope_sgemm(dev):
+    from vllt.ops import apply_rope, matmul, rms_norm
+    from vllt.model import rope_tables
+
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((37, 384)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(384)).astype(np.float32)
+    got = rms_norm(torch.from_numpy(x).to(dev), torch.from_numpy(w).to(dev)).cpu().numpy()
+    np.testing.assert_allclose(got, OM.rms_norm(x, w), rtol=2e-6, atol=1e-6)
+    idx = np.asarray([5, 0, 36, 5], np.int32)
+    got = rms_norm(torch.from_numpy(x).to(dev), torch.from_numpy(w).to(dev), idx=idx).cpu().numpy()
+    np.testing.assert_allclose(got, OM.rms_norm(x[idx], w), rtol=2e-6, atol=1e-6)
+
+    cos, sin = rope_tables(48, 512)
+    xr = rng.standard_normal((29, 8, 48)).astype(np.float32)
+    pos = rng.integers(0, 512, size=29)
+    t = torch.from_numpy(xr.copy()).to(dev)
+    apply_rope(t, pos, torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev))
+    np.testing.assert_array_equal(t.cpu().numpy(), A.rotate(xr, pos, cos, sin))
+
+    for M, N, K in ((1, 768, 384), (16, 2048, 384), (100, 384, 1024), (1024, 264, 384), (300, 64, 64)):
+        a = rng.standard_normal((M, K)).astype(np.float32)
+        b = rng.standard_normal((K, N)).astype(np.float32)
+        got = matmul(torch.from_numpy(a).to(dev), torch.from_numpy(b).to(dev)).cpu().numpy()
+        want = a.astype(np.float64) @ b.astype(np.float64)
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-4 * np.sqrt(K) * 1e-1)
+
+
+def test_sampling_kernels_match_reference(dev):
+    from vllt.ops import greedy, sample_top_p, verify
+
+    z = F.load("sampling.npz")
+    rows = z["rows"]
+    R, V = rows.shape
+    # greedy with min_tokens EOS mask and repetition penalty (sampling.py:41-57)
+    mask = np.zeros(R, np.uint8)
+    pen = np.ones(R, np.float32)
+    bits = np.zeros((R, (V + 31) // 32), np.uint32)
+    o = 0
+    for (i, p, mint, ngen, tok, nseen) in z["greedy"]:
+        i = int(i)
+        mask[i] = 1 if ngen < mint else 0
+        pen[i] = p
+        for t in np.unique(z["greedy_seen"][o:o + int(nseen)]):
+            bits[i, t >> 5] |= np.uint32(1) << np.uint32(t & 31)
+        o += int(nseen)
+    got = greedy(torch.from_numpy(rows).to(dev), eos_mask=torch.from_numpy(mask).to(dev),
+                 penalty=torch.from_numpy(pen).to(dev), seen_bits=torch.from_numpy(bits).to(dev)).cpu().numpy()
+    assert got.tolist() == [int(t) for t in z["greedy"][:, 4]]
+    # batched verify (speculative.py:86-100)
+    k, nt, acc = z["verify_k"], z["verify_ntok"], z["verify_accepted"]
+    cu = np.concatenate([[0], np.cumsum(k + 1)])
+    doff = np.concatenate([[0], np.cumsum(k)[:-1]])
+    toks, a = verify(torch.from_numpy(z["verify_logits"]).to(dev), cu, z["verify_drafts"], doff)
+    toks, a = toks.cpu().numpy(), a.cpu().numpy()
+    assert a.tolist() == acc.tolist()
+    to = 0
+    for s in range(len(k)):
+        assert toks[cu[s]:cu[s] + nt[s]].tolist() == z["verify_tokens"][to:to + nt[s]].tolist()
+        to += nt[s]
+    # top-p: the drawn token always lies in the reference's keep set, and a
+    # draw with the same uniform lands on numpy's choice() pick
+    ps = z["top_p"]
+    for j, p in enumerate(ps):
+        u = np.random.default_rng(j).random(R).astype(np.float32)
+        out = sample_top_p(torch.from_numpy(rows).to(dev), torch.ones(R, device=dev),
+                           torch.zeros(R, dtype=torch.int32, device=dev), torch.full((R,), float(p), device=dev),
+                           torch.from_numpy(u).to(dev)).cpu().numpy()
+        for i in range(R):
+            keep = z["keep"][i, j]
+            assert keep[out[i]], (i, p)
+            lg = np.where(keep, rows[i], -np.inf)
+            pr = np.exp(lg - lg.max())
+            pr /= pr.sum()
+            cdf = np.cumsum(pr.astype(np.float64))
+            cdf /= cdf[-1]
+            want = int(np.searchsorted(cdf, float(u[i]), side="right"))
+            if abs(cdf[min(want, V - 1)] - u[i]) > 1e-5 and (want == 0 or abs(cdf[want - 1] - u[i]) > 1e-5):
+                assert out[i] == want, (i, p)
+
+
+def test_batch_meta_matches_reference_flatten(dev):
+    """Device-built positions / slots / logit rows equal runner.py:66-90."""
+    import ctypes
+
+    from vllt import _lib
+    from vllt.runner import pack_step, tile_positions
+
+    L = _lib.lib()
+    for seqs, cow, _ in F.replay_steps("replay_spec.npz"):
+        bs = 4
+        out = F.as_scheduler_output(seqs, cow)
+        rec, bounds, rows, (S, T, R, W) = pack_step(out, bs, 512, 261, 512, tile_positions(2))
+        caps = _lib.Caps(S + 3, T + 5, R + 2, W + 1)
+        meta = torch.zeros(L.vllt_meta_bytes(ctypes.byref(caps)) // 4, dtype=torch.int32, device=dev)
+        drec = torch.from_numpy(rec).to(dev)
+        _lib.check(L.vllt_build_batch_meta(drec.data_ptr(), ctypes.byref(caps), bs, 512, 2, meta.data_ptr(),
+                                           _lib.stream_handle()))
+        torch.cuda.synchronize()
+        base = meta.data_ptr()
+
+        def field(i, n):
+            off = (L.vllt_meta_field(ctypes.c_void_p(base), ctypes.byref(caps), i) - base) // 4
+            return meta[off:off + n].cpu().numpy()
+
+        cnt = field(0, 16)
+        assert cnt[:4].tolist() == [S, T, R, W] and cnt[7] == 0
+        tok, pos, smeta, last, orows = OR.flatten(seqs, bs)
+        assert field(4, T).tolist() == pos.tolist()
+        wslots = np.concatenate([m[2] for m in smeta])
+        assert field(5, T).tolist() == wslots.tolist()
+        assert field(6, R).tolist() == last.tolist()
+        assert field(1, S + 1).tolist() == [0] + np.cumsum([s["n"] for s in seqs]).tolist()
+        assert cnt[4] == bounds.decode_seqs and cnt[5] == bounds.tiles
+
+
+def test_batch_meta_flags_bad_tables_without_faulting(dev):
+    import ctypes
+
+    from vllt import _lib
+
+    L = _lib.lib()
+    caps = _lib.Caps(4, 16, 16, 4)
+    rec = np.asarray([1, 3, 1, 1, 0, 3, 1, 256, 1, 2, 777], np.int32)  # block 777 >= num_blocks
+    meta = torch.zeros(L.vllt_meta_bytes(ctypes.byref(caps)) // 4, dtype=torch.int32, device=dev)
+    _lib.check(L.vllt_build_batch_meta(torch.from_numpy(rec).to(dev).data_ptr(), ctypes.byref(caps), 16, 64, 2,
+                                       meta.data_ptr(), _lib.stream_handle()))
+    cnt = meta[:16].cpu().numpy()
+    assert cnt[7] & 2
+    rec_big = np.asarray([9, 3, 1, 1], np.int32)  # more sequences than capacity
+    rec_big = np.concatenate([rec_big, np.zeros(40, np.int32)])
+    _lib.check(L.vllt_build_batch_meta(torch.from_numpy(rec_big).to(dev).data_ptr(), ctypes.byref(caps), 16, 64,
+                                       2, meta.data_ptr(), _lib.stream_handle()))
+    assert meta[7].item() & 1
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_attention_decode_split_k(dev, dtype):
+    """A pure decode batch with contexts long enough to split across CTAs."""
+    from vllt.ops import paged_attention_varlen
+
+    rng = np.random.default_rng(11)
+    H, KV, D, bs = 32, 8, 128, 16
+    ctxs = [1, 513, 4096, 2000, 17, 1024, 3333]
+    qlens = [1] * len(ctxs)
+    q, ck, cv, tables, tab = ragged_batch(rng, H, KV, D, bs, qlens, ctxs, np.float32 if dtype == "f32" else "bf16")
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    got = paged_attention_varlen(torch.from_numpy(q).to(dev, tdt), torch.from_numpy(to_lib_layout(ck, bs)).to(dev, tdt),
+                                 torch.from_numpy(to_lib_layout(cv, bs)).to(dev, tdt), tab,
+                                 np.arange(len(ctxs) + 1), ctxs, 1.0 / np.sqrt(D)).float().cpu().numpy()
+    for i, c in enumerate(ctxs):
+        slots = A.table_slots(tables[i], bs, c)
+        want = A.dense_attention(q[i:i + 1], ck[slots], cv[slots], KV, 1.0 / np.sqrt(D))
+        tol = 1e-4 if dtype == "f32" else 2e-2
+        np.testing.assert_allclose(got[i:i + 1], want, rtol=tol, atol=tol / 10 if dtype == "f32" else tol)

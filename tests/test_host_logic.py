@@ -1,0 +1,139 @@
+"""CPU: host-side logic of the product (no device work).
+
+  * the C ABI library loads and exports every symbol include/vllt.h declares;
+  * the step record packed by the runner describes the same flatten as the
+    reference's ModelRunner.execute (oracle.runner.flatten);
+  * the seeded workloads and weights of the product equal the reference's.
+"""
+
+import hashlib
+import os
+import re
+
+import numpy as np
+import pytest
+
+from oracle import model as OM
+from oracle import runner as OR
+from tests import fixtures as F
+from tests.conftest import ROOT, needs_vllmlite
+
+
+def header_functions():
+    src = open(os.path.join(ROOT, "include", "vllt.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(vllt_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    import ctypes
+
+    from vllt import _lib
+
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    names = header_functions()
+    assert len(names) >= 18
+    for n in names:
+        assert hasattr(lib, n), f"libvllt.so does not export {n}"
+    # and the Python binding declares a signature for each of them
+    assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
+
+
+def test_library_calls_reject_bad_arguments_without_a_gpu():
+    import ctypes
+
+    from vllt import _lib
+
+    L = _lib.lib()
+    assert L.vllt_version() >= 100
+    # argument validation happens on the host before any launch
+    rc = L.vllt_reshape_and_cache(None, None, None, None, None, 3, 0, 8, 16, 4, 0, None)
+    assert rc == _lib.VLLT_ERR_ARG
+    assert b"bad sizes" in L.vllt_last_error()
+    assert L.vllt_sgemm(None, None, None, 4, 4, 4, None) == _lib.VLLT_ERR_ARG
+    caps = _lib.Caps(16, 1024, 1024, 32)
+    assert L.vllt_meta_bytes(ctypes.byref(caps)) > 0
+    assert L.vllt_meta_bytes(ctypes.byref(_lib.Caps(0, 1, 1, 1))) == -1
+
+
+def _record_to_flatten(rec):
+    S, T, R, W = (int(x) for x in rec[:4])
+    o = 4
+    starts, qlens, counts = rec[o:o + S], rec[o + S:o + 2 * S], rec[o + 2 * S:o + 3 * S]
+    o += 3 * S
+    toks = rec[o:o + T]
+    tabs = rec[o + T:o + T + S * W].reshape(S, W)
+    return S, T, R, W, starts, qlens, counts, toks, tabs
+
+
+@pytest.mark.parametrize("name,bs", [("replay_bench.npz", 16), ("replay_spec.npz", 4)])
+def test_packed_record_matches_reference_flatten(name, bs):
+    from vllt.runner import pack_step, tile_positions
+
+    for seqs, cow, want in F.replay_steps(name):
+        out = F.as_scheduler_output(seqs, cow)
+        rec, bounds, rows, (S, T, R, W) = pack_step(out, bs, 512, 261, 512, tile_positions(2))
+        tok, pos, meta, last, orows = OR.flatten(seqs, bs)
+        S2, T2, R2, W2, starts, qlens, counts, toks, tabs = _record_to_flatten(rec)
+        assert (S2, T2, R2) == (len(seqs), len(tok), len(last)) == (S, T, R)
+        assert rows == orows
+        assert toks.tolist() == tok.tolist()
+        # positions and slots the device derives from the record
+        for i, (off, n, wslots, rslots) in enumerate(meta):
+            p = np.arange(starts[i], starts[i] + qlens[i])
+            assert p.tolist() == pos[off:off + n].tolist()
+            slots = tabs[i][p // bs] * bs + p % bs
+            assert slots.tolist() == wslots.tolist()
+        assert want.shape[0] == R
+        assert bounds.tokens == T and bounds.rows == R
+        assert bounds.decode_seqs == int((qlens == 1).sum())
+
+
+def test_pack_rejects_what_the_reference_cannot_index():
+    from vllt.runner import pack_step
+
+    good = dict(start=0, n=3, count=1, tokens=[256, 1, 2], block_ids=[5], drafts=[])
+    with pytest.raises(IndexError):
+        pack_step(F.as_scheduler_output([dict(good, block_ids=[9999])]), 16, 512, 261, 512, 8)
+    with pytest.raises(IndexError):
+        pack_step(F.as_scheduler_output([dict(good, tokens=[256, 1, 999])]), 16, 512, 261, 512, 8)
+    with pytest.raises(IndexError):
+        pack_step(F.as_scheduler_output([dict(good, n=20, tokens=list(range(20)))]), 16, 512, 261, 512, 8)
+    with pytest.raises(IndexError):
+        pack_step(F.as_scheduler_output([dict(good, start=510, tokens=[0] * 3)]), 16, 512, 261, 512, 8)
+
+
+def test_product_seeded_weights_equal_reference():
+    from vllt.model import seeded_weights
+
+    for name in ("tiny", "bench"):
+        man = F.weights_manifest()[name]
+        cfg = OM.Shape(vocab_size=261, **man["shape"])
+        w = seeded_weights(cfg)
+        got = {k: hashlib.sha256(np.ascontiguousarray(v).tobytes()).hexdigest() for k, v in w.items()}
+        assert got == man["sha256"]
+
+
+def test_product_rope_tables_equal_reference():
+    from vllt.model import rope_tables
+
+    z = F.load("rope.npz")
+    for key in z.files:
+        if key.startswith("cos_"):
+            _, D, P = key.split("_")
+            c, s = rope_tables(int(D), int(P))
+            np.testing.assert_array_equal(c, z[key])
+            np.testing.assert_array_equal(s, z[f"sin_{D}_{P}"])
+
+
+@needs_vllmlite
+def test_workloads_equal_reference_generator():
+    from vllt.workloads import mixed_workload
+
+    z = F.load("workload.npz")
+    for name, prefix in (("mixed", 0), ("shared", 256)):
+        reqs = mixed_workload(48, 0, prefix)
+        lens = [len(r[1]) for r in reqs]
+        assert lens == z[f"{name}_lens"].tolist()
+        assert [t for r in reqs for t in r[1]] == z[f"{name}_tokens"].tolist()
+        assert [r[2].max_tokens for r in reqs] == z[f"{name}_max_tokens"].tolist()

@@ -1,0 +1,191 @@
+// On-device batch flatten: the per-step bookkeeping of ModelRunner.execute
+// (vllmlite/runner.py:66-90) and gather_slots (vllmlite/attention.py:40-44).
+//
+// One CTA of 1024 threads: the work is a few thousand integer ops, so a single
+// CTA (no grid sync, no second launch) has the lowest latency.
+
+#include "meta.cuh"
+
+namespace vllt {
+
+namespace {
+
+constexpr int kThreads = 1024;
+
+// Block-wide exclusive scan of an int4 (four independent counters).
+__device__ int4 block_exclusive_scan(int4 v, int4* warp_tot, int4* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int4 incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int4 n;
+    n.x = __shfl_up_sync(0xffffffffu, incl.x, o);
+    n.y = __shfl_up_sync(0xffffffffu, incl.y, o);
+    n.z = __shfl_up_sync(0xffffffffu, incl.z, o);
+    n.w = __shfl_up_sync(0xffffffffu, incl.w, o);
+    if (lane >= o) { incl.x += n.x; incl.y += n.y; incl.z += n.z; incl.w += n.w; }
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int4 t = warp_tot[lane];
+    int4 it = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int4 n;
+      n.x = __shfl_up_sync(0xffffffffu, it.x, o);
+      n.y = __shfl_up_sync(0xffffffffu, it.y, o);
+      n.z = __shfl_up_sync(0xffffffffu, it.z, o);
+      n.w = __shfl_up_sync(0xffffffffu, it.w, o);
+      if (lane >= o) { it.x += n.x; it.y += n.y; it.z += n.z; it.w += n.w; }
+    }
+    warp_tot[lane] = make_int4(it.x - t.x, it.y - t.y, it.z - t.z, it.w - t.w);
+    if (lane == 31) *total = it;
+  }
+  __syncthreads();
+  int4 base = warp_tot[warp];
+  int4 r = make_int4(base.x + incl.x - v.x, base.y + incl.y - v.y, base.z + incl.z - v.z,
+                     base.w + incl.w - v.w);
+  __syncthreads();
+  return r;
+}
+
+// Largest i in [0, n) with a[i] <= key (a ascending, a[0] == 0 <= key).
+__device__ __forceinline__ int upper_index(const int32_t* a, int n, int key) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (a[mid] <= key) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __restrict__ rec,
+                                                              MetaLayout L, int bs, int num_blocks,
+                                                              int qp, int32_t* __restrict__ meta) {
+  __shared__ int4 warp_tot[32];
+  __shared__ int4 total;
+  __shared__ int s_max_ctx, s_max_q, s_err;
+  const int S = rec[0], T = rec[1], R = rec[2], W = rec[3];
+  int32_t* cnt = meta;
+  const bool fits = S >= 0 && T >= 0 && R >= 0 && W >= 0 && S <= L.S_cap && T <= L.T_cap &&
+                    R <= L.R_cap && W <= L.W_cap;
+  if (!fits) {  // uniform across the CTA: every thread takes this branch
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < kCntWords; ++i) cnt[i] = 0;
+      cnt[kCntError] = 1;
+    }
+    return;
+  }
+  const int32_t* start = rec + 4;
+  const int32_t* qlen = start + S;
+  const int32_t* count = qlen + S;
+  const int32_t* tokens = count + S;
+  const int32_t* tables = tokens + T;
+  int32_t* cu_q = meta + L.cu_q;
+  int32_t* cu_rows = meta + L.cu_rows;
+  int32_t* ctx = meta + L.ctx;
+  int32_t* mstart = meta + L.start;
+  if (threadIdx.x == 0) { s_max_ctx = 0; s_max_q = 0; s_err = 0; }
+  __syncthreads();
+
+  // Phase 1: exclusive scans over sequences of (qlen, count, is_decode, tiles).
+  int32_t* cu_tiles = meta + L.cu_tiles;
+  int4 carry = make_int4(0, 0, 0, 0);
+  for (int base = 0; base < S; base += kThreads) {
+    const int s = base + threadIdx.x;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (s < S) {
+      const int q = qlen[s];
+      v = make_int4(q, count[s], q == 1 ? 1 : 0, q > 1 ? ceil_div(q, qp) : 0);
+      const int c = start[s] + q;
+      atomicMax(&s_max_ctx, c);
+      atomicMax(&s_max_q, q);
+      if (q < 1 || count[s] < 1 || count[s] > q || start[s] < 0 || c > W * bs) atomicOr(&s_err, 2);
+    }
+    int4 ex = block_exclusive_scan(v, warp_tot, &total);
+    if (s < S) {
+      cu_q[s] = carry.x + ex.x;
+      cu_rows[s] = carry.y + ex.y;
+      ctx[s] = start[s] + qlen[s];
+      mstart[s] = start[s];
+      cu_tiles[s] = carry.w + ex.w;
+      if (v.z) meta[L.dec_seq + carry.z + ex.z] = s;
+    }
+    carry.x += total.x; carry.y += total.y; carry.z += total.z; carry.w += total.w;
+  }
+  if (threadIdx.x == 0) {
+    cu_q[S] = carry.x;
+    cu_rows[S] = carry.y;
+    cu_tiles[S] = carry.w;
+    if (carry.x != T || carry.y != R || carry.w > L.tiles_cap) atomicOr(&s_err, 1);
+  }
+  __syncthreads();
+  if (s_err) {  // uniform: nothing downstream may index with inconsistent counts
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < kCntWords; ++i) cnt[i] = 0;
+      cnt[kCntError] = s_err;
+    }
+    return;
+  }
+
+  // Phase 2: block tables into the fixed-width copy, validated.
+  for (int i = threadIdx.x; i < S * W; i += kThreads) {
+    const int s = i / W, b = i % W;
+    int blk = tables[i];
+    const int used = ceil_div(ctx[s], bs);
+    if (b < used && (blk < 0 || blk >= num_blocks)) { atomicOr(&s_err, 2); blk = -1; }
+    meta[L.tables + (int64_t)s * L.W_cap + b] = blk;
+  }
+  __syncthreads();
+
+  // Phase 3: per token -> sequence, position, flat slot (runner.py:75, :83-84).
+  const int Tv = min(T, cu_q[S]);
+  for (int t = threadIdx.x; t < Tv; t += kThreads) {
+    const int s = upper_index(cu_q, S + 1, t);
+    const int p = start[s] + (t - cu_q[s]);
+    const int b = p / bs;  // p >= 0 and p < W * bs were validated in phase 1
+    const int blk = b < W ? meta[L.tables + (int64_t)s * L.W_cap + b] : -1;
+    meta[L.pos + t] = p;
+    meta[L.tok_seq + t] = s;
+    meta[L.tokens + t] = tokens[t];
+    meta[L.slot + t] = blk < 0 ? -1 : blk * bs + p % bs;
+  }
+  // Phase 4: logit rows = the last `count` tokens of each sequence (runner.py:86-90).
+  const int Rv = min(R, cu_rows[S]);
+  for (int r = threadIdx.x; r < Rv; r += kThreads) {
+    const int s = upper_index(cu_rows, S + 1, r);
+    meta[L.rows + r] = cu_q[s] + qlen[s] - count[s] + (r - cu_rows[s]);
+  }
+  // Phase 5: multi-token query tiles (seq, first query index).
+  const int n_tiles = cu_tiles[S];
+  for (int i = threadIdx.x; i < n_tiles; i += kThreads) {
+    const int s = upper_index(cu_tiles, S + 1, i);
+    meta[L.tile_seq + i] = s;
+    meta[L.tile_q0 + i] = (i - cu_tiles[s]) * qp;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    cnt[kCntSeqs] = S;
+    cnt[kCntTokens] = T;
+    cnt[kCntRows] = R;
+    cnt[kCntWidth] = W;
+    cnt[kCntDecode] = carry.z;
+    cnt[kCntTiles] = carry.w;
+    cnt[kCntMaxCtx] = s_max_ctx;
+    cnt[kCntMaxQlen] = s_max_q;
+    cnt[kCntError] = s_err;  // table errors (bit 1) leave the step runnable: slots are -1
+  }
+}
+
+}  // namespace
+
+int build_batch_meta(const int32_t* rec, const MetaLayout& L, int bs, int num_blocks, int n_rep,
+                     int32_t* meta, cudaStream_t st) {
+  VLLT_REQUIRE(rec && meta, "build_batch_meta: null pointer");
+  VLLT_REQUIRE(bs > 0 && num_blocks > 0 && n_rep > 0, "build_batch_meta: bad sizes");
+  build_meta_kernel<<<1, kThreads, 0, st>>>(rec, L, bs, num_blocks, tile_positions(n_rep), meta);
+  return check_launch("build_batch_meta");
+}
+
+}  // namespace vllt

@@ -1,0 +1,112 @@
+// Row-wise layer pieces: RMSNorm (optionally gathering rows), token embedding,
+// standalone RoPE.
+
+#include "common.cuh"
+
+namespace vllt {
+
+namespace {
+
+// One warp per output row. out = x / sqrt(mean(x^2) + eps) * w, the order of
+// vllmlite/model.py:17-19 (a true division and a true square root; no rsqrt).
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const int32_t* __restrict__ idx,
+                               const float* __restrict__ w, float* __restrict__ out, int rows_cap,
+                               const int32_t* __restrict__ rows_dev, int dim, float eps) {
+  const int rows = rows_dev ? min(*rows_dev, rows_cap) : rows_cap;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int src = idx ? idx[r] : r;
+  const float* xr = x + (int64_t)src * dim;
+  float ss = 0.f;
+  for (int c = lane * 4; c < dim; c += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + c);
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  ss = warp_sum(ss);
+  const float denom = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
+  float* orow = out + (int64_t)r * dim;
+  for (int c = lane * 4; c < dim; c += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + c);
+    const float4 g = *reinterpret_cast<const float4*>(w + c);
+    float4 o;
+    o.x = __fmul_rn(__fdiv_rn(v.x, denom), g.x);
+    o.y = __fmul_rn(__fdiv_rn(v.y, denom), g.y);
+    o.z = __fmul_rn(__fdiv_rn(v.z, denom), g.z);
+    o.w = __fmul_rn(__fdiv_rn(v.w, denom), g.w);
+    *reinterpret_cast<float4*>(orow + c) = o;
+  }
+}
+
+// x[t] = emb[token[t]] (vllmlite/model.py:93). Out-of-range ids give zeros.
+__global__ void embed_kernel(const float* __restrict__ emb, const int32_t* __restrict__ tok,
+                             float* __restrict__ x, int T_cap, const int32_t* __restrict__ T_dev,
+                             int dim, int vocab) {
+  const int T = T_dev ? min(*T_dev, T_cap) : T_cap;
+  const int vec = dim / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)T * vec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / vec), c = (int)(i % vec) * 4;
+    const int id = tok[t];
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (id >= 0 && id < vocab) v = *reinterpret_cast<const float4*>(emb + (int64_t)id * dim + c);
+    *reinterpret_cast<float4*>(x + (int64_t)t * dim + c) = v;
+  }
+}
+
+// In-place interleaved-pair rotation (vllmlite/attention.py:28-37).
+__global__ void rope_kernel(float* __restrict__ x, const int32_t* __restrict__ positions,
+                            const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                            int T, int heads, int D, int max_pos) {
+  const int half = D / 2;
+  const int64_t total = (int64_t)T * heads * half;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int pi = (int)(i % half);
+    const int64_t th = i / half;
+    const int t = (int)(th / heads);
+    const int p = min(max(positions[t], 0), max_pos - 1);
+    const float c = cos_t[(int64_t)p * half + pi], s = sin_t[(int64_t)p * half + pi];
+    float* e = x + th * D + 2 * pi;
+    const float x1 = e[0], x2 = e[1];
+    e[0] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    e[1] = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+  }
+}
+
+}  // namespace
+
+int rmsnorm(const float* x, const int32_t* idx, const float* w, float* out, int rows_cap,
+            const int32_t* rows_dev, int dim, float eps, cudaStream_t st) {
+  if (rows_cap <= 0) return VLLT_OK;
+  VLLT_REQUIRE(dim % 4 == 0, "rmsnorm: dim must be a multiple of 4");
+  const int threads = 256;
+  const int blocks = ceil_div(rows_cap * 32, threads);
+  rmsnorm_kernel<<<blocks, threads, 0, st>>>(x, idx, w, out, rows_cap, rows_dev, dim, eps);
+  return check_launch("rmsnorm");
+}
+
+int embed(const float* emb, const int32_t* tok, float* x, int T_cap, const int32_t* T_dev, int dim,
+          int vocab, cudaStream_t st) {
+  if (T_cap <= 0) return VLLT_OK;
+  VLLT_REQUIRE(dim % 4 == 0, "embed: dim must be a multiple of 4");
+  const int64_t vecs = (int64_t)T_cap * dim / 4;
+  const int blocks = (int)std::min<int64_t>((vecs + 255) / 256, 148 * 8);
+  embed_kernel<<<blocks, 256, 0, st>>>(emb, tok, x, T_cap, T_dev, dim, vocab);
+  return check_launch("embed");
+}
+
+int rope(float* x, const int32_t* positions, const float* cos_t, const float* sin_t, int T,
+         int heads, int D, int max_pos, cudaStream_t st) {
+  if (T <= 0) return VLLT_OK;
+  VLLT_REQUIRE(D % 2 == 0, "rope: head_dim must be even");
+  const int64_t total = (int64_t)T * heads * (D / 2);
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
+  rope_kernel<<<blocks, 256, 0, st>>>(x, positions, cos_t, sin_t, T, heads, D, max_pos);
+  return check_launch("rope");
+}
+
+}  // namespace vllt

@@ -1,0 +1,228 @@
+"""CudaRunner: the B200 forward pass behind vllm-lite's ModelRunner interface.
+
+Drop-in for `vllmlite.runner.NumpyRunner` (vllmlite/runner.py:35-100): same
+constructor arguments (ModelConfig, CacheConfig), same
+`execute(SchedulerOutput) -> (logits float32 [n_rows, V], rows)` contract,
+`vocab_size` and `cache_bytes`. It
+  * applies `out.cow` before any KV write (runner.py:63-64) with one copy kernel;
+  * packs the step (per-sequence start / qlen / logit count, the pushed token
+    ids and the block tables) into one int32 record, uploads it with one
+    host-to-device copy, and lets the device build positions, slots and rows
+    (runner.py:66-90);
+  * runs the whole TinyLlama forward (model.py:80-120) in libvllt with one call;
+  * downloads only the logit rows.
+
+There is no CPU fallback: without a CUDA device or without libvllt.so the
+constructor raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import numpy as np
+
+from . import _lib
+from ._lib import Caps, ModelDesc, StepBounds, check, lib
+from .model import DeviceWeights, seeded_weights
+
+try:  # the plug-in ABC of the host engine, when vllm-lite is importable
+    from vllmlite.runner import ModelRunner as _Base
+except Exception:  # pragma: no cover - standalone use of the runner
+    from abc import ABC as _Base
+
+EOS_ID = 257  # ByteTokenizer.eos_id (vllmlite/tokenizer.py:10)
+
+
+def tile_positions(n_rep: int) -> int:
+    """Query positions per attention tile (16 (position, head) rows)."""
+    return 1 if n_rep >= 16 else 16 // n_rep
+
+
+def pack_step(out, block_size: int, num_blocks: int, vocab: int, max_pos: int, qp: int):
+    """Host side of the batch flatten: (record int32 words, StepBounds, rows, (S, T, R, W)).
+
+    Reads exactly what vllmlite/runner.py:72-90 reads: item.start_pos,
+    item.num_tokens, seq.token_ids, seq.draft_token_ids, seq.table.block_ids.
+    The record layout is documented in include/vllt.h. Metadata that the
+    reference would fail on (numpy IndexError) raises here, before anything
+    reaches the device.
+    """
+    items = out.scheduled
+    S = len(items)
+    starts = np.empty(S, np.int64)
+    qlens = np.empty(S, np.int64)
+    counts = np.empty(S, np.int64)
+    toks, tables = [], []
+    for i, item in enumerate(items):
+        seq = item.seq
+        start, n = item.start_pos, item.num_tokens
+        starts[i], qlens[i] = start, n
+        counts[i] = min(1 + len(seq.draft_token_ids), n)
+        toks.append(seq.token_ids[start:start + n])
+        tables.append(seq.table.block_ids)
+    T = int(qlens.sum())
+    R = int(counts.sum())
+    W = max((len(t) for t in tables), default=1) or 1
+    ctx = starts + qlens
+    if S and qlens.min() < 1:
+        raise ValueError("a scheduled sequence has no tokens")
+    if S and int(ctx.max()) > max_pos:
+        raise IndexError(f"position {int(ctx.max()) - 1} beyond max_seq_len {max_pos}")
+    flat_tok = np.fromiter((t for seg in toks for t in seg), np.int64, T)
+    if T and (flat_tok.min() < 0 or flat_tok.max() >= vocab):
+        raise IndexError("token id out of the vocabulary")
+    tab = np.zeros((S, W), np.int64)
+    for i, t in enumerate(tables):
+        if len(t) * block_size < ctx[i]:
+            raise IndexError(f"block table of sequence {i} too short for {int(ctx[i])} positions")
+        tab[i, :len(t)] = t
+    if tab.size and (tab.min() < 0 or tab.max() >= num_blocks):
+        raise IndexError("block id out of range")
+    rec = np.concatenate([np.asarray([S, T, R, W], np.int64), starts, qlens, counts, flat_tok,
+                          tab.reshape(-1)]).astype(np.int32)
+    multi = qlens[qlens > 1]
+    bounds = StepBounds(T, R, int((qlens == 1).sum()), int(np.sum((multi + qp - 1) // qp)),
+                        int(ctx.max()) if S else 1)
+    rows, r0 = [], 0
+    for c in counts:
+        rows.append((r0, int(c)))
+        r0 += int(c)
+    return rec, bounds, rows, (S, T, R, W)
+
+
+class CudaRunner(_Base):
+    """fp32 parity-mode forward pass on one GPU."""
+
+    def __init__(self, model_cfg, cache_cfg, sched_cfg=None, *, weights=None, device=None,
+                 max_seqs: int | None = None, max_tokens: int | None = None):
+        import torch
+
+        if not torch.cuda.is_available():
+            raise RuntimeError("CudaRunner needs a CUDA device; there is no CPU fallback")
+        self.torch = torch
+        self.L = lib()
+        self.model_cfg = model_cfg
+        self.block_size = cache_cfg.block_size
+        self.num_blocks = cache_cfg.num_blocks
+        self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.head_dim = model_cfg.d_model // model_cfg.n_heads
+        self.n_rep = model_cfg.n_heads // model_cfg.n_kv_heads
+        self.qp = tile_positions(self.n_rep)
+        with torch.cuda.device(self.dev):
+            w = weights if weights is not None else seeded_weights(model_cfg)
+            self.w = DeviceWeights(model_cfg, w, self.dev)
+            shape = (model_cfg.n_layers, self.num_blocks, model_cfg.n_kv_heads, self.block_size, self.head_dim)
+            self.cache_k = torch.zeros(shape, dtype=torch.float32, device=self.dev)
+            self.cache_v = torch.zeros(shape, dtype=torch.float32, device=self.dev)
+        self._ptrs = self.w.pointer_arrays()
+        self.desc = self._make_desc()
+        self.caps = Caps(0, 0, 0, 0)
+        seqs = max_seqs or (sched_cfg.max_seqs if sched_cfg is not None else 64)
+        toks = max_tokens or (sched_cfg.max_batched_tokens if sched_cfg is not None else 2048)
+        self._reserve(seqs, toks, toks, self._table_width_for(model_cfg.max_seq_len))
+        self.steps = 0
+        self.h2d_bytes = 0  # host->device bytes copied by execute()/launch()
+        self.d2h_bytes = 0  # device->host bytes copied by execute()
+
+    # ---- ModelRunner properties ------------------------------------------------
+    @property
+    def vocab_size(self) -> int:
+        return self.model_cfg.vocab_size
+
+    @property
+    def cache_bytes(self) -> int:
+        return self.cache_k.numel() * 4 * 2
+
+    # ---- buffers -----------------------------------------------------------------
+    def _table_width_for(self, ctx: int) -> int:
+        return max(1, math.ceil(ctx / self.block_size))
+
+    def _make_desc(self) -> ModelDesc:
+        cfg, w, p = self.model_cfg, self.w, self._ptrs
+        d = ModelDesc()
+        d.n_layers, d.n_heads, d.n_kv_heads = cfg.n_layers, cfg.n_heads, cfg.n_kv_heads
+        d.head_dim, d.d_model, d.d_ff = self.head_dim, cfg.d_model, cfg.d_ff
+        d.vocab, d.vocab_padded = cfg.vocab_size, w.vocab_padded
+        d.max_seq_len, d.block_size, d.num_blocks = w.rope_len, self.block_size, self.num_blocks
+        d.rms_eps, d.dtype = 1e-5, _lib.VLLT_F32
+        d.tok_emb, d.final_norm, d.lm_head = w.tok_emb.data_ptr(), w.final_norm.data_ptr(), w.lm_head.data_ptr()
+        d.rope_cos, d.rope_sin = w.rope_cos.data_ptr(), w.rope_sin.data_ptr()
+        for k in ("attn_norm", "wqkv", "wo", "ffn_norm", "w_gu", "w_down"):
+            setattr(d, k, C.cast(p[k], C.POINTER(C.c_void_p)))
+        d.k_cache, d.v_cache = self.cache_k.data_ptr(), self.cache_v.data_ptr()
+        return d
+
+    def _reserve(self, S: int, T: int, R: int, W: int) -> None:
+        """Grow the step buffers to at least (S, T, R, W); never shrinks."""
+        torch = self.torch
+        c = self.caps
+        if S <= c.max_seqs and T <= c.max_tokens and R <= c.max_rows and W <= c.max_table_width:
+            return
+        torch.cuda.current_stream(self.dev).synchronize()
+        caps = Caps(max(S, c.max_seqs), max(T, c.max_tokens), max(R, c.max_rows), max(W, c.max_table_width))
+        rec_words = 4 + 3 * caps.max_seqs + caps.max_tokens + caps.max_seqs * caps.max_table_width
+        meta_bytes = self.L.vllt_meta_bytes(C.byref(caps))
+        ws_bytes = self.L.vllt_forward_workspace_bytes(C.byref(self.desc), C.byref(caps))
+        if meta_bytes < 0 or ws_bytes < 0:
+            raise ValueError("bad runner capacities")
+        kw = dict(device=self.dev)
+        self.rec_host = torch.empty(rec_words, dtype=torch.int32, pin_memory=True)
+        self.rec_dev = torch.empty(rec_words, dtype=torch.int32, **kw)
+        self.meta = torch.empty((meta_bytes + 3) // 4, dtype=torch.int32, **kw)
+        self.ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, **kw)
+        self.logits_dev = torch.empty((caps.max_rows, self.w.vocab_padded), dtype=torch.float32, **kw)
+        self.logits_host = torch.empty((caps.max_rows, self.w.vocab_padded), dtype=torch.float32, pin_memory=True)
+        self.counters_host = torch.empty(16, dtype=torch.int32, pin_memory=True)
+        self.caps = caps
+
+    # ---- the step ------------------------------------------------------------------
+    def pack(self, out):
+        return pack_step(out, self.block_size, self.num_blocks, self.model_cfg.vocab_size,
+                         self.w.rope_len, self.qp)
+
+    def copy_on_write(self, pairs) -> None:
+        """Apply (src_block, dst_block) copies in every layer (runner.py:54-60)."""
+        if not pairs:
+            return
+        torch = self.torch
+        p = torch.tensor(np.asarray(pairs, np.int32).reshape(-1, 2), device=self.dev)
+        if int(p.min()) < 0 or int(p.max()) >= self.num_blocks:
+            raise IndexError("copy-on-write block id out of range")
+        cfg = self.model_cfg
+        check(self.L.vllt_copy_blocks(self.cache_k.data_ptr(), self.cache_v.data_ptr(), p.data_ptr(),
+                                      len(pairs), cfg.n_layers, self.num_blocks, cfg.n_kv_heads,
+                                      self.block_size, self.head_dim, _lib.VLLT_F32,
+                                      _lib.stream_handle()))
+
+    def launch(self, out):
+        """Enqueue CoW + H2D + forward for one SchedulerOutput; returns (rows, R)."""
+        torch = self.torch
+        self.copy_on_write(out.cow)
+        rec, bounds, rows, (S, T, R, W) = self.pack(out)
+        self._reserve(S, T, R, W)
+        n = rec.size
+        self.rec_host[:n].numpy()[:] = rec
+        self.rec_dev[:n].copy_(self.rec_host[:n], non_blocking=True)
+        self.h2d_bytes += 4 * n + 8 * len(out.cow)
+        check(self.L.vllt_forward(C.byref(self.desc), self.rec_dev.data_ptr(), C.byref(self.caps),
+                                  C.byref(bounds), self.meta.data_ptr(), self.ws.data_ptr(),
+                                  self.ws.numel(), self.logits_dev.data_ptr(), _lib.stream_handle()))
+        self.steps += 1
+        return rows, R
+
+    def execute(self, out):
+        """(logits float32 [n_rows, vocab], rows), as vllmlite/runner.py:62-100."""
+        torch = self.torch
+        with torch.cuda.device(self.dev):
+            rows, R = self.launch(out)
+            self.logits_host[:R].copy_(self.logits_dev[:R], non_blocking=True)
+            self.counters_host.copy_(self.meta[:16], non_blocking=True)
+            self.d2h_bytes += R * self.w.vocab_padded * 4 + 64
+            torch.cuda.current_stream(self.dev).synchronize()
+        err = int(self.counters_host[7])
+        if err:
+            raise RuntimeError(f"libvllt rejected the step metadata on the device (flags {err})")
+        logits = self.logits_host[:R, :self.model_cfg.vocab_size].numpy().copy()
+        return logits, rows
