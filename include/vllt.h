@@ -118,8 +118,10 @@ int32_t* vllt_meta_field(void* meta, const vllt_caps* caps, int32_t which);
 /* Attention                                                                */
 /* ------------------------------------------------------------------------ */
 
-/* Workspace bytes for vllt_paged_attention_varlen's split-K partials
- * (0 when max_ctx is short enough that single-query sequences are not split). */
+/* Workspace bytes for vllt_paged_attention_varlen: a 256-byte header whose
+ * first int32 receives device error flags (bit 2: a bounded wait on a TMA
+ * copy expired; zero it before a call to observe that call), then split-K
+ * partials for long single-query contexts. */
 int64_t vllt_attention_workspace_bytes(int32_t num_tokens, int32_t n_heads, int32_t head_dim,
                                        int32_t max_ctx);
 
@@ -134,8 +136,10 @@ int64_t vllt_attention_workspace_bytes(int32_t num_tokens, int32_t n_heads, int3
  *   ctx_lens [num_seqs] (tokens in the cache including this pass's).
  * Query j of sequence s sits at position ctx_lens[s] - qlen_s + j and sees
  * keys 0..that position; head h reads KV head h / (n_heads / n_kv).
- * max_qlen and max_ctx bound the work launched. With a NULL or short
- * workspace, long single-query contexts are walked by one CTA (no split-K). */
+ * max_qlen and max_ctx bound the work launched. With a NULL workspace the
+ * generic kernel walks each context in one CTA (no split-K, no TMA path);
+ * single-query bf16 work with head_dim 128 and block_size 16 takes the TMA
+ * decode kernel when a workspace is given. */
 int vllt_paged_attention_varlen(const void* q, const void* k_cache, const void* v_cache,
                                 const int32_t* block_tables, int32_t table_width,
                                 const int32_t* cu_seqlens_q, const int32_t* ctx_lens,

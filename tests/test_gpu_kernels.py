@@ -274,13 +274,15 @@ def test_batch_meta_flags_bad_tables_without_faulting(dev):
     caps = _lib.Caps(4, 16, 16, 4)
     rec = np.asarray([1, 3, 1, 1, 0, 3, 1, 256, 1, 2, 777], np.int32)  # block 777 >= num_blocks
     meta = torch.zeros(L.vllt_meta_bytes(ctypes.byref(caps)) // 4, dtype=torch.int32, device=dev)
-    _lib.check(L.vllt_build_batch_meta(torch.from_numpy(rec).to(dev).data_ptr(), ctypes.byref(caps), 16, 64, 2,
+    drec = torch.from_numpy(rec).to(dev)
+    _lib.check(L.vllt_build_batch_meta(drec.data_ptr(), ctypes.byref(caps), 16, 64, 2,
                                        meta.data_ptr(), _lib.stream_handle()))
     cnt = meta[:16].cpu().numpy()
     assert cnt[7] & 2
     rec_big = np.asarray([9, 3, 1, 1], np.int32)  # more sequences than capacity
     rec_big = np.concatenate([rec_big, np.zeros(40, np.int32)])
-    _lib.check(L.vllt_build_batch_meta(torch.from_numpy(rec_big).to(dev).data_ptr(), ctypes.byref(caps), 16, 64,
+    drec_big = torch.from_numpy(rec_big).to(dev)
+    _lib.check(L.vllt_build_batch_meta(drec_big.data_ptr(), ctypes.byref(caps), 16, 64,
                                        2, meta.data_ptr(), _lib.stream_handle()))
     assert meta[7].item() & 1
 

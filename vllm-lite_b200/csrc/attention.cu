@@ -27,6 +27,8 @@
 
 #include <math.h>
 
+#include <algorithm>
+
 #include "ops.cuh"
 
 namespace vllt {
@@ -357,6 +359,7 @@ int dispatch_dim(const AttnParams& p, int D, int rows, int grid_items, int split
 
 template <typename T>
 int merge_dim(const AttnParams& p, int D, int items, int splits, cudaStream_t st) {
+  if (items <= 0) return VLLT_OK;
   const int warps = items * p.H;
   const int blocks = ceil_div(warps * 32, 256);
   switch (D) {
@@ -373,31 +376,79 @@ int merge_dim(const AttnParams& p, int D, int items, int splits, cudaStream_t st
 
 }  // namespace
 
-// Keys per split-K chunk and the context length from which decode items split.
+// Keys per split-K chunk of the generic kernel.
 constexpr int kSplitLen = 512;
+constexpr int64_t kFlagBytes = 256;  // attention workspace header: device error word
+
+int64_t decode_ws_bytes(int T_cap, int H, int max_ctx);
+bool decode_supported(const AttnCall& c);
+int decode_pass(const AttnCall& c, const int32_t* item_seq, const int32_t* n_items, int items_cap, int num_seqs,
+                int max_ctx, int* err, cudaStream_t st,
+                int (*merge)(const AttnCall&, const int32_t*, const int32_t*, int, int, int, cudaStream_t));
 
 int64_t attention_ws_bytes(int T_cap, int H, int D, int max_ctx) {
   const int splits = ceil_div(max_ctx, kSplitLen);
-  if (splits <= 1) return 0;
-  return (int64_t)splits * T_cap * H * (D + 2) * sizeof(float);
+  const int64_t generic = splits <= 1 ? 0 : (int64_t)splits * T_cap * H * (D + 2) * sizeof(float);
+  const int64_t dec = D == 128 ? decode_ws_bytes(T_cap, H, max_ctx) : 0;
+  return kFlagBytes + std::max(generic, dec);
 }
 
-// Shared entry for the forward pass and the C ABI.
-//  decode pass: items = single-query sequences (item_seq = dec list)
-//  tile pass:   items = (seq, q0) tiles
-int attention_pass(const AttnCall& c, const int32_t* item_seq, const int32_t* item_q0,
-                   const int32_t* n_items, int items_cap, int items_per_seq, int num_seqs,
-                   bool single_query, int max_ctx, cudaStream_t st) {
+namespace {
+
+AttnParams params_of(const AttnCall& c) {
   AttnParams p{};
   p.q = c.q; p.kc = c.kc; p.vc = c.vc; p.out = c.out;
   p.tables = c.tables; p.W = c.W; p.cu_q = c.cu_q; p.ctx = c.ctx;
-  p.item_seq = item_seq; p.item_q0 = item_q0; p.n_items = n_items;
-  p.items_per_seq = items_per_seq; p.num_seqs = num_seqs;
   p.H = c.H; p.n_kv = c.n_kv; p.n_rep = c.H / c.n_kv; p.bs = c.bs; p.num_blocks = c.num_blocks;
   p.scale = c.scale; p.T_cap = c.T_cap;
+  return p;
+}
+
+// Merge of the decode kernel's splits (1024-token chunks), workspace after the flags header.
+int merge_decode_splits(const AttnCall& c, const int32_t* item_seq, const int32_t* n_items, int items,
+                        int num_seqs, int splits, cudaStream_t st) {
+  AttnParams p = params_of(c);
+  p.item_seq = item_seq;
+  p.n_items = n_items;
+  p.num_seqs = num_seqs;
+  p.split_len = 1024;
+  p.ws_o = c.ws;
+  p.ws_ml = c.ws + (int64_t)splits * c.T_cap * c.H * c.D;
+  return c.dtype == VLLT_F32 ? merge_dim<float>(p, c.D, items, splits, st)
+                             : merge_dim<__nv_bfloat16>(p, c.D, items, splits, st);
+}
+
+}  // namespace
+
+// Shared entry for the forward pass and the C ABI.
+//  single-query pass: items = sequences with one query token (item_seq = dec list)
+//  tile pass:         items = (seq, q0) tiles
+// `c.ws` points at the attention workspace (flags header first) or is NULL.
+int attention_pass(const AttnCall& c0, const int32_t* item_seq, const int32_t* item_q0,
+                   const int32_t* n_items, int items_cap, int items_per_seq, int num_seqs,
+                   bool single_query, int max_ctx, cudaStream_t st) {
+  if (items_cap <= 0) return VLLT_OK;
+  VLLT_REQUIRE(c0.H / c0.n_kv <= 16, "attention: n_heads / n_kv must be <= 16");
+  // split the workspace into the flags header and the partials area
+  AttnCall c = c0;
+  int* flags = nullptr;
+  if (c0.ws && c0.ws_bytes >= kFlagBytes) {
+    flags = reinterpret_cast<int*>(c0.ws);
+    c.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(c0.ws) + kFlagBytes);
+    c.ws_bytes = c0.ws_bytes - kFlagBytes;
+  } else {
+    c.ws = nullptr;
+    c.ws_bytes = 0;
+  }
+  if (c0.err) flags = c0.err;
+  if (single_query && decode_supported(c) && flags)
+    return decode_pass(c, item_seq, n_items, items_cap, num_seqs, max_ctx, flags, st, merge_decode_splits);
+
+  AttnParams p = params_of(c);
+  p.item_seq = item_seq; p.item_q0 = item_q0; p.n_items = n_items;
+  p.items_per_seq = items_per_seq; p.num_seqs = num_seqs;
   p.qp = single_query ? 1 : tile_positions(p.n_rep);
   const int rows = p.qp * p.n_rep;
-  VLLT_REQUIRE(p.n_rep <= 16, "attention: n_heads / n_kv must be <= 16");
   int splits = 1;
   if (single_query && max_ctx > kSplitLen) {
     splits = ceil_div(max_ctx, kSplitLen);
@@ -410,13 +461,11 @@ int attention_pass(const AttnCall& c, const int32_t* item_seq, const int32_t* it
       splits = 1;  // no workspace: one CTA walks the whole context
     }
   }
-  const int grid_items = items_cap;
-  if (grid_items == 0) return VLLT_OK;
-  int rc = c.dtype == VLLT_F32 ? dispatch_dim<float>(p, c.D, rows, grid_items, splits, st)
-                               : dispatch_dim<__nv_bfloat16>(p, c.D, rows, grid_items, splits, st);
+  int rc = c.dtype == VLLT_F32 ? dispatch_dim<float>(p, c.D, rows, items_cap, splits, st)
+                               : dispatch_dim<__nv_bfloat16>(p, c.D, rows, items_cap, splits, st);
   if (rc != VLLT_OK || splits == 1) return rc;
-  return c.dtype == VLLT_F32 ? merge_dim<float>(p, c.D, grid_items, splits, st)
-                             : merge_dim<__nv_bfloat16>(p, c.D, grid_items, splits, st);
+  return c.dtype == VLLT_F32 ? merge_dim<float>(p, c.D, items_cap, splits, st)
+                             : merge_dim<__nv_bfloat16>(p, c.D, items_cap, splits, st);
 }
 
 }  // namespace vllt

@@ -137,6 +137,7 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   ac.T_cap = caps->max_tokens;
   ac.ws = w.attn_ws;
   ac.ws_bytes = w.attn_ws_bytes;
+  ac.err = meta + kCntError;  // bounded-wait timeouts surface in the step's error counter
 
   for (int l = 0; l < m->n_layers; ++l) {
     float* kc = reinterpret_cast<float*>(m->k_cache) + l * layer_elems;
@@ -267,6 +268,7 @@ int vllt_paged_attention_varlen(const void* q, const void* k_cache, const void* 
   c.dtype = dtype; c.scale = scale; c.T_cap = num_tokens;
   c.ws = reinterpret_cast<float*>(workspace);
   c.ws_bytes = workspace ? workspace_bytes : 0;
+  c.err = nullptr;  // the workspace header carries the error word
   cudaStream_t st = as_stream(stream);
   const int n_rep = n_heads / n_kv;
   if (max_qlen <= 1) {  // pure decode batch: one item per sequence, split-K allowed

@@ -34,8 +34,9 @@ struct AttnCall {
   int W, H, n_kv, D, bs, num_blocks, dtype;
   float scale;
   int T_cap;
-  float* ws;
+  float* ws;        // attention workspace: 256-byte flags header, then split partials
   int64_t ws_bytes;
+  int* err;         // device error word (overrides the header's), may be NULL
 };
 int64_t attention_ws_bytes(int T_cap, int H, int D, int max_ctx);
 int attention_pass(const AttnCall& c, const int32_t* item_seq, const int32_t* item_q0,

@@ -136,9 +136,13 @@ def _make_gpu_engine(Base):
             check(L.vllt_sample_greedy(run.logits_dev.data_ptr(), R, V, ld, _lib.ptr(d_mask),
                                        eos if eos is not None else -1, _lib.ptr(d_pen), _lib.ptr(bits),
                                        picks.data_ptr(), st))
+            # device temporaries stay referenced until their kernels are enqueued:
+            # a tensor freed earlier could be handed to the next copy by the
+            # caching allocator and overwritten before the kernel reads it
             if drafts:
-                check(L.vllt_spec_accept(h2d(cu).data_ptr(), h2d(np.asarray(drafts, np.int32)).data_ptr(),
-                                         h2d(doff).data_ptr(), S, picks.data_ptr(), acc.data_ptr(), st))
+                d_cu, d_dr, d_doff = h2d(cu), h2d(np.asarray(drafts, np.int32)), h2d(doff)
+                check(L.vllt_spec_accept(d_cu.data_ptr(), d_dr.data_ptr(), d_doff.data_ptr(), S,
+                                         picks.data_ptr(), acc.data_ptr(), st))
             sampled_tok = {}
             plain = [(i, r) for i, r in sampled
                      if sched.scheduled[i].seq.params.repetition_penalty == 1.0
@@ -148,13 +152,15 @@ def _make_gpu_engine(Base):
                 prm = [sched.scheduled[i].seq.params for i, _ in plain]
                 # the request's generator supplies the uniform numpy's choice() would draw
                 u = np.asarray([self.rngs[sched.scheduled[i].seq.request_id].random() for i, _ in plain], np.float32)
-                sub = run.logits_dev.index_select(0, h2d(np.asarray([r for _, r in plain], np.int64))).contiguous()
+                sel = h2d(np.asarray([r for _, r in plain], np.int64))
+                sub = run.logits_dev.index_select(0, sel).contiguous()
                 out = torch.empty(len(plain), dtype=torch.int32, device=dev)
-                check(L.vllt_sample_top_p(sub.data_ptr(), len(plain), V, ld,
-                                          h2d(np.asarray([q.temperature for q in prm], np.float32)).data_ptr(),
-                                          h2d(np.asarray([q.top_k for q in prm], np.int32)).data_ptr(),
-                                          h2d(np.asarray([q.top_p for q in prm], np.float32)).data_ptr(),
-                                          h2d(u).data_ptr(), out.data_ptr(), st))
+                d_t = h2d(np.asarray([q.temperature for q in prm], np.float32))
+                d_k = h2d(np.asarray([q.top_k for q in prm], np.int32))
+                d_p = h2d(np.asarray([q.top_p for q in prm], np.float32))
+                d_u = h2d(u)
+                check(L.vllt_sample_top_p(sub.data_ptr(), len(plain), V, ld, d_t.data_ptr(), d_k.data_ptr(),
+                                          d_p.data_ptr(), d_u.data_ptr(), out.data_ptr(), st))
                 for (i, _), t in zip(plain, out.cpu().numpy()):
                     sampled_tok[i] = int(t)
             for i, r in other:  # temperature with penalty / min_tokens: the reference sampler on that row

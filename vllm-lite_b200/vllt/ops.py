@@ -48,7 +48,8 @@ def write_kv(cache_k, cache_v, k, v, slots) -> None:
     """cache[slot[t]] = k[t], v[t]; caches [NB, n_kv, bs, D], k/v [T, n_kv, D]."""
     nb, n_kv, bs, D = cache_k.shape
     sl = _i32(slots, cache_k.device)
-    check(lib().vllt_reshape_and_cache(ptr(k.contiguous()), ptr(v.contiguous()), ptr(cache_k),
+    k, v = k.contiguous(), v.contiguous()  # keep temporaries alive past the launch
+    check(lib().vllt_reshape_and_cache(ptr(k), ptr(v), ptr(cache_k),
                                        ptr(cache_v), ptr(sl), k.shape[0], n_kv, D, bs, nb,
                                        _dtype_code(cache_k), stream_handle()))
 
@@ -78,15 +79,23 @@ def paged_attention_varlen(q, cache_k, cache_v, block_tables, cu_seqlens_q, ctx_
         max_qlen = int((cu[1:] - cu[:-1]).max()) if S else 0
     if max_ctx is None:
         max_ctx = int(cl.max()) if S else 0
+    q = q.contiguous()
     out = torch.empty_like(q)
     if workspace is None:
         nbytes = lib().vllt_attention_workspace_bytes(T, H, D, max_ctx)
-        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device) if nbytes > 0 else None
+        workspace = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=q.device)
     check(lib().vllt_paged_attention_varlen(
-        ptr(q.contiguous()), ptr(cache_k), ptr(cache_v), ptr(bt), bt.shape[1], ptr(cu), ptr(cl), S, T,
+        ptr(q), ptr(cache_k), ptr(cache_v), ptr(bt), bt.shape[1], ptr(cu), ptr(cl), S, T,
         max_qlen, max_ctx, H, n_kv, D, bs, nb, float(scale), _dtype_code(q), ptr(out), ptr(workspace),
         workspace.numel() if workspace is not None else 0, stream_handle()))
+    if workspace is not None:
+        paged_attention_varlen.last_workspace = workspace  # flags readable by callers
     return out
+
+
+def attention_flags(workspace) -> int:
+    """Device error flags from an attention workspace header (syncs)."""
+    return int(workspace[:4].view(__import__("torch").int32).item())
 
 
 def paged_attention(q, cache_k, cache_v, read_slots, n_kv_heads, scale):
@@ -121,7 +130,8 @@ def rms_norm(x, w, eps=1e-5, idx=None):
     rows = idx.shape[0] if idx is not None else x.shape[0]
     out = torch.empty((rows, x.shape[1]), dtype=torch.float32, device=x.device)
     ix = _i32(idx, x.device) if idx is not None else None
-    check(lib().vllt_rmsnorm(ptr(x.contiguous()), ptr(ix), ptr(w), ptr(out), rows, x.shape[1], float(eps),
+    x = x.contiguous()
+    check(lib().vllt_rmsnorm(ptr(x), ptr(ix), ptr(w), ptr(out), rows, x.shape[1], float(eps),
                              stream_handle()))
     return out
 
@@ -141,7 +151,8 @@ def matmul(a, b):
     M, K = a.shape
     N = b.shape[1]
     c = torch.empty((M, N), dtype=torch.float32, device=a.device)
-    check(lib().vllt_sgemm(ptr(a.contiguous()), ptr(b.contiguous()), ptr(c), M, N, K, stream_handle()))
+    a, b = a.contiguous(), b.contiguous()
+    check(lib().vllt_sgemm(ptr(a), ptr(b), ptr(c), M, N, K, stream_handle()))
     return c
 
 
