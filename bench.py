@@ -176,44 +176,57 @@ def decode_setup(torch, dev, seqs=256, H=32, KV=8, D=128, bs=16, seed=0, max_ctx
                 alg_bytes=alg_bytes, attn_bytes=sum_ctx * KV * D * 4 + 2 * seqs * H * D * 2 + int(nblk.sum()) * 4)
 
 
-def decode_step(torch, s, ws, out):
+def decode_write(s):
+    """One new token per sequence into the paged cache (reshape_and_cache)."""
     from vllt import _lib
 
     L = _lib.lib()
-    st = _lib.stream_handle()
     _lib.check(L.vllt_reshape_and_cache(s["knew"].data_ptr(), s["vnew"].data_ptr(), s["kc"].data_ptr(),
                                         s["vc"].data_ptr(), s["slots"].data_ptr(), s["seqs"], s["KV"], s["D"],
-                                        s["bs"], s["pool"], _lib.VLLT_BF16, st))
+                                        s["bs"], s["pool"], _lib.VLLT_BF16, _lib.stream_handle()))
+
+
+def decode_attend(s, ws, out):
+    """Single-query paged attention over every sequence (TMA decode kernel + split merge)."""
+    from vllt import _lib
+
+    L = _lib.lib()
     _lib.check(L.vllt_paged_attention_varlen(
         s["q"].data_ptr(), s["kc"].data_ptr(), s["vc"].data_ptr(), s["tables"].data_ptr(), s["W"],
         s["cu"].data_ptr(), s["ctx"].data_ptr(), s["seqs"], s["seqs"], 1, s["max_ctx"], s["H"], s["KV"], s["D"],
         s["bs"], s["pool"], float(1.0 / s["D"] ** 0.5), _lib.VLLT_BF16, out.data_ptr(), ws.data_ptr(),
-        ws.numel(), st))
+        ws.numel(), _lib.stream_handle()))
 
 
 def decode_bench(torch, dev, steps, warmup):
-    """Time K decode steps (cache write + attention) with CUDA events; the
-    attention kernel alone is timed too, for the roofline."""
+    """Time K decode steps (cache write + attention) with CUDA events on the
+    launching stream, L2 flushed before each; the attention call is bracketed
+    by its own events for the roofline. Returns (setup, step s, attention s)."""
     from vllt import _lib
 
     s = decode_setup(torch, dev)
     nbytes = _lib.lib().vllt_attention_workspace_bytes(s["seqs"], s["H"], s["D"], s["max_ctx"])
-    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
     out = torch.empty_like(s["q"])
     for _ in range(max(warmup, 3)):
-        decode_step(torch, s, ws, out)
+        decode_write(s)
+        decode_attend(s, ws, out)
     torch.cuda.synchronize()
-    times = []
+    step_t, attn_t = [], []
     for _ in range(max(steps, 5)):
         flush_l2(torch, dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
-        decode_step(torch, s, ws, out)
+        decode_write(s)
         e1.record()
-        e1.synchronize()
-        times.append(e0.elapsed_time(e1) / 1e3)
-    t = statistics.median(times)
-    return s, t
+        decode_attend(s, ws, out)
+        e2.record()
+        e2.synchronize()
+        step_t.append(e0.elapsed_time(e2) / 1e3)
+        attn_t.append(e1.elapsed_time(e2) / 1e3)
+    if int(ws[:4].view(torch.int32).item()) != 0:
+        raise RuntimeError("decode attention reported a device-side timeout")
+    return s, statistics.median(step_t), statistics.median(attn_t)
 
 
 # ---- our arm -------------------------------------------------------------------------------
@@ -280,9 +293,9 @@ def main_ours(args):
         t_ours, t_e2e = float(v[0]), float(v[1])
         toks, toks_e2e = float(n[0]), float(n[1])
     ttft_all = [x for r in res for x in r[2]]
-    decode_s, decode_t = decode_bench(torch, dev, 10, 3)
+    decode_s, _, decode_t = decode_bench(torch, dev, 10, 3)
     hbm, peak_kind = peaks()
-    achieved = decode_s["attn_bytes"] / decode_t / 1e9  # kernel roofline uses the attention bytes
+    achieved = decode_s["attn_bytes"] / decode_t / 1e9  # attention bytes / attention-call time
     cpu = cpu_baseline(wl) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if world > 1:
         torch.distributed.barrier()
@@ -330,13 +343,15 @@ def main_ours(args):
 
 
 def main_decode(args, torch, dev, rank, world):
-    s, t = decode_bench(torch, dev, args.steps, args.warmup)
+    s, t_step, t = decode_bench(torch, dev, args.steps, args.warmup)
     hbm, kind = peaks()
     if rank == 0:
         ach = s["attn_bytes"] / t / 1e9
         print(json.dumps({
             "metric": "paged-attention decode HBM GB/s", "value": round(ach, 1), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 4), "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_step * 1e3, 4),
+            "attention_ms": round(t * 1e3, 4), "step_gbs": round(s["alg_bytes"] / t_step / 1e9, 1),
+            "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1)",
             "config": {"workload": "C3 decode: 256 seqs, ctx U[1,4096], H32/KV8/D128, block 16",
                        "l2": "flushed before each step; KV > L2"},

@@ -75,6 +75,22 @@ def test_runner_replay_logits(name, bs):
     assert worst < 1e-4, worst
 
 
+def test_graph_replay_is_bit_identical_to_eager():
+    """CUDA-graph replays (bucketed bounds) give exactly the eager logits."""
+    from vllmlite.config import CacheConfig
+
+    from vllt.runner import CudaRunner
+
+    steps = F.replay_steps("replay_spec.npz")
+    eager = CudaRunner(model_cfg(F.BENCH), CacheConfig(block_size=4, num_blocks=512), use_graphs=False)
+    graph = CudaRunner(model_cfg(F.BENCH), CacheConfig(block_size=4, num_blocks=512), use_graphs=True)
+    for seqs, cow, want in steps + steps:  # the second pass replays captured graphs
+        a, _ = eager.execute(F.as_scheduler_output(seqs, cow))
+        b, _ = graph.execute(F.as_scheduler_output(seqs, cow))
+        np.testing.assert_array_equal(a, b)
+    assert len(graph.graphs) >= 2
+
+
 def test_runner_copy_on_write_before_writes():
     """A CoW pair in the same step as the write into the copy (runner.py:63-64)."""
     from vllmlite.config import CacheConfig

@@ -287,13 +287,15 @@ def test_batch_meta_flags_bad_tables_without_faulting(dev):
     assert meta[7].item() & 1
 
 
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
-def test_attention_decode_split_k(dev, dtype):
-    """A pure decode batch with contexts long enough to split across CTAs."""
-    from vllt.ops import paged_attention_varlen
+@pytest.mark.parametrize("dtype,H,KV", [("f32", 32, 8), ("bf16", 32, 8), ("bf16", 8, 8), ("bf16", 16, 8),
+                                        ("bf16", 64, 8), ("bf16", 12, 6)])
+def test_attention_decode_split_k(dev, dtype, H, KV):
+    """A pure decode batch with contexts long enough to split across CTAs
+    (bf16 / head_dim 128 / block 16 takes the TMA decode kernel)."""
+    from vllt.ops import attention_flags, paged_attention_varlen
 
-    rng = np.random.default_rng(11)
-    H, KV, D, bs = 32, 8, 128, 16
+    rng = np.random.default_rng(11 + H)
+    D, bs = 128, 16
     ctxs = [1, 513, 4096, 2000, 17, 1024, 3333]
     qlens = [1] * len(ctxs)
     q, ck, cv, tables, tab = ragged_batch(rng, H, KV, D, bs, qlens, ctxs, np.float32 if dtype == "f32" else "bf16")
@@ -306,3 +308,29 @@ def test_attention_decode_split_k(dev, dtype):
         want = A.dense_attention(q[i:i + 1], ck[slots], cv[slots], KV, 1.0 / np.sqrt(D))
         tol = 1e-4 if dtype == "f32" else 2e-2
         np.testing.assert_allclose(got[i:i + 1], want, rtol=tol, atol=tol / 10 if dtype == "f32" else tol)
+    assert attention_flags(paged_attention_varlen.last_workspace) == 0
+
+
+def test_decode_kernel_matches_generic_kernel(dev):
+    """The TMA decode kernel and the generic kernel (no workspace) agree."""
+    from vllt import _lib
+    from vllt.ops import paged_attention_varlen
+
+    rng = np.random.default_rng(5)
+    H, KV, D, bs = 32, 8, 128, 16
+    ctxs = [4096, 1, 16, 17, 2047, 100]
+    q, ck, cv, tables, tab = ragged_batch(rng, H, KV, D, bs, [1] * len(ctxs), ctxs, "bf16")
+    args = (torch.from_numpy(q).to(dev, torch.bfloat16), torch.from_numpy(to_lib_layout(ck, bs)).to(dev, torch.bfloat16),
+            torch.from_numpy(to_lib_layout(cv, bs)).to(dev, torch.bfloat16))
+    fast = paged_attention_varlen(*args, tab, np.arange(len(ctxs) + 1), ctxs, 1.0 / np.sqrt(D)).float()
+    # generic: pass an explicit NULL workspace through the C ABI
+    L = _lib.lib()
+    out = torch.empty_like(args[0])
+    bt = torch.from_numpy(tab).to(dev)
+    cu = torch.arange(len(ctxs) + 1, dtype=torch.int32, device=dev)
+    cl = torch.tensor(ctxs, dtype=torch.int32, device=dev)
+    _lib.check(L.vllt_paged_attention_varlen(args[0].data_ptr(), args[1].data_ptr(), args[2].data_ptr(), bt.data_ptr(),
+                                             tab.shape[1], cu.data_ptr(), cl.data_ptr(), len(ctxs), len(ctxs), 1,
+                                             max(ctxs), H, KV, D, bs, args[1].shape[0], float(1 / np.sqrt(D)),
+                                             _lib.VLLT_BF16, out.data_ptr(), None, 0, _lib.stream_handle()))
+    np.testing.assert_allclose(fast.cpu().numpy(), out.float().cpu().numpy(), rtol=2e-2, atol=2e-2)

@@ -9,7 +9,7 @@
 //     boxes per tile for K and for V) with the 128-byte swizzle, so the
 //     per-token reads of the score loop and the per-column reads of the P.V
 //     loop are bank-conflict free without padding. Each warp owns a private
-//     3-stage ring (8 KB per stage) guarded by mbarriers; one lane issues the
+//     2-stage ring (8 KB per stage) guarded by mbarriers; one lane issues the
 //     copies, all lanes wait (bounded).
 //   * Math: CUDA cores. Scores: lane (token t = lane % 16, half = lane / 16)
 //     dots its token's 64-element half with the NREP query heads of the KV
@@ -33,7 +33,7 @@ namespace {
 constexpr int kD = 128;
 constexpr int kBS = 16;
 constexpr int kWarps = 4;
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 constexpr int kBox = 16 * 128;            // one 16 x 64 bf16 box: 2 KB
 constexpr int kStageBytes = 4 * kBox;     // K lo, K hi, V lo, V hi
 constexpr uint64_t kWaitNs = 1000000000;  // bounded mbarrier wait: 1 s
@@ -104,7 +104,7 @@ __device__ __forceinline__ float2 bf2(uint32_t w) {
 __device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
 template <int NREP>
-__global__ void __launch_bounds__(kWarps * 32, 2)
+__global__ void __launch_bounds__(kWarps * 32, 3)
 decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, DecodeParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-align the stage ring (the swizzle pattern is defined on 1 KB atoms)
@@ -182,6 +182,11 @@ decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CU
   }
 
   const int tq = lane & 15, half = lane >> 4;
+  int koff[8];  // this lane's 8 score-loop chunk offsets (row tq of a swizzled box)
+#pragma unroll
+  for (int c = 0; c < 8; ++c) koff[c] = half * kBox + swz(tq, c);
+  const int c16 = lane >> 1;  // P.V: 16-byte chunk of the 256-byte row this lane reads
+  const int vbase = 2 * kBox + (c16 >> 3) * kBox + (lane & 1) * 8;
   bool failed = false;
   int j = 0;
   for (; j < my_n; ++j) {
@@ -199,11 +204,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CU
     float2 sc2[NREP];
 #pragma unroll
     for (int h = 0; h < NREP; ++h) sc2[h] = make_float2(0.f, 0.f);
-    const unsigned char* kbox = stage + half * kBox;
     const float* qh = q_s + half * 64;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const uint4 kw = *reinterpret_cast<const uint4*>(kbox + swz(tq, c));
+      const uint4 kw = *reinterpret_cast<const uint4*>(stage + koff[c]);
       const float2 k0 = bf2(kw.x), k1 = bf2(kw.y), k2 = bf2(kw.z), k3 = bf2(kw.w);
 #pragma unroll
       for (int h = 0; h < NREP; ++h) {
@@ -245,18 +249,25 @@ decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CU
     __syncwarp();
 
     // ---- P.V: lane owns columns 4*lane .. 4*lane+3 ---------------------------------
-    const int c16 = lane >> 1;                    // 16-byte chunk of the 256-byte row
-    const unsigned char* vbox = stage + 2 * kBox + (c16 >> 3) * kBox;
-    const int vsub = (lane & 1) * 8;
+    const unsigned char* vrow = stage + vbase;
 #pragma unroll
     for (int t = 0; t < kBS; ++t) {
-      const uint2 vw = *reinterpret_cast<const uint2*>(vbox + swz(t, c16 & 7) + vsub);
+      const uint2 vw = *reinterpret_cast<const uint2*>(vrow + t * 128 + (((c16 & 7) ^ (t & 7)) << 4));
       const float2 v01 = bf2(vw.x), v23 = bf2(vw.y);
+      if constexpr (NREP == 1) {
+        const float2 pp = pw[t];
+        acc[0][0] = __ffma2_rn(pp, v01, acc[0][0]);
+        acc[0][1] = __ffma2_rn(pp, v23, acc[0][1]);
+      } else {
 #pragma unroll
-      for (int h = 0; h < NREP; ++h) {
-        const float2 pp = pw[t * NREP + h];
-        acc[h][0] = __ffma2_rn(pp, v01, acc[h][0]);
-        acc[h][1] = __ffma2_rn(pp, v23, acc[h][1]);
+        for (int h = 0; h < NREP; h += 2) {  // two heads' (p, p) pairs per 16-byte load
+          const float4 pq = *reinterpret_cast<const float4*>(&pw[t * NREP + h]);
+          const float2 p0 = make_float2(pq.x, pq.y), p1 = make_float2(pq.z, pq.w);
+          acc[h][0] = __ffma2_rn(p0, v01, acc[h][0]);
+          acc[h][1] = __ffma2_rn(p0, v23, acc[h][1]);
+          acc[h + 1][0] = __ffma2_rn(p1, v01, acc[h + 1][0]);
+          acc[h + 1][1] = __ffma2_rn(p1, v23, acc[h + 1][1]);
+        }
       }
     }
     __syncwarp();  // every lane is done with this stage before it is refilled

@@ -53,6 +53,7 @@ MetaLayout layout_of(const vllt_caps* c) {
 struct FwdWs {
   float *x, *h, *q, *attn, *act, *rows_h, *attn_ws;
   int64_t attn_ws_bytes, total_bytes;
+  GemmScratch gemm;
 };
 
 FwdWs carve(const vllt_model_desc* m, const vllt_caps* c, char* base) {
@@ -73,6 +74,12 @@ FwdWs carve(const vllt_model_desc* m, const vllt_caps* c, char* base) {
   w.rows_h = take(R * m->d_model * 4);
   w.attn_ws_bytes = attention_ws_bytes((int)T, m->n_heads, m->head_dim, m->max_seq_len);
   w.attn_ws = take(w.attn_ws_bytes);
+  const int n_max = std::max({(m->n_heads + 2 * m->n_kv_heads) * m->head_dim, 2 * m->d_ff, m->d_model,
+                              m->vocab_padded});
+  w.gemm.partial_floats = gemm_scratch_floats(n_max);
+  w.gemm.n_counters = gemm_scratch_counters(n_max);
+  w.gemm.partials = take(w.gemm.partial_floats * 4);
+  w.gemm.counters = reinterpret_cast<int*>(take((int64_t)w.gemm.n_counters * 4));
   w.total_bytes = off;
   return w;
 }
@@ -146,7 +153,7 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
     VLLT_TRY(rmsnorm(w.x, nullptr, m->attn_norm[l], w.h, T_cap, T_dev, d, eps, st));
     EpiQKV eq{w.q, kc, vc, meta + L.pos, meta + L.slot, m->rope_cos, m->rope_sin,
               H, KV, D, m->block_size, m->max_seq_len, (int64_t)m->num_blocks * m->block_size};
-    VLLT_TRY(sgemm_launch(w.h, d, m->wqkv[l], qkv_n, T_cap, T_dev, qkv_n, d, eq, st));
+    VLLT_TRY(sgemm_launch(w.h, d, m->wqkv[l], qkv_n, T_cap, T_dev, qkv_n, d, eq, st, &w.gemm));
     // attention: single-query sequences, then multi-token tiles
     ac.kc = kc;
     ac.vc = vc;
@@ -155,18 +162,18 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
     VLLT_TRY(attention_pass(ac, meta + L.tile_seq, meta + L.tile_q0, meta + kCntTiles, tiles_cap,
                             0, 0, false, max_ctx, st));
     // x += attn @ wo
-    VLLT_TRY(sgemm_launch(w.attn, H * D, m->wo[l], d, T_cap, T_dev, d, H * D, EpiResidual{w.x, d}, st));
+    VLLT_TRY(sgemm_launch(w.attn, H * D, m->wo[l], d, T_cap, T_dev, d, H * D, EpiResidual{w.x, d}, st, &w.gemm));
     // x += (silu(h @ w_gate) * (h @ w_up)) @ w_down
     VLLT_TRY(rmsnorm(w.x, nullptr, m->ffn_norm[l], w.h, T_cap, T_dev, d, eps, st));
     VLLT_TRY(sgemm_launch(w.h, d, m->w_gu[l], 2 * m->d_ff, T_cap, T_dev, 2 * m->d_ff, d,
-                          EpiSwiGLU{w.act, m->d_ff}, st));
+                          EpiSwiGLU{w.act, m->d_ff}, st, &w.gemm));
     VLLT_TRY(sgemm_launch(w.act, m->d_ff, m->w_down[l], d, T_cap, T_dev, d, m->d_ff,
-                          EpiResidual{w.x, d}, st));
+                          EpiResidual{w.x, d}, st, &w.gemm));
   }
   // logits only for the wanted rows (model.py:119-120)
   VLLT_TRY(rmsnorm(w.x, meta + L.rows, m->final_norm, w.rows_h, R_cap, R_dev, d, eps, st));
   VLLT_TRY(sgemm_launch(w.rows_h, d, m->lm_head, m->vocab_padded, R_cap, R_dev, m->vocab_padded, d,
-                        EpiStore{logits, m->vocab_padded, m->vocab_padded}, st));
+                        EpiStore{logits, m->vocab_padded, m->vocab_padded}, st, &w.gemm));
   return VLLT_OK;
 }
 

@@ -1,79 +1,64 @@
 // fp32 SIMT GEMM with fused epilogues (parity mode: true fp32, no TF32).
 //
 // C[M][N] = A[M][K] @ B[K][N], both row-major (the reference's [in][out]
-// weights, vllmlite/model.py:34-43). Register-blocked FFMA tiles, double-
-// buffered through shared memory. The epilogue functor receives TN
-// consecutive output columns of one row.
+// weights, vllmlite/model.py:34-43). Register-blocked FFMA tiles fed by a
+// 3-stage cp.async pipeline (BK = 32).
+//
+// Decode steps have few rows (M ~ batch), so one CTA per output tile would
+// walk all of K serially with a handful of CTAs on 148 SMs: latency bound.
+// For small M the K range is split across CTAs (grid.z). Every slice writes
+// its partial tile to a workspace; the last slice to finish (an atomic
+// counter per tile) sums the partials in slice order -- deterministic -- runs
+// the epilogue and resets the counter, so the kernel can be replayed from a
+// CUDA graph.
 #pragma once
+
+#include <algorithm>
 
 #include "common.cuh"
 
 namespace vllt {
 
-template <int BM, int BN, int TM, int TN, class Epi>
-__global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ A, int lda,
-                                                    const float* __restrict__ B, int ldb,
-                                                    int M_cap, const int* __restrict__ M_dev,
-                                                    int N, int K, Epi epi) {
-  constexpr int BK = 16;
+constexpr int kGemmStages = 3;
+
+template <int BM, int BN, int BK, int TM, int TN, int THREADS, class Epi>
+__global__ void __launch_bounds__(THREADS) sgemm_kernel(const float* __restrict__ A, int lda,
+                                                        const float* __restrict__ B, int ldb,
+                                                        int M_cap, const int* __restrict__ M_dev,
+                                                        int N, int K, int k_slice,
+                                                        float* __restrict__ ws, int* __restrict__ counters,
+                                                        Epi epi) {
+  constexpr int NS = kGemmStages;
   constexpr int TX = BN / TN, TY = BM / TM;
-  static_assert(TX * TY == 256, "256 threads");
-  constexpr int A_VEC = BM * BK / 4;
-  constexpr int A_PER = (A_VEC + 255) / 256;
-  constexpr int B_VEC = BK * BN / 4;
-  constexpr int B_PER = (B_VEC + 255) / 256;
-  __shared__ __align__(16) float As[2][BK][BM];
-  __shared__ __align__(16) float Bs[2][BK][BN];
+  static_assert(TX * TY == THREADS, "thread tile");
+  constexpr int AST = BK + 4;  // A tile row stride (floats), keeps 16-byte alignment
+  constexpr int A_CH = BM * BK / 4, B_CH = BK * BN / 4;  // 16-byte chunks per stage
+  __shared__ __align__(16) float As[NS][BM * AST];
+  __shared__ __align__(16) float Bs[NS][BK * BN];
+  __shared__ int s_last;
 
   const int M = M_dev ? min(*M_dev, M_cap) : M_cap;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   if (m0 >= M) return;
   const int tid = threadIdx.x, tx = tid % TX, ty = tid / TX;
+  const int ks = gridDim.z, z = blockIdx.z;
+  const int kb = z * k_slice, ke = min(K, kb + k_slice);
+  const int nk = (ke - kb + BK - 1) / BK;
 
-  float4 a_reg[A_PER], b_reg[B_PER];
-  auto load = [&](int k0) {
+  auto load_stage = [&](int stage, int k0) {
 #pragma unroll
-    for (int i = 0; i < A_PER; ++i) {
-      const int v = tid + i * 256;
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (v < A_VEC) {
-        const int r = v / (BK / 4), c = (v % (BK / 4)) * 4;
-        const int gm = m0 + r, gk = k0 + c;
-        if (gm < M && gk < K) x = *reinterpret_cast<const float4*>(A + (int64_t)gm * lda + gk);
-      }
-      a_reg[i] = x;
+    for (int i = tid; i < A_CH; i += THREADS) {
+      const int r = i / (BK / 4), c = (i % (BK / 4)) * 4;
+      const int gm = m0 + r, gk = k0 + c;
+      const bool ok = gm < M && gk < ke;
+      cp_async16(&As[stage][r * AST + c], ok ? (const void*)(A + (int64_t)gm * lda + gk) : (const void*)A, ok);
     }
 #pragma unroll
-    for (int i = 0; i < B_PER; ++i) {
-      const int v = tid + i * 256;
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (v < B_VEC) {
-        const int r = v / (BN / 4), c = (v % (BN / 4)) * 4;
-        const int gk = k0 + r, gn = n0 + c;
-        if (gk < K && gn < N) x = *reinterpret_cast<const float4*>(B + (int64_t)gk * ldb + gn);
-      }
-      b_reg[i] = x;
-    }
-  };
-  auto store = [&](int buf) {
-#pragma unroll
-    for (int i = 0; i < A_PER; ++i) {
-      const int v = tid + i * 256;
-      if (v < A_VEC) {
-        const int r = v / (BK / 4), c = (v % (BK / 4)) * 4;
-        As[buf][c + 0][r] = a_reg[i].x;
-        As[buf][c + 1][r] = a_reg[i].y;
-        As[buf][c + 2][r] = a_reg[i].z;
-        As[buf][c + 3][r] = a_reg[i].w;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < B_PER; ++i) {
-      const int v = tid + i * 256;
-      if (v < B_VEC) {
-        const int r = v / (BN / 4), c = (v % (BN / 4)) * 4;
-        *reinterpret_cast<float4*>(&Bs[buf][r][c]) = b_reg[i];
-      }
+    for (int i = tid; i < B_CH; i += THREADS) {
+      const int r = i / (BN / 4), c = (i % (BN / 4)) * 4;
+      const int gk = k0 + r, gn = n0 + c;
+      const bool ok = gk < ke && gn < N;
+      cp_async16(&Bs[stage][r * BN + c], ok ? (const void*)(B + (int64_t)gk * ldb + gn) : (const void*)B, ok);
     }
   };
 
@@ -83,30 +68,71 @@ __global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ A,
 #pragma unroll
     for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
 
-  load(0);
-  store(0);
-  __syncthreads();
-  for (int k0 = 0, it = 0; k0 < K; k0 += BK, ++it) {
-    const int cur = it & 1;
-    const bool more = k0 + BK < K;
-    if (more) load(k0 + BK);
+#pragma unroll
+  for (int s = 0; s < NS - 1; ++s) {
+    if (s < nk) load_stage(s, kb + s * BK);
+    cp_async_commit();
+  }
+  for (int it = 0; it < nk; ++it) {
+    cp_async_wait<NS - 2>();
+    __syncthreads();
+    const int nxt = it + NS - 1;
+    if (nxt < nk) load_stage(nxt % NS, kb + nxt * BK);
+    cp_async_commit();
+    const float* as = As[it % NS];
+    const float* bs = Bs[it % NS];
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
       float a[TM], b[TN];
 #pragma unroll
-      for (int i = 0; i < TM; ++i) a[i] = As[cur][kk][ty * TM + i];
+      for (int i = 0; i < TM; ++i) a[i] = as[(ty * TM + i) * AST + kk];
 #pragma unroll
-      for (int j = 0; j < TN; ++j) b[j] = Bs[cur][kk][tx * TN + j];
+      for (int j = 0; j < TN; j += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(&bs[kk * BN + tx * TN + j]);
+        b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
+      }
 #pragma unroll
       for (int i = 0; i < TM; ++i)
 #pragma unroll
         for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
-    if (more) store(cur ^ 1);
-    __syncthreads();
   }
+  cp_async_wait<0>();
 
   const int col = n0 + tx * TN;
+  if (ks > 1) {
+    // partial tile -> workspace; the last slice reduces in slice order
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    float* mine = ws + ((int64_t)tile * ks + z) * (BM * BN);
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+      for (int j = 0; j < TN; j += 4)
+        *reinterpret_cast<float4*>(&mine[(ty * TM + i) * BN + tx * TN + j]) =
+            make_float4(acc[i][j], acc[i][j + 1], acc[i][j + 2], acc[i][j + 3]);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&counters[tile], 1) == ks - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* base = ws + (int64_t)tile * ks * (BM * BN);
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+      for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+    for (int zz = 0; zz < ks; ++zz) {
+      const float* part = base + (int64_t)zz * (BM * BN);
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; j += 4) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(&part[(ty * TM + i) * BN + tx * TN + j]));
+          acc[i][j] += v.x; acc[i][j + 1] += v.y; acc[i][j + 2] += v.z; acc[i][j + 3] += v.w;
+        }
+    }
+    if (tid == 0) counters[tile] = 0;  // ready for the next launch / graph replay
+  }
   if (col >= N) return;
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
@@ -198,26 +224,53 @@ struct EpiQKV {
   }
 };
 
+// Split-K scratch for the small-M path: partial tiles and per-tile counters.
+struct GemmScratch {
+  float* partials;
+  int* counters;        // zeroed once; every reducer resets its own
+  int64_t partial_floats;
+  int n_counters;
+};
+
+// K slice length: whole K unless M is small; then ~4 k-steps per slice, at
+// most 8 slices, and never more partial floats / counters than the scratch has.
+inline int gemm_k_slice(int M_cap, int N, int K, int BM, int BN, int BK, const GemmScratch* sc) {
+  if (!sc || M_cap > 64) return K;
+  const int tiles = ceil_div(N, BN) * ceil_div(M_cap, BM);
+  int ks = std::min(8, ceil_div(K, 4 * BK));
+  while (ks > 1 && ((int64_t)tiles * ks * BM * BN > sc->partial_floats || tiles > sc->n_counters)) --ks;
+  if (ks <= 1) return K;
+  return ceil_div(ceil_div(K, ks), BK) * BK;
+}
+
+// Scratch the split-K path may use for up to 64 rows and N columns.
+inline int64_t gemm_scratch_floats(int N) { return (int64_t)ceil_div(N, 64) * 64 * 64 * 8; }
+inline int gemm_scratch_counters(int N) { return ceil_div(N, 64) * 4; }
+
+template <int BM, int BN, int BK, int TM, int TN, int THREADS, class Epi>
+int sgemm_go(const float* A, int lda, const float* B, int ldb, int M_cap, const int* M_dev, int N, int K,
+             const Epi& epi, const GemmScratch* sc, cudaStream_t st) {
+  const int k_slice = gemm_k_slice(M_cap, N, K, BM, BN, BK, sc);
+  const int ks = ceil_div(K, k_slice);
+  dim3 grid(ceil_div(N, BN), ceil_div(M_cap, BM), ks);
+  sgemm_kernel<BM, BN, BK, TM, TN, THREADS, Epi><<<grid, THREADS, 0, st>>>(
+      A, lda, B, ldb, M_cap, M_dev, N, K, k_slice, ks > 1 ? sc->partials : nullptr,
+      ks > 1 ? sc->counters : nullptr, epi);
+  return check_launch("sgemm");
+}
+
 // Tile choice by the row capacity of the launch.
 template <class Epi>
 int sgemm_launch(const float* A, int lda, const float* B, int ldb, int M_cap, const int* M_dev,
-                 int N, int K, const Epi& epi, cudaStream_t st) {
+                 int N, int K, const Epi& epi, cudaStream_t st, const GemmScratch* sc = nullptr) {
   if (M_cap <= 0) return VLLT_OK;
   VLLT_REQUIRE(K % 4 == 0 && N % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0,
                "sgemm: K, N and leading dims must be multiples of 4 (K=%d N=%d)", K, N);
   VLLT_REQUIRE(((uintptr_t)A % 16) == 0 && ((uintptr_t)B % 16) == 0, "sgemm: operands must be 16-byte aligned");
-  constexpr int BN = 64;
-  const int gx = ceil_div(N, BN);
-  if (M_cap <= 16) {
-    sgemm_kernel<16, BN, 1, 4, Epi><<<dim3(gx, ceil_div(M_cap, 16)), 256, 0, st>>>(A, lda, B, ldb, M_cap, M_dev, N, K, epi);
-  } else if (M_cap <= 32) {
-    sgemm_kernel<32, BN, 2, 4, Epi><<<dim3(gx, ceil_div(M_cap, 32)), 256, 0, st>>>(A, lda, B, ldb, M_cap, M_dev, N, K, epi);
-  } else if (M_cap <= 256) {
-    sgemm_kernel<64, BN, 4, 4, Epi><<<dim3(gx, ceil_div(M_cap, 64)), 256, 0, st>>>(A, lda, B, ldb, M_cap, M_dev, N, K, epi);
-  } else {
-    sgemm_kernel<128, BN, 8, 4, Epi><<<dim3(gx, ceil_div(M_cap, 128)), 256, 0, st>>>(A, lda, B, ldb, M_cap, M_dev, N, K, epi);
-  }
-  return check_launch("sgemm");
+  if (M_cap <= 16) return sgemm_go<16, 64, 32, 2, 4, 128>(A, lda, B, ldb, M_cap, M_dev, N, K, epi, sc, st);
+  if (M_cap <= 32) return sgemm_go<32, 64, 32, 4, 4, 128>(A, lda, B, ldb, M_cap, M_dev, N, K, epi, sc, st);
+  if (M_cap <= 64) return sgemm_go<64, 64, 16, 4, 4, 256>(A, lda, B, ldb, M_cap, M_dev, N, K, epi, sc, st);
+  return sgemm_go<128, 64, 16, 8, 4, 256>(A, lda, B, ldb, M_cap, M_dev, N, K, epi, sc, st);
 }
 
 }  // namespace vllt

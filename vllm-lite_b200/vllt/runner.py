@@ -51,44 +51,50 @@ def pack_step(out, block_size: int, num_blocks: int, vocab: int, max_pos: int, q
     """
     items = out.scheduled
     S = len(items)
-    starts = np.empty(S, np.int64)
-    qlens = np.empty(S, np.int64)
-    counts = np.empty(S, np.int64)
-    toks, tables = [], []
+    starts, qlens, counts, toks, tabs = [], [], [], [], []
+    W = 1
+    max_ctx = 1
     for i, item in enumerate(items):
         seq = item.seq
         start, n = item.start_pos, item.num_tokens
-        starts[i], qlens[i] = start, n
-        counts[i] = min(1 + len(seq.draft_token_ids), n)
-        toks.append(seq.token_ids[start:start + n])
-        tables.append(seq.table.block_ids)
-    T = int(qlens.sum())
-    R = int(counts.sum())
-    W = max((len(t) for t in tables), default=1) or 1
-    ctx = starts + qlens
-    if S and qlens.min() < 1:
-        raise ValueError("a scheduled sequence has no tokens")
-    if S and int(ctx.max()) > max_pos:
-        raise IndexError(f"position {int(ctx.max()) - 1} beyond max_seq_len {max_pos}")
-    flat_tok = np.fromiter((t for seg in toks for t in seg), np.int64, T)
-    if T and (flat_tok.min() < 0 or flat_tok.max() >= vocab):
+        if n < 1:
+            raise ValueError("a scheduled sequence has no tokens")
+        ctx = start + n
+        if ctx > max_pos:
+            raise IndexError(f"position {ctx - 1} beyond max_seq_len {max_pos}")
+        bl = seq.table.block_ids
+        if len(bl) * block_size < ctx:
+            raise IndexError(f"block table of sequence {i} too short for {ctx} positions")
+        if bl and (min(bl) < 0 or max(bl) >= num_blocks):
+            raise IndexError("block id out of range")
+        starts.append(start)
+        qlens.append(n)
+        counts.append(min(1 + len(seq.draft_token_ids), n))
+        toks += seq.token_ids[start:ctx]
+        tabs.append(bl)
+        W = max(W, len(bl))
+        max_ctx = max(max_ctx, ctx)
+    T = len(toks)
+    R = sum(counts)
+    if T and (min(toks) < 0 or max(toks) >= vocab):
         raise IndexError("token id out of the vocabulary")
-    tab = np.zeros((S, W), np.int64)
-    for i, t in enumerate(tables):
-        if len(t) * block_size < ctx[i]:
-            raise IndexError(f"block table of sequence {i} too short for {int(ctx[i])} positions")
-        tab[i, :len(t)] = t
-    if tab.size and (tab.min() < 0 or tab.max() >= num_blocks):
-        raise IndexError("block id out of range")
-    rec = np.concatenate([np.asarray([S, T, R, W], np.int64), starts, qlens, counts, flat_tok,
-                          tab.reshape(-1)]).astype(np.int32)
-    multi = qlens[qlens > 1]
-    bounds = StepBounds(T, R, int((qlens == 1).sum()), int(np.sum((multi + qp - 1) // qp)),
-                        int(ctx.max()) if S else 1)
+    words = [S, T, R, W]
+    words += starts
+    words += qlens
+    words += counts
+    words += toks
+    for bl in tabs:
+        words += bl
+        if len(bl) < W:
+            words += [0] * (W - len(bl))
+    rec = np.array(words, dtype=np.int32)
+    n_dec = qlens.count(1)
+    tiles = sum((q + qp - 1) // qp for q in qlens if q > 1)
+    bounds = StepBounds(T, R, n_dec, tiles, max_ctx)
     rows, r0 = [], 0
     for c in counts:
-        rows.append((r0, int(c)))
-        r0 += int(c)
+        rows.append((r0, c))
+        r0 += c
     return rec, bounds, rows, (S, T, R, W)
 
 
@@ -96,7 +102,7 @@ class CudaRunner(_Base):
     """fp32 parity-mode forward pass on one GPU."""
 
     def __init__(self, model_cfg, cache_cfg, sched_cfg=None, *, weights=None, device=None,
-                 max_seqs: int | None = None, max_tokens: int | None = None):
+                 max_seqs: int | None = None, max_tokens: int | None = None, use_graphs: bool = True):
         import torch
 
         if not torch.cuda.is_available():
@@ -119,6 +125,8 @@ class CudaRunner(_Base):
         self._ptrs = self.w.pointer_arrays()
         self.desc = self._make_desc()
         self.caps = Caps(0, 0, 0, 0)
+        self.use_graphs = use_graphs
+        self.graphs = {}  # token bucket -> (CUDAGraph, StepBounds)
         seqs = max_seqs or (sched_cfg.max_seqs if sched_cfg is not None else 64)
         toks = max_tokens or (sched_cfg.max_batched_tokens if sched_cfg is not None else 2048)
         self._reserve(seqs, toks, toks, self._table_width_for(model_cfg.max_seq_len))
@@ -171,11 +179,12 @@ class CudaRunner(_Base):
         self.rec_host = torch.empty(rec_words, dtype=torch.int32, pin_memory=True)
         self.rec_dev = torch.empty(rec_words, dtype=torch.int32, **kw)
         self.meta = torch.empty((meta_bytes + 3) // 4, dtype=torch.int32, **kw)
-        self.ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, **kw)
+        self.ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, **kw)  # split-K counters start at 0
         self.logits_dev = torch.empty((caps.max_rows, self.w.vocab_padded), dtype=torch.float32, **kw)
         self.logits_host = torch.empty((caps.max_rows, self.w.vocab_padded), dtype=torch.float32, pin_memory=True)
         self.counters_host = torch.empty(16, dtype=torch.int32, pin_memory=True)
         self.caps = caps
+        self.graphs = {}  # captured pointers are stale now
 
     # ---- the step ------------------------------------------------------------------
     def pack(self, out):
@@ -206,11 +215,43 @@ class CudaRunner(_Base):
         self.rec_host[:n].numpy()[:] = rec
         self.rec_dev[:n].copy_(self.rec_host[:n], non_blocking=True)
         self.h2d_bytes += 4 * n + 8 * len(out.cow)
+        if self.use_graphs:
+            self._forward_graph(bounds)
+        else:
+            self._forward(bounds)
+        self.steps += 1
+        return rows, R
+
+    def _forward(self, bounds) -> None:
         check(self.L.vllt_forward(C.byref(self.desc), self.rec_dev.data_ptr(), C.byref(self.caps),
                                   C.byref(bounds), self.meta.data_ptr(), self.ws.data_ptr(),
                                   self.ws.numel(), self.logits_dev.data_ptr(), _lib.stream_handle()))
-        self.steps += 1
-        return rows, R
+
+    def bucket(self, b) -> StepBounds:
+        """Bounds of the graph that serves a step: tokens rounded up to a power
+        of two (>= 16); everything else derived from that, so the graph is
+        valid for every step whose token count fits."""
+        c = self.caps
+        T = 16
+        while T < b.tokens:
+            T *= 2
+        T = min(T, c.max_tokens)
+        return StepBounds(T, min(T, c.max_rows), min(T, c.max_seqs), T // self.qp + c.max_seqs, self.w.rope_len)
+
+    def _forward_graph(self, bounds) -> None:
+        """Replay the captured forward of this step's bucket; the first step of
+        a bucket runs eagerly (that run is the step's result) and is captured."""
+        torch = self.torch
+        gb = self.bucket(bounds)
+        hit = self.graphs.get(gb.tokens)
+        if hit is not None:
+            hit[0].replay()
+            return
+        self._forward(gb)  # eager: this step's result, and first-use setup of every kernel
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._forward(gb)  # captured only; replays recompute a step idempotently
+        self.graphs[gb.tokens] = (g, gb)
 
     def execute(self, out):
         """(logits float32 [n_rows, vocab], rows), as vllmlite/runner.py:62-100."""
