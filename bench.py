@@ -265,12 +265,17 @@ def main_ours(args):
             torch.distributed.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        l0 = L.vllt_kernel_launches()
+        run = engine.runner
+
+        def launched():  # kernels executed: direct launches + graph replays - capture-time calls
+            return L.vllt_kernel_launches() + run.replayed_kernels - run.captured_kernels
+
+        l0 = launched()
         e0.record()
         toks, ttft, steps = run_workload(engine, reqs, tag)
         e1.record()
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / 1e3, toks, ttft, steps, L.vllt_kernel_launches() - l0
+        return e0.elapsed_time(e1) / 1e3, toks, ttft, steps, launched() - l0
 
     res = []
     with Clocks(local) as clk:

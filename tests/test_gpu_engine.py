@@ -75,20 +75,28 @@ def test_runner_replay_logits(name, bs):
     assert worst < 1e-4, worst
 
 
-def test_graph_replay_is_bit_identical_to_eager():
-    """CUDA-graph replays (bucketed bounds) give exactly the eager logits."""
+def test_graph_replay_matches_eager():
+    """CUDA-graph replays equal eager runs with the same (bucketed) bounds bit
+    for bit; against eager runs with exact bounds they differ only by fp32
+    reassociation (the split-K slicing follows the row capacity)."""
     from vllmlite.config import CacheConfig
 
     from vllt.runner import CudaRunner
 
     steps = F.replay_steps("replay_spec.npz")
-    eager = CudaRunner(model_cfg(F.BENCH), CacheConfig(block_size=4, num_blocks=512), use_graphs=False)
-    graph = CudaRunner(model_cfg(F.BENCH), CacheConfig(block_size=4, num_blocks=512), use_graphs=True)
+    mk = lambda **kw: CudaRunner(model_cfg(F.BENCH), CacheConfig(block_size=4, num_blocks=512), **kw)
+    eager = mk(use_graphs=False)
+    eager_b = mk(use_graphs=False, bucket_bounds=True)
+    graph = mk(use_graphs=True)
     for seqs, cow, want in steps + steps:  # the second pass replays captured graphs
-        a, _ = eager.execute(F.as_scheduler_output(seqs, cow))
-        b, _ = graph.execute(F.as_scheduler_output(seqs, cow))
-        np.testing.assert_array_equal(a, b)
-    assert len(graph.graphs) >= 2
+        out = F.as_scheduler_output(seqs, cow)
+        a, _ = eager.execute(out)
+        ab, _ = eager_b.execute(out)
+        b, _ = graph.execute(out)
+        np.testing.assert_array_equal(ab, b)
+        np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-5)
+        assert (a.argmax(1) == b.argmax(1)).all()
+    assert len(graph.graphs) >= 2 and graph.replayed_kernels > 0
 
 
 def test_runner_copy_on_write_before_writes():

@@ -102,7 +102,8 @@ class CudaRunner(_Base):
     """fp32 parity-mode forward pass on one GPU."""
 
     def __init__(self, model_cfg, cache_cfg, sched_cfg=None, *, weights=None, device=None,
-                 max_seqs: int | None = None, max_tokens: int | None = None, use_graphs: bool = True):
+                 max_seqs: int | None = None, max_tokens: int | None = None, use_graphs: bool = True,
+                 bucket_bounds: bool = False):
         import torch
 
         if not torch.cuda.is_available():
@@ -126,7 +127,10 @@ class CudaRunner(_Base):
         self.desc = self._make_desc()
         self.caps = Caps(0, 0, 0, 0)
         self.use_graphs = use_graphs
-        self.graphs = {}  # token bucket -> (CUDAGraph, StepBounds)
+        self.bucket_bounds = bucket_bounds  # eager runs with the graphs' bounds (tests)
+        self.graphs = {}  # token bucket -> (CUDAGraph, StepBounds, kernels in the graph)
+        self.replayed_kernels = 0  # kernels launched by graph replays
+        self.captured_kernels = 0  # launch-site calls made while capturing (not executed)
         seqs = max_seqs or (sched_cfg.max_seqs if sched_cfg is not None else 64)
         toks = max_tokens or (sched_cfg.max_batched_tokens if sched_cfg is not None else 2048)
         self._reserve(seqs, toks, toks, self._table_width_for(model_cfg.max_seq_len))
@@ -218,7 +222,7 @@ class CudaRunner(_Base):
         if self.use_graphs:
             self._forward_graph(bounds)
         else:
-            self._forward(bounds)
+            self._forward(self.bucket(bounds) if self.bucket_bounds else bounds)
         self.steps += 1
         return rows, R
 
@@ -246,12 +250,16 @@ class CudaRunner(_Base):
         hit = self.graphs.get(gb.tokens)
         if hit is not None:
             hit[0].replay()
+            self.replayed_kernels += hit[2]
             return
         self._forward(gb)  # eager: this step's result, and first-use setup of every kernel
         g = torch.cuda.CUDAGraph()
+        n0 = self.L.vllt_kernel_launches()
         with torch.cuda.graph(g):
             self._forward(gb)  # captured only; replays recompute a step idempotently
-        self.graphs[gb.tokens] = (g, gb)
+        n = self.L.vllt_kernel_launches() - n0
+        self.captured_kernels += n
+        self.graphs[gb.tokens] = (g, gb, n)
 
     def execute(self, out):
         """(logits float32 [n_rows, vocab], rows), as vllmlite/runner.py:62-100."""
