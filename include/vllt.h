@@ -149,6 +149,35 @@ int vllt_paged_attention_varlen(const void* q, const void* k_cache, const void* 
                                 float scale, int32_t dtype, void* out, void* workspace,
                                 int64_t workspace_bytes, void* stream);
 
+/* The same attention, for callers that cannot allocate device memory: it
+ * takes no workspace and keeps its split-K scratch and error word in a static
+ * device array inside this library. No counterpart in the reference (which has
+ * no device code); it exists for integrations that run under a device-memory
+ * budget owned by someone else, that must not call cudaMalloc on their hot path
+ * (cudaMalloc can synchronize the device), or whose interface hands them only
+ * input and output buffers.
+ *   - Scratch: 16 MiB per device, held by every GPU that loads the library
+ *     until the process exits. A batch needing more (vllt_attention_workspace_bytes
+ *     > 16 MiB, e.g. ~250 single-query sequences x 32 heads at 4096 context) is
+ *     rejected with VLLT_ERR_ARG.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ *   - Every call shares the one array and it keeps the last call's contents;
+ *     the error word is cleared at the start of each call. Calls that overlap
+ *     on the GPU (other streams, other threads) race on it: serialize them.
+ *   - device_flags (optional device int32) receives the call's error flags
+ *     (bit 2: a bounded wait on a TMA copy expired).
+ * Allocates nothing: no cudaMalloc / cudaFree, no allocating library call. */
+int vllt_paged_attention_varlen_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                        const int32_t* block_tables, int32_t table_width,
+                                        const int32_t* cu_seqlens_q, const int32_t* ctx_lens,
+                                        int32_t num_seqs, int32_t num_tokens, int32_t max_qlen,
+                                        int32_t max_ctx, int32_t n_heads, int32_t n_kv,
+                                        int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                                        float scale, int32_t dtype, void* out,
+                                        int32_t* device_flags, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Layer pieces                                                             */
 /* ------------------------------------------------------------------------ */

@@ -54,6 +54,8 @@ SIGNATURES = {
     "vllt_attention_workspace_bytes": (i64, [i32, i32, i32, i32]),
     "vllt_paged_attention_varlen": (C.c_int, [vp, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, i32,
                                               i32, i32, i32, i32, f32, i32, vp, vp, i64, vp]),
+    "vllt_paged_attention_varlen_noalloc": (C.c_int, [vp, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, i32,
+                                                      i32, i32, i32, i32, f32, i32, vp, vp, vp]),
     "vllt_rmsnorm": (C.c_int, [vp, vp, vp, vp, i32, i32, f32, vp]),
     "vllt_rope": (C.c_int, [vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "vllt_sgemm": (C.c_int, [vp, vp, vp, i32, i32, i32, vp]),
