@@ -199,6 +199,14 @@ int vllt_rope(float* x, const int32_t* positions, const float* cos_t, const floa
 int vllt_sgemm(const float* A, const float* B, float* C, int32_t M, int32_t N, int32_t K,
                void* stream);
 
+/* C[M][N] = A[M][K] . W[N][K]^T on the tcgen05 tensor cores: bf16 A and W (both
+ * K-major, i.e. W is stored [out][in]), fp32 accumulate in tensor memory, fp32 C.
+ * K must be a multiple of 64; device_flags (device int32) receives bit 2 if a
+ * bounded wait expired. The bf16 projections of the Llama-3-8B-shaped model
+ * (the bf16 counterpart of vllmlite/model.py:98-120) run on this kernel. */
+int vllt_gemm_bf16(const void* A, const void* W, float* C, int32_t M, int32_t N, int32_t K,
+                   int32_t* device_flags, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Sampling (vllmlite/sampling.py:41-64, vllmlite/speculative.py:86-100)    */
 /* ------------------------------------------------------------------------ */

@@ -59,6 +59,7 @@ SIGNATURES = {
     "vllt_rmsnorm": (C.c_int, [vp, vp, vp, vp, i32, i32, f32, vp]),
     "vllt_rope": (C.c_int, [vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "vllt_sgemm": (C.c_int, [vp, vp, vp, i32, i32, i32, vp]),
+    "vllt_gemm_bf16": (C.c_int, [vp, vp, vp, i32, i32, i32, vp, vp]),
     "vllt_sample_greedy": (C.c_int, [vp, i32, i32, i32, vp, i32, vp, vp, vp, vp]),
     "vllt_sample_top_p": (C.c_int, [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp]),
     "vllt_spec_verify": (C.c_int, [vp, i32, i32, vp, i32, vp, vp, i32, vp, vp, vp]),
