@@ -250,29 +250,42 @@ int vllt_spec_accept(const int32_t* cu_rows, const int32_t* drafts, const int32_
 /* ------------------------------------------------------------------------ */
 
 typedef struct vllt_model_desc {
-  /* shape */
+  /* shape of THIS rank's shard: n_heads, n_kv_heads, d_ff, vocab and
+   * vocab_padded are per rank when tp_size > 1 (heads / FFN columns / vocab
+   * rows split evenly); d_model, head_dim and embed_rows are global. */
   int32_t n_layers, n_heads, n_kv_heads, head_dim, d_model, d_ff, vocab, vocab_padded;
   int32_t max_seq_len, block_size, num_blocks;
   float rms_eps;
-  int32_t dtype; /* VLLT_F32 (parity mode) */
-  /* weights (device, fp32). Per-layer arrays hold n_layers host-side pointers:
+  int32_t dtype;      /* VLLT_F32: fp32 parity path; VLLT_BF16: bf16 weights/activations */
+  int32_t tp_size;    /* tensor-parallel ranks (1 = none) */
+  int32_t embed_rows; /* rows of tok_emb (the full vocabulary) */
+  void* tp_comm;      /* communicator from vllt_tp_init when tp_size > 1 */
+  /* weights (device). Per-layer arrays hold n_layers host-side pointers.
+   * VLLT_F32 (all fp32, the reference's [in][out] orientation):
    *   wqkv[l]   [d_model][(n_heads + 2*n_kv_heads)*head_dim]  = [wq | wk | wv]
    *   wo[l]     [n_heads*head_dim][d_model]
    *   w_gu[l]   [d_model][2*d_ff], column 2j = w_gate[:, j], 2j+1 = w_up[:, j]
    *   w_down[l] [d_ff][d_model]
-   *   lm_head   [d_model][vocab_padded] (zero columns past vocab)          */
-  const float* tok_emb;
+   *   lm_head   [d_model][vocab_padded] (zero columns past vocab)
+   * VLLT_BF16 (bf16, K-major [out][in] for the tcgen05 GEMM; norms fp32):
+   *   wqkv[l]   [(n_heads + 2*n_kv_heads)*head_dim][d_model]  rows [q | k | v]
+   *   wo[l]     [d_model][n_heads*head_dim]
+   *   w_gu[l]   [2*d_ff][d_model], row 2j = gate_j, 2j+1 = up_j
+   *   w_down[l] [d_model][d_ff]
+   *   lm_head   [vocab][d_model]  (this rank's vocabulary rows)
+   *   tok_emb   [embed_rows][d_model] bf16                                   */
+  const void* tok_emb;
   const float* final_norm;
-  const float* lm_head;
+  const void* lm_head;
   const float* rope_cos; /* [max_seq_len][head_dim/2] */
   const float* rope_sin;
   const float* const* attn_norm;
-  const float* const* wqkv;
-  const float* const* wo;
+  const void* const* wqkv;
+  const void* const* wo;
   const float* const* ffn_norm;
-  const float* const* w_gu;
-  const float* const* w_down;
-  /* KV cache base: [n_layers][num_blocks][n_kv][block_size][head_dim] */
+  const void* const* w_gu;
+  const void* const* w_down;
+  /* KV cache base: [n_layers][num_blocks][n_kv][block_size][head_dim], dtype */
   void* k_cache;
   void* v_cache;
 } vllt_model_desc;
@@ -297,10 +310,31 @@ int64_t vllt_forward_workspace_bytes(const vllt_model_desc* m, const vllt_caps* 
  * fused in its epilogue -> paged attention -> o_proj + residual -> RMSNorm ->
  * gate/up GEMM with SwiGLU -> down + residual), then the final RMSNorm and
  * lm_head on the logit rows only. logits: [max_rows][vocab_padded] fp32;
- * rows >= R are left untouched. */
+ * rows >= R are left untouched. With dtype VLLT_BF16 the projections run on
+ * the tcgen05 GEMM, the residual stream stays fp32, and with tp_size > 1 the
+ * o_proj / down_proj partials are all-reduced (NCCL, bf16) before they join
+ * the residual; logits are this rank's vocabulary slice. */
 int vllt_forward(const vllt_model_desc* m, const int32_t* step_record, const vllt_caps* caps,
                  const vllt_step_bounds* bounds, void* meta, void* workspace,
                  int64_t workspace_bytes, float* logits, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Tensor parallelism (bf16 model): NCCL, loaded at run time                */
+/* ------------------------------------------------------------------------ */
+
+/* 128-byte communicator id, made on one rank and shared with the others. */
+int vllt_tp_unique_id(uint8_t* out128);
+/* Join the communicator (call on every rank concurrently, device current). */
+int vllt_tp_init(const uint8_t* id128, int32_t rank, int32_t world, void** comm_out);
+int vllt_tp_destroy(void* comm);
+/* In-place sum over ranks of a bf16 buffer (used between row-parallel layers). */
+int vllt_tp_allreduce_bf16(void* buf, int64_t count, void* comm, void* stream);
+
+/* Per logit row: the maximum and the FIRST index of it (np.argmax), index
+ * shifted by vocab_offset (this rank's first vocabulary row). Vocab-parallel
+ * greedy: each rank reduces its slice, the host or a gather picks the max. */
+int vllt_argmax_rows(const float* logits, int32_t rows, int32_t vocab, int32_t ld, int32_t vocab_offset,
+                     float* out_val, int32_t* out_idx, void* stream);
 
 #ifdef __cplusplus
 }

@@ -33,6 +33,10 @@ int check_launch(const char* what) {
   return VLLT_OK;
 }
 
+int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* caps, const vllt_step_bounds* b,
+                 void* meta_v, void* ws, int64_t ws_bytes, float* logits, cudaStream_t st);
+int64_t forward_bf16_ws_bytes(const vllt_model_desc* m, const vllt_caps* caps);
+
 namespace {
 
 #define VLLT_TRY(expr)             \
@@ -86,7 +90,10 @@ FwdWs carve(const vllt_model_desc* m, const vllt_caps* c, char* base) {
 
 int check_desc(const vllt_model_desc* m) {
   VLLT_REQUIRE(m, "model desc is NULL");
-  VLLT_REQUIRE(m->dtype == VLLT_F32, "vllt_forward: only the fp32 parity path is built");
+  VLLT_REQUIRE(m->dtype == VLLT_F32 || m->dtype == VLLT_BF16, "vllt_forward: dtype must be F32 or BF16");
+  VLLT_REQUIRE(m->tp_size >= 1 && (m->tp_size == 1 || m->dtype == VLLT_BF16),
+               "vllt_forward: tensor parallelism is built for the bf16 model only");
+  VLLT_REQUIRE(m->embed_rows >= (m->tp_size == 1 ? m->vocab : 1), "vllt_forward: embed_rows too small");
   VLLT_REQUIRE(m->n_layers > 0 && m->n_heads > 0 && m->n_kv_heads > 0 &&
                    m->n_heads % m->n_kv_heads == 0 && m->head_dim > 0 && m->d_model > 0 &&
                    m->d_ff > 0 && m->vocab > 0 && m->vocab_padded >= m->vocab &&
@@ -109,6 +116,7 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
                  float* logits, cudaStream_t st) {
   VLLT_TRY(check_desc(m));
   VLLT_REQUIRE(caps_ok(caps) && b && rec && meta_v && ws && logits, "vllt_forward: bad arguments");
+  if (m->dtype == VLLT_BF16) return forward_bf16(m, rec, caps, b, meta_v, ws, ws_bytes, logits, st);
   const FwdWs w = carve(m, caps, reinterpret_cast<char*>(ws));
   VLLT_REQUIRE(ws_bytes >= w.total_bytes, "vllt_forward: workspace too small (%lld < %lld)",
                (long long)ws_bytes, (long long)w.total_bytes);
@@ -129,7 +137,7 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   const float eps = m->rms_eps;
 
   VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks, n_rep, meta, st));
-  VLLT_TRY(embed(m->tok_emb, meta + L.tokens, w.x, T_cap, T_dev, d, m->vocab, st));
+  VLLT_TRY(embed(reinterpret_cast<const float*>(m->tok_emb), meta + L.tokens, w.x, T_cap, T_dev, d, m->vocab, st));
 
   AttnCall ac{};
   ac.q = w.q;
@@ -153,7 +161,8 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
     VLLT_TRY(rmsnorm(w.x, nullptr, m->attn_norm[l], w.h, T_cap, T_dev, d, eps, st));
     EpiQKV eq{w.q, kc, vc, meta + L.pos, meta + L.slot, m->rope_cos, m->rope_sin,
               H, KV, D, m->block_size, m->max_seq_len, (int64_t)m->num_blocks * m->block_size};
-    VLLT_TRY(sgemm_launch(w.h, d, m->wqkv[l], qkv_n, T_cap, T_dev, qkv_n, d, eq, st, &w.gemm));
+    VLLT_TRY(sgemm_launch(w.h, d, reinterpret_cast<const float*>(m->wqkv[l]), qkv_n, T_cap, T_dev, qkv_n, d, eq, st,
+                          &w.gemm));
     // attention: single-query sequences, then multi-token tiles
     ac.kc = kc;
     ac.vc = vc;
@@ -162,17 +171,19 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
     VLLT_TRY(attention_pass(ac, meta + L.tile_seq, meta + L.tile_q0, meta + kCntTiles, tiles_cap,
                             0, 0, false, max_ctx, st));
     // x += attn @ wo
-    VLLT_TRY(sgemm_launch(w.attn, H * D, m->wo[l], d, T_cap, T_dev, d, H * D, EpiResidual{w.x, d}, st, &w.gemm));
+    VLLT_TRY(sgemm_launch(w.attn, H * D, reinterpret_cast<const float*>(m->wo[l]), d, T_cap, T_dev, d, H * D,
+                          EpiResidual{w.x, d}, st, &w.gemm));
     // x += (silu(h @ w_gate) * (h @ w_up)) @ w_down
     VLLT_TRY(rmsnorm(w.x, nullptr, m->ffn_norm[l], w.h, T_cap, T_dev, d, eps, st));
-    VLLT_TRY(sgemm_launch(w.h, d, m->w_gu[l], 2 * m->d_ff, T_cap, T_dev, 2 * m->d_ff, d,
+    VLLT_TRY(sgemm_launch(w.h, d, reinterpret_cast<const float*>(m->w_gu[l]), 2 * m->d_ff, T_cap, T_dev, 2 * m->d_ff, d,
                           EpiSwiGLU{w.act, m->d_ff}, st, &w.gemm));
-    VLLT_TRY(sgemm_launch(w.act, m->d_ff, m->w_down[l], d, T_cap, T_dev, d, m->d_ff,
+    VLLT_TRY(sgemm_launch(w.act, m->d_ff, reinterpret_cast<const float*>(m->w_down[l]), d, T_cap, T_dev, d, m->d_ff,
                           EpiResidual{w.x, d}, st, &w.gemm));
   }
   // logits only for the wanted rows (model.py:119-120)
   VLLT_TRY(rmsnorm(w.x, meta + L.rows, m->final_norm, w.rows_h, R_cap, R_dev, d, eps, st));
-  VLLT_TRY(sgemm_launch(w.rows_h, d, m->lm_head, m->vocab_padded, R_cap, R_dev, m->vocab_padded, d,
+  VLLT_TRY(sgemm_launch(w.rows_h, d, reinterpret_cast<const float*>(m->lm_head), m->vocab_padded, R_cap, R_dev,
+                        m->vocab_padded, d,
                         EpiStore{logits, m->vocab_padded, m->vocab_padded}, st, &w.gemm));
   return VLLT_OK;
 }
@@ -352,6 +363,15 @@ int vllt_spec_verify(const float* logits, int32_t ld, int32_t vocab, const int32
   return spec_accept(cu_rows, drafts, draft_offsets, num_seqs, out_tokens, n_accepted, st);
 }
 
+int vllt_argmax_rows(const float* logits, int32_t rows, int32_t vocab, int32_t ld, int32_t vocab_offset,
+                     float* out_val, int32_t* out_idx, void* stream) {
+  clear_error();
+  VLLT_REQUIRE(rows >= 0 && vocab > 0 && ld >= vocab, "argmax_rows: bad sizes");
+  if (rows == 0) return VLLT_OK;
+  VLLT_REQUIRE(logits && out_val && out_idx, "argmax_rows: null pointer");
+  return argmax_rows(logits, rows, nullptr, vocab, ld, vocab_offset, out_val, out_idx, as_stream(stream));
+}
+
 int vllt_spec_accept(const int32_t* cu_rows, const int32_t* drafts, const int32_t* draft_offsets,
                      int32_t num_seqs, const int32_t* picks, int32_t* n_accepted, void* stream) {
   clear_error();
@@ -363,6 +383,7 @@ int vllt_spec_accept(const int32_t* cu_rows, const int32_t* drafts, const int32_
 
 int64_t vllt_forward_workspace_bytes(const vllt_model_desc* m, const vllt_caps* caps) {
   if (!m || !caps_ok(caps)) return -1;
+  if (m->dtype == VLLT_BF16) return forward_bf16_ws_bytes(m, caps);
   return carve(m, caps, nullptr).total_bytes;
 }
 

@@ -233,3 +233,163 @@ struct EpiStoreBF16 {  // C bf16 [M][ldc], columns < n_valid
 };
 
 }  // namespace vllt
+
+namespace vllt {
+
+// x[row][col..] += acc (fp32 residual stream; tensor-parallel size 1)
+struct EpiResidualF32 {
+  float* x;
+  int ld;
+  template <int TN> __device__ void apply(int row, int col, const float (&v)[TN]) const {
+    float* dst = x + (int64_t)row * ld + col;
+#pragma unroll
+    for (int j = 0; j < TN; j += 4) {
+      float4 o = *reinterpret_cast<float4*>(dst + j);
+      o.x += v[j]; o.y += v[j + 1]; o.z += v[j + 2]; o.w += v[j + 3];
+      *reinterpret_cast<float4*>(dst + j) = o;
+    }
+  }
+};
+
+// columns interleaved (gate_j, up_j) -> act[row][col/2 + j] = silu(gate_j) * up_j, bf16
+struct EpiSwiGLUBF16 {
+  __nv_bfloat16* act;
+  int ld;
+  template <int TN> __device__ void apply(int row, int col, const float (&v)[TN]) const {
+    __nv_bfloat16* dst = act + (int64_t)row * ld + col / 2;
+#pragma unroll
+    for (int j = 0; j < TN / 2; j += 2) {
+      const float g0 = v[2 * j], u0 = v[2 * j + 1], g1 = v[2 * j + 2], u1 = v[2 * j + 3];
+      const float a0 = g0 / (1.0f + __expf(-g0)) * u0, a1 = g1 / (1.0f + __expf(-g1)) * u1;
+      *reinterpret_cast<__nv_bfloat162*>(dst + j) = __floats2bfloat162_rn(a0, a1);
+    }
+  }
+};
+
+// QKV projection (bf16 model): RoPE on q and k columns (interleaved pairs,
+// vllmlite/attention.py:28-37), q -> bf16 buffer, k and v -> bf16 paged cache
+// at the token's slot. 32 columns never straddle a head (head_dim % 32 == 0).
+struct EpiQKVBF16 {
+  __nv_bfloat16* q_out;  // [T][H*D]
+  __nv_bfloat16* kc;     // layer base [NB][n_kv][bs][D]
+  __nv_bfloat16* vc;
+  const int32_t* pos;
+  const int32_t* slot;
+  const float* cos_t;    // [max_pos][D/2]
+  const float* sin_t;
+  int H, n_kv, D, bs, max_pos;
+  int64_t num_slots;
+  template <int TN> __device__ void apply(int row, int col, const float (&v)[TN]) const {
+    const int qw = H * D, kw = n_kv * D;
+    float o[TN];
+    if (col < qw + kw) {
+      const int d0 = col % D;
+      const int p = min(max(pos[row], 0), max_pos - 1);
+      const float* cr = cos_t + (int64_t)p * (D / 2) + d0 / 2;
+      const float* sr = sin_t + (int64_t)p * (D / 2) + d0 / 2;
+#pragma unroll
+      for (int j = 0; j < TN; j += 2) {
+        const float c = cr[j / 2], s = sr[j / 2];
+        o[j] = v[j] * c - v[j + 1] * s;
+        o[j + 1] = v[j] * s + v[j + 1] * c;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < TN; ++j) o[j] = v[j];
+    }
+    __nv_bfloat16* dst;
+    if (col < qw) {
+      dst = q_out + (int64_t)row * qw + col;
+    } else {
+      const int64_t sl = slot[row];
+      if (sl < 0 || sl >= num_slots) return;
+      const int64_t blk = sl / bs, off = sl % bs;
+      const bool is_k = col < qw + kw;
+      const int c = col - qw - (is_k ? 0 : kw);
+      dst = (is_k ? kc : vc) + ((blk * n_kv + c / D) * bs + off) * D + c % D;
+    }
+#pragma unroll
+    for (int j = 0; j < TN; j += 8) {
+      uint4 w;
+      __nv_bfloat162 t0 = __floats2bfloat162_rn(o[j], o[j + 1]), t1 = __floats2bfloat162_rn(o[j + 2], o[j + 3]);
+      __nv_bfloat162 t2 = __floats2bfloat162_rn(o[j + 4], o[j + 5]), t3 = __floats2bfloat162_rn(o[j + 6], o[j + 7]);
+      w.x = *reinterpret_cast<uint32_t*>(&t0); w.y = *reinterpret_cast<uint32_t*>(&t1);
+      w.z = *reinterpret_cast<uint32_t*>(&t2); w.w = *reinterpret_cast<uint32_t*>(&t3);
+      *reinterpret_cast<uint4*>(dst + j) = w;
+    }
+  }
+};
+
+}  // namespace vllt
+
+// ---- host launcher ----------------------------------------------------------------
+namespace vllt {
+
+namespace tc {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  }
+  return fn;
+}
+
+// K-major bf16 matrix [rows][K]: boxes of 64 (K) x box_rows, 128-byte swizzle.
+inline int kmajor_map(CUtensorMap* m, const void* base, int64_t rows, int K, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    set_error("gemm_bf16: cuTensorMapEncodeTiled unavailable");
+    return VLLT_ERR_CUDA;
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)tc::BK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("gemm_bf16: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return VLLT_ERR_CUDA;
+  }
+  return VLLT_OK;
+}
+
+}  // namespace tc
+
+// D = A . W^T through an epilogue. A [M_cap][K], W [N][K] bf16, K % 64 == 0.
+template <class Epi>
+inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const void* W, int N, int K, const Epi& epi,
+                     int* err, cudaStream_t st) {
+  if (M_cap <= 0 || N <= 0) return VLLT_OK;
+  VLLT_REQUIRE(K > 0 && K % tc::BK == 0, "gemm_bf16: K must be a positive multiple of 64 (K=%d)", K);
+  VLLT_REQUIRE(((uintptr_t)A & 15) == 0 && ((uintptr_t)W & 15) == 0, "gemm_bf16: operands must be 16-byte aligned");
+  VLLT_REQUIRE(err, "gemm_bf16: device error word required");
+  CUtensorMap ta, tb;
+  int rc = tc::kmajor_map(&ta, A, M_cap, K, tc::BM);
+  if (rc != VLLT_OK) return rc;
+  rc = tc::kmajor_map(&tb, W, N, K, tc::BN);
+  if (rc != VLLT_OK) return rc;
+  static unsigned configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 32 && !(configured & (1u << dev))) {
+    cudaFuncSetAttribute(tc::gemm_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
+    configured |= 1u << dev;
+  }
+  dim3 grid(ceil_div(N, tc::BN), ceil_div(M_cap, tc::BM));
+  tc::gemm_kernel<Epi><<<grid, 128, tc::SMEM_BYTES, st>>>(ta, tb, M_cap, M_dev, N, K, epi, err);
+  return check_launch("gemm_bf16");
+}
+
+}  // namespace vllt
+

@@ -15,6 +15,12 @@ int rmsnorm(const float* x, const int32_t* idx, const float* w, float* out, int 
             const int32_t* rows_dev, int dim, float eps, cudaStream_t st);
 int embed(const float* emb, const int32_t* tok, float* x, int T_cap, const int32_t* T_dev, int dim,
           int vocab, cudaStream_t st);
+int embed_bf16(const void* emb, const int32_t* tok, float* x, int T_cap, const int32_t* T_dev, int dim,
+               int vocab, cudaStream_t st);
+int rmsnorm_bf16(float* x, const void* add, const int32_t* idx, const float* w, void* out, int rows_cap,
+                 const int32_t* rows_dev, int dim, float eps, cudaStream_t st);
+int argmax_rows(const float* logits, int rows_cap, const int32_t* rows_dev, int vocab, int ld, int offset,
+                float* val, int32_t* idx, cudaStream_t st);
 int rope(float* x, const int32_t* positions, const float* cos_t, const float* sin_t, int T,
          int heads, int D, int max_pos, cudaStream_t st);
 

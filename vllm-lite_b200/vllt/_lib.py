@@ -34,7 +34,7 @@ class ModelDesc(C.Structure):
         ("n_layers", i32), ("n_heads", i32), ("n_kv_heads", i32), ("head_dim", i32),
         ("d_model", i32), ("d_ff", i32), ("vocab", i32), ("vocab_padded", i32),
         ("max_seq_len", i32), ("block_size", i32), ("num_blocks", i32),
-        ("rms_eps", f32), ("dtype", i32),
+        ("rms_eps", f32), ("dtype", i32), ("tp_size", i32), ("embed_rows", i32), ("tp_comm", vp),
         ("tok_emb", vp), ("final_norm", vp), ("lm_head", vp), ("rope_cos", vp), ("rope_sin", vp),
         ("attn_norm", PP), ("wqkv", PP), ("wo", PP), ("ffn_norm", PP), ("w_gu", PP), ("w_down", PP),
         ("k_cache", vp), ("v_cache", vp),
@@ -64,6 +64,11 @@ SIGNATURES = {
     "vllt_sample_top_p": (C.c_int, [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp]),
     "vllt_spec_verify": (C.c_int, [vp, i32, i32, vp, i32, vp, vp, i32, vp, vp, vp]),
     "vllt_spec_accept": (C.c_int, [vp, vp, vp, i32, vp, vp, vp]),
+    "vllt_tp_unique_id": (C.c_int, [vp]),
+    "vllt_tp_init": (C.c_int, [vp, i32, i32, C.POINTER(vp)]),
+    "vllt_tp_destroy": (C.c_int, [vp]),
+    "vllt_tp_allreduce_bf16": (C.c_int, [vp, i64, vp, vp]),
+    "vllt_argmax_rows": (C.c_int, [vp, i32, i32, i32, i32, vp, vp, vp]),
     "vllt_forward_workspace_bytes": (i64, [C.POINTER(ModelDesc), C.POINTER(Caps)]),
     "vllt_forward": (C.c_int, [C.POINTER(ModelDesc), vp, C.POINTER(Caps), C.POINTER(StepBounds),
                                vp, vp, i64, vp, vp]),

@@ -24,16 +24,20 @@ from .runner import CudaRunner
 
 
 def cuda_engine(cfg=None, tokenizer=None, speculative_tokens: int = 0, weights=None, device=None,
-                engine_cls=None):
-    """Build an LLMEngine (or `engine_cls`) with a CudaRunner behind it."""
+                engine_cls=None, runner_cls=None, **runner_kw):
+    """Build an LLMEngine (or `engine_cls`) with a CudaRunner (or `runner_cls`,
+    e.g. vllt.llama.LlamaRunner / vllt.tp.TPLlamaRunner) behind it."""
     import vllmlite.engine as E
     from vllmlite.config import EngineConfig
 
     cfg = cfg or EngineConfig()
     orig = E.NumpyRunner
+    cls_r = runner_cls or CudaRunner
+    if weights is not None:
+        runner_kw["weights"] = weights
 
     def factory(model_cfg, cache_cfg):
-        return CudaRunner(model_cfg, cache_cfg, cfg.scheduler, weights=weights, device=device)
+        return cls_r(model_cfg, cache_cfg, cfg.scheduler, device=device, **runner_kw)
 
     E.NumpyRunner = factory
     try:
@@ -68,9 +72,10 @@ class GpuLLMEngine(metaclass=_Lazy):
     """Use `gpu_engine(cfg, ...)`; instances are LLMEngine subclasses."""
 
 
-def gpu_engine(cfg=None, tokenizer=None, speculative_tokens: int = 0, weights=None, device=None):
+def gpu_engine(cfg=None, tokenizer=None, speculative_tokens: int = 0, weights=None, device=None,
+               runner_cls=None, **runner_kw):
     return cuda_engine(cfg, tokenizer, speculative_tokens, weights, device,
-                       engine_cls=GpuLLMEngine.resolve())
+                       engine_cls=GpuLLMEngine.resolve(), runner_cls=runner_cls, **runner_kw)
 
 
 def _make_gpu_engine(Base):
@@ -118,9 +123,21 @@ def _make_gpu_engine(Base):
             def h2d(a):
                 return torch.from_numpy(np.ascontiguousarray(a)).to(dev, non_blocking=True)
 
-            picks = torch.empty(max(R, 1), dtype=torch.int32, device=dev)
             acc = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
             L = run.L
+            if getattr(run, "tp_size", 1) > 1:
+                # vocab-parallel greedy; rows needing masks or sampling are not supported across shards
+                if eos_mask.any() or (penalty != 1.0).any() or sampled:
+                    raise NotImplementedError("tensor-parallel engine: greedy rows without min_tokens / "
+                                              "repetition penalty only")
+                picks = run.greedy_picks(R)
+                if drafts:
+                    d_cu, d_dr, d_doff = h2d(cu), h2d(np.asarray(drafts, np.int32)), h2d(doff)
+                    check(L.vllt_spec_accept(d_cu.data_ptr(), d_dr.data_ptr(), d_doff.data_ptr(), S,
+                                             picks.data_ptr(), acc.data_ptr(), st))
+                acc_h = acc[:S].cpu().numpy() if drafts else np.zeros(S, np.int32)
+                return picks[:R].cpu().numpy(), acc_h, {}
+            picks = torch.empty(max(R, 1), dtype=torch.int32, device=dev)
             d_mask = h2d(eos_mask) if eos_mask.any() else None
             d_pen = bits = None
             if (penalty != 1.0).any():

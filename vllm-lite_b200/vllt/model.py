@@ -83,7 +83,9 @@ def rope_tables(head_dim: int, max_pos: int, theta: float = 10000.0):
 class DeviceWeights:
     """fp32 device copies in libvllt's layout; keeps the tensors alive."""
 
-    def __init__(self, cfg, weights: dict[str, np.ndarray], device="cuda", rope_len: int | None = None):
+    def __init__(self, cfg, weights: dict, device="cuda", rope_len: int | None = None):
+        """weights: NumPy arrays or torch tensors (any device) in the reference's
+        naming and [in][out] orientation."""
         import torch
 
         d, hd, H, KV, dff, V = _dims(cfg)
@@ -91,28 +93,29 @@ class DeviceWeights:
         dev = torch.device(device)
 
         def up(a):
+            if isinstance(a, torch.Tensor):
+                return a.to(device=dev, dtype=torch.float32).contiguous()
             return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
 
         self.tok_emb = up(weights["tok_emb"])
         self.final_norm = up(weights["final_norm"])
-        lm = np.zeros((d, self.vocab_padded), np.float32)
-        lm[:, :V] = weights["lm_head"]
-        self.lm_head = up(lm)
+        self.lm_head = torch.zeros((d, self.vocab_padded), dtype=torch.float32, device=dev)
+        self.lm_head[:, :V] = up(weights["lm_head"])
         cos, sin = rope_tables(hd, rope_len or cfg.max_seq_len)
         self.rope_cos, self.rope_sin = up(cos), up(sin)
         self.rope_len = cos.shape[0]
         self.layers = []
         for i in range(cfg.n_layers):
             p = f"layers.{i}."
-            gu = np.empty((d, 2 * dff), np.float32)
-            gu[:, 0::2] = weights[p + "w_gate"]
-            gu[:, 1::2] = weights[p + "w_up"]
+            gu = torch.empty((d, 2 * dff), dtype=torch.float32, device=dev)
+            gu[:, 0::2] = up(weights[p + "w_gate"])
+            gu[:, 1::2] = up(weights[p + "w_up"])
             self.layers.append(dict(
                 attn_norm=up(weights[p + "attn_norm"]),
-                wqkv=up(np.concatenate([weights[p + "wq"], weights[p + "wk"], weights[p + "wv"]], 1)),
+                wqkv=torch.cat([up(weights[p + "wq"]), up(weights[p + "wk"]), up(weights[p + "wv"])], 1).contiguous(),
                 wo=up(weights[p + "wo"]),
                 ffn_norm=up(weights[p + "ffn_norm"]),
-                w_gu=up(gu),
+                w_gu=gu,
                 w_down=up(weights[p + "w_down"]),
             ))
 

@@ -118,11 +118,7 @@ class CudaRunner(_Base):
         self.n_rep = model_cfg.n_heads // model_cfg.n_kv_heads
         self.qp = tile_positions(self.n_rep)
         with torch.cuda.device(self.dev):
-            w = weights if weights is not None else seeded_weights(model_cfg)
-            self.w = DeviceWeights(model_cfg, w, self.dev)
-            shape = (model_cfg.n_layers, self.num_blocks, model_cfg.n_kv_heads, self.block_size, self.head_dim)
-            self.cache_k = torch.zeros(shape, dtype=torch.float32, device=self.dev)
-            self.cache_v = torch.zeros(shape, dtype=torch.float32, device=self.dev)
+            self._init_model(weights)
         self._ptrs = self.w.pointer_arrays()
         self.desc = self._make_desc()
         self.caps = Caps(0, 0, 0, 0)
@@ -133,10 +129,20 @@ class CudaRunner(_Base):
         self.captured_kernels = 0  # launch-site calls made while capturing (not executed)
         seqs = max_seqs or (sched_cfg.max_seqs if sched_cfg is not None else 64)
         toks = max_tokens or (sched_cfg.max_batched_tokens if sched_cfg is not None else 2048)
-        self._reserve(seqs, toks, toks, self._table_width_for(model_cfg.max_seq_len))
+        # logit rows: one per sequence plus drafts; grown on demand (_reserve)
+        self._reserve(seqs, toks, min(toks, 4 * seqs), self._table_width_for(model_cfg.max_seq_len))
         self.steps = 0
         self.h2d_bytes = 0  # host->device bytes copied by execute()/launch()
         self.d2h_bytes = 0  # device->host bytes copied by execute()
+
+    def _init_model(self, weights) -> None:
+        """fp32 parity weights in libvllt's layout and the fp32 paged KV cache."""
+        torch, cfg = self.torch, self.model_cfg
+        w = weights if weights is not None else seeded_weights(cfg)
+        self.w = DeviceWeights(cfg, w, self.dev)
+        shape = (cfg.n_layers, self.num_blocks, cfg.n_kv_heads, self.block_size, self.head_dim)
+        self.cache_k = torch.zeros(shape, dtype=torch.float32, device=self.dev)
+        self.cache_v = torch.zeros(shape, dtype=torch.float32, device=self.dev)
 
     # ---- ModelRunner properties ------------------------------------------------
     @property
@@ -145,7 +151,7 @@ class CudaRunner(_Base):
 
     @property
     def cache_bytes(self) -> int:
-        return self.cache_k.numel() * 4 * 2
+        return self.cache_k.numel() * self.cache_k.element_size() * 2
 
     # ---- buffers -----------------------------------------------------------------
     def _table_width_for(self, ctx: int) -> int:
@@ -159,6 +165,7 @@ class CudaRunner(_Base):
         d.vocab, d.vocab_padded = cfg.vocab_size, w.vocab_padded
         d.max_seq_len, d.block_size, d.num_blocks = w.rope_len, self.block_size, self.num_blocks
         d.rms_eps, d.dtype = 1e-5, _lib.VLLT_F32
+        d.tp_size, d.embed_rows, d.tp_comm = 1, cfg.vocab_size, None
         d.tok_emb, d.final_norm, d.lm_head = w.tok_emb.data_ptr(), w.final_norm.data_ptr(), w.lm_head.data_ptr()
         d.rope_cos, d.rope_sin = w.rope_cos.data_ptr(), w.rope_sin.data_ptr()
         for k in ("attn_norm", "wqkv", "wo", "ffn_norm", "w_gu", "w_down"):
@@ -185,7 +192,8 @@ class CudaRunner(_Base):
         self.meta = torch.empty((meta_bytes + 3) // 4, dtype=torch.int32, **kw)
         self.ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, **kw)  # split-K counters start at 0
         self.logits_dev = torch.empty((caps.max_rows, self.w.vocab_padded), dtype=torch.float32, **kw)
-        self.logits_host = torch.empty((caps.max_rows, self.w.vocab_padded), dtype=torch.float32, pin_memory=True)
+        self.logits_host = None  # pinned, allocated by the first execute()
+        self._on_reserve(caps)
         self.counters_host = torch.empty(16, dtype=torch.int32, pin_memory=True)
         self.caps = caps
         self.graphs = {}  # captured pointers are stale now
@@ -208,6 +216,9 @@ class CudaRunner(_Base):
                                       len(pairs), cfg.n_layers, self.num_blocks, cfg.n_kv_heads,
                                       self.block_size, self.head_dim, _lib.VLLT_F32,
                                       _lib.stream_handle()))
+
+    def _on_reserve(self, caps) -> None:
+        """Hook for subclasses that size extra buffers by the capacities."""
 
     def launch(self, out):
         """Enqueue CoW + H2D + forward for one SchedulerOutput; returns (rows, R)."""
@@ -266,6 +277,8 @@ class CudaRunner(_Base):
         torch = self.torch
         with torch.cuda.device(self.dev):
             rows, R = self.launch(out)
+            if self.logits_host is None or self.logits_host.shape[0] < self.logits_dev.shape[0]:
+                self.logits_host = torch.empty(self.logits_dev.shape, dtype=torch.float32, pin_memory=True)
             self.logits_host[:R].copy_(self.logits_dev[:R], non_blocking=True)
             self.counters_host.copy_(self.meta[:16], non_blocking=True)
             self.d2h_bytes += R * self.w.vocab_padded * 4 + 64
