@@ -121,8 +121,8 @@ int32_t* vllt_meta_field(void* meta, const vllt_caps* caps, int32_t which);
 /* Workspace bytes for vllt_paged_attention_varlen: a 256-byte header whose
  * first int32 receives device error flags (bit 2: a bounded wait on a TMA
  * copy expired; zero it before a call to observe that call), then split-K
- * partials for long single-query contexts. */
-int64_t vllt_attention_workspace_bytes(int32_t num_tokens, int32_t n_heads, int32_t head_dim,
+ * partials for long single-query contexts (indexed by sequence). */
+int64_t vllt_attention_workspace_bytes(int32_t num_seqs, int32_t n_heads, int32_t head_dim,
                                        int32_t max_ctx);
 
 /* Varlen causal paged attention over a ragged batch (decode, chunked
@@ -300,6 +300,11 @@ typedef struct vllt_step_bounds {
   int32_t tiles;       /* >= multi-token query tiles (16 (position, head) rows each) */
   int32_t max_ctx;     /* >= longest context (start + qlen) */
 } vllt_step_bounds;
+
+/* Query positions per multi-token attention tile the forward pass uses for
+ * this model (the tensor-core prefill kernel takes 128 / n_rep, the generic
+ * kernel 16 / n_rep); hosts size vllt_step_bounds.tiles with it. */
+int32_t vllt_query_tile_positions(const vllt_model_desc* m);
 
 /* Activation workspace bytes for the given capacities. */
 int64_t vllt_forward_workspace_bytes(const vllt_model_desc* m, const vllt_caps* caps);

@@ -85,3 +85,28 @@ def test_bf16_llama8b_two_layer_slice_matches_fp32_rerun():
     print(f"llama-8b 2-layer slice: max rel logit err {worst:.3e}, greedy agreement {agree:.2%}, "
           f"{decided} clear rows")
     assert worst <= 5e-2
+
+
+def test_llama_engine_serves_requests_to_completion():
+    """The bf16 runner behind the unmodified scheduler: chunked prefill, decode,
+    every request reaches max_tokens, blocks all returned."""
+    from vllmlite.config import CacheConfig, EngineConfig, ModelConfig, SchedulerConfig
+
+    from vllt.engine import gpu_engine
+    from vllt.llama import LlamaRunner
+    from vllt.workloads import llama_workload
+
+    mc = ModelConfig(n_layers=2, n_heads=8, n_kv_heads=2, d_model=1024, d_ff=2048, vocab_size=1000,
+                     max_seq_len=2048, seed=1)
+    cfg = EngineConfig(model=mc, cache=CacheConfig(block_size=16, num_blocks=512, enable_prefix_caching=False),
+                       scheduler=SchedulerConfig(max_seqs=8, max_batched_tokens=256))
+    eng = gpu_engine(cfg, runner_cls=LlamaRunner)
+    reqs = llama_workload(12, seed=5, vocab=1000, prompt_mean=200, out_mean=20)
+    for rid, ids, p in reqs:
+        eng.add_request(params=p, request_id=rid, prompt_token_ids=[min(t, 999) for t in ids])
+    while eng.has_work:
+        eng.step()
+    for rid, ids, p in reqs:
+        assert len(eng.seqs[rid].output_token_ids) == p.max_tokens
+    a = eng.scheduler.blocks.allocator
+    assert a.num_free == a.num_blocks

@@ -46,7 +46,7 @@ def _case(rng, H, KV, D, bs, qlens, ctxs, dtype):
 def _with_workspace(L, c):
     from vllt import _lib
 
-    n = L.vllt_attention_workspace_bytes(c["T"], c["H"], c["D"], c["max_ctx"])
+    n = L.vllt_attention_workspace_bytes(c["S"], c["H"], c["D"], c["max_ctx"])
     ws = torch.zeros(max(n, 256), dtype=torch.uint8, device=c["q"].device)
     out = torch.empty_like(c["q"])
     _lib.check(L.vllt_paged_attention_varlen(

@@ -59,9 +59,9 @@ struct AttnParams {
   float scale;
   // split-K
   int split_len;      // keys per split (multiple of kWarps*kKeys); 0 = no split
-  float* ws_o;        // [splits][T_cap][H][D]
-  float* ws_ml;       // [splits][T_cap][H][2]
-  int T_cap;
+  float* ws_o;        // [splits][P_cap][H][D]  (P_cap = sequence capacity)
+  float* ws_ml;       // [splits][P_cap][H][2]
+  int P_cap;
 };
 
 template <typename T, int D>
@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(kWarps * 32) attention_kernel(AttnParams p) {
     const int h = kvh * p.n_rep + rep;
     const int t = tok0 + q0 + jp;
     if (p.split_len > 0) {
-      const int64_t base = ((int64_t)split * p.T_cap + t) * p.H + h;
+      const int64_t base = ((int64_t)split * p.P_cap + s) * p.H + h;
       p.ws_o[base * D + d] = L > 0.f ? O / L : 0.f;
       if (d == 0) {
         p.ws_ml[base * 2] = M;
@@ -287,12 +287,12 @@ __global__ void merge_splits_kernel(AttnParams p, int max_splits) {
   const int t = p.cu_q[s];
   const int nsplit = min(max_splits, ceil_div(p.ctx[s], p.split_len));
   float M = -INFINITY;
-  for (int z = 0; z < nsplit; ++z) M = fmaxf(M, p.ws_ml[(((int64_t)z * p.T_cap + t) * p.H + h) * 2]);
+  for (int z = 0; z < nsplit; ++z) M = fmaxf(M, p.ws_ml[(((int64_t)z * p.P_cap + s) * p.H + h) * 2]);
   float L = 0.f, O[(D + 31) / 32];
 #pragma unroll
   for (int i = 0; i < (D + 31) / 32; ++i) O[i] = 0.f;
   for (int z = 0; z < nsplit; ++z) {
-    const int64_t base = ((int64_t)z * p.T_cap + t) * p.H + h;
+    const int64_t base = ((int64_t)z * p.P_cap + s) * p.H + h;
     const float mz = p.ws_ml[base * 2], lz = p.ws_ml[base * 2 + 1];
     if (mz == -INFINITY) continue;
     const float w = lz * expf(mz - M);
@@ -380,16 +380,16 @@ int merge_dim(const AttnParams& p, int D, int items, int splits, cudaStream_t st
 constexpr int kSplitLen = 512;
 constexpr int64_t kFlagBytes = 256;  // attention workspace header: device error word
 
-int64_t decode_ws_bytes(int T_cap, int H, int max_ctx);
+int64_t decode_ws_bytes(int P_cap, int H, int max_ctx);
 bool decode_supported(const AttnCall& c);
 int decode_pass(const AttnCall& c, const int32_t* item_seq, const int32_t* n_items, int items_cap, int num_seqs,
                 int max_ctx, int* err, cudaStream_t st,
                 int (*merge)(const AttnCall&, const int32_t*, const int32_t*, int, int, int, cudaStream_t));
 
-int64_t attention_ws_bytes(int T_cap, int H, int D, int max_ctx) {
+int64_t attention_ws_bytes(int P_cap, int H, int D, int max_ctx) {
   const int splits = ceil_div(max_ctx, kSplitLen);
-  const int64_t generic = splits <= 1 ? 0 : (int64_t)splits * T_cap * H * (D + 2) * sizeof(float);
-  const int64_t dec = D == 128 ? decode_ws_bytes(T_cap, H, max_ctx) : 0;
+  const int64_t generic = splits <= 1 ? 0 : (int64_t)splits * P_cap * H * (D + 2) * sizeof(float);
+  const int64_t dec = D == 128 ? decode_ws_bytes(P_cap, H, max_ctx) : 0;
   return kFlagBytes + std::max(generic, dec);
 }
 
@@ -400,7 +400,7 @@ AttnParams params_of(const AttnCall& c) {
   p.q = c.q; p.kc = c.kc; p.vc = c.vc; p.out = c.out;
   p.tables = c.tables; p.W = c.W; p.cu_q = c.cu_q; p.ctx = c.ctx;
   p.H = c.H; p.n_kv = c.n_kv; p.n_rep = c.H / c.n_kv; p.bs = c.bs; p.num_blocks = c.num_blocks;
-  p.scale = c.scale; p.T_cap = c.T_cap;
+  p.scale = c.scale; p.P_cap = c.P_cap;
   return p;
 }
 
@@ -413,7 +413,7 @@ int merge_decode_splits(const AttnCall& c, const int32_t* item_seq, const int32_
   p.num_seqs = num_seqs;
   p.split_len = 1024;
   p.ws_o = c.ws;
-  p.ws_ml = c.ws + (int64_t)splits * c.T_cap * c.H * c.D;
+  p.ws_ml = c.ws + (int64_t)splits * c.P_cap * c.H * c.D;
   return c.dtype == VLLT_F32 ? merge_dim<float>(p, c.D, items, splits, st)
                              : merge_dim<__nv_bfloat16>(p, c.D, items, splits, st);
 }
@@ -424,10 +424,21 @@ int merge_decode_splits(const AttnCall& c, const int32_t* item_seq, const int32_
 //  single-query pass: items = sequences with one query token (item_seq = dec list)
 //  tile pass:         items = (seq, q0) tiles
 // `c.ws` points at the attention workspace (flags header first) or is NULL.
+bool prefill_tc_supported(const AttnCall& c);
+int prefill_tc_positions(int n_rep);
+int prefill_tc_pass(const AttnCall& c, int T_rows, const int32_t* item_seq, const int32_t* item_q0,
+                    const int32_t* n_items, int items_cap, int items_per_seq, int num_seqs, int* err,
+                    cudaStream_t st);
+
+int query_tile_positions(int dtype, int head_dim, int block_size, int n_rep) {
+  AttnCall c{};
+  c.dtype = dtype; c.D = head_dim; c.bs = block_size; c.H = n_rep; c.n_kv = 1;
+  return prefill_tc_supported(c) ? prefill_tc_positions(n_rep) : tile_positions(n_rep);
+}
+
 int attention_pass(const AttnCall& c0, const int32_t* item_seq, const int32_t* item_q0,
-                   const int32_t* n_items, int items_cap, int items_per_seq, int num_seqs,
+                   const int32_t* n_items, int items_cap, int num_seqs, int max_qlen,
                    bool single_query, int max_ctx, cudaStream_t st) {
-  if (items_cap <= 0) return VLLT_OK;
   VLLT_REQUIRE(c0.H / c0.n_kv <= 16, "attention: n_heads / n_kv must be <= 16");
   // split the workspace into the flags header and the partials area
   AttnCall c = c0;
@@ -441,8 +452,20 @@ int attention_pass(const AttnCall& c0, const int32_t* item_seq, const int32_t* i
     c.ws_bytes = 0;
   }
   if (c0.err) flags = c0.err;
+  const int n_rep = c.H / c.n_kv;
+  // standalone: (sequence, tile) items from the batch shape
+  int items_per_seq = 1;
+  if (!item_seq) {
+    const int qp = single_query ? 1 : query_tile_positions(c.dtype, c.D, c.bs, n_rep);
+    items_per_seq = single_query ? 1 : ceil_div(std::max(max_qlen, 1), qp);
+    VLLT_REQUIRE((int64_t)items_per_seq * num_seqs < (1ll << 31), "attention: too many tiles");
+    items_cap = items_per_seq * num_seqs;
+  }
+  if (items_cap <= 0) return VLLT_OK;
   if (single_query && decode_supported(c) && flags)
     return decode_pass(c, item_seq, n_items, items_cap, num_seqs, max_ctx, flags, st, merge_decode_splits);
+  if (!single_query && prefill_tc_supported(c) && flags)
+    return prefill_tc_pass(c, c.T_rows, item_seq, item_q0, n_items, items_cap, items_per_seq, num_seqs, flags, st);
 
   AttnParams p = params_of(c);
   p.item_seq = item_seq; p.item_q0 = item_q0; p.n_items = n_items;
@@ -452,11 +475,11 @@ int attention_pass(const AttnCall& c0, const int32_t* item_seq, const int32_t* i
   int splits = 1;
   if (single_query && max_ctx > kSplitLen) {
     splits = ceil_div(max_ctx, kSplitLen);
-    const int64_t need = (int64_t)splits * c.T_cap * c.H * (c.D + 2) * sizeof(float);
+    const int64_t need = (int64_t)splits * c.P_cap * c.H * (c.D + 2) * sizeof(float);
     if (c.ws && c.ws_bytes >= need) {
       p.split_len = kSplitLen;
       p.ws_o = c.ws;
-      p.ws_ml = c.ws + (int64_t)splits * c.T_cap * c.H * c.D;
+      p.ws_ml = c.ws + (int64_t)splits * c.P_cap * c.H * c.D;
     } else {
       splits = 1;  // no workspace: one CTA walks the whole context
     }

@@ -51,9 +51,9 @@ struct DecodeParams {
   int H, n_kv, num_blocks;
   float qscale;       // softmax scale * log2(e)
   int split_blocks;   // blocks per split; 0 = whole context in one CTA
-  float* ws_o;        // [splits][T_cap][H][128]
-  float* ws_ml;       // [splits][T_cap][H][2] (max in natural-log units, sum)
-  int T_cap;
+  float* ws_o;        // [splits][P_cap][H][128]  (P_cap = sequence capacity)
+  float* ws_ml;       // [splits][P_cap][H][2] (max in natural-log units, sum)
+  int P_cap;
   int* err;           // bit 2: a bounded wait expired
 };
 
@@ -315,7 +315,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CU
     }
     const int head = kvh * NREP + h;
     if (p.split_blocks > 0) {
-      const int64_t base = ((int64_t)split * p.T_cap + t_tok) * p.H + head;
+      const int64_t base = ((int64_t)split * p.P_cap + s) * p.H + head;
       p.ws_o[base * kD + d] = L > 0.f ? O / L : 0.f;
       if (d == 0) {
         p.ws_ml[base * 2] = M == -INFINITY ? -INFINITY : M * kLn2;
@@ -391,9 +391,9 @@ int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const DecodePara
 
 constexpr int kDecodeSplitBlocks = 64;
 
-int64_t decode_ws_bytes(int T_cap, int H, int max_ctx) {
+int64_t decode_ws_bytes(int P_cap, int H, int max_ctx) {
   const int splits = ceil_div(ceil_div(max_ctx, kBS), kDecodeSplitBlocks);
-  return splits <= 1 ? 0 : (int64_t)splits * T_cap * H * (kD + 2) * sizeof(float);
+  return splits <= 1 ? 0 : (int64_t)splits * P_cap * H * (kD + 2) * sizeof(float);
 }
 
 bool decode_supported(const AttnCall& c) {
@@ -427,15 +427,15 @@ int decode_pass(const AttnCall& c, const int32_t* item_seq, const int32_t* n_ite
   p.n_kv = c.n_kv;
   p.num_blocks = c.num_blocks;
   p.qscale = c.scale * 1.4426950408889634f;
-  p.T_cap = c.T_cap;
+  p.P_cap = c.P_cap;
   p.err = err;
   int splits = ceil_div(ceil_div(max_ctx, kBS), kDecodeSplitBlocks);
   if (splits > 1) {
-    const int64_t need = (int64_t)splits * c.T_cap * c.H * (kD + 2) * sizeof(float);
+    const int64_t need = (int64_t)splits * c.P_cap * c.H * (kD + 2) * sizeof(float);
     if (c.ws && c.ws_bytes >= need) {
       p.split_blocks = kDecodeSplitBlocks;
       p.ws_o = c.ws;
-      p.ws_ml = c.ws + (int64_t)splits * c.T_cap * c.H * kD;
+      p.ws_ml = c.ws + (int64_t)splits * c.P_cap * c.H * kD;
     } else {
       splits = 1;
     }

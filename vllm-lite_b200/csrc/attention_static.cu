@@ -76,7 +76,7 @@ extern "C" int vllt_paged_attention_varlen_noalloc(
                    num_blocks > 0 && table_width > 0,
                "paged_attention_noalloc: bad sizes");
   VLLT_REQUIRE(dtype == VLLT_F32 || dtype == VLLT_BF16, "paged_attention_noalloc: bad dtype");
-  const int64_t need = attention_ws_bytes(num_tokens, n_heads, head_dim, max_ctx);
+  const int64_t need = attention_ws_bytes(num_seqs, n_heads, head_dim, max_ctx);
   VLLT_REQUIRE(need <= kStaticScratchBytes,
                "paged_attention_noalloc: this batch needs %lld bytes of scratch; the static scratch "
                "holds %lld (use vllt_paged_attention_varlen with a caller workspace)",
@@ -97,19 +97,12 @@ extern "C" int vllt_paged_attention_varlen_noalloc(
   c.q = q; c.kc = k_cache; c.vc = v_cache; c.out = out;
   c.tables = block_tables; c.W = table_width; c.cu_q = cu_seqlens_q; c.ctx = ctx_lens;
   c.H = n_heads; c.n_kv = n_kv; c.D = head_dim; c.bs = block_size; c.num_blocks = num_blocks;
-  c.dtype = dtype; c.scale = scale; c.T_cap = num_tokens;
+  c.dtype = dtype; c.scale = scale; c.P_cap = num_seqs;
   c.ws = reinterpret_cast<float*>(scratch);
   c.ws_bytes = kStaticScratchBytes;
   c.err = nullptr;  // the scratch header carries the error word
-  const int n_rep = n_heads / n_kv;
-  if (max_qlen <= 1) {
-    rc = attention_pass(c, nullptr, nullptr, nullptr, num_seqs, 1, num_seqs, true, max_ctx, st);
-  } else {
-    const int per_seq = ceil_div(max_qlen, tile_positions(n_rep));
-    VLLT_REQUIRE((int64_t)per_seq * num_seqs < (1ll << 31), "paged_attention_noalloc: too many tiles");
-    rc = attention_pass(c, nullptr, nullptr, nullptr, per_seq * num_seqs, per_seq, num_seqs, false, max_ctx,
-                        st);
-  }
+  c.T_rows = num_tokens;
+  rc = attention_pass(c, nullptr, nullptr, nullptr, 0, num_seqs, max_qlen, max_qlen <= 1, max_ctx, st);
   if (rc != VLLT_OK) return rc;
   if (device_flags &&
       cudaMemcpyAsync(device_flags, scratch, sizeof(int32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess) {

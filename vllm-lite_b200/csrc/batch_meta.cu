@@ -180,11 +180,11 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
 
 }  // namespace
 
-int build_batch_meta(const int32_t* rec, const MetaLayout& L, int bs, int num_blocks, int n_rep,
+int build_batch_meta(const int32_t* rec, const MetaLayout& L, int bs, int num_blocks, int qp,
                      int32_t* meta, cudaStream_t st) {
   VLLT_REQUIRE(rec && meta, "build_batch_meta: null pointer");
-  VLLT_REQUIRE(bs > 0 && num_blocks > 0 && n_rep > 0, "build_batch_meta: bad sizes");
-  build_meta_kernel<<<1, kThreads, 0, st>>>(rec, L, bs, num_blocks, tile_positions(n_rep), meta);
+  VLLT_REQUIRE(bs > 0 && num_blocks > 0 && qp > 0, "build_batch_meta: bad sizes");
+  build_meta_kernel<<<1, kThreads, 0, st>>>(rec, L, bs, num_blocks, qp, meta);
   return check_launch("build_batch_meta");
 }
 

@@ -76,7 +76,7 @@ FwdWs carve(const vllt_model_desc* m, const vllt_caps* c, char* base) {
   w.attn = take(T * qw * 4);
   w.act = take(T * m->d_ff * 4);
   w.rows_h = take(R * m->d_model * 4);
-  w.attn_ws_bytes = attention_ws_bytes((int)T, m->n_heads, m->head_dim, m->max_seq_len);
+  w.attn_ws_bytes = attention_ws_bytes(c->max_seqs, m->n_heads, m->head_dim, m->max_seq_len);
   w.attn_ws = take(w.attn_ws_bytes);
   const int n_max = std::max({(m->n_heads + 2 * m->n_kv_heads) * m->head_dim, 2 * m->d_ff, m->d_model,
                               m->vocab_padded});
@@ -136,7 +136,8 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   const int64_t layer_elems = (int64_t)m->num_blocks * KV * m->block_size * D;
   const float eps = m->rms_eps;
 
-  VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks, n_rep, meta, st));
+  VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks,
+                            query_tile_positions(VLLT_F32, D, m->block_size, n_rep), meta, st));
   VLLT_TRY(embed(reinterpret_cast<const float*>(m->tok_emb), meta + L.tokens, w.x, T_cap, T_dev, d, m->vocab, st));
 
   AttnCall ac{};
@@ -149,7 +150,8 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   ac.H = H; ac.n_kv = KV; ac.D = D; ac.bs = m->block_size; ac.num_blocks = m->num_blocks;
   ac.dtype = VLLT_F32;
   ac.scale = (float)(1.0 / sqrt((double)D));  // float64 then rounded, as model.py:58
-  ac.T_cap = caps->max_tokens;
+  ac.P_cap = caps->max_seqs;
+  ac.T_rows = caps->max_tokens;
   ac.ws = w.attn_ws;
   ac.ws_bytes = w.attn_ws_bytes;
   ac.err = meta + kCntError;  // bounded-wait timeouts surface in the step's error counter
@@ -236,7 +238,8 @@ int vllt_build_batch_meta(const int32_t* step_record, const vllt_caps* caps, int
                           int32_t num_blocks, int32_t n_rep, void* meta, void* stream) {
   clear_error();
   VLLT_REQUIRE(caps_ok(caps), "build_batch_meta: bad capacities");
-  return build_batch_meta(step_record, layout_of(caps), block_size, num_blocks, n_rep,
+  VLLT_REQUIRE(n_rep > 0, "build_batch_meta: bad n_rep");
+  return build_batch_meta(step_record, layout_of(caps), block_size, num_blocks, tile_positions(n_rep),
                           reinterpret_cast<int32_t*>(meta), as_stream(stream));
 }
 
@@ -257,9 +260,9 @@ int32_t* vllt_meta_field(void* meta, const vllt_caps* caps, int32_t which) {
   }
 }
 
-int64_t vllt_attention_workspace_bytes(int32_t num_tokens, int32_t n_heads, int32_t head_dim,
+int64_t vllt_attention_workspace_bytes(int32_t num_seqs, int32_t n_heads, int32_t head_dim,
                                        int32_t max_ctx) {
-  return attention_ws_bytes(num_tokens, n_heads, head_dim, max_ctx);
+  return attention_ws_bytes(num_seqs, n_heads, head_dim, max_ctx);
 }
 
 int vllt_paged_attention_varlen(const void* q, const void* k_cache, const void* v_cache,
@@ -283,19 +286,14 @@ int vllt_paged_attention_varlen(const void* q, const void* k_cache, const void* 
   c.q = q; c.kc = k_cache; c.vc = v_cache; c.out = out;
   c.tables = block_tables; c.W = table_width; c.cu_q = cu_seqlens_q; c.ctx = ctx_lens;
   c.H = n_heads; c.n_kv = n_kv; c.D = head_dim; c.bs = block_size; c.num_blocks = num_blocks;
-  c.dtype = dtype; c.scale = scale; c.T_cap = num_tokens;
+  c.dtype = dtype; c.scale = scale; c.P_cap = num_seqs;
   c.ws = reinterpret_cast<float*>(workspace);
   c.ws_bytes = workspace ? workspace_bytes : 0;
   c.err = nullptr;  // the workspace header carries the error word
-  cudaStream_t st = as_stream(stream);
-  const int n_rep = n_heads / n_kv;
-  if (max_qlen <= 1) {  // pure decode batch: one item per sequence, split-K allowed
-    return attention_pass(c, nullptr, nullptr, nullptr, num_seqs, 1, num_seqs, true, max_ctx, st);
-  }
-  const int per_seq = ceil_div(max_qlen, tile_positions(n_rep));
-  VLLT_REQUIRE((int64_t)per_seq * num_seqs < (1ll << 31), "paged_attention: too many tiles");
-  return attention_pass(c, nullptr, nullptr, nullptr, per_seq * num_seqs, per_seq, num_seqs, false,
-                        max_ctx, st);
+  c.T_rows = num_tokens;
+  // a pure decode batch (max_qlen <= 1) is one single-query item per sequence (split-K allowed)
+  return attention_pass(c, nullptr, nullptr, nullptr, 0, num_seqs, max_qlen, max_qlen <= 1, max_ctx,
+                        as_stream(stream));
 }
 
 int vllt_rmsnorm(const float* x, const int32_t* idx, const float* w, float* out, int32_t rows,
@@ -379,6 +377,11 @@ int vllt_spec_accept(const int32_t* cu_rows, const int32_t* drafts, const int32_
   if (num_seqs == 0) return VLLT_OK;
   VLLT_REQUIRE(cu_rows && drafts && draft_offsets && picks && n_accepted, "spec_accept: null pointer");
   return spec_accept(cu_rows, drafts, draft_offsets, num_seqs, picks, n_accepted, as_stream(stream));
+}
+
+int32_t vllt_query_tile_positions(const vllt_model_desc* m) {
+  if (!m || m->n_kv_heads <= 0 || m->n_heads % m->n_kv_heads) return -1;
+  return query_tile_positions(m->dtype, m->head_dim, m->block_size, m->n_heads / m->n_kv_heads);
 }
 
 int64_t vllt_forward_workspace_bytes(const vllt_model_desc* m, const vllt_caps* caps) {

@@ -58,7 +58,7 @@ Bf16Ws carve_bf16(const vllt_model_desc* m, const vllt_caps* c, char* base) {
   w.attn = reinterpret_cast<__nv_bfloat16*>(take(T * qw * 2));
   w.act = reinterpret_cast<__nv_bfloat16*>(take(T * m->d_ff * 2));
   w.rows_h = reinterpret_cast<__nv_bfloat16*>(take(R * d * 2));
-  w.attn_ws_bytes = attention_ws_bytes((int)T, m->n_heads, m->head_dim, m->max_seq_len);
+  w.attn_ws_bytes = attention_ws_bytes(c->max_seqs, m->n_heads, m->head_dim, m->max_seq_len);
   w.attn_ws = reinterpret_cast<float*>(take(w.attn_ws_bytes));
   w.total_bytes = off;
   return w;
@@ -96,7 +96,8 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   const float eps = m->rms_eps;
   const bool tp = m->tp_size > 1;
 
-  VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks, n_rep, meta, st));
+  VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks,
+                            query_tile_positions(VLLT_BF16, D, m->block_size, n_rep), meta, st));
   VLLT_TRY(embed_bf16(m->tok_emb, meta + L.tokens, w.x, T_cap, T_dev, d, m->embed_rows, st));
 
   AttnCall ac{};
@@ -109,7 +110,8 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   ac.H = H; ac.n_kv = KV; ac.D = D; ac.bs = m->block_size; ac.num_blocks = m->num_blocks;
   ac.dtype = VLLT_BF16;
   ac.scale = (float)(1.0 / sqrt((double)D));
-  ac.T_cap = caps->max_tokens;
+  ac.P_cap = caps->max_seqs;
+  ac.T_rows = caps->max_tokens;
   ac.ws = w.attn_ws;
   ac.ws_bytes = w.attn_ws_bytes;
   ac.err = err;

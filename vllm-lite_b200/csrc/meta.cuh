@@ -59,7 +59,8 @@ struct MetaLayout {
 // a tile holds up to 16 (position, head) rows.
 __host__ __device__ inline int tile_positions(int n_rep) { return n_rep >= 16 ? 1 : 16 / n_rep; }
 
-int build_batch_meta(const int32_t* rec, const MetaLayout& L, int bs, int num_blocks, int n_rep,
+// qp: query positions per multi-token attention tile (see query_tile_positions).
+int build_batch_meta(const int32_t* rec, const MetaLayout& L, int bs, int num_blocks, int qp,
                      int32_t* meta, cudaStream_t st);
 
 }  // namespace vllt

@@ -39,14 +39,21 @@ struct AttnCall {
   const int32_t *tables, *cu_q, *ctx;
   int W, H, n_kv, D, bs, num_blocks, dtype;
   float scale;
-  int T_cap;
+  int P_cap;        // sequences the split-K partials are indexed by
+  int T_rows;       // rows of q / out (the tensor-core prefill's Q map)
   float* ws;        // attention workspace: 256-byte flags header, then split partials
   int64_t ws_bytes;
   int* err;         // device error word (overrides the header's), may be NULL
 };
-int64_t attention_ws_bytes(int T_cap, int H, int D, int max_ctx);
+int64_t attention_ws_bytes(int P_cap, int H, int D, int max_ctx);
+// One attention pass. With item lists (forward): items_cap bounds the grid and
+// the lists come from the meta builder. Without (standalone, item_seq == NULL):
+// items are (sequence, tile) pairs derived from num_seqs and max_qlen.
 int attention_pass(const AttnCall& c, const int32_t* item_seq, const int32_t* item_q0,
-                   const int32_t* n_items, int items_cap, int items_per_seq, int num_seqs,
+                   const int32_t* n_items, int items_cap, int num_seqs, int max_qlen,
                    bool single_query, int max_ctx, cudaStream_t st);
+// Query positions per multi-token tile for this call's kernel (tensor-core
+// prefill: 128 / n_rep; generic: 16 / n_rep).
+int query_tile_positions(int dtype, int head_dim, int block_size, int n_rep);
 
 }  // namespace vllt

@@ -69,6 +69,7 @@ SIGNATURES = {
     "vllt_tp_destroy": (C.c_int, [vp]),
     "vllt_tp_allreduce_bf16": (C.c_int, [vp, i64, vp, vp]),
     "vllt_argmax_rows": (C.c_int, [vp, i32, i32, i32, i32, vp, vp, vp]),
+    "vllt_query_tile_positions": (i32, [C.POINTER(ModelDesc)]),
     "vllt_forward_workspace_bytes": (i64, [C.POINTER(ModelDesc), C.POINTER(Caps)]),
     "vllt_forward": (C.c_int, [C.POINTER(ModelDesc), vp, C.POINTER(Caps), C.POINTER(StepBounds),
                                vp, vp, i64, vp, vp]),

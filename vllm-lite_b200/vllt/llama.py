@@ -169,6 +169,33 @@ class LlamaRunner(CudaRunner):
         d.k_cache, d.v_cache = self.cache_k.data_ptr(), self.cache_v.data_ptr()
         return d
 
+    # ---- per-step roofline (for the benchmark) -----------------------------------
+    def step_roofline(self, rec, bounds, hbm_gbs: float, tflops: float) -> float:
+        """Lower bound on one forward pass's time on this rank: the larger of
+        (weights + KV read/written) / HBM bandwidth and (GEMM + attention
+        FLOPs) / tensor peak. Attention FLOPs count the causal pairs only."""
+        cfg, n = self.model_cfg, self.tp_size
+        S, T, R = int(rec[0]), int(rec[1]), int(rec[2])
+        starts = rec[4:4 + S].astype(np.int64)
+        qlens = rec[4 + S:4 + 2 * S].astype(np.int64)
+        ctx = starts + qlens
+        d, f, D = cfg.d_model, cfg.d_ff, self.head_dim
+        layer_params = d * (cfg.n_heads + 2 * cfg.n_kv_heads) * D + d * cfg.n_heads * D + 3 * d * f
+        w_bytes = 2 * (cfg.n_layers * layer_params + cfg.vocab_size * d) / n
+        kv_token = 2 * cfg.n_layers * cfg.n_kv_heads * D * 2 / n
+        kv_bytes = kv_token * (float(ctx.sum()) + T)
+        # causal (query, key) pairs: query j of a chunk sees start + j + 1 keys
+        pairs = float(np.sum(qlens * starts + qlens * (qlens + 1) // 2))
+        flops = (2 * T * cfg.n_layers * layer_params + 2 * R * cfg.vocab_size * d
+                 + 4 * cfg.n_layers * cfg.n_heads * D * pairs) / n
+        return max((w_bytes + kv_bytes) / (hbm_gbs * 1e9), flops / (tflops * 1e12))
+
+    def launch(self, out):
+        rows, R = super().launch(out)
+        if getattr(self, "roofline_peaks", None):
+            self.roofline_s += self.step_roofline(self.rec_host[:self._last_n].numpy(), None, *self.roofline_peaks)
+        return rows, R
+
     def execute(self, out):
         if self.tp_size > 1:
             raise NotImplementedError("host logits are not gathered across vocabulary shards; use gpu_engine")

@@ -82,7 +82,7 @@ def paged_attention_varlen(q, cache_k, cache_v, block_tables, cu_seqlens_q, ctx_
     q = q.contiguous()
     out = torch.empty_like(q)
     if workspace is None:
-        nbytes = lib().vllt_attention_workspace_bytes(T, H, D, max_ctx)
+        nbytes = lib().vllt_attention_workspace_bytes(S, H, D, max_ctx)
         workspace = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=q.device)
     check(lib().vllt_paged_attention_varlen(
         ptr(q), ptr(cache_k), ptr(cache_v), ptr(bt), bt.shape[1], ptr(cu), ptr(cl), S, T,

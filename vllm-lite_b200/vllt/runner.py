@@ -40,6 +40,24 @@ def tile_positions(n_rep: int) -> int:
     return 1 if n_rep >= 16 else 16 // n_rep
 
 
+def _tokens(seq, start: int, n: int) -> list:
+    """seq.token_ids[start:start+n] (prompt + output + drafts, vllmlite/sequence.py:70)
+    without building the whole concatenation."""
+    p = getattr(seq, "prompt_token_ids", None)
+    if p is None:  # a duck-typed sequence that only carries token_ids
+        return seq.token_ids[start:start + n]
+    end, out = start + n, []
+    for part in (p, seq.output_token_ids, seq.draft_token_ids):
+        ln = len(part)
+        if start < ln and end > 0:
+            out += part[max(start, 0):min(end, ln)]
+        start -= ln
+        end -= ln
+        if end <= 0:
+            break
+    return out
+
+
 def pack_step(out, block_size: int, num_blocks: int, vocab: int, max_pos: int, qp: int):
     """Host side of the batch flatten: (record int32 words, StepBounds, rows, (S, T, R, W)).
 
@@ -70,7 +88,7 @@ def pack_step(out, block_size: int, num_blocks: int, vocab: int, max_pos: int, q
         starts.append(start)
         qlens.append(n)
         counts.append(min(1 + len(seq.draft_token_ids), n))
-        toks += seq.token_ids[start:ctx]
+        toks += _tokens(seq, start, n)
         tabs.append(bl)
         W = max(W, len(bl))
         max_ctx = max(max_ctx, ctx)
@@ -121,6 +139,7 @@ class CudaRunner(_Base):
             self._init_model(weights)
         self._ptrs = self.w.pointer_arrays()
         self.desc = self._make_desc()
+        self.qp = self.L.vllt_query_tile_positions(C.byref(self.desc))  # tile height the forward uses
         self.caps = Caps(0, 0, 0, 0)
         self.use_graphs = use_graphs
         self.bucket_bounds = bucket_bounds  # eager runs with the graphs' bounds (tests)
@@ -227,6 +246,7 @@ class CudaRunner(_Base):
         rec, bounds, rows, (S, T, R, W) = self.pack(out)
         self._reserve(S, T, R, W)
         n = rec.size
+        self._last_n = n
         self.rec_host[:n].numpy()[:] = rec
         self.rec_dev[:n].copy_(self.rec_host[:n], non_blocking=True)
         self.h2d_bytes += 4 * n + 8 * len(out.cow)

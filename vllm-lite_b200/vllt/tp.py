@@ -24,8 +24,9 @@ import numpy as np
 from . import _lib
 from ._lib import StepBounds, check, lib
 from .llama import LlamaRunner
+from .runner import CudaRunner
 
-OP_FORWARD, OP_STOP = 1, 2
+OP_FORWARD, OP_STOP, OP_MARK = 1, 2, 3
 CTRL_WORDS = 8  # [op, tokens, rows, decode_seqs, tiles, max_ctx, greedy, record words]
 
 
@@ -91,13 +92,16 @@ class TPLlamaRunner(LlamaRunner):
         self.rec_host = torch.empty(extra.numel(), dtype=torch.int32, pin_memory=True)
 
     # ---- rank 0 -------------------------------------------------------------------
-    def launch(self, out):
+    def launch(self, out):  # replaces LlamaRunner.launch (which is CudaRunner's plus the roofline)
         rec, bounds, rows, (S, T, R, W) = self.pack(out)
         self._reserve(S, T, R, W)
         self._broadcast(OP_FORWARD, rec, bounds, greedy=1)
+        self._last_n = rec.size
         self._run(bounds)
         self.steps += 1
         self._pending_rows = R
+        if getattr(self, "roofline_peaks", None):
+            self.roofline_s += self.step_roofline(rec, bounds, *self.roofline_peaks)
         return rows, R
 
     def _broadcast(self, op, rec=None, bounds=None, greedy=0):
@@ -141,6 +145,26 @@ class TPLlamaRunner(LlamaRunner):
     def stop_workers(self):
         self._broadcast(OP_STOP)
 
+    def mark(self, tag: int):
+        """Broadcast a timing mark (tag 0 = start, 1 = end); workers record a
+        CUDA event, rank 0 records its own."""
+        self._broadcast(OP_MARK, bounds=StepBounds(tag, 0, 0, 0, 1))
+        return self._record_mark(tag)
+
+    def _record_mark(self, tag: int):
+        import torch
+
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        if not hasattr(self, "marks"):
+            self.marks = {}
+        self.marks[tag] = ev
+        return ev
+
+    def marked_seconds(self) -> float:
+        self.marks[1].synchronize()
+        return self.marks[0].elapsed_time(self.marks[1]) / 1e3
+
     # ---- ranks > 0 ------------------------------------------------------------------
     def worker_loop(self):
         """Serve rank 0's forward passes until it broadcasts the stop record."""
@@ -153,6 +177,9 @@ class TPLlamaRunner(LlamaRunner):
             ctrl = self.ctrl_host.numpy()
             if ctrl[0] == OP_STOP:
                 break
+            if ctrl[0] == OP_MARK:
+                self._record_mark(int(ctrl[1]))
+                continue
             bounds = StepBounds(*[int(x) for x in ctrl[1:6]])
             self._run(bounds)
             if ctrl[6]:

@@ -60,3 +60,21 @@ def periodic_lengths(n: int = 128, seed: int = 0, max_tokens: int = 256):
 def periodic_workload(n: int = 128, seed: int = 0, max_tokens: int = 256):
     return [(f"p{i}", ids, _greedy_params(m))
             for i, (ids, m) in enumerate(periodic_lengths(n, seed, max_tokens))]
+
+
+def llama_lengths(n: int = 512, seed: int = 0, vocab: int = 128256, prompt_mean: float = 1024,
+                  out_mean: float = 256):
+    """The Llama-3-8B-shaped serving workload: lognormal prompts (mean 1024,
+    sigma 0.6, clipped to [32, 8192]) and outputs (mean 256, sigma 0.7, clipped
+    to [16, 1024]); prompt tokens uniform over the vocabulary."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n):
+        plen = int(np.clip(rng.lognormal(np.log(prompt_mean) - 0.6 ** 2 / 2, 0.6), 32, 8192))
+        olen = int(np.clip(rng.lognormal(np.log(out_mean) - 0.7 ** 2 / 2, 0.7), 16, 1024))
+        out.append(([int(t) for t in rng.integers(0, vocab, size=plen)], olen))
+    return out
+
+
+def llama_workload(n: int = 512, seed: int = 0, **kw):
+    return [(f"l{i}", ids, _greedy_params(m)) for i, (ids, m) in enumerate(llama_lengths(n, seed, **kw))]
