@@ -334,3 +334,42 @@ def test_decode_kernel_matches_generic_kernel(dev):
                                              max(ctxs), H, KV, D, bs, args[1].shape[0], float(1 / np.sqrt(D)),
                                              _lib.VLLT_BF16, out.data_ptr(), None, 0, _lib.stream_handle()))
     np.testing.assert_allclose(fast.cpu().numpy(), out.float().cpu().numpy(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("H,KV", [(32, 8), (8, 8), (16, 8), (64, 8)])
+def test_attention_prefill_tensor_core(dev, H, KV):
+    """Multi-token tiles of bf16 / head_dim 128 / block 16 take the tcgen05
+    prefill kernel: long prompts (several query and key tiles, diagonal
+    masking), chunked prefill over a cached prefix, verify-sized rows and a
+    single-token row in the same launch. Checked against the float64 oracle
+    and against the generic kernel (no workspace)."""
+    from vllt import _lib
+    from vllt.ops import attention_flags, paged_attention_varlen
+
+    rng = np.random.default_rng(H + 7)
+    D, bs = 128, 16
+    qlens = [300, 64, 5, 1, 129, 9]
+    ctxs = [300, 1000, 260, 77, 129, 2049]
+    q, ck, cv, tables, tab = ragged_batch(rng, H, KV, D, bs, qlens, ctxs, "bf16")
+    tq = torch.from_numpy(q).to(dev, torch.bfloat16)
+    tk = torch.from_numpy(to_lib_layout(ck, bs)).to(dev, torch.bfloat16)
+    tv = torch.from_numpy(to_lib_layout(cv, bs)).to(dev, torch.bfloat16)
+    cu = np.concatenate([[0], np.cumsum(qlens)])
+    scale = 1.0 / np.sqrt(D)
+    got = paged_attention_varlen(tq, tk, tv, tab, cu, ctxs, scale).float().cpu().numpy()
+    assert attention_flags(paged_attention_varlen.last_workspace) == 0
+    for i, c in enumerate(ctxs):
+        slots = A.table_slots(tables[i], bs, c)
+        want = A.dense_attention(q[cu[i]:cu[i + 1]], ck[slots], cv[slots], KV, scale)
+        np.testing.assert_allclose(got[cu[i]:cu[i + 1]], want, rtol=2e-2, atol=2e-2, err_msg=f"seq {i}")
+    # the generic kernel (NULL workspace) on the same batch
+    L = _lib.lib()
+    out = torch.empty_like(tq)
+    bt = torch.from_numpy(tab).to(dev)
+    dcu = torch.from_numpy(cu.astype(np.int32)).to(dev)
+    dcl = torch.tensor(ctxs, dtype=torch.int32, device=dev)
+    _lib.check(L.vllt_paged_attention_varlen(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), bt.data_ptr(), tab.shape[1],
+                                             dcu.data_ptr(), dcl.data_ptr(), len(ctxs), int(cu[-1]), max(qlens),
+                                             max(ctxs), H, KV, D, bs, tk.shape[0], float(scale), _lib.VLLT_BF16,
+                                             out.data_ptr(), None, 0, _lib.stream_handle()))
+    np.testing.assert_allclose(got, out.float().cpu().numpy(), rtol=2e-2, atol=2e-2)

@@ -58,62 +58,99 @@ def _tokens(seq, start: int, n: int) -> list:
     return out
 
 
-def pack_step(out, block_size: int, num_blocks: int, vocab: int, max_pos: int, qp: int):
-    """Host side of the batch flatten: (record int32 words, StepBounds, rows, (S, T, R, W)).
+class StepPacker:
+    """Host side of the batch flatten: SchedulerOutput -> (record int32 words,
+    StepBounds, rows, (S, T, R, W)).
 
     Reads exactly what vllmlite/runner.py:72-90 reads: item.start_pos,
-    item.num_tokens, seq.token_ids, seq.draft_token_ids, seq.table.block_ids.
-    The record layout is documented in include/vllt.h. Metadata that the
-    reference would fail on (numpy IndexError) raises here, before anything
-    reaches the device.
+    item.num_tokens, seq.token_ids (via _tokens), seq.draft_token_ids,
+    seq.table.block_ids. The record layout is documented in include/vllt.h.
+    Metadata the reference would fail on (NumPy IndexError) raises here, before
+    anything reaches the device.
+
+    Block tables are cached per sequence as int32 arrays between passes: only
+    entries from the block being written onward can change (appended blocks, a
+    copy-on-write replacement, block_manager.py:77-93), so only those are
+    copied and validated; a table replaced after preemption or retirement
+    (a new BlockTable object) is reloaded whole.
     """
-    items = out.scheduled
-    S = len(items)
-    starts, qlens, counts, toks, tabs = [], [], [], [], []
-    W = 1
-    max_ctx = 1
-    for i, item in enumerate(items):
-        seq = item.seq
-        start, n = item.start_pos, item.num_tokens
-        if n < 1:
-            raise ValueError("a scheduled sequence has no tokens")
-        ctx = start + n
-        if ctx > max_pos:
-            raise IndexError(f"position {ctx - 1} beyond max_seq_len {max_pos}")
-        bl = seq.table.block_ids
-        if len(bl) * block_size < ctx:
-            raise IndexError(f"block table of sequence {i} too short for {ctx} positions")
-        if bl and (min(bl) < 0 or max(bl) >= num_blocks):
-            raise IndexError("block id out of range")
-        starts.append(start)
-        qlens.append(n)
-        counts.append(min(1 + len(seq.draft_token_ids), n))
-        toks += _tokens(seq, start, n)
-        tabs.append(bl)
-        W = max(W, len(bl))
-        max_ctx = max(max_ctx, ctx)
-    T = len(toks)
-    R = sum(counts)
-    if T and (min(toks) < 0 or max(toks) >= vocab):
-        raise IndexError("token id out of the vocabulary")
-    words = [S, T, R, W]
-    words += starts
-    words += qlens
-    words += counts
-    words += toks
-    for bl in tabs:
-        words += bl
-        if len(bl) < W:
-            words += [0] * (W - len(bl))
-    rec = np.array(words, dtype=np.int32)
-    n_dec = qlens.count(1)
-    tiles = sum((q + qp - 1) // qp for q in qlens if q > 1)
-    bounds = StepBounds(T, R, n_dec, tiles, max_ctx)
-    rows, r0 = [], 0
-    for c in counts:
-        rows.append((r0, c))
-        r0 += c
-    return rec, bounds, rows, (S, T, R, W)
+
+    def __init__(self, block_size: int, num_blocks: int, vocab: int, max_pos: int, qp: int):
+        self.bs, self.nb, self.vocab, self.max_pos, self.qp = block_size, num_blocks, vocab, max_pos, qp
+        self.cache = {}
+
+    def _table(self, key, seq, start: int, new_cache) -> np.ndarray:
+        tbl = seq.table
+        ids = tbl.block_ids
+        n = len(ids)
+        ent = self.cache.get(key)
+        if ent is None or ent[0] is not tbl or ent[2] > n:
+            arr = np.asarray(ids, dtype=np.int64).astype(np.int32) if n else np.zeros(0, np.int32)
+            first = 0
+        else:
+            arr, first = ent[1], min(ent[2], start // self.bs)
+            if arr.size < n:
+                grown = np.empty(max(n, 2 * arr.size), np.int32)
+                grown[:arr.size] = arr
+                arr = grown
+            if n > first:
+                arr[first:n] = ids[first:n]
+        if n > first:
+            seg = arr[first:n]
+            if int(seg.min()) < 0 or int(seg.max()) >= self.nb:
+                raise IndexError("block id out of range")
+        new_cache[key] = (tbl, arr, n)
+        return arr[:n]
+
+    def pack(self, out):
+        items = out.scheduled
+        S = len(items)
+        starts, qlens, counts, toks, tabs = [], [], [], [], []
+        new_cache = {}
+        W, max_ctx = 1, 1
+        for i, item in enumerate(items):
+            seq = item.seq
+            start, n = item.start_pos, item.num_tokens
+            if n < 1:
+                raise ValueError("a scheduled sequence has no tokens")
+            ctx = start + n
+            if ctx > self.max_pos:
+                raise IndexError(f"position {ctx - 1} beyond max_seq_len {self.max_pos}")
+            key = getattr(seq, "request_id", None) or id(seq)
+            tab = self._table(key, seq, start, new_cache)
+            if tab.size * self.bs < ctx:
+                raise IndexError(f"block table of sequence {i} too short for {ctx} positions")
+            starts.append(start)
+            qlens.append(n)
+            counts.append(min(1 + len(seq.draft_token_ids), n))
+            toks += _tokens(seq, start, n)
+            tabs.append(tab)
+            W = max(W, tab.size)
+            max_ctx = max(max_ctx, ctx)
+        self.cache = new_cache
+        T = len(toks)
+        R = sum(counts)
+        if T and (min(toks) < 0 or max(toks) >= self.vocab):
+            raise IndexError("token id out of the vocabulary")
+        head = np.asarray([S, T, R, W] + starts + qlens + counts + toks, dtype=np.int64).astype(np.int32)
+        table = np.zeros((S, W), np.int32)
+        for i, tab in enumerate(tabs):
+            table[i, :tab.size] = tab
+        rec = np.concatenate([head, table.reshape(-1)])
+        n_dec = qlens.count(1)
+        qp = self.qp
+        tiles = sum((q + qp - 1) // qp for q in qlens if q > 1)
+        bounds = StepBounds(T, R, n_dec, tiles, max_ctx)
+        rows, r0 = [], 0
+        for c in counts:
+            rows.append((r0, c))
+            r0 += c
+        return rec, bounds, rows, (S, T, R, W)
+
+
+def pack_step(out, block_size: int, num_blocks: int, vocab: int, max_pos: int, qp: int):
+    """One-off packing (no table cache); see StepPacker."""
+    return StepPacker(block_size, num_blocks, vocab, max_pos, qp).pack(out)
 
 
 class CudaRunner(_Base):
@@ -219,8 +256,10 @@ class CudaRunner(_Base):
 
     # ---- the step ------------------------------------------------------------------
     def pack(self, out):
-        return pack_step(out, self.block_size, self.num_blocks, self.model_cfg.vocab_size,
-                         self.w.rope_len, self.qp)
+        if getattr(self, "packer", None) is None or self.packer.qp != self.qp:
+            self.packer = StepPacker(self.block_size, self.num_blocks, self.model_cfg.vocab_size,
+                                     self.w.rope_len, self.qp)
+        return self.packer.pack(out)
 
     def copy_on_write(self, pairs) -> None:
         """Apply (src_block, dst_block) copies in every layer (runner.py:54-60)."""
