@@ -252,6 +252,10 @@ def main_ours(args):
         return main_decode(args, torch, dev, rank, world)
     if wl == "llama8b":
         return main_llama(args, torch, dev, rank, world)
+    if wl == "gemm":
+        return main_gemm(args, torch, dev, rank, world)
+    if wl == "prefill":
+        return main_prefill(args, torch, dev, rank, world)
     cfg = engine_config(wl)
     reqs = requests(wl, seed=rank)  # each replica its own seeded workload
     eng = gpu_engine(cfg)
@@ -349,6 +353,124 @@ def main_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def _tc_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def _event_times(torch, fn, steps, warmup, dev):
+    """Median CUDA-event seconds of fn() over max(steps, 3) launches, L2
+    flushed before each, after max(warmup, 3) untimed launches."""
+    for _ in range(max(warmup, 3)):
+        fn()
+    ts = []
+    for _ in range(max(steps, 3)):
+        flush_l2(torch, dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1) / 1e3)
+    return statistics.median(ts)
+
+
+def main_gemm(args, torch, dev, rank, world):
+    """tcgen05 bf16 GEMM on the Llama-3-8B projection shapes, prefill (M=8192)
+    and decode (M=512, 64) batches: TFLOP/s against the measured cuBLAS bf16
+    peak, and weight GB/s for the decode batches. The forward's own split-K
+    choice is used for the small-M shapes."""
+    from vllt import _lib
+
+    L = _lib.lib()
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    shapes = [("qkv", 6144, 4096), ("o_proj", 4096, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336)]
+    peak, kind = _tc_peak()
+    res = {}
+    tot_flops = tot_t = 0.0
+    for M in (8192, 512, 64):
+        A = torch.randn((M, 14336), device=dev).to(torch.bfloat16)
+        for name, N, K in shapes:
+            W = torch.randn((N, K), device=dev).to(torch.bfloat16)
+            C_ = torch.empty((M, N), device=dev)
+            a = A[:, :K].contiguous()
+            splits = int(L.vllt_gemm_bf16_auto_splits(M, N, K))
+            ws = torch.zeros(max(int(L.vllt_gemm_bf16_splitk_workspace_bytes(M, N, splits)), 256),
+                             dtype=torch.uint8, device=dev)
+
+            def run():
+                _lib.check(L.vllt_gemm_bf16_splitk(a.data_ptr(), W.data_ptr(), C_.data_ptr(), M, N, K, splits,
+                                                   ws.data_ptr(), ws.numel(), flags.data_ptr(),
+                                                   _lib.stream_handle()))
+            t = _event_times(torch, run, args.steps, args.warmup, dev)
+            fl = 2.0 * M * N * K
+            res[f"M{M}_{name}"] = {"tflops": round(fl / t / 1e12, 1), "us": round(t * 1e6, 1), "splits": splits,
+                                   "frac": round(fl / t / 1e12 / peak, 3),
+                                   "weight_gbs": round(N * K * 2 / t / 1e9, 1)}
+            if M == 8192:
+                tot_flops += fl
+                tot_t += t
+            del W, C_, ws
+    assert int(flags.item()) == 0, "bounded wait expired in the GEMM"
+    if rank == 0:
+        v = tot_flops / tot_t / 1e12
+        print(json.dumps({"metric": "tcgen05 bf16 GEMM TFLOP/s (Llama-3-8B projections, M=8192)", "value": round(v, 1),
+                          "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                          "data": "synthetic N(0,1)",
+                          "config": {"workload": "the four GEMM shapes of one Llama-3-8B layer",
+                                     "l2": "flushed before each launch"},
+                          "roofline": {"bound": "tensor", "achieved": round(v, 1), "peak": peak, "unit": "TFLOP/s",
+                                       "frac": round(v / peak, 3), "peak_kind": kind, "traffic": None},
+                          "shapes": res}), flush=True)
+
+
+def main_prefill(args, torch, dev, rank, world):
+    """tcgen05 prefill attention: 16 sequences x 2048-token prompts (causal),
+    32 / 8 heads, head_dim 128, bf16, block 16; FLOPs = 4 * D * H per causal
+    (query, key) pair."""
+    import numpy as np
+
+    from vllt import _lib
+
+    L = _lib.lib()
+    S, P, H, KV, D, bs = 16, 2048, 32, 8, 128, 16
+    nb = S * P // bs
+    rng = np.random.default_rng(0)
+    tables = torch.from_numpy(rng.permutation(nb).astype(np.int32).reshape(S, P // bs)).to(dev)
+    kc = torch.randn((nb, KV, bs, D), device=dev).to(torch.bfloat16)
+    vc = torch.randn((nb, KV, bs, D), device=dev).to(torch.bfloat16)
+    q = torch.randn((S * P, H, D), device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    cu = torch.arange(0, S * P + 1, P, dtype=torch.int32, device=dev)
+    ctx = torch.full((S,), P, dtype=torch.int32, device=dev)
+    ws = torch.zeros(max(L.vllt_attention_workspace_bytes(S, H, D, P), 256), dtype=torch.uint8, device=dev)
+
+    def run():
+        _lib.check(L.vllt_paged_attention_varlen(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), tables.data_ptr(),
+                                                 P // bs, cu.data_ptr(), ctx.data_ptr(), S, S * P, P, P, H, KV, D,
+                                                 bs, nb, float(1 / np.sqrt(D)), _lib.VLLT_BF16, out.data_ptr(),
+                                                 ws.data_ptr(), ws.numel(), _lib.stream_handle()))
+    t = _event_times(torch, run, args.steps, args.warmup, dev)
+    assert int(ws[:4].view(torch.int32).item()) == 0
+    fl = 4.0 * D * H * S * P * (P + 1) / 2
+    peak, kind = _tc_peak()
+    if rank == 0:
+        v = fl / t / 1e12
+        print(json.dumps({"metric": "prefill attention TFLOP/s (causal, tcgen05)", "value": round(v, 1),
+                          "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": round(t * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1)",
+                          "config": {"workload": f"{S} x {P}-token prompts, H{H}/KV{KV}/D{D}, block {bs}",
+                                     "l2": "flushed before each launch"},
+                          "roofline": {"bound": "tensor", "achieved": round(v, 1), "peak": peak, "unit": "TFLOP/s",
+                                       "frac": round(v / peak, 3), "peak_kind": kind, "traffic": None}}),
+              flush=True)
+
+
 def main_decode(args, torch, dev, rank, world):
     s, t_step, t = decode_bench(torch, dev, args.steps, args.warmup)
     hbm, kind = peaks()
@@ -408,6 +530,7 @@ def main_llama(args, torch, dev, rank, world):
     reqs = llama_workload(args.llama_requests, seed=0)
     run.roofline_peaks = (hbm, tfl)
     run.roofline_s = 0.0
+    run.pass_log = []
     flush_l2(torch, dev)
     torch.cuda.synchronize()
     l0 = run.L.vllt_kernel_launches() + run.replayed_kernels - run.captured_kernels
@@ -453,6 +576,8 @@ def main_llama(args, torch, dev, rank, world):
                      "bf16_tflops": tfl, "traffic": None},
         "clocks": clk.summary(),
     }
+    ps = run.pass_summary()
+    line["breakdown"] = dict(ps, host_and_other_s=round(elapsed - ps["gpu_s"], 3))
     print(json.dumps(line), flush=True)
 
 
@@ -526,7 +651,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="mixed", choices=["mixed", "shared", "decode", "llama8b"])
+    ap.add_argument("--workload", default="mixed", choices=["mixed", "shared", "decode", "llama8b", "gemm", "prefill"])
     ap.add_argument("--llama-requests", type=int, default=512)
     ap.add_argument("--llama-blocks", type=int, default=45000)
     ap.add_argument("--no-cpu-baseline", action="store_true")

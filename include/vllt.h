@@ -207,6 +207,21 @@ int vllt_sgemm(const float* A, const float* B, float* C, int32_t M, int32_t N, i
 int vllt_gemm_bf16(const void* A, const void* W, float* C, int32_t M, int32_t N, int32_t K,
                    int32_t* device_flags, void* stream);
 
+/* The same GEMM with K cut into `splits` slices (1 <= splits <= K/64), one CTA
+ * per (tile, slice), for small M where the tile grid alone leaves SMs idle.
+ * The last slice of each tile to finish sums the fp32 partials in slice order
+ * (deterministic) and writes C. `workspace` (device, at least
+ * vllt_gemm_bf16_splitk_workspace_bytes(M, N, splits) bytes; unused when
+ * splits == 1) must be zero before its first use and is left reusable.
+ * vllt_gemm_bf16_auto_splits gives the slice count the forward pass picks for
+ * an (M, N, K) projection. No reference counterpart (vllm-lite multiplies with
+ * NumPy); these expose the forward's small-M path to tests and callers. */
+int64_t vllt_gemm_bf16_splitk_workspace_bytes(int32_t M, int32_t N, int32_t splits);
+int32_t vllt_gemm_bf16_auto_splits(int32_t M, int32_t N, int32_t K);
+int vllt_gemm_bf16_splitk(const void* A, const void* W, float* C, int32_t M, int32_t N, int32_t K,
+                          int32_t splits, void* workspace, int64_t workspace_bytes, int32_t* device_flags,
+                          void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Sampling (vllmlite/sampling.py:41-64, vllmlite/speculative.py:86-100)    */
 /* ------------------------------------------------------------------------ */

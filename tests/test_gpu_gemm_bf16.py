@@ -26,8 +26,10 @@ def gemm(A, W):
     return C
 
 
+# the last three give the persistent kernel several tiles per CTA (both TMEM
+# accumulators, ring phases carried across tiles, fewer k-blocks than stages)
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 256, 64), (300, 520, 1024), (129, 4096, 512),
-                                   (512, 768, 4096)])
+                                   (512, 768, 4096), (1024, 8192, 256), (4096, 4096, 128), (2000, 6144, 1024)])
 def test_gemm_bf16_matches_float64(M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
     A = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
@@ -41,4 +43,59 @@ def test_gemm_bf16_rejects_bad_k():
     from vllt import _lib
 
     rc = _lib.lib().vllt_gemm_bf16(None, None, None, 4, 4, 100, None, None)
+    assert rc == _lib.VLLT_ERR_ARG
+
+
+def gemm_splitk(A, W, splits, ws=None):
+    from vllt import _lib
+
+    L = _lib.lib()
+    M, K = A.shape
+    N = W.shape[0]
+    C = torch.full((M, N), float("nan"), dtype=torch.float32, device=A.device)
+    flags = torch.zeros(1, dtype=torch.int32, device=A.device)
+    if ws is None:
+        ws = torch.zeros(L.vllt_gemm_bf16_splitk_workspace_bytes(M, N, splits), dtype=torch.uint8, device=A.device)
+    _lib.check(L.vllt_gemm_bf16_splitk(A.data_ptr(), W.data_ptr(), C.data_ptr(), M, N, K, splits, ws.data_ptr(),
+                                       ws.numel(), flags.data_ptr(), _lib.stream_handle()))
+    torch.cuda.synchronize()
+    assert int(flags.item()) == 0
+    return C, ws
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(1, 4096, 4096, 8), (37, 6144, 4096, 6), (256, 4096, 14336, 4),
+                                          (130, 520, 1024, 16), (64, 256, 256, 3)])
+def test_gemm_bf16_split_k_matches_float64_and_is_reusable(M, N, K, splits):
+    g = torch.Generator(device="cuda").manual_seed(M + N * 3 + K + splits)
+    A = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+    W = torch.randn((N, K), generator=g, device="cuda").to(torch.bfloat16)
+    want = (A.double() @ W.double().T).cpu().numpy()
+    got, ws = gemm_splitk(A, W, splits)
+    np.testing.assert_allclose(got.cpu().double().numpy(), want, rtol=1e-3, atol=1e-3 * np.sqrt(K))
+    # counters left at zero: a second call on the same scratch gives the same bits
+    again, _ = gemm_splitk(A, W, splits, ws)
+    assert torch.equal(got, again)
+    # close to the unsplit kernel (only the fp32 summation order differs)
+    np.testing.assert_allclose(got.cpu().numpy(), gemm(A, W).cpu().numpy(), rtol=1e-4, atol=1e-4 * np.sqrt(K))
+
+
+def test_gemm_bf16_forward_split_choice():
+    from vllt import _lib
+
+    L = _lib.lib()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    # decode batches of the Llama-3-8B projections are split; prefill batches are not
+    assert L.vllt_gemm_bf16_auto_splits(64, 4096, 14336) > 1
+    assert L.vllt_gemm_bf16_auto_splits(512, 4096, 4096) > 1
+    assert L.vllt_gemm_bf16_auto_splits(8192, 4096, 4096) == 1
+    for M, N, K in [(64, 4096, 14336), (512, 6144, 4096), (16, 4096, 4096)]:
+        s = L.vllt_gemm_bf16_auto_splits(M, N, K)
+        tiles = -(-N // 256) * -(-M // 128)
+        assert s * tiles <= sms and s <= K // 64 // 4
+
+
+def test_gemm_bf16_split_k_rejects_more_slices_than_k_blocks():
+    from vllt import _lib
+
+    rc = _lib.lib().vllt_gemm_bf16_splitk(None, None, None, 4, 256, 128, 3, None, 0, None, None)
     assert rc == _lib.VLLT_ERR_ARG

@@ -1,0 +1,30 @@
+"""GPU (2+ devices): tensor-parallel forward against the 1-GPU forward.
+
+Runs tests/tp_parity.py under torchrun on two GPUs (one process each, NCCL,
+NVLS off as for every multi-rank test here). Skipped on a 1-GPU box.
+Tolerance: logits of this rank's vocabulary slice within 5e-2 of the 1-GPU
+logits' max magnitude (the bf16 all-reduce reorders the sums), greedy picks
+equal on all rows but at most one near-tie.
+"""
+
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tensor_parallel_two_gpus_matches_one_gpu():
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", CUDA_VISIBLE_DEVICES=os.environ.get("CUDA_VISIBLE_DEVICES", "0,1"))
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29517",
+           os.path.join(root, "tests", "tp_parity.py")]
+    r = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "TP_PARITY ok" in r.stdout, r.stdout[-3000:]

@@ -1,0 +1,112 @@
+"""CPU, two gloo ranks: the tensor-parallel host protocol.
+
+The GPU path (vllt.tp.TPLlamaRunner) broadcasts one int32 message per forward
+pass (step record + control words) and merges per-rank (max, index) pairs for
+vocab-parallel greedy. Both pieces run here exactly as the GPU path uses them,
+over gloo with CPU tensors and a recording stand-in for the forward:
+  * every message rank 0 sends arrives intact and in order, records of
+    different lengths included, with marks interleaved, and the stop message
+    ends the worker loop with the right pass count;
+  * the merged argmax equals np.argmax over the full (unsharded) logits,
+    with planted ties inside a slice and across the slice boundary;
+  * an oversize record is refused on rank 0 before anything is broadcast.
+"""
+
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+FIELDS = ("tokens", "rows", "decode_seqs", "tiles", "max_ctx")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _messages():
+    from vllt._lib import StepBounds
+
+    rng = np.random.default_rng(5)
+    out = []
+    for i in range(6):
+        n = int(rng.integers(4, 60))
+        rec = rng.integers(-5, 1 << 20, size=n).astype(np.int32)
+        b = StepBounds(*[int(x) for x in rng.integers(1, 5000, size=5)])
+        out.append((rec, b, i % 2))
+    return out
+
+
+def _logits(R, V):
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((R, V)).astype(np.float32)
+    half = V // 2
+    x[0, 3] = x[0, half + 1] = 50.0          # tie across the two slices -> rank 0's index
+    x[1, half + 2] = x[1, half + 7] = 60.0   # tie inside rank 1's slice -> the first
+    x[2, 5] = x[2, 6] = 70.0                 # tie inside rank 0's slice
+    x[3, :] = 1.0                            # every entry equal -> index 0
+    return x
+
+
+def _rank(rank, world, port, result_dir):
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "vllm-lite_b200")]
+    import torch.distributed as dist
+
+    from vllt.tp import CTRL_WORDS, OP_FORWARD, OP_MARK, OP_STOP, ControlPlane, merge_argmax, serve
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        plane = ControlPlane(torch.zeros(64 + CTRL_WORDS, dtype=torch.int32))
+        msgs = _messages()
+        if rank == 0:
+            with pytest.raises(ValueError):
+                plane.send(OP_FORWARD, np.zeros(65, np.int32))
+            plane.send(OP_MARK)
+            for rec, b, g in msgs:
+                plane.send(OP_FORWARD, rec, b, g)
+            plane.send(OP_MARK)
+            plane.send(OP_STOP)
+        else:
+            seen, marks = [], []
+
+            def forward(bounds, greedy):
+                n = int(plane.ctrl[7])
+                seen.append((plane.buf[:n].numpy().copy(), bounds, greedy))
+
+            assert serve(plane, forward, marks.append) == len(msgs)
+            assert marks == [0, 0]
+            for (rec, b, g), (got, gb, gg) in zip(msgs, seen):
+                np.testing.assert_array_equal(got, rec)
+                assert [getattr(gb, f) for f in FIELDS] == [getattr(b, f) for f in FIELDS] and gg == g
+
+        # vocab-parallel greedy: rank r owns columns [r*V/2, (r+1)*V/2)
+        R, V = 8, 40
+        x = _logits(R, V)
+        vl = V // world
+        sl = x[:, rank * vl:(rank + 1) * vl]
+        val = torch.from_numpy(sl.max(1))
+        idx = torch.from_numpy((sl.argmax(1) + rank * vl).astype(np.int32))
+        vals = torch.empty(world * R, dtype=torch.float32)
+        idxs = torch.empty(world * R, dtype=torch.int32)
+        dist.all_gather(list(vals.view(world, R)), val)
+        dist.all_gather(list(idxs.view(world, R)), idx)
+        got = merge_argmax(vals.view(world, R), idxs.view(world, R)).numpy()
+        np.testing.assert_array_equal(got, x.argmax(1))
+        open(os.path.join(result_dir, f"ok{rank}"), "w").close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_control_plane_and_vocab_parallel_greedy_over_gloo(tmp_path):
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    assert sorted(os.listdir(tmp_path)) == ["ok0", "ok1"]

@@ -1,0 +1,65 @@
+"""Tensor-parallel parity check, run under torchrun by tests/test_gpu_tp.py.
+
+Every rank builds its shard of a full-width 2-layer slice of the Llama-3-8B
+shape; rank 0 drives a fixed three-pass schedule through TPLlamaRunner
+(record broadcast, NCCL all-reduces in the forward, vocab-parallel greedy) and
+compares logits and picks with a 1-GPU LlamaRunner on the same weights.
+Prints one line "TP_PARITY ok <max rel err> <agree>/<rows>" on success.
+"""
+
+import datetime
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for p in (ROOT, os.path.join(ROOT, "vllm-lite_b200"), os.path.join(ROOT, "baseline", "_ref")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def main():
+    from types import SimpleNamespace
+
+    from tests import fixtures as F
+    from tests.test_gpu_llama import schedule
+    from vllt.llama import LlamaRunner, LlamaShape
+    from vllt.tp import TPGroup, TPLlamaRunner
+
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    rank = dist.get_rank()
+    shape = LlamaShape(n_layers=2, max_seq_len=2048)
+    cache = SimpleNamespace(block_size=16, num_blocks=64)
+    sched = SimpleNamespace(max_seqs=8, max_batched_tokens=256)
+    group = TPGroup()
+    run = TPLlamaRunner(shape, cache, sched, group=group, max_rows=32, use_graphs=False)
+    if rank != 0:
+        run.worker_loop()
+    else:
+        ref = LlamaRunner(shape, cache, sched, use_graphs=False)
+        worst, agree, rows = 0.0, 0, 0
+        for seqs in schedule(shape.vocab_size, np.random.default_rng(3)):
+            out = F.as_scheduler_output(seqs)
+            _, R = run.launch(out)
+            picks = run.greedy_picks(R).cpu().numpy()
+            local_logits = run.logits_dev[:R, :run.w.vocab_local].cpu().numpy()
+            want, _ = ref.execute(out)
+            sl = want[:, run.w.vocab_offset:run.w.vocab_offset + run.w.vocab_local]
+            worst = max(worst, float(np.abs(local_logits - sl).max() / np.abs(want).max()))
+            agree += int((picks == want.argmax(1)).sum())
+            rows += R
+        run.stop_workers()
+        ok = worst < 5e-2 and agree >= rows - 1
+        print(f"TP_PARITY {'ok' if ok else 'FAIL'} {worst:.3e} {agree}/{rows}", flush=True)
+    group.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

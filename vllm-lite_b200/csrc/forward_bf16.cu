@@ -39,6 +39,7 @@ struct Bf16Ws {
   __nv_bfloat16* rows_h; // [R][d]
   float* attn_ws;
   int64_t attn_ws_bytes, total_bytes;
+  SplitKScratch sk;      // small-M projections: partial tiles + per-tile counters
 };
 
 Bf16Ws carve_bf16(const vllt_model_desc* m, const vllt_caps* c, char* base) {
@@ -60,6 +61,9 @@ Bf16Ws carve_bf16(const vllt_model_desc* m, const vllt_caps* c, char* base) {
   w.rows_h = reinterpret_cast<__nv_bfloat16*>(take(R * d * 2));
   w.attn_ws_bytes = attention_ws_bytes(c->max_seqs, m->n_heads, m->head_dim, m->max_seq_len);
   w.attn_ws = reinterpret_cast<float*>(take(w.attn_ws_bytes));
+  w.sk = forward_splitk_scratch(nullptr);
+  w.sk.part = reinterpret_cast<float*>(take(w.sk.part_bytes));
+  w.sk.counters = reinterpret_cast<int*>(take((int64_t)w.sk.n_counters * 4));
   w.total_bytes = off;
   return w;
 }
@@ -124,29 +128,29 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
     pending = nullptr;
     EpiQKVBF16 eq{w.q, kc, vc, meta + L.pos, meta + L.slot, m->rope_cos, m->rope_sin,
                   H, KV, D, m->block_size, m->max_seq_len, (int64_t)m->num_blocks * m->block_size};
-    VLLT_TRY(gemm_bf16_launch(w.h, T_cap, T_dev, m->wqkv[l], qkv_n, d, eq, err, st));
+    VLLT_TRY(gemm_bf16_launch(w.h, T_cap, T_dev, m->wqkv[l], qkv_n, d, eq, err, st, &w.sk));
     ac.kc = kc;
     ac.vc = vc;
     VLLT_TRY(attention_pass(ac, meta + L.dec_seq, nullptr, meta + kCntDecode, dec_cap, 0, 0, true, max_ctx, st));
     VLLT_TRY(attention_pass(ac, meta + L.tile_seq, meta + L.tile_q0, meta + kCntTiles, tiles_cap, 0, 0, false,
                             max_ctx, st));
     if (tp) {
-      VLLT_TRY(gemm_bf16_launch(w.attn, T_cap, T_dev, m->wo[l], d, H * D, EpiStoreBF16{w.y, d, d}, err, st));
+      VLLT_TRY(gemm_bf16_launch(w.attn, T_cap, T_dev, m->wo[l], d, H * D, EpiStoreBF16{w.y, d, d}, err, st, &w.sk));
       VLLT_TRY(tp_allreduce_bf16(w.y, (int64_t)T_cap * d, m->tp_comm, st));
       pending = w.y;
     } else {
-      VLLT_TRY(gemm_bf16_launch(w.attn, T_cap, T_dev, m->wo[l], d, H * D, EpiResidualF32{w.x, d}, err, st));
+      VLLT_TRY(gemm_bf16_launch(w.attn, T_cap, T_dev, m->wo[l], d, H * D, EpiResidualF32{w.x, d}, err, st, &w.sk));
     }
     VLLT_TRY(rmsnorm_bf16(w.x, pending, nullptr, m->ffn_norm[l], w.h, T_cap, T_dev, d, eps, st));
     pending = nullptr;
     VLLT_TRY(gemm_bf16_launch(w.h, T_cap, T_dev, m->w_gu[l], 2 * m->d_ff, d, EpiSwiGLUBF16{w.act, m->d_ff}, err,
-                              st));
+                              st, &w.sk));
     if (tp) {
-      VLLT_TRY(gemm_bf16_launch(w.act, T_cap, T_dev, m->w_down[l], d, m->d_ff, EpiStoreBF16{w.y, d, d}, err, st));
+      VLLT_TRY(gemm_bf16_launch(w.act, T_cap, T_dev, m->w_down[l], d, m->d_ff, EpiStoreBF16{w.y, d, d}, err, st, &w.sk));
       VLLT_TRY(tp_allreduce_bf16(w.y, (int64_t)T_cap * d, m->tp_comm, st));
       pending = w.y;
     } else {
-      VLLT_TRY(gemm_bf16_launch(w.act, T_cap, T_dev, m->w_down[l], d, m->d_ff, EpiResidualF32{w.x, d}, err, st));
+      VLLT_TRY(gemm_bf16_launch(w.act, T_cap, T_dev, m->w_down[l], d, m->d_ff, EpiResidualF32{w.x, d}, err, st, &w.sk));
     }
   }
   VLLT_TRY(rmsnorm_bf16(w.x, pending, meta + L.rows, m->final_norm, w.rows_h, R_cap, R_dev, d, eps, st));

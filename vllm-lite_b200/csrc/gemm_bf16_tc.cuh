@@ -11,12 +11,24 @@
 //   * after the last commit all four warps drain the accumulator with
 //     tcgen05.ld.32x32b.x32 (warp w owns rows 32w..32w+31) and hand 32 consecutive
 //     columns at a time to the epilogue functor.
-// No cluster launch and no TMA multicast: the kernel is safe in multi-GPU processes.
+// Two forms share this pipeline:
+//   * gemm_persistent_kernel (unsplit): one CTA per SM walks the tiles in a
+//     grouped raster; 6 warps (TMA, MMA, 4 epilogue) and two TMEM accumulators,
+//     so a tile's epilogue overlaps the next tile's main loop;
+//   * gemm_kernel with split-K (gridDim.z > 1, for the small-M decode passes
+//     whose tile grid would leave most SMs idle): CTA z accumulates k-blocks
+//     [z*nk/s, (z+1)*nk/s), stores its fp32 tile to a partials buffer, and the
+//     last CTA of each tile to arrive (per-tile counter) sums the partials in z
+//     order, so the result does not depend on arrival order, applies the
+//     epilogue and resets the counter.
+// No cluster launch and no TMA multicast: the kernels are safe in multi-GPU processes.
 // Every mbarrier wait is bounded; on expiry the kernel sets an error bit, lets its
 // copies land (bounded), frees its tensor memory and returns.
 #pragma once
 
 #include <cuda.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 
@@ -24,6 +36,7 @@ namespace vllt {
 namespace tc {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int GROUP_M = 16;  // row tiles per raster group
 constexpr int A_BYTES = BM * BK * 2;            // 16 KB
 constexpr int B_BYTES = BN * BK * 2;            // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
@@ -58,6 +71,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
   while (!mbar_try_wait(bar, parity))
     if (global_ns() - t0 > kWaitNs) return false;
   return true;
+}
+// As mbar_wait, but also gives up as soon as another role of the CTA has set *abort.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, unsigned parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (global_ns() - t0 > kWaitNs) return false;
+  }
+  return true;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
@@ -104,21 +130,42 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Grouped raster order of output tiles (both kernels): consecutive tile ids
+// walk up to GROUP_M row tiles of one column tile, then the next column tile,
+// so the CTAs resident at one time share a few A row slabs and W column slabs
+// in L2 instead of streaming all of W once per row slab.
+__device__ __forceinline__ void tile_origin(int t, int n_tiles, int m_tiles, int& m0, int& n0) {
+  const int per_group = GROUP_M * n_tiles;
+  const int first_m = (t / per_group) * GROUP_M, gm = min(m_tiles - first_m, GROUP_M);
+  const int r = t % per_group;
+  m0 = (first_m + r % gm) * BM;
+  n0 = (r / gm) * BN;
+}
+
+struct SplitK {
+  float* part;    // [splits][tiles][BM][BN] fp32 partial tiles
+  int* counters;  // [tiles], zero between launches
+};
+
 template <class Epi>
 __global__ void __launch_bounds__(128, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, int M_cap,
-            const int* __restrict__ M_dev, int N, int K, Epi epi, int* __restrict__ err) {
+            const int* __restrict__ M_dev, int N, int K, Epi epi, int* __restrict__ err, SplitK sk) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
   __shared__ uint64_t full[STAGES], empty[STAGES], accf;
   __shared__ uint32_t tmem_base_s;
-  __shared__ int failed_s;
+  __shared__ int failed_s, last_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = M_dev ? min(*M_dev, M_cap) : M_cap;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  if (m0 >= M) return;  // uniform over the CTA
-  const int nk = K / BK;
+  const int n_tiles = (N + BN - 1) / BN;
+  int m0, n0;
+  tile_origin(blockIdx.x, n_tiles, gridDim.x / n_tiles, m0, n0);
+  if (m0 >= M) return;  // uniform over the CTA (and over every split of this tile)
+  const int splits = gridDim.z;
+  const int kb0 = (int)((int64_t)blockIdx.z * (K / BK) / splits);
+  const int nk = (int)((int64_t)(blockIdx.z + 1) * (K / BK) / splits) - kb0;  // >= 1 (host: splits <= K/BK)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -150,8 +197,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       }
       unsigned char* a = smem + s * STAGE_BYTES;
       mbar_expect_tx(&full[s], STAGE_BYTES);
-      tma_load_2d(a, &ta, &full[s], kb * BK, m0);
-      tma_load_2d(a + A_BYTES, &tb, &full[s], kb * BK, n0);
+      tma_load_2d(a, &ta, &full[s], (kb0 + kb) * BK, m0);
+      tma_load_2d(a + A_BYTES, &tb, &full[s], (kb0 + kb) * BK, n0);
     }
     if (failed_s) {  // let the copies already issued land before the CTA can exit
       for (int j = max(0, kb - STAGES); j < kb; ++j) (void)mbar_wait(&full[j % STAGES], (j / STAGES) & 1);
@@ -182,15 +229,57 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
   const bool have = __all_sync(0xffffffffu, mbar_wait(&accf, 0));  // uniform per warp (.aligned loads)
   if (!have && lane == 0) atomicOr(err, 4);
   fence_after();
-  if (have) {
-    const int row = m0 + warp * 32 + lane;
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  const int row = m0 + warp * 32 + lane;
+  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  if (splits == 1) {
+    if (have) {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      if (n0 + c >= N) break;  // uniform over the warp
-      float v[32];
-      tmem_ld32(lane_addr + c, v);
-      if (row < M) epi.template apply<32>(row, n0 + c, v);
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= N) break;  // uniform over the warp
+        float v[32];
+        tmem_ld32(lane_addr + c, v);
+        if (row < M) epi.template apply<32>(row, n0 + c, v);
+      }
+    }
+  } else {
+    const int tiles = gridDim.x, tile = blockIdx.x;
+    const int64_t zstride = (int64_t)tiles * BM * BN;
+    float* mine = sk.part + (int64_t)tile * BM * BN + (int64_t)(warp * 32 + lane) * BN;
+    if (have) {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= N) break;
+        float v[32];
+        tmem_ld32(lane_addr + c, v);
+        float4* dst = reinterpret_cast<float4*>(mine + blockIdx.z * zstride + c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) __stcg(dst + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last_s = atomicAdd(&sk.counters[tile], 1) == splits - 1;
+    __syncthreads();
+    if (last_s) {  // every split has stored its tile: sum them in z order
+      __threadfence();
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= N) break;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+#pragma unroll 1
+        for (int z = 0; z < splits; ++z) {
+          const float4* src = reinterpret_cast<const float4*>(mine + z * zstride + c);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 t = __ldcg(src + j);
+            v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+          }
+        }
+        if (row < M) epi.template apply<32>(row, n0 + c, v);
+      }
+      if (threadIdx.x == 0) sk.counters[tile] = 0;  // ready for the next launch on this stream
     }
   }
   fence_before();
@@ -198,6 +287,153 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
   if (warp == 0) {
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// Persistent, warp-specialized form for the unsplit case: one CTA per SM walks
+// tiles blockIdx.x, blockIdx.x + gridDim.x, ... Warp 0 streams k-blocks through
+// the shared-memory ring without pausing between tiles, warp 1 issues the MMAs
+// into one of two 256-column TMEM accumulators (512 columns), and warps 2-5
+// drain the other accumulator through the epilogue at the same time.
+constexpr int P_THREADS = 192;
+constexpr int P_TMEM_COLS = 512;
+
+template <class Epi>
+__global__ void __launch_bounds__(P_THREADS, 1)
+gemm_persistent_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, int M_cap,
+                       const int* __restrict__ M_dev, int N, int K, Epi epi, int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
+  __shared__ uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = M_dev ? min(*M_dev, M_cap) : M_cap;
+  const int n_tiles = (N + BN - 1) / BN, m_tiles = (M + BM - 1) / BM;
+  const int total = n_tiles * m_tiles, nk = K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&drain, 1);
+    abort_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base_s)),
+                 "r"(P_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer ----
+      int g = 0;
+      bool failed = false;
+      for (int t = blockIdx.x; t < total && !failed; t += gridDim.x) {
+        int m0, n0;
+        tile_origin(t, n_tiles, m_tiles, m0, n0);
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          if (g >= STAGES && !mbar_wait_or_abort(&empty[s], ((g / STAGES) & 1) ^ 1, &abort_s)) {
+            failed = true;
+            break;
+          }
+          unsigned char* a = smem + s * STAGE_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(a, &ta, &full[s], kb * BK, m0);
+          tma_load_2d(a + A_BYTES, &tb, &full[s], kb * BK, n0);
+        }
+      }
+      if (failed) {
+        atomicOr(err, 4);
+        abort_s = 1;
+        // let the copies already issued land before the CTA can exit
+        for (int j = max(0, g - STAGES); j < g; ++j) (void)mbar_wait(&full[j % STAGES], (j / STAGES) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer ----
+      int g = 0, i = 0;
+      bool failed = false;
+      for (int t = blockIdx.x; t < total && !failed; t += gridDim.x, ++i) {
+        const int a = i & 1;
+        if (i >= 2 && !mbar_wait_or_abort(&acc_empty[a], ((i >> 1) & 1) ^ 1, &abort_s)) {
+          failed = true;
+          break;
+        }
+        fence_after();
+        const uint32_t d = tmem + a * BN;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          if (!mbar_wait_or_abort(&full[s], (g / STAGES) & 1, &abort_s)) {
+            failed = true;
+            break;
+          }
+          fence_after();
+          const unsigned char* sa = smem + s * STAGE_BYTES;
+          const unsigned char* sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16(d, smem_desc(sa + k * 32), smem_desc(sb + k * 32), (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        if (!failed) mma_commit(&acc_full[a]);
+      }
+      if (failed) {
+        atomicOr(err, 4);
+        abort_s = 1;
+      }
+      if (g > 0) {  // every MMA this thread issued has finished before the columns are freed
+        mma_commit(&drain);
+        (void)mbar_wait(&drain, 0);
+      }
+    }
+  } else {  // ---- epilogue warps 2..5: TMEM lane quarter (warp % 4) ----
+    const int q = warp & 3;
+    int i = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+      const int a = i & 1;
+      const bool have = __all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[a], (i >> 1) & 1, &abort_s));
+      if (!have) {
+        if (lane == 0) {
+          atomicOr(err, 4);
+          abort_s = 1;
+        }
+        break;
+      }
+      fence_after();
+      int m0, n0;
+      tile_origin(t, n_tiles, m_tiles, m0, n0);
+      const int row = m0 + q * 32 + lane;
+      const uint32_t lane_addr = tmem + a * BN + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= N) break;  // uniform over the warp
+        float v[32];
+        tmem_ld32(lane_addr + c, v);
+        if (row < M) epi.template apply<32>(row, n0 + c, v);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P_TMEM_COLS));
   }
 }
 
@@ -366,10 +602,61 @@ inline int kmajor_map(CUtensorMap* m, const void* base, int64_t rows, int K, int
 
 }  // namespace tc
 
+// Split-K scratch the caller owns: partial tiles and per-tile counters (zeroed
+// once; every launch leaves them zero). max_splits <= 1 disables splitting.
+struct SplitKScratch {
+  float* part = nullptr;
+  int64_t part_bytes = 0;
+  int* counters = nullptr;
+  int n_counters = 0;
+  int max_splits = 0;
+};
+
+inline int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// How many K slices a launch of this shape gets: enough CTAs to cover the SMs
+// when the tile grid covers fewer than half of them, at least 4 k-blocks per
+// slice, within the scratch. Depends only on (M_cap, N, K) and the scratch, so
+// eager runs and graph replays of one shape split alike.
+inline int choose_splits(int M_cap, int N, int K, const SplitKScratch* sk) {
+  if (!sk || sk->max_splits <= 1 || !sk->part || !sk->counters || M_cap <= 0 || N <= 0) return 1;
+  const int tiles = ceil_div(N, tc::BN) * ceil_div(M_cap, tc::BM);
+  const int sms = sm_count();
+  if (tiles * 2 > sms || tiles > sk->n_counters) return 1;
+  int s = std::min(std::min(sms / tiles, (K / tc::BK) / 4), sk->max_splits);
+  while (s > 1 && (int64_t)s * tiles * tc::BM * tc::BN * 4 > sk->part_bytes) --s;
+  return std::max(s, 1);
+}
+
+// The forward pass's split-K scratch: room for 160 partial tiles (at least one
+// per SM of one GPU) and 128 tile counters; `base` (may be null for sizing)
+// holds the partials followed by the counters.
+inline SplitKScratch forward_splitk_scratch(char* base) {
+  SplitKScratch sk;
+  sk.part_bytes = 160ll * tc::BM * tc::BN * 4;
+  sk.n_counters = 128;
+  sk.max_splits = 8;
+  sk.part = base ? reinterpret_cast<float*>(base) : nullptr;
+  sk.counters = base ? reinterpret_cast<int*>(base + sk.part_bytes) : nullptr;
+  return sk;
+}
+
 // D = A . W^T through an epilogue. A [M_cap][K], W [N][K] bf16, K % 64 == 0.
+// `splits` > 0 forces that many K slices (tests); 0 lets choose_splits decide.
 template <class Epi>
 inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const void* W, int N, int K, const Epi& epi,
-                     int* err, cudaStream_t st) {
+                     int* err, cudaStream_t st, const SplitKScratch* sk = nullptr, int splits = 0) {
   if (M_cap <= 0 || N <= 0) return VLLT_OK;
   VLLT_REQUIRE(K > 0 && K % tc::BK == 0, "gemm_bf16: K must be a positive multiple of 64 (K=%d)", K);
   VLLT_REQUIRE(((uintptr_t)A & 15) == 0 && ((uintptr_t)W & 15) == 0, "gemm_bf16: operands must be 16-byte aligned");
@@ -379,15 +666,31 @@ inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const vo
   if (rc != VLLT_OK) return rc;
   rc = tc::kmajor_map(&tb, W, N, K, tc::BN);
   if (rc != VLLT_OK) return rc;
-  static unsigned configured = 0;
+  static unsigned configured = 0;  // per device: dynamic shared memory opted in for both kernels
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 32 && !(configured & (1u << dev))) {
     cudaFuncSetAttribute(tc::gemm_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
+    cudaFuncSetAttribute(tc::gemm_persistent_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         tc::SMEM_BYTES);
     configured |= 1u << dev;
   }
-  dim3 grid(ceil_div(N, tc::BN), ceil_div(M_cap, tc::BM));
-  tc::gemm_kernel<Epi><<<grid, 128, tc::SMEM_BYTES, st>>>(ta, tb, M_cap, M_dev, N, K, epi, err);
+  if (splits <= 0) splits = choose_splits(M_cap, N, K, sk);
+  const int64_t tiles = (int64_t)ceil_div(N, tc::BN) * ceil_div(M_cap, tc::BM);
+  VLLT_REQUIRE(tiles < (1ll << 31), "gemm_bf16: too many tiles");
+  if (splits == 1) {  // persistent: one CTA per SM (at most one per tile)
+    const unsigned ctas = (unsigned)std::min<int64_t>(tiles, sm_count());
+    tc::gemm_persistent_kernel<Epi><<<ctas, tc::P_THREADS, tc::SMEM_BYTES, st>>>(ta, tb, M_cap, M_dev, N, K, epi,
+                                                                                 err);
+    return check_launch("gemm_bf16");
+  }
+  VLLT_REQUIRE(sk && sk->part && sk->counters && tiles <= sk->n_counters &&
+                   splits * tiles * tc::BM * tc::BN * 4 <= sk->part_bytes && splits <= K / tc::BK,
+               "gemm_bf16: split-K scratch too small for %d slices of %lld tiles (or more slices than k-blocks)",
+               splits, (long long)tiles);
+  const tc::SplitK ks{sk->part, sk->counters};
+  dim3 grid((unsigned)tiles, 1, splits);
+  tc::gemm_kernel<Epi><<<grid, 128, tc::SMEM_BYTES, st>>>(ta, tb, M_cap, M_dev, N, K, epi, err, ks);
   return check_launch("gemm_bf16");
 }
 

@@ -289,12 +289,45 @@ class CudaRunner(_Base):
         self.rec_host[:n].numpy()[:] = rec
         self.rec_dev[:n].copy_(self.rec_host[:n], non_blocking=True)
         self.h2d_bytes += 4 * n + 8 * len(out.cow)
+        self._timed_forward(bounds)
+        self.steps += 1
+        return rows, R
+
+    def _timed_forward(self, bounds) -> None:
+        """Enqueue the forward (graph or eager); with `pass_log` set (a list),
+        bracket it with CUDA events and log (tokens, decode_seqs, e0, e1)."""
+        log = getattr(self, "pass_log", None)
+        if log is not None:
+            e0 = self.torch.cuda.Event(enable_timing=True)
+            e1 = self.torch.cuda.Event(enable_timing=True)
+            e0.record()
+        self._dispatch(bounds)
+        if log is not None:
+            e1.record()
+            log.append((bounds.tokens, bounds.decode_seqs, e0, e1))
+
+    def _dispatch(self, bounds) -> None:
         if self.use_graphs:
             self._forward_graph(bounds)
         else:
             self._forward(self.bucket(bounds) if self.bucket_bounds else bounds)
-        self.steps += 1
-        return rows, R
+
+    def pass_summary(self) -> dict:
+        """GPU seconds of the logged passes, split into passes with prompt
+        tokens (tokens > decode sequences) and decode-only passes."""
+        log = getattr(self, "pass_log", None) or []
+        if log:
+            log[-1][3].synchronize()
+        pre = dec = 0.0
+        n_pre = n_dec = 0
+        for tokens, dec_seqs, e0, e1 in log:
+            t = e0.elapsed_time(e1) / 1e3
+            if tokens > dec_seqs:
+                pre, n_pre = pre + t, n_pre + 1
+            else:
+                dec, n_dec = dec + t, n_dec + 1
+        return {"passes": len(log), "gpu_s": round(pre + dec, 3), "prefill_passes": n_pre,
+                "prefill_pass_gpu_s": round(pre, 3), "decode_passes": n_dec, "decode_pass_gpu_s": round(dec, 3)}
 
     def _forward(self, bounds) -> None:
         check(self.L.vllt_forward(C.byref(self.desc), self.rec_dev.data_ptr(), C.byref(self.caps),

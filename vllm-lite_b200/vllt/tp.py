@@ -56,6 +56,85 @@ class TPGroup:
             self.comm = None
 
 
+class ControlPlane:
+    """The per-pass message from rank 0 to the other ranks: the step record
+    followed by CTRL_WORDS control words, in one int32 buffer that is broadcast
+    whole, so every rank takes exactly one collective per message.
+
+    `buf` is the broadcast buffer (on the GPU for NCCL, on the CPU for gloo);
+    `host` is rank 0's staging copy (pinned memory on a GPU; omitted when `buf`
+    is already host memory)."""
+
+    def __init__(self, buf, host=None):
+        import torch
+
+        self.buf = buf
+        self.host = buf if host is None else host
+        self.capacity = buf.numel() - CTRL_WORDS
+        self.ctrl = torch.zeros(CTRL_WORDS, dtype=torch.int32)
+
+    def send(self, op: int, rec=None, bounds=None, greedy: int = 0) -> int:
+        """Rank 0: broadcast one message; returns the bytes staged host->device."""
+        import torch.distributed as dist
+
+        n = 0 if rec is None else int(rec.size)
+        if n > self.capacity:
+            raise ValueError(f"step record of {n} words exceeds the broadcast buffer ({self.capacity})")
+        if n:
+            self.host[:n].numpy()[:] = rec
+        b = bounds or StepBounds(0, 0, 0, 0, 1)
+        self.host[-CTRL_WORDS:].numpy()[:] = [op, b.tokens, b.rows, b.decode_seqs, b.tiles, b.max_ctx, greedy, n]
+        staged = 0
+        if self.host is not self.buf:
+            if n:
+                self.buf[:n].copy_(self.host[:n], non_blocking=True)
+            self.buf[-CTRL_WORDS:].copy_(self.host[-CTRL_WORDS:], non_blocking=True)
+            staged = 4 * (n + CTRL_WORDS)
+        dist.broadcast(self.buf, src=0)
+        return staged
+
+    def recv(self):
+        """Ranks > 0: take one message; returns (op, bounds, greedy, record words).
+        The record itself stays in `buf[:n]` where the forward reads it."""
+        import torch.distributed as dist
+
+        dist.broadcast(self.buf, src=0)
+        self.ctrl.copy_(self.buf[-CTRL_WORDS:])
+        c = [int(x) for x in self.ctrl.tolist()]
+        return c[0], StepBounds(*c[1:6]), c[6], c[7]
+
+
+def serve(plane: ControlPlane, forward, mark) -> int:
+    """Worker dispatch loop: forward(bounds, greedy) for each OP_FORWARD,
+    mark(tag) for each OP_MARK, return the number of passes at OP_STOP.
+    An unknown op is a protocol error (rank 0 never sends one)."""
+    passes = 0
+    while True:
+        op, bounds, greedy, _ = plane.recv()
+        if op == OP_STOP:
+            return passes
+        if op == OP_MARK:
+            mark(bounds.tokens)
+        elif op == OP_FORWARD:
+            forward(bounds, greedy)
+            passes += 1
+        else:
+            raise RuntimeError(f"tensor-parallel control: unknown op {op}")
+
+
+def merge_argmax(vals, idxs):
+    """Vocab-parallel greedy: vals/idxs [ranks][R] hold each rank's (max logit,
+    global index of its first maximum) per row, rank r owning the r-th
+    vocabulary slice. Returns the global argmax per row with np.argmax's tie
+    rule: among equal maxima the lowest index, i.e. the lowest rank."""
+    import torch
+
+    n = vals.shape[0]
+    best = vals.max(0).values
+    score = torch.where(vals == best, torch.arange(n, 0, -1, device=vals.device).view(n, 1), 0)
+    return idxs.gather(0, score.argmax(0, keepdim=True)).view(-1)
+
+
 class TPLlamaRunner(LlamaRunner):
     """One tensor-parallel shard; on rank 0 it is the engine's runner."""
 
@@ -69,8 +148,7 @@ class TPLlamaRunner(LlamaRunner):
         self._fixed = True
         import torch
 
-        self.rec_words = self.rec_dev.numel()
-        self.ctrl_host = torch.zeros(CTRL_WORDS, dtype=torch.int32, pin_memory=True)
+        self.plane = ControlPlane(self.rec_dev, self.rec_host)
         self._val = torch.empty(self.caps.max_rows, dtype=torch.float32, device=self.dev)
         self._idx = torch.empty(self.caps.max_rows, dtype=torch.int32, device=self.dev)
         self._vals = torch.empty(group.world * self.caps.max_rows, dtype=torch.float32, device=self.dev)
@@ -97,7 +175,7 @@ class TPLlamaRunner(LlamaRunner):
         self._reserve(S, T, R, W)
         self._broadcast(OP_FORWARD, rec, bounds, greedy=1)
         self._last_n = rec.size
-        self._run(bounds)
+        self._timed_forward(bounds)
         self.steps += 1
         self._pending_rows = R
         if getattr(self, "roofline_peaks", None):
@@ -105,28 +183,10 @@ class TPLlamaRunner(LlamaRunner):
         return rows, R
 
     def _broadcast(self, op, rec=None, bounds=None, greedy=0):
-        import torch.distributed as dist
-
-        n = 0 if rec is None else rec.size
-        if rec is not None:
-            self.rec_host[:n].numpy()[:] = rec
-        b = bounds or StepBounds(0, 0, 0, 0, 1)
-        self.rec_host[-CTRL_WORDS:].numpy()[:] = [op, b.tokens, b.rows, b.decode_seqs, b.tiles, b.max_ctx, greedy, n]
-        if n:
-            self.rec_dev[:n].copy_(self.rec_host[:n], non_blocking=True)
-        self.rec_dev[-CTRL_WORDS:].copy_(self.rec_host[-CTRL_WORDS:], non_blocking=True)
-        self.h2d_bytes += 4 * (n + CTRL_WORDS)
-        dist.broadcast(self.rec_dev, src=0)
-
-    def _run(self, bounds):
-        if self.use_graphs:
-            self._forward_graph(bounds)
-        else:
-            self._forward(bounds)
+        self.h2d_bytes += self.plane.send(op, rec, bounds, greedy)
 
     def greedy_picks(self, R: int):
         """Global argmax token id per logit row (device tensor [R], int32)."""
-        import torch
         import torch.distributed as dist
 
         w = self.w
@@ -136,11 +196,7 @@ class TPLlamaRunner(LlamaRunner):
         vals, idxs = self._vals[:n * R], self._idxs[:n * R]
         dist.all_gather_into_tensor(vals, self._val[:R])
         dist.all_gather_into_tensor(idxs, self._idx[:R])
-        vals, idxs = vals.view(n, R), idxs.view(n, R)
-        best = vals.max(0).values
-        # ties: the lowest rank holds the lowest global index (first max wins)
-        score = torch.where(vals == best, torch.arange(n, 0, -1, device=self.dev).view(n, 1), 0)
-        return idxs.gather(0, score.argmax(0, keepdim=True)).view(R)
+        return merge_argmax(vals.view(n, R), idxs.view(n, R))
 
     def stop_workers(self):
         self._broadcast(OP_STOP)
@@ -167,21 +223,15 @@ class TPLlamaRunner(LlamaRunner):
 
     # ---- ranks > 0 ------------------------------------------------------------------
     def worker_loop(self):
-        """Serve rank 0's forward passes until it broadcasts the stop record."""
+        """Serve rank 0's forward passes until it broadcasts the stop record.
+        Runs the same dispatch as rank 0 (graph bucket or eager bounds), so
+        every rank launches the same kernels and collectives."""
         import torch
-        import torch.distributed as dist
 
-        while True:
-            dist.broadcast(self.rec_dev, src=0)
-            self.ctrl_host.copy_(self.rec_dev[-CTRL_WORDS:])
-            ctrl = self.ctrl_host.numpy()
-            if ctrl[0] == OP_STOP:
-                break
-            if ctrl[0] == OP_MARK:
-                self._record_mark(int(ctrl[1]))
-                continue
-            bounds = StepBounds(*[int(x) for x in ctrl[1:6]])
-            self._run(bounds)
-            if ctrl[6]:
-                self.greedy_picks(int(ctrl[2]))
+        def forward(bounds, greedy):
+            self._dispatch(bounds)
+            if greedy:
+                self.greedy_picks(bounds.rows)
             torch.cuda.current_stream(self.dev).synchronize()
+
+        return serve(self.plane, forward, self._record_mark)
