@@ -252,6 +252,8 @@ def main_ours(args):
         return main_decode(args, torch, dev, rank, world)
     if wl == "llama8b":
         return main_llama(args, torch, dev, rank, world)
+    if wl == "spec":
+        return main_spec(args, torch, dev, rank, world)
     if wl == "gemm":
         return main_gemm(args, torch, dev, rank, world)
     if wl == "prefill":
@@ -351,6 +353,83 @@ def main_ours(args):
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def spec_config():
+    """C5: the bench model with room for 257-token prompts + 256 outputs."""
+    from vllmlite.config import CacheConfig, EngineConfig, ModelConfig, SchedulerConfig
+
+    mc = ModelConfig(vocab_size=261, max_seq_len=1024, **MODEL)
+    return EngineConfig(model=mc, cache=CacheConfig(block_size=16, num_blocks=4096, enable_prefix_caching=False),
+                        scheduler=SchedulerConfig(max_seqs=64, max_batched_tokens=2048))
+
+
+def main_spec(args, torch, dev, rank, world):
+    """C5: 128 periodic prompts, 256 greedy tokens each, n-gram speculation with
+    k drafts verified on the device; token streams must equal k = 0."""
+    from vllt import _lib
+    from vllt.engine import gpu_engine
+    from vllt.workloads import periodic_workload
+
+    L = _lib.lib()
+    k = args.spec_k
+    reqs = periodic_workload(128, seed=rank)
+
+    def streams(eng, tag):
+        return [list(eng.seqs[f"{tag}-{rid}"].output_token_ids) for rid, _, _ in reqs]
+
+    base = gpu_engine(spec_config(), speculative_tokens=0)
+    eng = gpu_engine(spec_config(), speculative_tokens=k)
+    for i in range(args.warmup):
+        run_workload(eng, reqs, f"w{i}")
+    # identity against k = 0 (outputs read before release)
+    for rid, ids, params in reqs:
+        base.add_request(params=params, request_id=f"b-{rid}", prompt_token_ids=ids)
+        eng.add_request(params=params, request_id=f"c-{rid}", prompt_token_ids=ids)
+    while base.has_work:
+        base.step()
+    while eng.has_work:
+        eng.step()
+    same = streams(base, "b") == streams(eng, "c")
+    eng.spec.proposed = eng.spec.accepted = 0
+    ts, toks, ttft, launches = [], 0, [], 0
+    run = eng.runner
+    with Clocks(int(os.environ.get("LOCAL_RANK", 0))) as clk:
+        for i in range(args.steps):
+            flush_l2(torch, dev)
+            torch.cuda.synchronize()
+            l0 = L.vllt_kernel_launches() + run.replayed_kernels - run.captured_kernels
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            n, tt, _ = run_workload(eng, reqs, f"t{i}")
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) / 1e3)
+            launches = L.vllt_kernel_launches() + run.replayed_kernels - run.captured_kernels - l0
+            toks += n
+            ttft += tt
+    t = sum(ts)
+    if world > 1:
+        import torch.distributed as dist
+
+        v = torch.tensor([t, toks], device=dev, dtype=torch.float64)
+        dist.all_reduce(v[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(v[1:], op=dist.ReduceOp.SUM)
+        t, toks = float(v[0]), float(v[1])
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"engine output tok/s (C5: 128 periodic prompts, speculative k={k})",
+            "value": round(toks / t, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1e3 * t / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "vllt",
+            "data": "synthetic (reference-seeded weights, seeded periodic prompts)",
+            "config": {"workload": f"C5: 128 periodic prompts (period 8-32, length 64-256), 256 greedy tokens, "
+                                   f"n-gram proposer k={k}, 6L/384d fp32, max_seqs 64, budget 2048",
+                       "parallelism": f"replicas x{world}", "l2": "flushed before each timed step"},
+            "token_identical_to_k0": bool(same),
+            "acceptance": round(eng.spec.accepted / max(eng.spec.proposed, 1), 4),
+            "ttft_p50_ms": round(1e3 * statistics.median(ttft), 2) if ttft else None,
+            "gpu_launches": int(launches), "e2e": None, "clocks": clk.summary()}), flush=True)
 
 
 def _tc_peak():
@@ -651,7 +730,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="mixed", choices=["mixed", "shared", "decode", "llama8b", "gemm", "prefill"])
+    ap.add_argument("--workload", default="mixed", choices=["mixed", "shared", "decode", "llama8b", "spec", "gemm",
+                                                               "prefill"])
+    ap.add_argument("--spec-k", type=int, default=4)
     ap.add_argument("--llama-requests", type=int, default=512)
     ap.add_argument("--llama-blocks", type=int, default=45000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
