@@ -63,13 +63,24 @@ def requests(workload: str, seed: int):
     return mixed_workload(48, seed, 256 if workload == "shared" else 0)
 
 
-def run_workload(eng, reqs, tag):
-    """Submit every request, drive step() until drained (bench/bench.py:83-88)."""
+def run_workload(eng, reqs, tag, nvtx_window=None):
+    """Submit every request, drive step() until drained (bench/bench.py:83-88).
+    nvtx_window=(a, b): steps a..b-1 of this run sit in an NVTX range
+    "vllt_window" (for `ncu --nvtx --nvtx-include vllt_window/`)."""
     for rid, ids, params in reqs:
         eng.add_request(params=params, request_id=f"{tag}-{rid}", prompt_token_ids=ids)
     steps0 = eng.total_steps
     while eng.has_work:
+        i = eng.total_steps - steps0
+        if nvtx_window and i == nvtx_window[0]:
+            import torch
+
+            torch.cuda.nvtx.range_push("vllt_window")
         eng.step()
+        if nvtx_window and i == nvtx_window[1] - 1:
+            import torch
+
+            torch.cuda.nvtx.range_pop()
     seqs = [eng.seqs[f"{tag}-{rid}"] for rid, _, _ in reqs]
     out_tokens = sum(len(s.output_token_ids) for s in seqs)
     ttft = [s.ttft for s in seqs if s.ttft is not None]
@@ -457,42 +468,75 @@ def _event_times(torch, fn, steps, warmup, dev):
     return statistics.median(ts)
 
 
+def _graph_time(torch, fns, reps):
+    """Seconds per call of fns (cycled), captured back to back in one CUDA graph
+    and replayed: no host launch latency inside the timed region. Median of
+    max(reps, 3) replays, L2 flushed before each."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in fns:
+            f()
+    g.replay()
+    ts = []
+    for _ in range(max(reps, 3)):
+        flush_l2(torch, torch.device("cuda", torch.cuda.current_device()))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1) / 1e3)
+    del g
+    return statistics.median(ts) / len(fns)
+
+
 def main_gemm(args, torch, dev, rank, world):
     """tcgen05 bf16 GEMM on the Llama-3-8B projection shapes, prefill (M=8192)
-    and decode (M=512, 64) batches: TFLOP/s against the measured cuBLAS bf16
-    peak, and weight GB/s for the decode batches. The forward's own split-K
-    choice is used for the small-M shapes."""
+    and decode (M=512, 256, 64) batches: TFLOP/s against the measured cuBLAS
+    bf16 peak, and weight GB/s for the decode batches. Each shape runs in the
+    form the forward pass picks for it ("splits" 0 = small-M stream-K form).
+    Launches are timed inside a CUDA graph (as the forward runs them), cycling
+    over enough weight copies that the weights of consecutive launches do not
+    fit in L2 together, like consecutive layers."""
     from vllt import _lib
 
     L = _lib.lib()
     flags = torch.zeros(1, dtype=torch.int32, device=dev)
     shapes = [("qkv", 6144, 4096), ("o_proj", 4096, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336)]
     peak, kind = _tc_peak()
+    hbm, _ = peaks()
     res = {}
     tot_flops = tot_t = 0.0
-    for M in (8192, 512, 64):
+    for M in (8192, 512, 256, 64):
         A = torch.randn((M, 14336), device=dev).to(torch.bfloat16)
         for name, N, K in shapes:
-            W = torch.randn((N, K), device=dev).to(torch.bfloat16)
+            copies = max(2, -(-320 * 2 ** 20 // (N * K * 2)))
+            Ws = [torch.randn((N, K), device=dev).to(torch.bfloat16) for _ in range(copies)]
             C_ = torch.empty((M, N), device=dev)
             a = A[:, :K].contiguous()
             splits = int(L.vllt_gemm_bf16_auto_splits(M, N, K))
-            ws = torch.zeros(max(int(L.vllt_gemm_bf16_splitk_workspace_bytes(M, N, splits)), 256),
+            ws = torch.zeros(max(int(L.vllt_gemm_bf16_splitk_workspace_bytes(M, N, K, splits)), 256),
                              dtype=torch.uint8, device=dev)
 
-            def run():
-                _lib.check(L.vllt_gemm_bf16_splitk(a.data_ptr(), W.data_ptr(), C_.data_ptr(), M, N, K, splits,
-                                                   ws.data_ptr(), ws.numel(), flags.data_ptr(),
-                                                   _lib.stream_handle()))
-            t = _event_times(torch, run, args.steps, args.warmup, dev)
+            def launcher(W):
+                def run():
+                    _lib.check(L.vllt_gemm_bf16_splitk(a.data_ptr(), W.data_ptr(), C_.data_ptr(), M, N, K, splits,
+                                                       ws.data_ptr(), ws.numel(), flags.data_ptr(),
+                                                       _lib.stream_handle()))
+                return run
+            fns = [launcher(W) for W in Ws] * max(1, 8 // copies)
+            for f in fns:  # untimed, outside capture: first-use setup
+                f()
+            t = _graph_time(torch, fns, args.steps)
             fl = 2.0 * M * N * K
-            res[f"M{M}_{name}"] = {"tflops": round(fl / t / 1e12, 1), "us": round(t * 1e6, 1), "splits": splits,
-                                   "frac": round(fl / t / 1e12 / peak, 3),
-                                   "weight_gbs": round(N * K * 2 / t / 1e9, 1)}
+            res[f"M{M}_{name}"] = {"tflops": round(fl / t / 1e12, 1), "us": round(t * 1e6, 2), "splits": splits,
+                                   "tc_frac": round(fl / t / 1e12 / peak, 3),
+                                   "weight_gbs": round(N * K * 2 / t / 1e9, 1),
+                                   "hbm_frac": round(N * K * 2 / t / 1e9 / hbm, 3)}
             if M == 8192:
                 tot_flops += fl
                 tot_t += t
-            del W, C_, ws
+            del Ws, C_, ws
     assert int(flags.item()) == 0, "bounded wait expired in the GEMM"
     if rank == 0:
         v = tot_flops / tot_t / 1e12
@@ -501,7 +545,8 @@ def main_gemm(args, torch, dev, rank, world):
                           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                           "data": "synthetic N(0,1)",
                           "config": {"workload": "the four GEMM shapes of one Llama-3-8B layer",
-                                     "l2": "flushed before each launch"},
+                                     "timing": "CUDA graph of 8 launches over rotating weight copies",
+                                     "l2": "flushed before each replay; weights of consecutive launches exceed L2"},
                           "roofline": {"bound": "tensor", "achieved": round(v, 1), "peak": peak, "unit": "TFLOP/s",
                                        "frac": round(v / peak, 3), "peak_kind": kind, "traffic": None},
                           "shapes": res}), flush=True)
@@ -618,8 +663,9 @@ def main_llama(args, torch, dev, rank, world):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     t_wall = time.perf_counter()
+    window = tuple(int(x) for x in args.nvtx_passes.split(":")) if args.nvtx_passes else None
     with Clocks(int(os.environ.get("LOCAL_RANK", 0))) as clk:
-        toks, ttft, steps = run_workload(eng, reqs, "t")
+        toks, ttft, steps = run_workload(eng, reqs, "t", window)
     e1.record()
     if world > 1:
         run.mark(1)
@@ -733,6 +779,8 @@ def main():
     ap.add_argument("--workload", default="mixed", choices=["mixed", "shared", "decode", "llama8b", "spec", "gemm",
                                                                "prefill"])
     ap.add_argument("--spec-k", type=int, default=4)
+    ap.add_argument("--nvtx-passes", default="", help="a:b - mark engine steps a..b-1 of the timed llama8b run "
+                                                      "with an NVTX range (profiling)")
     ap.add_argument("--llama-requests", type=int, default=512)
     ap.add_argument("--llama-blocks", type=int, default=45000)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -207,16 +207,22 @@ int vllt_sgemm(const float* A, const float* B, float* C, int32_t M, int32_t N, i
 int vllt_gemm_bf16(const void* A, const void* W, float* C, int32_t M, int32_t N, int32_t K,
                    int32_t* device_flags, void* stream);
 
-/* The same GEMM with K cut into `splits` slices (1 <= splits <= K/64), one CTA
- * per (tile, slice), for small M where the tile grid alone leaves SMs idle.
- * The last slice of each tile to finish sums the fp32 partials in slice order
- * (deterministic) and writes C. `workspace` (device, at least
- * vllt_gemm_bf16_splitk_workspace_bytes(M, N, splits) bytes; unused when
- * splits == 1) must be zero before its first use and is left reusable.
- * vllt_gemm_bf16_auto_splits gives the slice count the forward pass picks for
- * an (M, N, K) projection. No reference counterpart (vllm-lite multiplies with
- * NumPy); these expose the forward's small-M path to tests and callers. */
-int64_t vllt_gemm_bf16_splitk_workspace_bytes(int32_t M, int32_t N, int32_t splits);
+/* The same GEMM in the forms the forward pass uses for few token rows:
+ *   splits >= 2: K cut into `splits` slices (splits <= K/64), one CTA per
+ *     (tile, slice); the last slice of each tile to finish sums the fp32
+ *     partials in slice order (deterministic) and writes C;
+ *   splits == 0: the forward's own choice for (M, N, K): for M <= 256 (N a
+ *     multiple of 32) the small-M form (weights on the MMA's M side, the
+ *     (feature tile, k-block) iterations divided evenly over one CTA per SM,
+ *     split tiles summed in CTA order by a second kernel), else split-K as
+ *     vllt_gemm_bf16_auto_splits says, else the persistent kernel;
+ *   splits == 1: the persistent kernel (as vllt_gemm_bf16).
+ * `workspace` (device, at least vllt_gemm_bf16_splitk_workspace_bytes(M, N, K,
+ * splits) bytes) must be zero before its first use and is left reusable.
+ * vllt_gemm_bf16_auto_splits returns 0 when the small-M form applies, else the
+ * split count. No reference counterpart (vllm-lite multiplies with NumPy);
+ * these expose the forward's small-M paths to tests and callers. */
+int64_t vllt_gemm_bf16_splitk_workspace_bytes(int32_t M, int32_t N, int32_t K, int32_t splits);
 int32_t vllt_gemm_bf16_auto_splits(int32_t M, int32_t N, int32_t K);
 int vllt_gemm_bf16_splitk(const void* A, const void* W, float* C, int32_t M, int32_t N, int32_t K,
                           int32_t splits, void* workspace, int64_t workspace_bytes, int32_t* device_flags,

@@ -55,7 +55,8 @@ def gemm_splitk(A, W, splits, ws=None):
     C = torch.full((M, N), float("nan"), dtype=torch.float32, device=A.device)
     flags = torch.zeros(1, dtype=torch.int32, device=A.device)
     if ws is None:
-        ws = torch.zeros(L.vllt_gemm_bf16_splitk_workspace_bytes(M, N, splits), dtype=torch.uint8, device=A.device)
+        ws = torch.zeros(L.vllt_gemm_bf16_splitk_workspace_bytes(M, N, K, splits), dtype=torch.uint8,
+                         device=A.device)
     _lib.check(L.vllt_gemm_bf16_splitk(A.data_ptr(), W.data_ptr(), C.data_ptr(), M, N, K, splits, ws.data_ptr(),
                                        ws.numel(), flags.data_ptr(), _lib.stream_handle()))
     torch.cuda.synchronize()
@@ -79,16 +80,28 @@ def test_gemm_bf16_split_k_matches_float64_and_is_reusable(M, N, K, splits):
     np.testing.assert_allclose(got.cpu().numpy(), gemm(A, W).cpu().numpy(), rtol=1e-4, atol=1e-4 * np.sqrt(K))
 
 
-def test_gemm_bf16_forward_split_choice():
+# the small-M form (splits 0): stream-K spans that start and end inside tiles,
+# several tiles per CTA, token counts around the 32-column chunks, M = 1
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (16, 6144, 4096), (37, 4096, 14336), (64, 28672, 4096),
+                                   (100, 1024, 1024), (256, 4096, 4096), (200, 160, 640), (129, 128256, 4096)])
+def test_gemm_bf16_small_m_form_matches_float64(M, N, K):
+    from vllt import _lib
+
+    assert _lib.lib().vllt_gemm_bf16_auto_splits(M, N, K) == 0
+    test_gemm_bf16_split_k_matches_float64_and_is_reusable(M, N, K, 0)
+
+
+def test_gemm_bf16_forward_form_choice():
     from vllt import _lib
 
     L = _lib.lib()
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    # decode batches of the Llama-3-8B projections are split; prefill batches are not
-    assert L.vllt_gemm_bf16_auto_splits(64, 4096, 14336) > 1
+    # decode batches take the small-M form; 512-row batches with few tiles split K; prefill does neither
+    assert L.vllt_gemm_bf16_auto_splits(64, 4096, 14336) == 0
+    assert L.vllt_gemm_bf16_auto_splits(256, 4096, 4096) == 0
     assert L.vllt_gemm_bf16_auto_splits(512, 4096, 4096) > 1
     assert L.vllt_gemm_bf16_auto_splits(8192, 4096, 4096) == 1
-    for M, N, K in [(64, 4096, 14336), (512, 6144, 4096), (16, 4096, 4096)]:
+    for M, N, K in [(512, 6144, 4096), (512, 4096, 14336)]:
         s = L.vllt_gemm_bf16_auto_splits(M, N, K)
         tiles = -(-N // 256) * -(-M // 128)
         assert s * tiles <= sms and s <= K // 64 // 4

@@ -155,7 +155,7 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   }
   VLLT_TRY(rmsnorm_bf16(w.x, pending, meta + L.rows, m->final_norm, w.rows_h, R_cap, R_dev, d, eps, st));
   VLLT_TRY(gemm_bf16_launch(w.rows_h, R_cap, R_dev, m->lm_head, m->vocab, d,
-                            EpiStoreF32{logits, m->vocab_padded, m->vocab}, err, st));
+                            EpiStoreF32{logits, m->vocab_padded, m->vocab}, err, st, &w.sk));
   return VLLT_OK;
 }
 

@@ -437,6 +437,255 @@ gemm_persistent_kernel(const __grid_constant__ CUtensorMap ta, const __grid_cons
   }
 }
 
+// ---- small-M form (decode passes): weights on the MMA's M side -----------------------
+//
+// With few token rows (M <= 256) a 128-row token tile wastes most of the
+// tensor core and the tile grid covers few SMs, while the run time is set by
+// streaming W once from HBM. This form swaps the operands: the MMA computes
+// D^T[128 features][n_pad tokens] = W_tile . A^T (both K-major in shared
+// memory, M128 x N n_pad x K16), so one CTA covers 128 output features for
+// every token. Work is cut stream-K: the (feature tile, k-block) iterations
+// are divided evenly over one CTA per SM, so every SM streams the same number
+// of weight bytes whatever the shape. A CTA's span covers whole tiles, whose
+// epilogue it applies itself (transposed through shared memory so the
+// epilogue sees 32 consecutive features of one token), and at most two partial
+// tiles at its ends, which it stores as fp32 [token][128] slices; a second
+// kernel sums each split tile's slices in CTA order (deterministic) and
+// applies the epilogue.
+constexpr int SK_THREADS = 192;             // warps 0-3 epilogue, warp 4 TMA, warp 5 MMA
+constexpr int SK_W_BYTES = 128 * BK * 2;    // one 128-feature x 64 k weight tile (16 KB)
+constexpr int SK_MAX_STAGES = 8;
+constexpr int SK_RING_BYTES = 192 * 1024;
+constexpr int SK_TBUF_BYTES = 4 * 32 * 33 * 4;  // per-warp 32 x 33 transpose buffers
+
+struct SmallPlan {
+  int tiles;      // ceil(N / 128)
+  int nk;         // K / 64
+  int ctas;       // CTAs; CTA c owns iterations [c*total/ctas, (c+1)*total/ctas)
+  int n_pad;      // MMA N (tokens, padded: 32..256, power of two)
+  int stages;
+  int64_t total;  // tiles * nk
+};
+
+__device__ __forceinline__ int64_t sk_begin(int c, const SmallPlan& p) { return (int64_t)c * p.total / p.ctas; }
+__device__ __forceinline__ int sk_owner(int64_t it, const SmallPlan& p) {
+  return (int)(((it + 1) * p.ctas - 1) / p.total);
+}
+// slot of CTA c's partial slice of tile t: 2c for its first tile, 2c+1 for its last
+__device__ __forceinline__ int sk_slot(int c, int t, const SmallPlan& p) {
+  return 2 * c + (t == (int)(sk_begin(c, p) / p.nk) ? 0 : 1);
+}
+
+__device__ __forceinline__ void mma_bf16_n(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(SK_THREADS, 1)
+gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, int M_cap,
+                  const int* __restrict__ M_dev, int N, SmallPlan p, Epi epi, float* __restrict__ part,
+                  int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
+  __shared__ uint64_t full[SK_MAX_STAGES], empty[SK_MAX_STAGES], acc_full[2], acc_empty[2], drain;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = M_dev ? min(*M_dev, M_cap) : M_cap;
+  if (M <= 0) return;  // uniform over the CTA, before any barrier or TMEM use
+  const int stages = p.stages, nk = p.nk;
+  const uint32_t stage_bytes = SK_W_BYTES + (uint32_t)p.n_pad * 128;
+  float* tbuf = reinterpret_cast<float*>(smem + stages * stage_bytes);
+  const int64_t it_begin = sk_begin(blockIdx.x, p), it_end = sk_begin(blockIdx.x + 1, p);
+  const uint32_t tmem_cols = 2 * p.n_pad;  // two accumulators (64..512, a power of two)
+  const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.n_pad >> 3) << 17) |
+                         ((uint32_t)(128 >> 4) << 24);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(&drain, 1);
+    abort_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base_s)),
+                 "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 4) {
+    if (lane == 0) {  // ---- TMA producer: W tile and the token tile of each k-block ----
+      int g = 0;
+      bool failed = false;
+      for (int64_t it = it_begin; it < it_end; ++it, ++g) {
+        const int t = (int)(it / nk), kb = (int)(it % nk);
+        const int s = g % stages;
+        if (g >= stages && !mbar_wait_or_abort(&empty[s], ((g / stages) & 1) ^ 1, &abort_s)) {
+          failed = true;
+          break;
+        }
+        unsigned char* a = smem + s * stage_bytes;
+        mbar_expect_tx(&full[s], stage_bytes);
+        tma_load_2d(a, &tw, &full[s], kb * BK, t * 128);
+        tma_load_2d(a + SK_W_BYTES, &tx, &full[s], kb * BK, 0);
+      }
+      if (failed) {
+        atomicOr(err, 4);
+        abort_s = 1;
+        for (int j = max(0, g - stages); j < g; ++j) (void)mbar_wait(&full[j % stages], (j / stages) & 1);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {  // ---- MMA issuer: one accumulator per tile segment, alternating ----
+      int g = 0, seg = 0;
+      bool failed = false;
+      int64_t it = it_begin;
+      while (it < it_end && !failed) {
+        const int t = (int)(it / nk);
+        const int64_t seg_begin = it, seg_end = min(it_end, (int64_t)(t + 1) * nk);
+        const int a = seg & 1;
+        if (seg >= 2 && !mbar_wait_or_abort(&acc_empty[a], ((seg >> 1) & 1) ^ 1, &abort_s)) {
+          failed = true;
+          break;
+        }
+        fence_after();
+        const uint32_t d = tmem + a * p.n_pad;
+        for (; it < seg_end; ++it, ++g) {
+          const int s = g % stages;
+          if (!mbar_wait_or_abort(&full[s], (g / stages) & 1, &abort_s)) {
+            failed = true;
+            break;
+          }
+          fence_after();
+          const unsigned char* sw = smem + s * stage_bytes;
+          const unsigned char* sx = sw + SK_W_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16_n(d, smem_desc(sw + k * 32), smem_desc(sx + k * 32), idesc, (it > seg_begin || k > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        if (!failed) mma_commit(&acc_full[a]);
+        ++seg;
+      }
+      if (failed) {
+        atomicOr(err, 4);
+        abort_s = 1;
+      }
+      if (g > 0) {
+        mma_commit(&drain);
+        (void)mbar_wait(&drain, 0);
+      }
+    }
+  } else {  // ---- epilogue warps 0-3: features 32*warp .. +31 of the tile (TMEM lanes) ----
+    float* tb = tbuf + warp * 32 * 33;
+    int seg = 0;
+    int64_t it = it_begin;
+    const int t_first = (int)(it_begin / nk);
+    while (it < it_end) {
+      const int t = (int)(it / nk);
+      const int64_t seg_end = min(it_end, (int64_t)(t + 1) * nk);
+      const bool whole = (it == (int64_t)t * nk) && (seg_end == (int64_t)(t + 1) * nk);
+      const int a = seg & 1;
+      const bool have = __all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[a], (seg >> 1) & 1, &abort_s));
+      if (!have) {
+        if (lane == 0) {
+          atomicOr(err, 4);
+          abort_s = 1;
+        }
+        break;
+      }
+      fence_after();
+      const int f0 = t * 128 + warp * 32;
+      const uint32_t lane_addr = tmem + a * p.n_pad + ((uint32_t)(warp * 32) << 16);
+      float* slice = whole ? nullptr
+                           : part + (int64_t)(2 * blockIdx.x + (t == t_first ? 0 : 1)) * M_cap * 128 + warp * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < p.n_pad; c += 32) {
+        if (c >= M || f0 >= N) break;  // uniform over the warp
+        float v[32];
+        tmem_ld32(lane_addr + c, v);  // v[j] = D^T[feature f0 + lane][token c + j]
+        if (!whole) {                 // fp32 slice [token][128]: 32 consecutive floats per store
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c + j < M) __stcg(slice + (int64_t)(c + j) * 128, v[j]);
+          continue;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tb[lane * 33 + j] = v[j];
+        __syncwarp();
+        float u[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) u[i] = tb[i * 33 + lane];  // token c + lane, features f0 + i
+        __syncwarp();
+        if (c + lane < M) epi.template apply<32>(c + lane, f0, u);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      it = seg_end;
+      ++seg;
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
+  }
+}
+
+// Sum the slices of every tile that stream-K split between CTAs, in CTA order,
+// and apply the epilogue. blockIdx.y + 1 = CTA boundary b; the tile holding it
+// is handled by its lowest boundary. Thread = (token, 32-feature chunk).
+template <class Epi>
+__global__ void __launch_bounds__(128)
+gemm_small_reduce_kernel(const float* __restrict__ part, int M_cap, const int* __restrict__ M_dev, int N,
+                         SmallPlan p, Epi epi) {
+  const int b = blockIdx.y + 1;
+  const int64_t i = sk_begin(b, p);
+  if (i % p.nk == 0) return;  // boundary on a tile edge: no tile split here
+  const int t = (int)(i / p.nk);
+  const int64_t ip = sk_begin(b - 1, p);
+  if (ip / p.nk == t && ip % p.nk != 0) return;  // a lower boundary inside this tile handles it
+  const int M = M_dev ? min(*M_dev, M_cap) : M_cap;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = idx >> 2, q = idx & 3;
+  const int f = t * 128 + q * 32;
+  if (m >= M || f >= N) return;
+  const int c_lo = sk_owner((int64_t)t * p.nk, p), c_hi = sk_owner((int64_t)(t + 1) * p.nk - 1, p);
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = 0.f;
+  for (int c = c_lo; c <= c_hi; ++c) {
+    const float4* src =
+        reinterpret_cast<const float4*>(part + ((int64_t)sk_slot(c, t, p) * M_cap + m) * 128 + q * 32);
+    float4 r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __ldcg(src + j);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[4 * j] += r[j].x; v[4 * j + 1] += r[j].y; v[4 * j + 2] += r[j].z; v[4 * j + 3] += r[j].w;
+    }
+  }
+  epi.template apply<32>(m, f, v);
+}
+
 }  // namespace tc
 
 // ---- bf16-path epilogues (32 consecutive columns per call) --------------------------
@@ -639,12 +888,14 @@ inline int choose_splits(int M_cap, int N, int K, const SplitKScratch* sk) {
   return std::max(s, 1);
 }
 
-// The forward pass's split-K scratch: room for 160 partial tiles (at least one
-// per SM of one GPU) and 128 tile counters; `base` (may be null for sizing)
-// holds the partials followed by the counters.
+// The forward pass's GEMM scratch: partial slices / tiles for up to 160 SMs
+// and 128 tile counters; `base` (may be null for sizing) holds the partials
+// followed by the counters.
 inline SplitKScratch forward_splitk_scratch(char* base) {
   SplitKScratch sk;
-  sk.part_bytes = 160ll * tc::BM * tc::BN * 4;
+  // the small-M form's slices (2 per CTA, 256 tokens x 128 fp32) bound the size;
+  // the split-K form's 160 partial tiles fit in the same bytes
+  sk.part_bytes = 2ll * 160 * 256 * 128 * 4;
   sk.n_counters = 128;
   sk.max_splits = 8;
   sk.part = base ? reinterpret_cast<float*>(base) : nullptr;
@@ -652,8 +903,52 @@ inline SplitKScratch forward_splitk_scratch(char* base) {
   return sk;
 }
 
+// Plan of the small-M form for this shape, or false when it does not apply
+// (more than 256 token rows, N not a multiple of 32).
+inline bool small_plan(int M_cap, int N, int K, tc::SmallPlan* p) {
+  if (M_cap <= 0 || M_cap > 256 || N <= 0 || N % 32 || K % tc::BK) return false;
+  int n_pad = 32;
+  while (n_pad < M_cap) n_pad *= 2;
+  p->n_pad = n_pad;
+  p->tiles = ceil_div(N, 128);
+  p->nk = K / tc::BK;
+  p->total = (int64_t)p->tiles * p->nk;
+  p->ctas = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), p->total / 4));
+  const int stage_bytes = tc::SK_W_BYTES + n_pad * 128;
+  p->stages = std::min(tc::SK_MAX_STAGES, tc::SK_RING_BYTES / stage_bytes);
+  return true;
+}
+inline int64_t small_scratch_bytes(int M_cap, const tc::SmallPlan& p) { return 2ll * p.ctas * M_cap * 128 * 4; }
+
+template <class Epi>
+inline int gemm_small_launch(const void* A, int M_cap, const int* M_dev, const void* W, int N, int K,
+                             const Epi& epi, int* err, cudaStream_t st, const tc::SmallPlan& p, float* part) {
+  CUtensorMap tw, tx;
+  int rc = tc::kmajor_map(&tw, W, N, K, 128);
+  if (rc != VLLT_OK) return rc;
+  rc = tc::kmajor_map(&tx, A, M_cap, K, p.n_pad);
+  if (rc != VLLT_OK) return rc;
+  const int smem = 1024 + p.stages * (tc::SK_W_BYTES + p.n_pad * 128) + tc::SK_TBUF_BYTES;
+  static unsigned configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 32 && !(configured & (1u << dev))) {
+    cudaFuncSetAttribute(tc::gemm_small_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         1024 + tc::SK_RING_BYTES + tc::SK_TBUF_BYTES);
+    configured |= 1u << dev;
+  }
+  tc::gemm_small_kernel<Epi><<<p.ctas, tc::SK_THREADS, smem, st>>>(tw, tx, M_cap, M_dev, N, p, epi, part, err);
+  rc = check_launch("gemm_bf16 (small M)");
+  if (rc != VLLT_OK || p.ctas < 2) return rc;
+  dim3 grid(ceil_div(M_cap * 4, 128), p.ctas - 1);
+  tc::gemm_small_reduce_kernel<Epi><<<grid, 128, 0, st>>>(part, M_cap, M_dev, N, p, epi);
+  return check_launch("gemm_bf16 (small M reduce)");
+}
+
 // D = A . W^T through an epilogue. A [M_cap][K], W [N][K] bf16, K % 64 == 0.
-// `splits` > 0 forces that many K slices (tests); 0 lets choose_splits decide.
+// `splits` > 0 forces that many K slices of the split-K form (1 = the
+// persistent form); 0 picks the form: small-M stream-K when M_cap <= 256 and
+// the scratch holds its slices, else split-K when choose_splits says so.
 template <class Epi>
 inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const void* W, int N, int K, const Epi& epi,
                      int* err, cudaStream_t st, const SplitKScratch* sk = nullptr, int splits = 0) {
@@ -675,7 +970,12 @@ inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const vo
                          tc::SMEM_BYTES);
     configured |= 1u << dev;
   }
-  if (splits <= 0) splits = choose_splits(M_cap, N, K, sk);
+  if (splits <= 0) {
+    tc::SmallPlan sp;
+    if (sk && sk->part && small_plan(M_cap, N, K, &sp) && small_scratch_bytes(M_cap, sp) <= sk->part_bytes)
+      return gemm_small_launch(A, M_cap, M_dev, W, N, K, epi, err, st, sp, sk->part);
+    splits = choose_splits(M_cap, N, K, sk);
+  }
   const int64_t tiles = (int64_t)ceil_div(N, tc::BN) * ceil_div(M_cap, tc::BM);
   VLLT_REQUIRE(tiles < (1ll << 31), "gemm_bf16: too many tiles");
   if (splits == 1) {  // persistent: one CTA per SM (at most one per tile)

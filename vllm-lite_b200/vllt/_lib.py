@@ -60,7 +60,7 @@ SIGNATURES = {
     "vllt_rope": (C.c_int, [vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "vllt_sgemm": (C.c_int, [vp, vp, vp, i32, i32, i32, vp]),
     "vllt_gemm_bf16": (C.c_int, [vp, vp, vp, i32, i32, i32, vp, vp]),
-    "vllt_gemm_bf16_splitk_workspace_bytes": (i64, [i32, i32, i32]),
+    "vllt_gemm_bf16_splitk_workspace_bytes": (i64, [i32, i32, i32, i32]),
     "vllt_gemm_bf16_auto_splits": (i32, [i32, i32, i32]),
     "vllt_gemm_bf16_splitk": (C.c_int, [vp, vp, vp, i32, i32, i32, i32, vp, i64, vp, vp]),
     "vllt_sample_greedy": (C.c_int, [vp, i32, i32, i32, vp, i32, vp, vp, vp, vp]),
