@@ -503,11 +503,14 @@ def main_gemm(args, torch, dev, rank, world):
     L = _lib.lib()
     flags = torch.zeros(1, dtype=torch.int32, device=dev)
     shapes = [("qkv", 6144, 4096), ("o_proj", 4096, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336)]
+    if args.gemm_shape:
+        shapes = [x for x in shapes if x[0] in args.gemm_shape.split(",")]
     peak, kind = _tc_peak()
     hbm, _ = peaks()
     res = {}
     tot_flops = tot_t = 0.0
-    for M in (8192, 512, 256, 64):
+    ms = [int(x) for x in args.gemm_m.split(",")] if args.gemm_m else [8192, 512, 256, 64]
+    for M in ms:
         A = torch.randn((M, 14336), device=dev).to(torch.bfloat16)
         for name, N, K in shapes:
             copies = max(2, -(-320 * 2 ** 20 // (N * K * 2)))
@@ -539,7 +542,7 @@ def main_gemm(args, torch, dev, rank, world):
             del Ws, C_, ws
     assert int(flags.item()) == 0, "bounded wait expired in the GEMM"
     if rank == 0:
-        v = tot_flops / tot_t / 1e12
+        v = tot_flops / tot_t / 1e12 if tot_t else 0.0
         print(json.dumps({"metric": "tcgen05 bf16 GEMM TFLOP/s (Llama-3-8B projections, M=8192)", "value": round(v, 1),
                           "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -779,6 +782,8 @@ def main():
     ap.add_argument("--workload", default="mixed", choices=["mixed", "shared", "decode", "llama8b", "spec", "gemm",
                                                                "prefill"])
     ap.add_argument("--spec-k", type=int, default=4)
+    ap.add_argument("--gemm-m", default="", help="token counts of the gemm workload (default 8192,512,256,64)")
+    ap.add_argument("--gemm-shape", default="", help="projections of the gemm workload (qkv,o_proj,gate_up,down)")
     ap.add_argument("--nvtx-passes", default="", help="a:b - mark engine steps a..b-1 of the timed llama8b run "
                                                       "with an NVTX range (profiling)")
     ap.add_argument("--llama-requests", type=int, default=512)

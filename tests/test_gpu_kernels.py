@@ -336,6 +336,41 @@ def test_decode_kernel_matches_generic_kernel(dev):
     np.testing.assert_allclose(fast.cpu().numpy(), out.float().cpu().numpy(), rtol=2e-2, atol=2e-2)
 
 
+def test_attention_prefill_tensor_core_rising_and_falling_scores(dev):
+    """Scores that climb by about 10 (log2 units) per 128-key tile make the
+    tcgen05 prefill kernel move its running max and rescale O on every tile;
+    falling scores keep the first tile's max throughout. Both against the
+    float64 oracle on the same bf16 inputs."""
+    from vllt.ops import attention_flags, paged_attention_varlen
+
+    rng = np.random.default_rng(11)
+    H, KV, D, bs = 32, 8, 128, 16
+    qlens, ctxs = [700, 300, 200], [700, 300, 456]
+    q, ck, cv, tables, tab = ragged_batch(rng, H, KV, D, bs, qlens, ctxs, "bf16")
+    u = rng.standard_normal((KV, D))
+    u *= np.sqrt(D) / np.linalg.norm(u, axis=1, keepdims=True)
+    ramps = [lambda t: 0.005 * t, lambda t: 0.005 * (300 - t), lambda t: 0.004 * t]
+    for i, c in enumerate(ctxs):
+        for t in range(c):
+            slot = tables[i][t // bs] * bs + t % bs
+            ck[slot] = u * ramps[i](t) + 0.1 * rng.standard_normal((KV, D))
+    cu = np.concatenate([[0], np.cumsum(qlens)])
+    for i in range(len(qlens)):
+        q[cu[i]:cu[i + 1]] = np.repeat(u, H // KV, axis=0)[None] + 0.1 * rng.standard_normal((qlens[i], H, D))
+    r = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).bfloat16().float().numpy()
+    q, ck = r(q), r(ck)
+    tq = torch.from_numpy(q).to(dev, torch.bfloat16)
+    tk = torch.from_numpy(to_lib_layout(ck, bs)).to(dev, torch.bfloat16)
+    tv = torch.from_numpy(to_lib_layout(cv, bs)).to(dev, torch.bfloat16)
+    scale = 1.0 / np.sqrt(D)
+    got = paged_attention_varlen(tq, tk, tv, tab, cu, ctxs, scale).float().cpu().numpy()
+    assert attention_flags(paged_attention_varlen.last_workspace) == 0
+    for i, c in enumerate(ctxs):
+        slots = A.table_slots(tables[i], bs, c)
+        want = A.dense_attention(q[cu[i]:cu[i + 1]], ck[slots], cv[slots], KV, scale)
+        np.testing.assert_allclose(got[cu[i]:cu[i + 1]], want, rtol=2e-2, atol=2e-2, err_msg=f"seq {i}")
+
+
 @pytest.mark.parametrize("H,KV", [(32, 8), (8, 8), (16, 8), (64, 8)])
 def test_attention_prefill_tensor_core(dev, H, KV):
     """Multi-token tiles of bf16 / head_dim 128 / block 16 take the tcgen05

@@ -273,6 +273,7 @@ __global__ void __launch_bounds__(kWarps * 32) attention_kernel(AttnParams p) {
 // Merge split-K partials of single-query work items: one warp per (item, head).
 template <typename T, int D>
 __global__ void merge_splits_kernel(AttnParams p, int max_splits) {
+  pdl_trigger();  // the o_proj projection may start its set-up (it waits for this grid)
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int item = gw / p.H, h = gw % p.H;

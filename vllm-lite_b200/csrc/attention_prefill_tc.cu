@@ -5,21 +5,19 @@
 // causal mask of :87-94) for the multi-token query tiles of a ragged batch.
 // A CTA owns one KV head and 128 query rows = (128 / NREP positions) x NREP
 // heads of the group, position-major, so every K/V tile it loads serves all
-// heads of the group.
-//
-//   Q  : one 3-D TMA load per 64-wide half of head_dim (tokens x heads x d box),
-//        128B swizzle -> K-major A operand.
-//   K,V: per 16-token block two 2-D TMA boxes (d halves) each; blocks past the
-//        context or with a bad id read the out-of-range zero fill. K is the
-//        K-major B operand of S = Q K^T; V is the MN-major B operand of O = P V.
-//   S  : tcgen05.mma M128 N128 K16 x 8 into tensor memory columns [0, 128).
-//   softmax: thread t owns row t (TMEM lane t): two passes over S (max, then
-//        p = 2^(s - m)), online across key tiles; P is written as bf16 into
-//        shared memory in the swizzled K-major layout.
-//   O  : tcgen05.mma (P from shared memory, V) into columns [128, 256); a
-//        row's O is rescaled in tensor memory only when its max moved.
-// K/V tiles are double buffered (next tile loads while this one is processed).
-// All waits are bounded; no clusters, no multicast.
+// heads of the group. Warp-specialized, 6 warps:
+//   warp 4 (loads): Q once by 3-D TMA (one box per 64-wide half of head_dim),
+//        then per 128-key tile the K and V blocks (2-D boxes per 16-token block
+//        and d half; blocks past the context or with a bad id read the
+//        out-of-range zero fill) into separate 2-stage K and V rings;
+//   warp 5 (MMA): S_j = Q K_j^T (M128 N128 K16 x 8) into one of two TMEM S
+//        buffers, issued one tile ahead so it runs under the softmax of the
+//        tile before; O += P_j V_j (V MN-major) into TMEM once P_j is ready;
+//   warps 0-3 (softmax, thread = row = TMEM lane): the row's 128 scores in
+//        registers, causal mask on the diagonal tile, p = 2^(s*scale - m) on
+//        MUFU, P as bf16 into shared memory (swizzled K-major A operand);
+//        O is rescaled in TMEM only when the running max grows by > 2^8.
+// Q, P, K and V are 128B-swizzled. All waits are bounded; no clusters, no multicast.
 
 #include <cuda.h>
 
@@ -99,30 +97,46 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// exp2 on the MUFU unit (flush-to-zero: scores below 2^-126 count as 0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The running max a row's probabilities are taken against moves only when a
+// tile's max exceeds it by more than 2^8 (log2 units): until then P <= 256,
+// exact in bf16's exponent range, and O needs no rescale. The result O / l
+// does not depend on which max was used.
+constexpr float kRescaleLog2 = 8.0f;
+
 template <int NREP>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(192, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, PrefillParams p) {
   constexpr int QP = kRows / NREP;  // query positions per CTA
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
-  unsigned char* q_s = smem;                   // 2 halves [128 rows][128 B]
-  unsigned char* p_s = q_s + 2 * kHalf;        // 2 key halves [128 rows][128 B]
-  unsigned char* kv_s = p_s + 2 * kHalf;       // 2 stages x (K 2 halves, V 2 halves)
-  __shared__ uint64_t bar_q, bar_kv[2], bar_s, bar_o;
+  unsigned char* q_s = smem;                // 2 halves [128 rows][128 B]
+  unsigned char* p_s = q_s + 2 * kHalf;     // 2 key halves [128 rows][128 B]
+  unsigned char* k_s = p_s + 2 * kHalf;     // 2 stages x K tile (2 d halves)
+  unsigned char* v_s = k_s + 2 * kTileBytes;  // 2 stages x V tile
+  __shared__ uint64_t bar_q, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full, o_done, drain;
   __shared__ uint32_t tmem_s;
-  __shared__ int fail_s;
+  __shared__ volatile int abort_s;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kvh = blockIdx.x;
   int s, q0;
-  if (p.item_seq) {
-    if ((int)blockIdx.y >= *p.n_items) return;
-    s = p.item_seq[blockIdx.y];
-    q0 = p.item_q0[blockIdx.y];
+  if (p.item_seq) {  // work list: heaviest (latest) items first
+    const int n = *p.n_items;
+    if ((int)blockIdx.y >= n) return;
+    const int it = n - 1 - (int)blockIdx.y;
+    s = p.item_seq[it];
+    q0 = p.item_q0[it];
   } else {
     s = blockIdx.y / p.items_per_seq;
-    q0 = (blockIdx.y % p.items_per_seq) * QP;
+    q0 = (p.items_per_seq - 1 - (int)(blockIdx.y % p.items_per_seq)) * QP;
     if (s >= p.num_seqs) return;
   }
   const int tok0 = p.cu_q[s];
@@ -136,209 +150,253 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 
   if (tid == 0) {
     mbar_init(&bar_q, 1);
-    mbar_init(&bar_kv[0], 1);
-    mbar_init(&bar_kv[1], 1);
-    mbar_init(&bar_s, 1);
-    mbar_init(&bar_o, 1);
-    fail_s = 0;
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+    }
+    mbar_init(&p_full, 128);
+    mbar_init(&o_done, 1);
+    mbar_init(&drain, 1);
+    abort_s = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_s)), "r"(256));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_s)), "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   fence_before();
   __syncthreads();
   fence_after();
-  const uint32_t tmem = tmem_s, t_S = tmem, t_O = tmem + 128;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t tmem = tmem_s, t_O = tmem + 256;  // S buffers at columns 0 and 128
 
-  // K/V tile j -> stage j & 1: 8 blocks x (K lo, K hi, V lo, V hi)
-  auto load_kv = [&](int j) {
-    unsigned char* st = kv_s + (j & 1) * kStageBytes;
-    uint64_t* bar = &bar_kv[j & 1];
-    mbar_expect_tx(bar, kStageBytes);
-#pragma unroll 1
-    for (int b = 0; b < kKeys / kBS; ++b) {
-      const int kb = j * (kKeys / kBS) + b;  // block index within the sequence
-      int blk = (kb * kBS < ctx) ? table[kb] : -1;
-      const int y = (blk >= 0 && blk < p.num_blocks) ? (blk * p.n_kv + kvh) * kBS : (int)p.cache_rows;
-      unsigned char* kdst = st + b * (kBS * 128);
-      tma_load_2d(kdst, &tk, bar, 0, y);
-      tma_load_2d(kdst + kHalf, &tk, bar, 64, y);
-      tma_load_2d(kdst + kTileBytes, &tv, bar, 0, y);
-      tma_load_2d(kdst + kTileBytes + kHalf, &tv, bar, 64, y);
+  if (warp == 4) {
+    if (lane == 0) {  // ---- loads: Q once, then K_j and V_j into 2-stage rings ----
+      mbar_expect_tx(&bar_q, 2 * kHalf);
+      tma_load_3d(q_s, &tq, &bar_q, 0, kvh * NREP, tok0 + q0);
+      tma_load_3d(q_s + kHalf, &tq, &bar_q, 64, kvh * NREP, tok0 + q0);
+      int jk = 0, jv = 0;  // tiles issued per ring
+      bool failed = false;
+      for (int j = 0; j < n_tiles && !failed; ++j) {
+        int y[kKeys / kBS];
+#pragma unroll
+        for (int b = 0; b < kKeys / kBS; ++b) {
+          const int kb = j * (kKeys / kBS) + b;  // block index within the sequence
+          const int blk = (kb * kBS < ctx) ? table[kb] : -1;
+          y[b] = (blk >= 0 && blk < p.num_blocks) ? (blk * p.n_kv + kvh) * kBS : (int)p.cache_rows;
+        }
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait_or_abort(&k_empty[st], ((j >> 1) & 1) ^ 1, &abort_s)) {
+          failed = true;
+          break;
+        }
+        mbar_expect_tx(&k_full[st], kTileBytes);
+#pragma unroll
+        for (int b = 0; b < kKeys / kBS; ++b) {
+          unsigned char* dst = k_s + st * kTileBytes + b * (kBS * 128);
+          tma_load_2d(dst, &tk, &k_full[st], 0, y[b]);
+          tma_load_2d(dst + kHalf, &tk, &k_full[st], 64, y[b]);
+        }
+        jk = j + 1;
+        if (j >= 2 && !mbar_wait_or_abort(&v_empty[st], ((j >> 1) & 1) ^ 1, &abort_s)) {
+          failed = true;
+          break;
+        }
+        mbar_expect_tx(&v_full[st], kTileBytes);
+#pragma unroll
+        for (int b = 0; b < kKeys / kBS; ++b) {
+          unsigned char* dst = v_s + st * kTileBytes + b * (kBS * 128);
+          tma_load_2d(dst, &tv, &v_full[st], 0, y[b]);
+          tma_load_2d(dst + kHalf, &tv, &v_full[st], 64, y[b]);
+        }
+        jv = j + 1;
+      }
+      if (failed) {  // let the copies in flight land before the CTA can exit (bounded)
+        atomicOr(p.err, 4);
+        abort_s = 1;
+        (void)mbar_wait(&bar_q, 0);
+        for (int t = max(0, jk - 2); t < jk; ++t) (void)mbar_wait(&k_full[t & 1], (t >> 1) & 1);
+        for (int t = max(0, jv - 2); t < jv; ++t) (void)mbar_wait(&v_full[t & 1], (t >> 1) & 1);
+      }
     }
-  };
-
-  int issued = 0, consumed = 0;  // K/V tiles (thread 0's bookkeeping for the failure path)
-  if (tid == 0) {
-    mbar_expect_tx(&bar_q, 2 * kHalf);
-    tma_load_3d(q_s, &tq, &bar_q, 0, kvh * NREP, tok0 + q0);
-    tma_load_3d(q_s + kHalf, &tq, &bar_q, 64, kvh * NREP, tok0 + q0);
-    load_kv(0);
-    issued = 1;
-    if (n_tiles > 1) {
-      load_kv(1);
-      issued = 2;
-    }
-  }
-
-  // this thread's row
-  const int row = tid;
-  const int qpos = first_qpos + row / NREP;
-  float m_run = -INFINITY, l_run = 0.f;
-  bool ok = true;
-
-  for (int j = 0; j < n_tiles && ok; ++j) {
-    if (tid == 0) {  // S = Q K_j^T
-      bool w = (j > 0 || mbar_wait(&bar_q, 0)) && mbar_wait(&bar_kv[j & 1], (j >> 1) & 1);
-      if (!w) {
-        fail_s = 1;
-      } else {
-        consumed = j + 1;
+  } else if (warp == 5) {
+    if (lane == 0) {  // ---- MMA: S_{j+1} = Q K^T ahead of the softmax, then O += P_j V_j ----
+      bool ok = mbar_wait_or_abort(&bar_q, 0, &abort_s) && mbar_wait_or_abort(&k_full[0], 0, &abort_s);
+      int issued = 0;
+      auto issue_s = [&](int j) {
         fence_after();
-        const unsigned char* kt = kv_s + (j & 1) * kStageBytes;
+        const unsigned char* kt = k_s + (j & 1) * kTileBytes;
+        const uint32_t t_S = tmem + (j & 1) * 128;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {
           const int h = k >> 2, off = (k & 3) * 32;
           umma<false>(t_S, desc_kmajor(q_s + h * kHalf + off), desc_kmajor(kt + h * kHalf + off), k > 0 ? 1u : 0u);
         }
-        mma_commit(&bar_s);
+        mma_commit(&s_full[j & 1]);
+        mma_commit(&k_empty[j & 1]);
+        ++issued;
+      };
+      if (ok) issue_s(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        // S buffer (j+1)&1 was last read by the softmax of tile j-1, complete since p_full(j-1)
+        if (j + 1 < n_tiles) {
+          if (!mbar_wait_or_abort(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, &abort_s)) {
+            ok = false;
+            break;
+          }
+          issue_s(j + 1);
+        }
+        if (!mbar_wait_or_abort(&p_full, j & 1, &abort_s) ||
+            !mbar_wait_or_abort(&v_full[j & 1], (j >> 1) & 1, &abort_s)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const unsigned char* vt = v_s + (j & 1) * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < kKeys / 16; ++k) {
+          const int h = k >> 2, off = (k & 3) * 32;
+          umma<true>(t_O, desc_kmajor(p_s + h * kHalf + off), desc_mnmajor(vt + k * 16 * 128),
+                     (j > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&v_empty[j & 1]);
+        mma_commit(&o_done);
+        ++issued;
+      }
+      if (!ok) {
+        atomicOr(p.err, 4);
+        abort_s = 1;
+      }
+      if (issued > 0) {  // every MMA finished before the columns are freed
+        mma_commit(&drain);
+        (void)mbar_wait(&drain, 0);
       }
     }
-    // every thread: wait for S
-    if (!__all_sync(0xffffffffu, mbar_wait(&bar_s, j & 1))) {
-      if (lane == 0) fail_s = 1;
-    }
-    __syncthreads();
-    if (fail_s) {
-      ok = false;
-      break;
-    }
-    fence_after();
-    // pass 1: row max of the masked, scaled scores
-    const int key0 = j * kKeys;
-    const bool full = key0 + kKeys - 1 <= first_qpos;  // no key of the tile is masked for any row
-    float mx = -INFINITY;
-#pragma unroll 1
-    for (int c = 0; c < kKeys; c += 32) {
-      float v[32];
-      tmem_ld32(t_S + lane_base + c, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const bool valid = full || key0 + c + i <= qpos;
-        mx = fmaxf(mx, valid ? v[i] * p.qscale : -INFINITY);
+  } else {  // ---- softmax warps 0-3: thread = query row = TMEM lane ----
+    const int row = tid;
+    const int qpos = first_qpos + row / NREP;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&s_full[j & 1], (j >> 1) & 1, &abort_s))) {
+        ok = false;
+        break;
       }
-    }
-    const float m_new = fmaxf(m_run, mx);
-    const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
-    // pass 2: p = 2^(s - m_new) -> bf16 P row (swizzled K-major), row sum
-    float sum = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < kKeys; c += 32) {
-      float v[32];
-      tmem_ld32(t_S + lane_base + c, v);
-      uint32_t pk[16];
+      fence_after();
+      float v[kKeys];
+      {
+        const uint32_t ta = tmem + (j & 1) * 128 + lane_base;
+        uint32_t r[kKeys];
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const bool v0 = full || key0 + c + i <= qpos, v1 = full || key0 + c + i + 1 <= qpos;
-        const float p0 = v0 ? exp2f(v[i] * p.qscale - m_new) : 0.f;
-        const float p1 = v1 ? exp2f(v[i + 1] * p.qscale - m_new) : 0.f;
+        for (int c = 0; c < kKeys; c += 32) {
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+              "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+              : "=r"(r[c + 0]), "=r"(r[c + 1]), "=r"(r[c + 2]), "=r"(r[c + 3]), "=r"(r[c + 4]), "=r"(r[c + 5]),
+                "=r"(r[c + 6]), "=r"(r[c + 7]), "=r"(r[c + 8]), "=r"(r[c + 9]), "=r"(r[c + 10]), "=r"(r[c + 11]),
+                "=r"(r[c + 12]), "=r"(r[c + 13]), "=r"(r[c + 14]), "=r"(r[c + 15]), "=r"(r[c + 16]),
+                "=r"(r[c + 17]), "=r"(r[c + 18]), "=r"(r[c + 19]), "=r"(r[c + 20]), "=r"(r[c + 21]),
+                "=r"(r[c + 22]), "=r"(r[c + 23]), "=r"(r[c + 24]), "=r"(r[c + 25]), "=r"(r[c + 26]),
+                "=r"(r[c + 27]), "=r"(r[c + 28]), "=r"(r[c + 29]), "=r"(r[c + 30]), "=r"(r[c + 31])
+              : "r"(ta + c));
+        }
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int i = 0; i < kKeys; ++i) v[i] = __uint_as_float(r[i]);
+      }
+      const int key0 = j * kKeys;
+      if (key0 + kKeys - 1 > first_qpos) {  // diagonal tile: mask keys past this row's position
+#pragma unroll
+        for (int i = 0; i < kKeys; ++i)
+          if (key0 + i > qpos) v[i] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kKeys; ++i) mx = fmaxf(mx, v[i]);
+      mx *= p.qscale;  // scale > 0: max(s) * scale = max(s * scale)
+      float m_use = m_run, alpha = 1.f;
+      if (mx > m_run + kRescaleLog2) {  // also the first tile with a finite max (m_run = -inf)
+        m_use = mx;
+        alpha = m_run == -INFINITY ? 0.f : ex2(m_run - mx);
+      }
+      float sum = 0.f;
+      uint32_t pk[kKeys / 2];
+#pragma unroll
+      for (int i = 0; i < kKeys; i += 2) {
+        const float p0 = ex2(fmaf(v[i], p.qscale, -m_use)), p1 = ex2(fmaf(v[i + 1], p.qscale, -m_use));
         sum += p0 + p1;
         const __nv_bfloat162 b = __floats2bfloat162_rn(p0, p1);
         pk[i / 2] = *reinterpret_cast<const uint32_t*>(&b);
       }
-      unsigned char* prow = p_s + (c >> 6) * kHalf + row * 128;
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {  // 4 chunks of 8 keys
-        const int chunk = ((c & 63) >> 3) + ch;
-        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) =
-            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-      }
-    }
-    l_run = l_run * alpha + sum;
-    m_run = m_new;
-    // O of the previous tile must be complete before it is rescaled and before P is reused
-    if (j > 0) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar_o, (j - 1) & 1))) {
-        if (lane == 0) fail_s = 1;
+      // P_{j-1} V_{j-1} complete: O is stable and the P buffer free
+      if (j > 0 && !__all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, (j - 1) & 1, &abort_s))) {
+        ok = false;
+        break;
       }
       fence_after();
-      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
         for (int c = 0; c < kD; c += 32) {
-          float v[32];
-          tmem_ld32(t_O + lane_base + c, v);
+          float o[32];
+          tmem_ld32(t_O + lane_base + c, o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st32(t_O + lane_base + c, v);
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(t_O + lane_base + c, o);
         }
       }
-      if (tid == 0 && j + 1 < n_tiles) {  // its stage held tile j - 1, now consumed
-        load_kv(j + 1);
-        issued = j + 2;
-      }
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P: generic writes -> MMA reads
-    fence_before();
-    __syncthreads();
-    if (fail_s) {
-      ok = false;
-      break;
-    }
-    if (tid == 0) {  // O += P V_j
-      fence_after();
-      const unsigned char* vt = kv_s + (j & 1) * kStageBytes + kTileBytes;
+      l_run = l_run * alpha + sum;
+      m_run = m_use;
 #pragma unroll
-      for (int k = 0; k < kKeys / 16; ++k) {
-        const int h = k >> 2, off = (k & 3) * 32;
-        umma<true>(t_O, desc_kmajor(p_s + h * kHalf + off), desc_mnmajor(vt + k * 16 * 128),
-                   (j > 0 || k > 0) ? 1u : 0u);
+      for (int c = 0; c < kKeys; c += 8) {  // 8 keys = one 16-byte chunk of the swizzled row
+        const int chunk = (c & 63) >> 3;
+        unsigned char* prow = p_s + (c >> 6) * kHalf + row * 128;
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) =
+            make_uint4(pk[c / 2], pk[c / 2 + 1], pk[c / 2 + 2], pk[c / 2 + 3]);
       }
-      mma_commit(&bar_o);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P: generic writes -> MMA reads
+      fence_before();
+      mbar_arrive(&p_full);
     }
-  }
-
-  // epilogue: O / l -> bf16 rows
-  const bool done = ok && __all_sync(0xffffffffu, mbar_wait(&bar_o, (n_tiles - 1) & 1));
-  if (!done) {
-    if (lane == 0) atomicOr(p.err, 4);
-  } else {
-    fence_after();
-    const int pos = q0 + row / NREP;
-    const int head = kvh * NREP + row % NREP;
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    __nv_bfloat16* dst = p.out + ((int64_t)(tok0 + pos) * p.H + head) * kD;
+    if (!ok) {
+      if (lane == 0) atomicOr(p.err, 4);
+      abort_s = 1;
+    } else if (__all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, (n_tiles - 1) & 1, &abort_s))) {
+      fence_after();  // epilogue: O / l -> bf16 rows
+      const int pos = q0 + row / NREP;
+      const int head = kvh * NREP + row % NREP;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* dst = p.out + ((int64_t)(tok0 + pos) * p.H + head) * kD;
 #pragma unroll 1
-    for (int c = 0; c < kD; c += 32) {
-      float v[32];
-      tmem_ld32(t_O + lane_base + c, v);
-      if (pos < qlen) {
+      for (int c = 0; c < kD; c += 32) {
+        float o[32];
+        tmem_ld32(t_O + lane_base + c, o);
+        if (pos < qlen) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          __nv_bfloat162 a = __floats2bfloat162_rn(v[i] * inv, v[i + 1] * inv);
-          __nv_bfloat162 b = __floats2bfloat162_rn(v[i + 2] * inv, v[i + 3] * inv);
-          __nv_bfloat162 cc = __floats2bfloat162_rn(v[i + 4] * inv, v[i + 5] * inv);
-          __nv_bfloat162 d = __floats2bfloat162_rn(v[i + 6] * inv, v[i + 7] * inv);
-          uint4 w;
-          w.x = *reinterpret_cast<uint32_t*>(&a); w.y = *reinterpret_cast<uint32_t*>(&b);
-          w.z = *reinterpret_cast<uint32_t*>(&cc); w.w = *reinterpret_cast<uint32_t*>(&d);
-          *reinterpret_cast<uint4*>(dst + c + i) = w;
+          for (int i = 0; i < 32; i += 8) {
+            __nv_bfloat162 a = __floats2bfloat162_rn(o[i] * inv, o[i + 1] * inv);
+            __nv_bfloat162 b = __floats2bfloat162_rn(o[i + 2] * inv, o[i + 3] * inv);
+            __nv_bfloat162 cc = __floats2bfloat162_rn(o[i + 4] * inv, o[i + 5] * inv);
+            __nv_bfloat162 d = __floats2bfloat162_rn(o[i + 6] * inv, o[i + 7] * inv);
+            uint4 w;
+            w.x = *reinterpret_cast<uint32_t*>(&a); w.y = *reinterpret_cast<uint32_t*>(&b);
+            w.z = *reinterpret_cast<uint32_t*>(&cc); w.w = *reinterpret_cast<uint32_t*>(&d);
+            *reinterpret_cast<uint4*>(dst + c + i) = w;
+          }
         }
       }
+    } else {
+      if (lane == 0) atomicOr(p.err, 4);
+      abort_s = 1;
     }
-  }
-  if (tid == 0 && !ok) {  // let issued copies land before the CTA exits (bounded)
-    (void)mbar_wait(&bar_q, 0);
-    for (int t = consumed; t < issued; ++t) (void)mbar_wait(&bar_kv[t & 1], (t >> 1) & 1);
-    atomicOr(p.err, 4);
   }
   fence_before();
   __syncthreads();
   if (warp == 0) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
 }
 
@@ -374,7 +432,7 @@ int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
     cudaFuncSetAttribute(prefill_tc_kernel<NREP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     configured |= 1u << dev;
   }
-  prefill_tc_kernel<NREP><<<dim3(p.n_kv, items), 128, kSmemBytes, st>>>(tq, tk, tv, p);
+  prefill_tc_kernel<NREP><<<dim3(p.n_kv, items), 192, kSmemBytes, st>>>(tq, tk, tv, p);
   return check_launch("prefill attention (tcgen05)");
 }
 

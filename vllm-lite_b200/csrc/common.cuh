@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/vllt.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -76,6 +78,67 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool va
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// Per-thread part of a row argmax over x[0, n) (float, 16-byte aligned),
+// threads t, t + nthreads, ... of a block: float4 loads, 8 in flight per
+// thread. (bv, bi) keeps the largest value and, among equal values, the
+// lowest index (np.argmax's rule); the caller reduces across threads.
+__device__ __forceinline__ void row_argmax_part(const float* __restrict__ x, int n, int t, int nthreads, float& bv,
+                                                int& bi) {
+  auto take = [&](float v, int c) {
+    if (v > bv || (v == bv && c < bi)) {
+      bv = v;
+      bi = c;
+    }
+  };
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const int n4 = n >> 2;
+  int c4 = t;
+  for (; c4 + 7 * nthreads < n4; c4 += 8 * nthreads) {
+    float4 a[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) a[u] = __ldg(x4 + c4 + u * nthreads);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = 4 * (c4 + u * nthreads);
+      take(a[u].x, c); take(a[u].y, c + 1); take(a[u].z, c + 2); take(a[u].w, c + 3);
+    }
+  }
+  for (; c4 < n4; c4 += nthreads) {
+    const float4 a = __ldg(x4 + c4);
+    const int c = 4 * c4;
+    take(a.x, c); take(a.y, c + 1); take(a.z, c + 2); take(a.w, c + 3);
+  }
+  for (int c = 4 * n4 + t; c < n; c += nthreads) take(x[c], c);
+}
+
+// Programmatic dependent launch. A kernel started with launch_pdl may begin
+// while the kernel before it on the stream is still running: everything it
+// does before pdl_wait() must neither read what earlier kernels write nor
+// write anything (barrier set-up, tensor-memory allocation, loads of
+// constant weights). pdl_wait() returns once the previous kernel has finished
+// and its writes are visible; every thread of a PDL-launched kernel passes it
+// before exiting, so its own completion implies its predecessors'.
+// pdl_trigger() lets the next PDL-launched kernel start launching now. Both
+// are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace vllt

@@ -108,6 +108,7 @@ __global__ void rmsnorm_bf16_kernel(float* __restrict__ x, const __nv_bfloat16* 
                                     const int32_t* __restrict__ idx, const float* __restrict__ w,
                                     __nv_bfloat16* __restrict__ out, int rows_cap,
                                     const int32_t* __restrict__ rows_dev, int dim, float eps) {
+  pdl_trigger();  // the projection that reads `out` may start its set-up (it waits for this grid)
   const int rows = rows_dev ? min(*rows_dev, rows_cap) : rows_cap;
   const int r = blockIdx.x;
   if (r >= rows) return;
@@ -158,9 +159,13 @@ __global__ void argmax_rows_kernel(const float* __restrict__ logits, int vocab, 
   const float* x = logits + (int64_t)r * ld;
   float bv = -INFINITY;
   int bi = INT32_MAX;
-  for (int c = threadIdx.x; c < vocab; c += blockDim.x) {
-    const float v = x[c];
-    if (v > bv || (v == bv && c < bi)) { bv = v; bi = c; }
+  if (((uintptr_t)x & 15) == 0) {
+    row_argmax_part(x, vocab, threadIdx.x, blockDim.x, bv, bi);
+  } else {
+    for (int c = threadIdx.x; c < vocab; c += blockDim.x) {
+      const float v = x[c];
+      if (v > bv || (v == bv && c < bi)) { bv = v; bi = c; }
+    }
   }
   __shared__ float sv[32];
   __shared__ int si[32];

@@ -80,12 +80,16 @@ __global__ void greedy_kernel(const float* __restrict__ logits, int vocab, int l
   const bool mask_eos = eos_mask && eos_mask[r];
   const float pen = penalty ? penalty[r] : 1.0f;
   ArgMax best{-INFINITY, INT32_MAX};
-  for (int c = threadIdx.x; c < vocab; c += kThreads) {
-    float v = x[c];
-    if (mask_eos && c == eos_id) v = -INFINITY;
-    if (pen != 1.0f && seen && ((seen[(int64_t)r * seen_words + (c >> 5)] >> (c & 31)) & 1u))
-      v = v > 0.f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);  // sampling.py:8-13
-    best = better(best, ArgMax{v, c});
+  if (!mask_eos && pen == 1.0f && ((uintptr_t)x & 15) == 0) {  // plain rows: vectorized scan
+    row_argmax_part(x, vocab, threadIdx.x, kThreads, best.v, best.i);
+  } else {
+    for (int c = threadIdx.x; c < vocab; c += kThreads) {
+      float v = x[c];
+      if (mask_eos && c == eos_id) v = -INFINITY;
+      if (pen != 1.0f && seen && ((seen[(int64_t)r * seen_words + (c >> 5)] >> (c & 31)) & 1u))
+        v = v > 0.f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);  // sampling.py:8-13
+      best = better(best, ArgMax{v, c});
+    }
   }
   best = block_argmax(best);
   if (threadIdx.x == 0) out[r] = best.i == INT32_MAX ? 0 : best.i;
