@@ -427,8 +427,11 @@ def main_spec(args, torch, dev, rank, world):
         dist.all_reduce(v[:1], op=dist.ReduceOp.MAX)
         dist.all_reduce(v[1:], op=dist.ReduceOp.SUM)
         t, toks = float(v[0]), float(v[1])
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = spec_cpu_baseline(k)
     if rank == 0:
-        print(json.dumps({
+        line = {
             "metric": f"engine output tok/s (C5: 128 periodic prompts, speculative k={k})",
             "value": round(toks / t, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1e3 * t / args.steps, 3), "higher_is_better": True,
@@ -440,7 +443,30 @@ def main_spec(args, torch, dev, rank, world):
             "token_identical_to_k0": bool(same),
             "acceptance": round(eng.spec.accepted / max(eng.spec.proposed, 1), 4),
             "ttft_p50_ms": round(1e3 * statistics.median(ttft), 2) if ttft else None,
-            "gpu_launches": int(launches), "e2e": None, "clocks": clk.summary()}), flush=True)
+            "gpu_launches": int(launches), "e2e": None, "clocks": clk.summary()}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def spec_cpu_baseline(k: int, n: int = 16):
+    """The unmodified reference engine (NumpyRunner, LLMEngine(speculative_tokens=k))
+    on the first n of the same periodic prompts: a bounded sample."""
+    try:
+        from vllmlite.engine import LLMEngine
+    except Exception as e:  # pragma: no cover
+        return {"value": None, "unit": "tok/s", "unavailable": f"vllm-lite not importable: {e}"}
+    from vllt.workloads import periodic_workload
+
+    reqs = periodic_workload(128, seed=0)[:n]
+    eng = LLMEngine(spec_config(), speculative_tokens=k)
+    run_workload(eng, reqs[:2], "cw")  # warm-up
+    t0 = time.perf_counter()
+    toks, _, _ = run_workload(eng, reqs, "c")
+    dt = time.perf_counter() - t0
+    return {"value": round(toks / dt, 1), "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
+            "sample": f"first {n} of the 128 periodic prompts, 256 tokens each, vllm-lite LLMEngine("
+                      f"speculative_tokens={k}) with NumpyRunner, after a 2-request warm-up"}
 
 
 def _tc_peak():
@@ -531,11 +557,24 @@ def main_gemm(args, torch, dev, rank, world):
             for f in fns:  # untimed, outside capture: first-use setup
                 f()
             t = _graph_time(torch, fns, args.steps)
+            # cuBLAS on the same operands and launch pattern, as a reference point only
+            outs = [torch.empty((M, N), device=dev, dtype=torch.bfloat16) for _ in Ws]
+
+            def lib_launcher(W, o):
+                def run():
+                    torch.matmul(a, W.t(), out=o)
+                return run
+            lib_fns = [lib_launcher(W, o) for W, o in zip(Ws, outs)] * max(1, 8 // copies)
+            for f in lib_fns:
+                f()
+            t_lib = _graph_time(torch, lib_fns, args.steps)
             fl = 2.0 * M * N * K
             res[f"M{M}_{name}"] = {"tflops": round(fl / t / 1e12, 1), "us": round(t * 1e6, 2), "splits": splits,
                                    "tc_frac": round(fl / t / 1e12 / peak, 3),
                                    "weight_gbs": round(N * K * 2 / t / 1e9, 1),
-                                   "hbm_frac": round(N * K * 2 / t / 1e9 / hbm, 3)}
+                                   "hbm_frac": round(N * K * 2 / t / 1e9 / hbm, 3),
+                                   "cublas_us": round(t_lib * 1e6, 2)}
+            del outs
             if M == 8192:
                 tot_flops += fl
                 tot_t += t

@@ -211,16 +211,19 @@ int vllt_gemm_bf16(const void* A, const void* W, float* C, int32_t M, int32_t N,
  *   splits >= 2: K cut into `splits` slices (splits <= K/64), one CTA per
  *     (tile, slice); the last slice of each tile to finish sums the fp32
  *     partials in slice order (deterministic) and writes C;
- *   splits == 0: the forward's own choice for (M, N, K): for M <= 256 (N a
- *     multiple of 32) the small-M form (weights on the MMA's M side, the
- *     (feature tile, k-block) iterations divided evenly over one CTA per SM,
- *     split tiles summed in CTA order by a second kernel), else split-K as
+ *   splits <= 0: the forward's own choice for (M, N, K). For M <= 256 (N a
+ *     multiple of 32) the weights go on the MMA's M side (128 features x all
+ *     tokens per CTA) and either the CTAs of a thread-block cluster split K
+ *     for one feature tile and sum their accumulators through distributed
+ *     shared memory (few tiles), or the (feature tile, k-block) iterations are
+ *     divided evenly over one CTA per SM and split tiles summed in CTA order
+ *     by a second kernel (stream-K); otherwise split-K as
  *     vllt_gemm_bf16_auto_splits says, else the persistent kernel;
  *   splits == 1: the persistent kernel (as vllt_gemm_bf16).
  * `workspace` (device, at least vllt_gemm_bf16_splitk_workspace_bytes(M, N, K,
  * splits) bytes) must be zero before its first use and is left reusable.
- * vllt_gemm_bf16_auto_splits returns 0 when the small-M form applies, else the
- * split count. No reference counterpart (vllm-lite multiplies with NumPy);
+ * vllt_gemm_bf16_auto_splits returns -S for the cluster form (S CTAs per
+ * feature tile), 0 for the stream-K form, else the split count. No reference counterpart (vllm-lite multiplies with NumPy);
  * these expose the forward's small-M paths to tests and callers. */
 int64_t vllt_gemm_bf16_splitk_workspace_bytes(int32_t M, int32_t N, int32_t K, int32_t splits);
 int32_t vllt_gemm_bf16_auto_splits(int32_t M, int32_t N, int32_t K);

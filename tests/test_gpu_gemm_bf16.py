@@ -80,14 +80,16 @@ def test_gemm_bf16_split_k_matches_float64_and_is_reusable(M, N, K, splits):
     np.testing.assert_allclose(got.cpu().numpy(), gemm(A, W).cpu().numpy(), rtol=1e-4, atol=1e-4 * np.sqrt(K))
 
 
-# the small-M form (splits 0): stream-K spans that start and end inside tiles,
-# several tiles per CTA, token counts around the 32-column chunks, M = 1
+# the small-M forms (splits 0): cluster split-K when the feature tiles are few
+# (auto_splits < 0), stream-K otherwise (auto_splits == 0); spans that start
+# and end inside tiles, several tiles per CTA, token counts around the 32-row
+# chunks, M = 1
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (16, 6144, 4096), (37, 4096, 14336), (64, 28672, 4096),
                                    (100, 1024, 1024), (256, 4096, 4096), (200, 160, 640), (129, 128256, 4096)])
-def test_gemm_bf16_small_m_form_matches_float64(M, N, K):
+def test_gemm_bf16_small_m_forms_match_float64(M, N, K):
     from vllt import _lib
 
-    assert _lib.lib().vllt_gemm_bf16_auto_splits(M, N, K) == 0
+    assert _lib.lib().vllt_gemm_bf16_auto_splits(M, N, K) <= 0
     test_gemm_bf16_split_k_matches_float64_and_is_reusable(M, N, K, 0)
 
 
@@ -96,9 +98,15 @@ def test_gemm_bf16_forward_form_choice():
 
     L = _lib.lib()
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    # decode batches take the small-M form; 512-row batches with few tiles split K; prefill does neither
-    assert L.vllt_gemm_bf16_auto_splits(64, 4096, 14336) == 0
-    assert L.vllt_gemm_bf16_auto_splits(256, 4096, 4096) == 0
+    # decode projections with few feature tiles: cluster split-K (-S CTAs per tile,
+    # all clusters resident at once); qkv's 48 tiles may fall back to stream-K
+    for M, N, K in [(64, 4096, 14336), (256, 4096, 4096), (16, 6144, 4096)]:
+        s = L.vllt_gemm_bf16_auto_splits(M, N, K)
+        assert s <= 0 and -s * (N // 128) <= sms and -s <= 8
+        assert s < 0 or N == 6144
+    # many feature tiles: stream-K; 512-row batches with few tiles split K; prefill does neither
+    assert L.vllt_gemm_bf16_auto_splits(64, 28672, 4096) == 0
+    assert L.vllt_gemm_bf16_auto_splits(256, 128256, 4096) == 0
     assert L.vllt_gemm_bf16_auto_splits(512, 4096, 4096) > 1
     assert L.vllt_gemm_bf16_auto_splits(8192, 4096, 4096) == 1
     for M, N, K in [(512, 6144, 4096), (512, 4096, 14336)]:

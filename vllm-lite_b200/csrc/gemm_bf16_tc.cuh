@@ -672,6 +672,210 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant_
   }
 }
 
+// ---- small-M form with few feature tiles: split-K inside a thread-block cluster ----
+//
+// When N / 128 feature tiles cannot cover the SMs, the S CTAs of a cluster
+// share one tile: CTA r (cluster rank) accumulates k-blocks [r*nk/S,
+// (r+1)*nk/S) in TMEM, stages the fp32 accumulator in its own shared memory as
+// [token][128 features], and after a cluster barrier sums token rows
+// [r*n/S, (r+1)*n/S) over the S CTAs' buffers (distributed shared memory,
+// rank order: deterministic) and applies the epilogue. No partials go through
+// global memory and no second kernel runs. The ring is reused for the staging
+// buffer once the last MMA has completed.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cta address -> the same offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+  return v;
+}
+
+struct ClusterPlan {
+  int tiles;   // ceil(N / 128)
+  int S;       // CTAs per tile = cluster size
+  int ksub, nk;  // k sub-blocks per stage; iterations of the whole K
+  int n_pad, stages;
+};
+
+template <class Epi>
+__global__ void __launch_bounds__(SK_THREADS, 1)
+gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, int M_cap,
+                    const int* __restrict__ M_dev, int N, ClusterPlan p, Epi epi, int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
+  __shared__ uint64_t full[SK_MAX_STAGES], empty[SK_MAX_STAGES], acc_full, drain;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int stages = p.stages, ksub = p.ksub;
+  const uint32_t x_bytes = (uint32_t)p.n_pad * 128;
+  const uint32_t stage_bytes = ksub * (SK_W_BYTES + x_bytes);
+  const int rank = (int)cluster_rank();
+  const int t = blockIdx.x / p.S;
+  const int kb0 = rank * p.nk / p.S, kb1 = (rank + 1) * p.nk / p.S, n_it = kb1 - kb0;
+  const uint32_t tmem_cols = p.n_pad < 32 ? 32 : p.n_pad;
+  const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.n_pad >> 3) << 17) |
+                         ((uint32_t)(128 >> 4) << 24);
+  float* stage_acc = reinterpret_cast<float*>(smem);  // [n_pad tokens][128 features], after the main loop
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full, 1);
+    mbar_init(&drain, 1);
+    abort_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base_s)),
+                 "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = tmem_base_s;
+  const int pre = min(stages, n_it);
+  if (warp == 4 && lane == 0) {  // weights first: they do not depend on the previous kernel
+    for (int g = 0; g < pre; ++g) {
+      mbar_expect_tx(&full[g], stage_bytes);
+      for (int u = 0; u < ksub; ++u)
+        tma_load_2d(smem + g * stage_bytes + u * SK_W_BYTES, &tw, &full[g], ((kb0 + g) * ksub + u) * BK, t * 128);
+    }
+  }
+  pdl_wait();
+  const int M = M_dev ? min(*M_dev, M_cap) : M_cap;
+
+  if (warp == 4) {
+    if (lane == 0) {  // ---- TMA producer ----
+      int g = 0;
+      bool failed = false;
+      for (; g < n_it; ++g) {
+        const int s = g % stages, kb = kb0 + g;
+        unsigned char* a = smem + s * stage_bytes;
+        unsigned char* ax = a + ksub * SK_W_BYTES;
+        if (g >= pre) {
+          if (!mbar_wait_or_abort(&empty[s], ((g / stages) & 1) ^ 1, &abort_s)) {
+            failed = true;
+            break;
+          }
+          mbar_expect_tx(&full[s], stage_bytes);
+          for (int u = 0; u < ksub; ++u) tma_load_2d(a + u * SK_W_BYTES, &tw, &full[s], (kb * ksub + u) * BK, t * 128);
+        }
+        for (int u = 0; u < ksub; ++u) tma_load_2d(ax + u * x_bytes, &tx, &full[s], (kb * ksub + u) * BK, 0);
+      }
+      if (failed) {
+        atomicOr(err, 4);
+        abort_s = 1;
+        for (int j = max(0, g - stages); j < g; ++j) (void)mbar_wait(&full[j % stages], (j / stages) & 1);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {  // ---- MMA issuer ----
+      int g = 0;
+      bool failed = false;
+      for (; g < n_it; ++g) {
+        const int s = g % stages;
+        if (!mbar_wait_or_abort(&full[s], (g / stages) & 1, &abort_s)) {
+          failed = true;
+          break;
+        }
+        fence_after();
+        const unsigned char* sw0 = smem + s * stage_bytes;
+        const unsigned char* sx0 = sw0 + ksub * SK_W_BYTES;
+        for (int u = 0; u < ksub; ++u) {
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16_n(tmem, smem_desc(sw0 + u * SK_W_BYTES + k * 32), smem_desc(sx0 + u * x_bytes + k * 32), idesc,
+                       (g > 0 || u > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty[s]);
+      }
+      if (!failed && n_it > 0) mma_commit(&acc_full);
+      if (failed) {
+        atomicOr(err, 4);
+        abort_s = 1;
+      }
+      if (g > 0) {
+        mma_commit(&drain);
+        (void)mbar_wait(&drain, 0);
+      }
+    }
+  } else {  // ---- epilogue warps 0-3: TMEM lanes = features 32*warp .. +31 -> staging buffer ----
+    const bool have = __all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full, 0, &abort_s));
+    if (!have) {
+      if (lane == 0) {
+        atomicOr(err, 4);
+        abort_s = 1;
+      }
+    } else {
+      fence_after();
+      const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < p.n_pad; c += 32) {
+        if (c >= M) break;
+        float v[32];
+        tmem_ld32(lane_addr + c, v);  // v[j] = D^T[feature 32*warp + lane][token c + j]
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stage_acc[(c + j) * 128 + warp * 32 + lane] = v[j];
+      }
+    }
+  }
+  // every CTA of the cluster has staged its accumulator (or failed; the error bit is set)
+  __syncthreads();
+  __syncwarp();
+  cluster_sync();
+  if (warp < 4 && !abort_s) {  // ---- reduction of token rows [r*n/S, (r+1)*n/S) ----
+    const int n_tok = min(M, p.n_pad);
+    const int r0 = rank * n_tok / p.S, r1 = (rank + 1) * n_tok / p.S;
+    const uint32_t base = saddr(stage_acc);
+    for (int item = threadIdx.x; item < (r1 - r0) * 4; item += 128) {
+      const int m = r0 + item / 4, q = item % 4;
+      const int f = t * 128 + q * 32;
+      if (f >= N) continue;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      const uint32_t off = (uint32_t)(m * 128 + q * 32) * 4;
+      for (int src = 0; src < p.S; ++src) {
+        const uint32_t ra = map_rank(base + off, src);
+        float4 r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = ld_dsmem4(ra + j * 16);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[4 * j] += r[j].x; v[4 * j + 1] += r[j].y; v[4 * j + 2] += r[j].z; v[4 * j + 3] += r[j].w;
+        }
+      }
+      epi.template apply<32>(m, f, v);
+    }
+  }
+  __syncwarp();
+  cluster_sync();  // no CTA leaves while another still reads its buffer
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
+  }
+}
+
 // Sum the slices of every tile that stream-K split between CTAs, in CTA order,
 // and apply the epilogue. blockIdx.y + 1 = CTA boundary b; the tile holding it
 // is handled by its lowest boundary. Thread = (token, 32-feature chunk).
@@ -966,6 +1170,104 @@ inline bool small_plan(int M_cap, int N, int K, tc::SmallPlan* p) {
 }
 inline int64_t small_scratch_bytes(int M_cap, const tc::SmallPlan& p) { return 2ll * p.ctas * M_cap * 128 * 4; }
 
+// Plan of the cluster split-K form: N / 128 feature tiles too few to cover
+// the SMs (at least 2 CTAs per tile fit), at most 8 CTAs per cluster, at least
+// 2 iterations per CTA. False when it does not apply.
+// How many clusters of S CTAs (each `smem` bytes of dynamic shared memory)
+// can be resident at once on this device (cached per device and S; the
+// epilogue type does not change the kernel's resources that bound it).
+inline int max_active_clusters(int S, int smem) {
+  static int cache[32][9] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 32 || S < 1 || S > 8) return 0;
+  if (!cache[dev][S]) {
+    auto fn = tc::gemm_cluster_kernel<EpiStoreF32>;
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 1024 + tc::SK_RING_BYTES);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S * 64);
+    cfg.blockDim = dim3(tc::SK_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = -1;  // unknown: the cluster form is not used
+    }
+    cache[dev][S] = n;
+  }
+  return cache[dev][S];
+}
+
+// Plan of the cluster split-K form: few N / 128 feature tiles, S (2..8) CTAs
+// per tile chosen as large as keeps every cluster resident in one wave and
+// at least 2 iterations per CTA. False when it does not apply.
+inline bool cluster_plan(int M_cap, int N, int K, tc::ClusterPlan* p) {
+  if (M_cap <= 0 || M_cap > 256 || N <= 0 || N % 32 || K % tc::BK) return false;
+  const int tiles = ceil_div(N, 128);
+  int n_pad = 32;
+  while (n_pad < M_cap) n_pad *= 2;
+  int ksub = kSmallKsubMax;
+  while (ksub > 1 && ((K / tc::BK) % ksub || 2 * ksub * (tc::SK_W_BYTES + n_pad * 128) > tc::SK_RING_BYTES)) ksub /= 2;
+  const int nk = K / (tc::BK * ksub);
+  const int stage_bytes = ksub * (tc::SK_W_BYTES + n_pad * 128);
+  const int stages = std::min(tc::SK_MAX_STAGES, tc::SK_RING_BYTES / stage_bytes);
+  if (stages * stage_bytes < n_pad * 128 * 4) return false;  // the staging buffer reuses the ring
+  const int smem = 1024 + stages * stage_bytes;
+  for (int S = std::min(8, sm_count() / tiles); S >= 2; --S) {
+    if (nk < 2 * S) continue;
+    if (tiles > max_active_clusters(S, smem)) continue;
+    *p = tc::ClusterPlan{tiles, S, ksub, nk, n_pad, stages};
+    return true;
+  }
+  return false;
+}
+
+template <class Epi>
+inline int gemm_cluster_launch(const void* A, int M_cap, const int* M_dev, const void* W, int N, int K,
+                               const Epi& epi, int* err, cudaStream_t st, const tc::ClusterPlan& p) {
+  CUtensorMap tw, tx;
+  int rc = tc::kmajor_map(&tw, W, N, K, 128);
+  if (rc != VLLT_OK) return rc;
+  rc = tc::kmajor_map(&tx, A, M_cap, K, p.n_pad);
+  if (rc != VLLT_OK) return rc;
+  const int smem = 1024 + p.stages * p.ksub * (tc::SK_W_BYTES + p.n_pad * 128);
+  static unsigned configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 32 && !(configured & (1u << dev))) {
+    cudaFuncSetAttribute(tc::gemm_cluster_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         1024 + tc::SK_RING_BYTES);
+    configured |= 1u << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.tiles * p.S);
+  cfg.blockDim = dim3(tc::SK_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, tc::gemm_cluster_kernel<Epi>, tw, tx, M_cap, M_dev, N, p, epi, err);
+  if (e != cudaSuccess) {
+    set_error("gemm_bf16 (cluster split-K): launch failed: %s", cudaGetErrorString(e));
+    return VLLT_ERR_CUDA;
+  }
+  return check_launch("gemm_bf16 (cluster split-K)");
+}
+
 template <class Epi>
 inline int gemm_small_launch(const void* A, int M_cap, const int* M_dev, const void* W, int N, int K,
                              const Epi& epi, int* err, cudaStream_t st, const tc::SmallPlan& p, float* part) {
@@ -1004,8 +1306,9 @@ inline int gemm_small_launch(const void* A, int M_cap, const int* M_dev, const v
 
 // D = A . W^T through an epilogue. A [M_cap][K], W [N][K] bf16, K % 64 == 0.
 // `splits` > 0 forces that many K slices of the split-K form (1 = the
-// persistent form); 0 picks the form: small-M stream-K when M_cap <= 256 and
-// the scratch holds its slices, else split-K when choose_splits says so.
+// persistent form); 0 picks the form: for M_cap <= 256 the cluster split-K
+// form when the feature tiles are few, else small-M stream-K when the scratch
+// holds its slices; otherwise split-K when choose_splits says so.
 template <class Epi>
 inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const void* W, int N, int K, const Epi& epi,
                      int* err, cudaStream_t st, const SplitKScratch* sk = nullptr, int splits = 0) {
@@ -1028,6 +1331,8 @@ inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const vo
     configured |= 1u << dev;
   }
   if (splits <= 0) {
+    tc::ClusterPlan cp;
+    if (cluster_plan(M_cap, N, K, &cp)) return gemm_cluster_launch(A, M_cap, M_dev, W, N, K, epi, err, st, cp);
     tc::SmallPlan sp;
     if (sk && sk->part && small_plan(M_cap, N, K, &sp) && small_scratch_bytes(M_cap, sp) <= sk->part_bytes)
       return gemm_small_launch(A, M_cap, M_dev, W, N, K, epi, err, st, sp, sk->part);
