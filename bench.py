@@ -301,6 +301,19 @@ def main_ours(args):
         for i in range(args.steps):
             res.append(timed(eng, f"t{i}"))
     e2e_res = [timed(ref_eng, f"e{i}") for i in range(max(1, min(args.steps, 3)))]
+    # untimed extra run: per-pass GPU time (CUDA events around each forward) vs the rest of a step
+    eng.runner.pass_log = []
+    flush_l2(torch, dev)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    run_workload(eng, reqs, "b")
+    e1.record()
+    torch.cuda.synchronize()
+    ps = eng.runner.pass_summary()
+    eng.runner.pass_log = None
+    breakdown = dict(ps, run_s=round(e0.elapsed_time(e1) / 1e3, 4),
+                     host_and_other_s=round(e0.elapsed_time(e1) / 1e3 - ps["gpu_s"], 4))
     # H2D / D2H bytes of one workload pass through the drop-in runner
     rr = ref_eng.runner
     t_ours = sum(r[0] for r in res)
@@ -360,6 +373,7 @@ def main_ours(args):
                      "bytes_per_launch": decode_s["attn_bytes"], "sum_ctx": decode_s["sum_ctx"],
                      "launch_ms": round(decode_t * 1e3, 4), "traffic": None},
         "clocks": clk.summary(),
+        "breakdown": breakdown,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
@@ -664,6 +678,11 @@ def llama_config(num_blocks: int, max_seqs: int = 512, budget: int = 8192):
                         scheduler=SchedulerConfig(max_seqs=max_seqs, max_batched_tokens=budget))
 
 
+def _progress(what: str) -> None:
+    """One line on stderr per stage of a multi-rank run (where a stall happened)."""
+    print(f"[rank {os.environ.get('RANK', '0')}] {what} {time.strftime('%H:%M:%S')}", file=sys.stderr, flush=True)
+
+
 def main_llama(args, torch, dev, rank, world):
     """Llama-3-8B-shaped continuous batching, tensor parallel over all ranks:
     512 requests (prompt mean 1024, output mean 256), greedy, bf16."""
@@ -682,17 +701,22 @@ def main_llama(args, torch, dev, rank, world):
         hbm, tfl, kind = 6650.0, 1400.0, "fallback"
     if rank != 0:
         runner = TPLlamaRunner(cfg.model, cfg.cache, cfg.scheduler, group=group)
+        _progress("worker ready")
         runner.worker_loop()
+        _progress("worker stopped")
         t = torch.tensor([runner.marked_seconds()], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        runner.release_graphs()
         group.close()
         torch.distributed.destroy_process_group()
         return
     kw = dict(group=group) if world > 1 else {}
     eng = gpu_engine(cfg, runner_cls=TPLlamaRunner if world > 1 else LlamaRunner, **kw)
     run = eng.runner
+    _progress("engine ready")
     for i in range(args.warmup):  # short requests: every graph bucket and kernel warmed
         run_workload(eng, llama_workload(16, seed=100 + i, out_mean=24), f"w{i}")
+        _progress(f"warm-up {i} done")
     reqs = llama_workload(args.llama_requests, seed=0)
     run.roofline_peaks = (hbm, tfl)
     run.roofline_s = 0.0
@@ -713,6 +737,7 @@ def main_llama(args, torch, dev, rank, world):
         run.mark(1)
     torch.cuda.synchronize()
     t_wall = time.perf_counter() - t_wall
+    _progress("timed run done")
     elapsed = e0.elapsed_time(e1) / 1e3
     launches = run.L.vllt_kernel_launches() + run.replayed_kernels - run.captured_kernels - l0
     if world > 1:
@@ -720,8 +745,6 @@ def main_llama(args, torch, dev, rank, world):
         t = torch.tensor([run.marked_seconds()], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         elapsed = max(elapsed, float(t[0]))
-        group.close()
-        torch.distributed.destroy_process_group()
     line = {
         "metric": f"engine output tok/s (Llama-3-8B shape, {len(reqs)} requests, tensor parallel {world})",
         "value": round(toks / elapsed, 1), "unit": "tok/s", "n_gpus": world, "steps": 1, "warmup": args.warmup,
@@ -746,6 +769,12 @@ def main_llama(args, torch, dev, rank, world):
     ps = run.pass_summary()
     line["breakdown"] = dict(ps, host_and_other_s=round(elapsed - ps["gpu_s"], 3))
     print(json.dumps(line), flush=True)
+    if world > 1:  # after the result line: graphs holding NCCL calls go before the communicators
+        _progress("teardown")
+        run.release_graphs()
+        group.close()
+        torch.distributed.destroy_process_group()
+        _progress("done")
 
 
 # ---- CPU baseline / reference arm ---------------------------------------------------------

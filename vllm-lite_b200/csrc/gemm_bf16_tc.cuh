@@ -21,7 +21,8 @@
 //     last CTA of each tile to arrive (per-tile counter) sums the partials in z
 //     order, so the result does not depend on arrival order, applies the
 //     epilogue and resets the counter.
-// No cluster launch and no TMA multicast: the kernels are safe in multi-GPU processes.
+// No TMA multicast anywhere (the cluster form shares data through distributed
+// shared memory only): the kernels are safe in multi-GPU processes.
 // Every mbarrier wait is bounded; on expiry the kernel sets an error bit, lets its
 // copies land (bounded), frees its tensor memory and returns.
 #pragma once

@@ -326,8 +326,8 @@ class CudaRunner(_Base):
                 pre, n_pre = pre + t, n_pre + 1
             else:
                 dec, n_dec = dec + t, n_dec + 1
-        return {"passes": len(log), "gpu_s": round(pre + dec, 3), "prefill_passes": n_pre,
-                "prefill_pass_gpu_s": round(pre, 3), "decode_passes": n_dec, "decode_pass_gpu_s": round(dec, 3)}
+        return {"passes": len(log), "gpu_s": round(pre + dec, 4), "prefill_passes": n_pre,
+                "prefill_pass_gpu_s": round(pre, 4), "decode_passes": n_dec, "decode_pass_gpu_s": round(dec, 4)}
 
     def _forward(self, bounds) -> None:
         check(self.L.vllt_forward(C.byref(self.desc), self.rec_dev.data_ptr(), C.byref(self.caps),

@@ -201,6 +201,19 @@ class TPLlamaRunner(LlamaRunner):
     def stop_workers(self):
         self._broadcast(OP_STOP)
 
+    def release_graphs(self):
+        """Drop the captured forwards (they hold this group's NCCL calls) and
+        wait for the device: must precede TPGroup.close and the process
+        group's destruction, which otherwise wait on the graphs' references."""
+        import gc
+
+        import torch
+
+        torch.cuda.synchronize(self.dev)
+        self.graphs.clear()
+        gc.collect()
+        torch.cuda.synchronize(self.dev)
+
     def mark(self, tag: int):
         """Broadcast a timing mark (tag 0 = start, 1 = end); workers record a
         CUDA event, rank 0 records its own."""
