@@ -224,6 +224,7 @@ def decode_bench(torch, dev, steps, warmup):
         decode_attend(s, ws, out)
     torch.cuda.synchronize()
     step_t, attn_t = [], []
+    torch.cuda.nvtx.range_push("vllt_decode")  # ncu --nvtx --nvtx-include vllt_decode/
     for _ in range(max(steps, 5)):
         flush_l2(torch, dev)
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
@@ -235,6 +236,7 @@ def decode_bench(torch, dev, steps, warmup):
         e2.synchronize()
         step_t.append(e0.elapsed_time(e2) / 1e3)
         attn_t.append(e1.elapsed_time(e2) / 1e3)
+    torch.cuda.nvtx.range_pop()
     if int(ws[:4].view(torch.int32).item()) != 0:
         raise RuntimeError("decode attention reported a device-side timeout")
     return s, statistics.median(step_t), statistics.median(attn_t)
@@ -297,9 +299,11 @@ def main_ours(args):
         return e0.elapsed_time(e1) / 1e3, toks, ttft, steps, launched() - l0
 
     res = []
+    torch.cuda.nvtx.range_push("vllt_timed")  # ncu --nvtx --nvtx-include vllt_timed/
     with Clocks(local) as clk:
         for i in range(args.steps):
             res.append(timed(eng, f"t{i}"))
+    torch.cuda.nvtx.range_pop()
     e2e_res = [timed(ref_eng, f"e{i}") for i in range(max(1, min(args.steps, 3)))]
     # untimed extra run: per-pass GPU time (CUDA events around each forward) vs the rest of a step
     eng.runner.pass_log = []
