@@ -312,13 +312,6 @@ typedef struct vllt_model_desc {
   /* KV cache base: [n_layers][num_blocks][n_kv][block_size][head_dim], dtype */
   void* k_cache;
   void* v_cache;
-  /* Peer-memory all-reduce for passes of at most peer_tokens tokens (tp_size
-   * > 1, bf16): peer_arena[r] is rank r's arena (vllt_tp_arena_bytes) as
-   * mapped in this process (vllt_tp_ipc_open; [tp_rank] = this rank's own),
-   * zeroed before first use. peer_tokens 0: every all-reduce uses NCCL. */
-  int32_t tp_rank;
-  int32_t peer_tokens;
-  void* peer_arena[8];
 } vllt_model_desc;
 
 /* Upper bounds of one step, used to size grids (exact counts are read on the
@@ -365,22 +358,6 @@ int vllt_tp_init(const uint8_t* id128, int32_t rank, int32_t world, void** comm_
 int vllt_tp_destroy(void* comm);
 /* In-place sum over ranks of a bf16 buffer (used between row-parallel layers). */
 int vllt_tp_allreduce_bf16(void* buf, int64_t count, void* comm, void* stream);
-
-/* Peer arenas for the fused all-reduce of small passes (no reference
- * counterpart: vllm-lite is single-device NumPy). The o_proj / down_proj GEMM
- * epilogue of each rank stores its bf16 partial straight into every rank's
- * arena over NVLink; the RMSNorm that follows raises this rank's flag on
- * every peer, waits (bounded) for all ranks' flags of the same epoch and adds
- * the partials in rank order, so all ranks hold bit-identical residuals.
- * Arena bytes for tp_size ranks, passes of up to max_tokens tokens: */
-int64_t vllt_tp_arena_bytes(int32_t tp_size, int32_t max_tokens, int32_t d_model);
-/* CUDA IPC handle (64 bytes) of the allocation holding dev_ptr, and dev_ptr's
- * offset inside it; another process on the node maps it with vllt_tp_ipc_open
- * (the pointer it gets is the allocation base + offset) and releases it with
- * vllt_tp_ipc_close. */
-int vllt_tp_ipc_handle(const void* dev_ptr, uint8_t* handle64, int64_t* offset);
-int vllt_tp_ipc_open(const uint8_t* handle64, int64_t offset, void** dev_ptr);
-int vllt_tp_ipc_close(void* dev_ptr, int64_t offset);
 
 /* Per logit row: the maximum and the FIRST index of it (np.argmax), index
  * shifted by vocab_offset (this rank's first vocabulary row). Vocab-parallel

@@ -1,9 +1,7 @@
 """GPU (2+ devices): tensor-parallel forward against the 1-GPU forward.
 
 Runs tests/tp_parity.py under torchrun on two GPUs (one process each, NCCL,
-NVLS off as for every multi-rank test here): once with the all-reduces fused
-through the peer arenas (NVLink stores from the projection epilogue, flag
-exchange in the next RMSNorm), once with NCCL. Skipped on a 1-GPU box.
+NVLS off as for every multi-rank test here). Skipped on a 1-GPU box.
 Tolerance: logits of this rank's vocabulary slice within 5e-2 of the 1-GPU
 logits' max magnitude (the bf16 all-reduce reorders the sums), greedy picks
 equal on all rows but at most one near-tie.
@@ -29,5 +27,4 @@ def test_tensor_parallel_two_gpus_matches_one_gpu():
            os.path.join(root, "tests", "tp_parity.py")]
     r = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert "TP_PARITY peer ok" in r.stdout, r.stdout[-3000:]
-    assert "TP_PARITY nccl ok" in r.stdout, r.stdout[-3000:]
+    assert "TP_PARITY ok" in r.stdout, r.stdout[-3000:]

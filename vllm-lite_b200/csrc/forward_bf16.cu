@@ -11,10 +11,6 @@
 //   h  = rmsnorm(x); act = silu(h.Wg^T) * (h.Wu^T) (one GEMM, interleaved columns) -> bf16
 //   x += act . Wdown^T                       -> as o_proj
 // then the final norm on the logit rows and lm_head (this rank's vocabulary rows).
-// With tp > 1 and a pass of at most peer_tokens tokens the two all-reduces per
-// layer are fused instead: the projection epilogue stores its partial into
-// every rank's peer arena (EpiPushBF16, NVLink) and the next RMSNorm adds the
-// ranks' partials in rank order after a flag exchange (rmsnorm_peer).
 
 #include <algorithm>
 
@@ -106,34 +102,6 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
 
   VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks,
                             query_tile_positions(VLLT_BF16, D, m->block_size, n_rep), meta, st));
-  // all-reduces of small passes go through the peer arenas (fused into the
-  // projection epilogue and the next RMSNorm); larger passes use NCCL
-  const bool peer = tp && m->peer_tokens > 0 && T_cap <= m->peer_tokens && m->tp_size <= kMaxPeers &&
-                    m->tp_rank >= 0 && m->tp_rank < m->tp_size && m->peer_arena[m->tp_rank];
-  PeerArena pa{};
-  VLLT_REQUIRE(!peer || 2 * m->n_layers < 128, "forward_bf16: too many layers for the peer epochs");
-  if (peer) {
-    for (int r = 0; r < m->tp_size; ++r) {
-      VLLT_REQUIRE(m->peer_arena[r], "forward_bf16: peer arena %d missing", r);
-      pa.base[r] = reinterpret_cast<unsigned char*>(m->peer_arena[r]);
-    }
-    pa.n = m->tp_size;
-    pa.rank = m->tp_rank;
-    pa.T = m->peer_tokens;
-    pa.d = d;
-    VLLT_TRY(peer_epoch_bump(pa, st));
-  }
-  int ar = 0;            // all-reduces issued in this forward
-  int pending_ar = -1;   // peer all-reduce still to join the residual
-  auto norm = [&](const float* wgt, void* out, const int32_t* idx, int rows_cap, const int32_t* rows_dev,
-                  const __nv_bfloat16* pending) -> int {
-    if (pending_ar >= 0) {
-      const int rc = rmsnorm_peer(w.x, pa, pending_ar, idx, wgt, out, rows_cap, rows_dev, d, eps, err, st);
-      pending_ar = -1;
-      return rc;
-    }
-    return rmsnorm_bf16(w.x, pending, idx, wgt, out, rows_cap, rows_dev, d, eps, st);
-  };
   VLLT_TRY(embed_bf16(m->tok_emb, meta + L.tokens, w.x, T_cap, T_dev, d, m->embed_rows, st));
 
   AttnCall ac{};
@@ -156,7 +124,7 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   for (int l = 0; l < m->n_layers; ++l) {
     __nv_bfloat16* kc = reinterpret_cast<__nv_bfloat16*>(m->k_cache) + l * layer_elems;
     __nv_bfloat16* vc = reinterpret_cast<__nv_bfloat16*>(m->v_cache) + l * layer_elems;
-    VLLT_TRY(norm(m->attn_norm[l], w.h, nullptr, T_cap, T_dev, pending));
+    VLLT_TRY(rmsnorm_bf16(w.x, pending, nullptr, m->attn_norm[l], w.h, T_cap, T_dev, d, eps, st));
     pending = nullptr;
     EpiQKVBF16 eq{w.q, kc, vc, meta + L.pos, meta + L.slot, m->rope_cos, m->rope_sin,
                   H, KV, D, m->block_size, m->max_seq_len, (int64_t)m->num_blocks * m->block_size};
@@ -166,25 +134,18 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
     VLLT_TRY(attention_pass(ac, meta + L.dec_seq, nullptr, meta + kCntDecode, dec_cap, 0, 0, true, max_ctx, st));
     VLLT_TRY(attention_pass(ac, meta + L.tile_seq, meta + L.tile_q0, meta + kCntTiles, tiles_cap, 0, 0, false,
                             max_ctx, st));
-    if (peer) {
-      VLLT_TRY(gemm_bf16_launch(w.attn, T_cap, T_dev, m->wo[l], d, H * D, EpiPushBF16{pa, ar & 1}, err, st, &w.sk));
-      pending_ar = ar++;
-    } else if (tp) {
+    if (tp) {
       VLLT_TRY(gemm_bf16_launch(w.attn, T_cap, T_dev, m->wo[l], d, H * D, EpiStoreBF16{w.y, d, d}, err, st, &w.sk));
       VLLT_TRY(tp_allreduce_bf16(w.y, (int64_t)T_cap * d, m->tp_comm, st));
       pending = w.y;
     } else {
       VLLT_TRY(gemm_bf16_launch(w.attn, T_cap, T_dev, m->wo[l], d, H * D, EpiResidualF32{w.x, d}, err, st, &w.sk));
     }
-    VLLT_TRY(norm(m->ffn_norm[l], w.h, nullptr, T_cap, T_dev, pending));
+    VLLT_TRY(rmsnorm_bf16(w.x, pending, nullptr, m->ffn_norm[l], w.h, T_cap, T_dev, d, eps, st));
     pending = nullptr;
     VLLT_TRY(gemm_bf16_launch(w.h, T_cap, T_dev, m->w_gu[l], 2 * m->d_ff, d, EpiSwiGLUBF16{w.act, m->d_ff}, err,
                               st, &w.sk));
-    if (peer) {
-      VLLT_TRY(gemm_bf16_launch(w.act, T_cap, T_dev, m->w_down[l], d, m->d_ff, EpiPushBF16{pa, ar & 1}, err, st,
-                                &w.sk));
-      pending_ar = ar++;
-    } else if (tp) {
+    if (tp) {
       VLLT_TRY(gemm_bf16_launch(w.act, T_cap, T_dev, m->w_down[l], d, m->d_ff, EpiStoreBF16{w.y, d, d}, err, st, &w.sk));
       VLLT_TRY(tp_allreduce_bf16(w.y, (int64_t)T_cap * d, m->tp_comm, st));
       pending = w.y;
@@ -192,7 +153,7 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
       VLLT_TRY(gemm_bf16_launch(w.act, T_cap, T_dev, m->w_down[l], d, m->d_ff, EpiResidualF32{w.x, d}, err, st, &w.sk));
     }
   }
-  VLLT_TRY(norm(m->final_norm, w.rows_h, meta + L.rows, R_cap, R_dev, pending));
+  VLLT_TRY(rmsnorm_bf16(w.x, pending, meta + L.rows, m->final_norm, w.rows_h, R_cap, R_dev, d, eps, st));
   VLLT_TRY(gemm_bf16_launch(w.rows_h, R_cap, R_dev, m->lm_head, m->vocab, d,
                             EpiStoreF32{logits, m->vocab_padded, m->vocab}, err, st, &w.sk));
   return VLLT_OK;

@@ -1,10 +1,7 @@
 // Row-wise layer pieces: RMSNorm (optionally gathering rows), token embedding,
 // standalone RoPE.
 
-#include <algorithm>
-
 #include "common.cuh"
-#include "peer.cuh"
 
 namespace vllt {
 
@@ -198,110 +195,6 @@ int embed_bf16(const void* emb, const int32_t* tok, float* x, int T_cap, const i
   const int blocks = (int)std::min<int64_t>((vecs + 255) / 256, 148 * 8);
   embed_bf16_kernel<<<blocks, 256, 0, st>>>((const __nv_bfloat16*)emb, tok, x, T_cap, T_dev, dim, vocab);
   return check_launch("embed_bf16");
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long timer_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__global__ void peer_epoch_kernel(PeerArena a) { *a.epoch() += 1ull; }
-
-// RMSNorm of the bf16 model whose residual add is the fused all-reduce of a
-// row-parallel projection: the partials of every rank already sit in this
-// rank's arena (pushed by their GEMM epilogues). Block 0 raises this rank's
-// flag on every rank (its own GEMM, the previous kernel, has finished its
-// pushes); every block then waits for all ranks' flags of this epoch, bounded
-// to one second (then error bit 8 and the sum uses whatever is there; once
-// bit 8 is set, later calls do not wait at all, so a lost rank costs one
-// second, not one per all-reduce).
-__global__ void rmsnorm_peer_kernel(float* __restrict__ x, PeerArena a, int ar_index,
-                                    const int32_t* __restrict__ idx, const float* __restrict__ w,
-                                    __nv_bfloat16* __restrict__ out, int rows_cap,
-                                    const int32_t* __restrict__ rows_dev, int dim, float eps, int* err) {
-  const unsigned long long epoch = *a.epoch() * 128ull + (unsigned long long)ar_index + 1ull;
-  if (blockIdx.x == 0 && (int)threadIdx.x < a.n) {
-    __threadfence_system();
-    st_release_sys(a.flags(threadIdx.x) + a.rank, epoch);
-  }
-  if (threadIdx.x == 0 && !(*reinterpret_cast<volatile int*>(err) & 8)) {  // after one timeout: no more waiting
-    const unsigned long long* f = a.flags(a.rank);
-    const unsigned long long t0 = timer_ns();
-    bool ok = true;
-    for (int s = 0; s < a.n && ok; ++s)
-      while (ld_acquire_sys(f + s) < epoch) {
-        if (timer_ns() - t0 > 1000000000ull) {
-          ok = false;
-          break;
-        }
-      }
-    if (!ok) atomicOr(err, 8);
-  }
-  __syncthreads();
-  const int rows = rows_dev ? min(*rows_dev, rows_cap) : rows_cap;
-  const int r = blockIdx.x;
-  if (r >= rows) return;
-  const int src = idx ? idx[r] : r;
-  float* xr = x + (int64_t)src * dim;
-  const int parity = ar_index & 1;
-  float ss = 0.f;
-  for (int c = threadIdx.x * 4; c < dim; c += blockDim.x * 4) {
-    float4 v = *reinterpret_cast<const float4*>(xr + c);
-    for (int s = 0; s < a.n; ++s) {  // rank order: the same sum on every rank
-      const uint2 p = *reinterpret_cast<const uint2*>(a.recv(a.rank, parity, s) + (int64_t)src * dim + c);
-      v.x += __uint_as_float(p.x << 16); v.y += __uint_as_float(p.x & 0xffff0000u);
-      v.z += __uint_as_float(p.y << 16); v.w += __uint_as_float(p.y & 0xffff0000u);
-    }
-    *reinterpret_cast<float4*>(xr + c) = v;
-    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-  }
-  __shared__ float red[8];
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < (int)(blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    t = warp_sum(t);
-    if (threadIdx.x == 0) red[0] = t;
-  }
-  __syncthreads();
-  const float inv = rsqrtf(red[0] / (float)dim + eps);
-  __nv_bfloat16* orow = out + (int64_t)r * dim;
-  for (int c = threadIdx.x * 4; c < dim; c += blockDim.x * 4) {
-    const float4 v = *reinterpret_cast<const float4*>(xr + c);
-    const float4 g = *reinterpret_cast<const float4*>(w + c);
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x * inv * g.x, v.y * inv * g.y);
-    const __nv_bfloat162 hi = __floats2bfloat162_rn(v.z * inv * g.z, v.w * inv * g.w);
-    uint2 o;
-    o.x = *reinterpret_cast<const uint32_t*>(&lo);
-    o.y = *reinterpret_cast<const uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(orow + c) = o;
-  }
-}
-
-int rmsnorm_peer(float* x, const PeerArena& a, int ar_index, const int32_t* idx, const float* w, void* out,
-                 int rows_cap, const int32_t* rows_dev, int dim, float eps, int* err, cudaStream_t st) {
-  VLLT_REQUIRE(dim % 4 == 0 && a.d == dim && a.n >= 1 && a.n <= kMaxPeers && err,
-               "rmsnorm_peer: bad arguments");
-  VLLT_REQUIRE(rows_cap <= a.T || idx, "rmsnorm_peer: more rows than the arena holds");
-  const int blocks = std::max(rows_cap, 1);  // block 0 always raises the flags
-  rmsnorm_peer_kernel<<<blocks, 256, 0, st>>>(x, a, ar_index, idx, w, reinterpret_cast<__nv_bfloat16*>(out),
-                                                rows_cap, rows_dev, dim, eps, err);
-  return check_launch("rmsnorm_peer");
-}
-
-int peer_epoch_bump(const PeerArena& a, cudaStream_t st) {
-  peer_epoch_kernel<<<1, 1, 0, st>>>(a);
-  return check_launch("peer_epoch_bump");
 }
 
 int rmsnorm_bf16(float* x, const void* add, const int32_t* idx, const float* w, void* out, int rows_cap,

@@ -2,7 +2,6 @@
 #pragma once
 
 #include "meta.cuh"
-#include "peer.cuh"
 
 namespace vllt {
 
@@ -20,13 +19,6 @@ int embed_bf16(const void* emb, const int32_t* tok, float* x, int T_cap, const i
                int vocab, cudaStream_t st);
 int rmsnorm_bf16(float* x, const void* add, const int32_t* idx, const float* w, void* out, int rows_cap,
                  const int32_t* rows_dev, int dim, float eps, cudaStream_t st);
-// x += the sum over ranks of all-reduce `ar_index`'s partials (peer arena,
-// parity ar_index & 1, rank order), then as rmsnorm_bf16. Raises this rank's
-// flag on every peer first and waits (bounded, error bit 8) for all ranks'.
-int rmsnorm_peer(float* x, const PeerArena& a, int ar_index, const int32_t* idx, const float* w, void* out,
-                 int rows_cap, const int32_t* rows_dev, int dim, float eps, int* err, cudaStream_t st);
-// Start of a forward that uses the peer arena: bump this rank's epoch base.
-int peer_epoch_bump(const PeerArena& a, cudaStream_t st);
 int argmax_rows(const float* logits, int rows_cap, const int32_t* rows_dev, int vocab, int ld, int offset,
                 float* val, int32_t* idx, cudaStream_t st);
 int rope(float* x, const int32_t* positions, const float* cos_t, const float* sin_t, int T,

@@ -3,7 +3,6 @@
 // Used by the bf16 forward for the all-reduce after o_proj and down_proj
 // (row-parallel projections) and by the vocab-parallel greedy pick.
 
-#include <cuda.h>
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -109,68 +108,6 @@ int vllt_tp_destroy(void* comm) {
 int vllt_tp_allreduce_bf16(void* buf, int64_t count, void* comm, void* stream) {
   clear_error();
   return tp_allreduce_bf16(buf, count, comm, as_stream(stream));
-}
-
-int64_t vllt_tp_arena_bytes(int32_t tp_size, int32_t max_tokens, int32_t d_model) {
-  if (tp_size < 1 || tp_size > kMaxPeers || max_tokens < 0 || d_model <= 0) return 0;
-  return peer_arena_bytes(tp_size, max_tokens, d_model);
-}
-
-int vllt_tp_ipc_handle(const void* dev_ptr, uint8_t* handle64, int64_t* offset) {
-  clear_error();
-  VLLT_REQUIRE(dev_ptr && handle64 && offset, "tp_ipc_handle: null argument");
-  // the driver's cuMemGetAddressRange through the runtime (no link-time libcuda dependency)
-  typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
-  static AddressRangeFn range_fn = nullptr;
-  if (!range_fn) {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      range_fn = reinterpret_cast<AddressRangeFn>(f);
-  }
-  CUdeviceptr base = 0;
-  size_t size = 0;
-  if (!range_fn || range_fn(&base, &size, (CUdeviceptr)dev_ptr) != CUDA_SUCCESS) {
-    set_error("tp_ipc_handle: pointer is not in a device allocation");
-    return VLLT_ERR_ARG;
-  }
-  cudaIpcMemHandle_t h;
-  const cudaError_t e = cudaIpcGetMemHandle(&h, (void*)base);
-  if (e != cudaSuccess) {
-    set_error("tp_ipc_handle: cudaIpcGetMemHandle failed: %s", cudaGetErrorString(e));
-    return VLLT_ERR_CUDA;
-  }
-  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
-  memcpy(handle64, &h, 64);
-  *offset = (int64_t)((CUdeviceptr)dev_ptr - base);
-  return VLLT_OK;
-}
-
-int vllt_tp_ipc_open(const uint8_t* handle64, int64_t offset, void** dev_ptr) {
-  clear_error();
-  VLLT_REQUIRE(handle64 && dev_ptr && offset >= 0, "tp_ipc_open: bad arguments");
-  cudaIpcMemHandle_t h;
-  memcpy(&h, handle64, 64);
-  void* base = nullptr;
-  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
-  if (e != cudaSuccess) {
-    set_error("tp_ipc_open: cudaIpcOpenMemHandle failed: %s", cudaGetErrorString(e));
-    return VLLT_ERR_CUDA;
-  }
-  *dev_ptr = (char*)base + offset;
-  return VLLT_OK;
-}
-
-int vllt_tp_ipc_close(void* dev_ptr, int64_t offset) {
-  clear_error();
-  if (!dev_ptr) return VLLT_OK;
-  const cudaError_t e = cudaIpcCloseMemHandle((char*)dev_ptr - offset);
-  if (e != cudaSuccess) {
-    set_error("tp_ipc_close: cudaIpcCloseMemHandle failed: %s", cudaGetErrorString(e));
-    return VLLT_ERR_CUDA;
-  }
-  return VLLT_OK;
 }
 
 }  // extern "C"

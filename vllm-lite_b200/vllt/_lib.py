@@ -38,7 +38,6 @@ class ModelDesc(C.Structure):
         ("tok_emb", vp), ("final_norm", vp), ("lm_head", vp), ("rope_cos", vp), ("rope_sin", vp),
         ("attn_norm", PP), ("wqkv", PP), ("wo", PP), ("ffn_norm", PP), ("w_gu", PP), ("w_down", PP),
         ("k_cache", vp), ("v_cache", vp),
-        ("tp_rank", i32), ("peer_tokens", i32), ("peer_arena", vp * 8),
     ]
 
 
@@ -71,10 +70,6 @@ SIGNATURES = {
     "vllt_tp_unique_id": (C.c_int, [vp]),
     "vllt_tp_init": (C.c_int, [vp, i32, i32, C.POINTER(vp)]),
     "vllt_tp_destroy": (C.c_int, [vp]),
-    "vllt_tp_arena_bytes": (i64, [i32, i32, i32]),
-    "vllt_tp_ipc_handle": (C.c_int, [vp, vp, C.POINTER(i64)]),
-    "vllt_tp_ipc_open": (C.c_int, [vp, i64, C.POINTER(vp)]),
-    "vllt_tp_ipc_close": (C.c_int, [vp, i64]),
     "vllt_tp_allreduce_bf16": (C.c_int, [vp, i64, vp, vp]),
     "vllt_argmax_rows": (C.c_int, [vp, i32, i32, i32, i32, vp, vp, vp]),
     "vllt_query_tile_positions": (i32, [C.POINTER(ModelDesc)]),

@@ -162,7 +162,6 @@ class LlamaRunner(CudaRunner):
         d.max_seq_len, d.block_size, d.num_blocks = w.rope_len, self.block_size, self.num_blocks
         d.rms_eps, d.dtype = 1e-5, _lib.VLLT_BF16
         d.tp_size, d.embed_rows, d.tp_comm = n, cfg.vocab_size, self.tp_comm
-        d.tp_rank, d.peer_tokens = self.tp_rank, 0
         d.tok_emb, d.final_norm, d.lm_head = w.tok_emb.data_ptr(), w.final_norm.data_ptr(), w.lm_head.data_ptr()
         d.rope_cos, d.rope_sin = w.rope_cos.data_ptr(), w.rope_sin.data_ptr()
         for k in ("attn_norm", "wqkv", "wo", "ffn_norm", "w_gu", "w_down"):

@@ -49,46 +49,8 @@ class TPGroup:
         comm = C.c_void_p()
         check(lib().vllt_tp_init(uid, self.rank, self.world, C.byref(comm)))
         self.comm = comm.value
-        self.arena = None
-        self.peer_ptrs = []
-        self.peer_tokens = 0
-        self._opened = []
-
-    def open_arenas(self, max_tokens: int, d_model: int, device) -> None:
-        """Allocate this rank's peer arena (zeroed) and map every rank's into
-        this process by CUDA IPC (handles exchanged through torch.distributed),
-        for the fused all-reduce of passes of up to max_tokens tokens."""
-        import torch
-        import torch.distributed as dist
-
-        L = lib()
-        nbytes = L.vllt_tp_arena_bytes(self.world, max_tokens, d_model)
-        if nbytes <= 0:
-            raise ValueError("peer arenas: bad sizes")
-        self.arena = torch.zeros(nbytes, dtype=torch.uint8, device=device)
-        torch.cuda.synchronize(device)
-        h, off = (C.c_uint8 * 64)(), C.c_int64()
-        check(L.vllt_tp_ipc_handle(self.arena.data_ptr(), h, C.byref(off)))
-        handles = [None] * self.world
-        dist.all_gather_object(handles, (bytes(h), off.value))
-        self.peer_ptrs = []
-        for r, (hb, o) in enumerate(handles):
-            if r == self.rank:
-                self.peer_ptrs.append(self.arena.data_ptr())
-                continue
-            p = C.c_void_p()
-            check(L.vllt_tp_ipc_open((C.c_uint8 * 64)(*hb), o, C.byref(p)))
-            self.peer_ptrs.append(p.value)
-            self._opened.append((p.value, o))
-        self.peer_tokens = max_tokens
-        dist.barrier()  # every rank has mapped every arena before a forward can write to it
 
     def close(self):
-        """Unmap the peers' arenas and destroy the communicator (after the
-        device has finished every forward that uses them)."""
-        for p, o in self._opened:
-            check(lib().vllt_tp_ipc_close(p, o))
-        self._opened = []
         if self.comm:
             check(lib().vllt_tp_destroy(self.comm))
             self.comm = None
@@ -176,8 +138,7 @@ def merge_argmax(vals, idxs):
 class TPLlamaRunner(LlamaRunner):
     """One tensor-parallel shard; on rank 0 it is the engine's runner."""
 
-    def __init__(self, model_cfg, cache_cfg, sched_cfg=None, *, group: TPGroup, max_rows: int | None = None,
-                 peer_tokens: int | None = None, **kw):
+    def __init__(self, model_cfg, cache_cfg, sched_cfg=None, *, group: TPGroup, max_rows: int | None = None, **kw):
         self.group = group
         super().__init__(model_cfg, cache_cfg, sched_cfg, tp_rank=group.rank, tp_size=group.world,
                          tp_comm=group.comm, **kw)
@@ -188,18 +149,6 @@ class TPLlamaRunner(LlamaRunner):
         import torch
 
         self.plane = ControlPlane(self.rec_dev, self.rec_host)
-        # passes of up to peer_tokens tokens all-reduce through the peer arenas
-        # (fused into the projections); 0 keeps NCCL for every pass
-        if peer_tokens is None:
-            peer_tokens = min(512, c.max_tokens)
-        if peer_tokens > 0 and group.world > 1:
-            if not group.peer_ptrs:
-                group.open_arenas(peer_tokens, model_cfg.d_model, self.dev)
-            elif group.peer_tokens < peer_tokens:
-                raise ValueError("the group's peer arenas are smaller than peer_tokens")
-            self.desc.peer_tokens = peer_tokens
-            for r, p in enumerate(group.peer_ptrs):
-                self.desc.peer_arena[r] = p
         self._val = torch.empty(self.caps.max_rows, dtype=torch.float32, device=self.dev)
         self._idx = torch.empty(self.caps.max_rows, dtype=torch.int32, device=self.dev)
         self._vals = torch.empty(group.world * self.caps.max_rows, dtype=torch.float32, device=self.dev)
