@@ -56,6 +56,37 @@ def test_library_calls_reject_bad_arguments_without_a_gpu():
     assert L.vllt_meta_bytes(ctypes.byref(_lib.Caps(0, 1, 1, 1))) == -1
 
 
+def test_gemm_form_choice_is_host_logic():
+    """The bf16 GEMM picks its form on the host from (M, N, K) alone, so eager
+    runs and graph replays of one shape agree. Without a device the SM count
+    falls back to 148 and the cluster occupancy query to "none", which leaves
+    stream-K for every small-M shape; on a GPU (tests/test_gpu_gemm_bf16.py)
+    few-tile shapes may take the cluster form (negative values) instead."""
+    from vllt import _lib
+
+    L = _lib.lib()
+    # decode batches (<= 256 tokens): weights-on-M forms
+    for M, N, K in [(1, 4096, 4096), (64, 28672, 4096), (256, 6144, 4096), (37, 4096, 14336)]:
+        assert L.vllt_gemm_bf16_auto_splits(M, N, K) <= 0
+    # prefill batches: the persistent kernel
+    assert L.vllt_gemm_bf16_auto_splits(8192, 4096, 4096) == 1
+    assert L.vllt_gemm_bf16_auto_splits(8192, 28672, 4096) == 1
+    # 257-512 tokens: split-K while the tile grid covers under half the SMs, within the
+    # SM count and with >= 4 k-blocks per slice; otherwise unsplit
+    for M, N, K in [(512, 4096, 4096), (300, 4096, 14336), (512, 6144, 4096)]:
+        s = L.vllt_gemm_bf16_auto_splits(M, N, K)
+        tiles = -(-N // 256) * -(-M // 128)
+        assert s >= 1 and s * tiles <= max(148, tiles) and s <= max(1, K // 64 // 4)
+        assert (s > 1) == (2 * tiles <= 148)
+    # same inputs, same answer
+    assert L.vllt_gemm_bf16_auto_splits(512, 4096, 4096) == L.vllt_gemm_bf16_auto_splits(512, 4096, 4096)
+    # workspace sizes: the forward's scratch for the automatic form, exact tiles for a forced split
+    assert L.vllt_gemm_bf16_splitk_workspace_bytes(64, 4096, 4096, 0) >= 2 * 148 * 64 * 128 * 4
+    assert L.vllt_gemm_bf16_splitk_workspace_bytes(512, 4096, 4096, 2) >= 2 * 64 * 128 * 256 * 4
+    # splits beyond K/64 are refused before any launch
+    assert L.vllt_gemm_bf16_splitk(None, None, None, 4, 256, 128, 3, None, 0, None, None) == _lib.VLLT_ERR_ARG
+
+
 def _record_to_flatten(rec):
     S, T, R, W = (int(x) for x in rec[:4])
     o = 4
