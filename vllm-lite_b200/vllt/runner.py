@@ -46,6 +46,15 @@ def _tokens(seq, start: int, n: int) -> list:
     p = getattr(seq, "prompt_token_ids", None)
     if p is None:  # a duck-typed sequence that only carries token_ids
         return seq.token_ids[start:start + n]
+    if n == 1 and start >= 0:  # a decode row: one token
+        if start < len(p):
+            return [p[start]]
+        j = start - len(p)
+        o = seq.output_token_ids
+        if j < len(o):
+            return [o[j]]
+        d = seq.draft_token_ids
+        return [d[j - len(o)]] if j - len(o) < len(d) else []
     end, out = start + n, []
     for part in (p, seq.output_token_ids, seq.draft_token_ids):
         ln = len(part)
@@ -79,34 +88,46 @@ class StepPacker:
         self.bs, self.nb, self.vocab, self.max_pos, self.qp = block_size, num_blocks, vocab, max_pos, qp
         self.cache = {}
 
-    def _table(self, key, seq, start: int, new_cache) -> np.ndarray:
+    def _table(self, key, seq, start: int, new_cache):
+        """(int32 buffer, length) of the sequence's block table, validated."""
         tbl = seq.table
         ids = tbl.block_ids
         n = len(ids)
+        nb = self.nb
         ent = self.cache.get(key)
         if ent is None or ent[0] is not tbl or ent[2] > n:
-            arr = np.asarray(ids, dtype=np.int64).astype(np.int32) if n else np.zeros(0, np.int32)
-            first = 0
+            full = np.asarray(ids, dtype=np.int64) if n else np.zeros(0, np.int64)
+            if n and (int(full.min()) < 0 or int(full.max()) >= nb):
+                raise IndexError("block id out of range")
+            arr = full.astype(np.int32)
         else:
             arr, first = ent[1], min(ent[2], start // self.bs)
             if arr.size < n:
                 grown = np.empty(max(n, 2 * arr.size), np.int32)
                 grown[:arr.size] = arr
                 arr = grown
-            if n > first:
-                arr[first:n] = ids[first:n]
-        if n > first:
-            seg = arr[first:n]
-            if int(seg.min()) < 0 or int(seg.max()) >= self.nb:
-                raise IndexError("block id out of range")
+            if n - first <= 8:  # a decode step touches one or two entries: plain Python is cheaper
+                for j in range(first, n):
+                    v = ids[j]
+                    if v < 0 or v >= nb:
+                        raise IndexError("block id out of range")
+                    arr[j] = v
+            else:
+                seg = np.asarray(ids[first:n], dtype=np.int64)
+                if int(seg.min()) < 0 or int(seg.max()) >= nb:
+                    raise IndexError("block id out of range")
+                arr[first:n] = seg
         new_cache[key] = (tbl, arr, n)
-        return arr[:n]
+        return arr, n
 
     def pack(self, out):
         items = out.scheduled
         S = len(items)
-        starts, qlens, counts, toks, tabs = [], [], [], [], []
+        starts, qlens, counts = [0] * S, [0] * S, [0] * S
+        tabs, tab_n = [None] * S, [0] * S
+        toks = []
         new_cache = {}
+        bs, max_pos = self.bs, self.max_pos
         W, max_ctx = 1, 1
         for i, item in enumerate(items):
             seq = item.seq
@@ -114,29 +135,40 @@ class StepPacker:
             if n < 1:
                 raise ValueError("a scheduled sequence has no tokens")
             ctx = start + n
-            if ctx > self.max_pos:
-                raise IndexError(f"position {ctx - 1} beyond max_seq_len {self.max_pos}")
+            if ctx > max_pos:
+                raise IndexError(f"position {ctx - 1} beyond max_seq_len {max_pos}")
             key = getattr(seq, "request_id", None) or id(seq)
-            tab = self._table(key, seq, start, new_cache)
-            if tab.size * self.bs < ctx:
+            arr, tn = self._table(key, seq, start, new_cache)
+            if tn * bs < ctx:
                 raise IndexError(f"block table of sequence {i} too short for {ctx} positions")
-            starts.append(start)
-            qlens.append(n)
-            counts.append(min(1 + len(seq.draft_token_ids), n))
+            starts[i] = start
+            qlens[i] = n
+            d = len(seq.draft_token_ids) + 1
+            counts[i] = d if d < n else n
             toks += _tokens(seq, start, n)
-            tabs.append(tab)
-            W = max(W, tab.size)
-            max_ctx = max(max_ctx, ctx)
+            tabs[i] = arr
+            tab_n[i] = tn
+            if tn > W:
+                W = tn
+            if ctx > max_ctx:
+                max_ctx = ctx
         self.cache = new_cache
         T = len(toks)
         R = sum(counts)
-        if T and (min(toks) < 0 or max(toks) >= self.vocab):
+        tok = np.asarray(toks, dtype=np.int64)
+        if T and (int(tok.min()) < 0 or int(tok.max()) >= self.vocab):
             raise IndexError("token id out of the vocabulary")
-        head = np.asarray([S, T, R, W] + starts + qlens + counts + toks, dtype=np.int64).astype(np.int32)
-        table = np.zeros((S, W), np.int32)
-        for i, tab in enumerate(tabs):
-            table[i, :tab.size] = tab
-        rec = np.concatenate([head, table.reshape(-1)])
+        hdr = 4 + 3 * S
+        rec = np.zeros(hdr + T + S * W, np.int32)
+        rec[0], rec[1], rec[2], rec[3] = S, T, R, W
+        rec[4:4 + S] = starts
+        rec[4 + S:4 + 2 * S] = qlens
+        rec[4 + 2 * S:hdr] = counts
+        rec[hdr:hdr + T] = tok
+        table = rec[hdr + T:].reshape(S, W)
+        for i in range(S):
+            tn = tab_n[i]
+            table[i, :tn] = tabs[i][:tn]
         n_dec = qlens.count(1)
         qp = self.qp
         tiles = sum((q + qp - 1) // qp for q in qlens if q > 1)
