@@ -375,7 +375,10 @@ def main_ours(args):
                      "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "peak_kind": peak_kind,
                      "unit": "GB/s", "frac": round(achieved / hbm, 3),
                      "bytes_per_launch": decode_s["attn_bytes"], "sum_ctx": decode_s["sum_ctx"],
-                     "launch_ms": round(decode_t * 1e3, 4), "traffic": None},
+                     "launch_ms": round(decode_t * 1e3, 4), "traffic": None,
+                     "traffic_note": "no ncu capture of the current decode kernel; the earlier version with "
+                                     "the same access pattern read 2.254 GB + wrote 0.014 GB per launch "
+                                     "(= algorithmic), profiles/paged_attention_decode_c3.md"},
         "clocks": clk.summary(),
         "breakdown": breakdown,
     }
