@@ -168,3 +168,31 @@ def test_workloads_equal_reference_generator():
         assert lens == z[f"{name}_lens"].tolist()
         assert [t for r in reqs for t in r[1]] == z[f"{name}_tokens"].tolist()
         assert [r[2].max_tokens for r in reqs] == z[f"{name}_max_tokens"].tolist()
+
+
+def test_pick_inputs_follow_the_reference_row_rules():
+    """Host inputs of the device token picks (vllt.engine.pick_inputs): verify
+    rows (sequences with drafts) take plain argmax and contribute their drafts;
+    temperature rows are sampled; EOS is masked while min_tokens is not reached
+    (sampling.py:51-52, only with an EOS id); the repetition penalty lands on
+    the sequence's last row (sampling.py:54)."""
+    from types import SimpleNamespace as NS
+
+    from vllt.engine import pick_inputs
+
+    def item(drafts=(), greedy=True, min_tokens=0, out=0, pen=1.0):
+        p = NS(greedy=greedy, min_tokens=min_tokens, repetition_penalty=pen)
+        return NS(seq=NS(draft_token_ids=list(drafts), params=p, output_token_ids=[7] * out))
+
+    sched = [item(), item(drafts=(11, 12, 13)), item(greedy=False), item(min_tokens=5, out=2),
+             item(min_tokens=5, out=5, pen=1.3)]
+    rows = [(0, 1), (1, 4), (5, 1), (6, 1), (7, 1)]
+    cu, doff, drafts, mask, pen, sampled = pick_inputs(sched, rows, 8, eos=257)
+    assert cu.tolist() == [0, 1, 5, 6, 7, 8] and cu.dtype == np.int32
+    assert doff.tolist() == [0, 0, 3, 3, 3]
+    assert drafts == [11, 12, 13]
+    assert sampled == [(2, 5)]
+    assert mask.tolist() == [0, 0, 0, 0, 0, 0, 1, 0]
+    assert pen.dtype == np.float32 and pen[7] == np.float32(1.3) and (pen[:7] == 1).all()
+    # no EOS id: min_tokens cannot mask anything
+    assert not pick_inputs(sched, rows, 8, eos=None)[3].any()

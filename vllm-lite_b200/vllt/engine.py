@@ -47,6 +47,44 @@ def cuda_engine(cfg=None, tokenizer=None, speculative_tokens: int = 0, weights=N
         E.NumpyRunner = orig
 
 
+def pick_inputs(scheduled, rows, R: int, eos):
+    """Host inputs of the device token picks for one step, following the
+    reference's per-row rules (vllmlite/engine.py:106-130, sampling.py:41-64):
+    cu_rows[S+1] and draft offsets[S] (int32), the flat draft tokens, eos_mask[R]
+    (min_tokens not reached), penalty[R] (repetition penalty of the row), and the
+    (sequence index, row) pairs that sample with temperature. Rows of sequences
+    that verify drafts take plain argmax (speculative.py:92)."""
+    S = len(scheduled)
+    cu, doff, drafts = [0] * (S + 1), [0] * S, []
+    mask_rows, pen_rows, pen_vals, sampled = [], [], [], []
+    for i, item in enumerate(scheduled):
+        seq = item.seq
+        r0, cnt = rows[i]
+        cu[i + 1] = r0 + cnt
+        doff[i] = len(drafts)
+        d = seq.draft_token_ids
+        if d:
+            drafts += d[:cnt - 1]
+            continue
+        p = seq.params
+        last = r0 + cnt - 1
+        if not p.greedy:
+            sampled.append((i, last))
+            continue
+        if eos is not None and p.min_tokens and len(seq.output_token_ids) < p.min_tokens:
+            mask_rows.append(last)
+        if p.repetition_penalty != 1.0:
+            pen_rows.append(last)
+            pen_vals.append(p.repetition_penalty)
+    eos_mask = np.zeros(R, np.uint8)
+    if mask_rows:
+        eos_mask[mask_rows] = 1
+    penalty = np.ones(R, np.float32)
+    if pen_rows:
+        penalty[pen_rows] = pen_vals
+    return np.asarray(cu, np.int32), np.asarray(doff, np.int32), drafts, eos_mask, penalty, sampled
+
+
 def _engine_base():
     from vllmlite.engine import LLMEngine
 
@@ -96,28 +134,7 @@ def _make_gpu_engine(Base):
             V = run.model_cfg.vocab_size
             ld = run.w.vocab_padded
             eos = self.tokenizer.eos_id
-            cu = np.zeros(S + 1, np.int32)
-            doff = np.zeros(S, np.int32)
-            drafts = []
-            eos_mask = np.zeros(R, np.uint8)
-            penalty = np.ones(R, np.float32)
-            sampled = []  # (seq index, row) of temperature > 0 picks
-            for i, item in enumerate(sched.scheduled):
-                seq, p = item.seq, item.seq.params
-                r0, cnt = rows[i]
-                cu[i + 1] = r0 + cnt
-                doff[i] = len(drafts)
-                drafts += list(seq.draft_token_ids[:cnt - 1])
-                if seq.draft_token_ids:
-                    continue  # verify rows use plain argmax (speculative.py:92)
-                last = r0 + cnt - 1
-                if not p.greedy:
-                    sampled.append((i, last))
-                    continue
-                if eos is not None and len(seq.output_token_ids) < p.min_tokens:
-                    eos_mask[last] = 1
-                if p.repetition_penalty != 1.0:
-                    penalty[last] = p.repetition_penalty
+            cu, doff, drafts, eos_mask, penalty, sampled = pick_inputs(sched.scheduled, rows, R, eos)
             st = _lib.stream_handle()
 
             def h2d(a):
