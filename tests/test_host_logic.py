@@ -196,3 +196,39 @@ def test_pick_inputs_follow_the_reference_row_rules():
     assert pen.dtype == np.float32 and pen[7] == np.float32(1.3) and (pen[:7] == 1).all()
     # no EOS id: min_tokens cannot mask anything
     assert not pick_inputs(sched, rows, 8, eos=None)[3].any()
+
+
+def test_graph_bucket_bounds_cover_every_step_of_the_bucket():
+    """A captured forward serves every step whose token count fits its bucket:
+    tokens round up to a power of two (>= 16, <= capacity) and the other bounds
+    are derived from that alone, so they hold for any step of the bucket."""
+    from types import SimpleNamespace as NS
+
+    from vllt._lib import Caps, StepBounds
+    from vllt.runner import CudaRunner
+
+    fake = NS(caps=Caps(64, 1024, 1024, 32), qp=4, w=NS(rope_len=2048))
+    for T in (1, 15, 16, 17, 100, 512, 1000, 1024):
+        b = CudaRunner.bucket(fake, StepBounds(T, min(T, 64), min(T, 64), 1, 2048))
+        assert b.tokens >= max(T, 16) and b.tokens <= 1024 and (b.tokens & (b.tokens - 1)) == 0
+        assert b.rows >= min(T, 64) and b.decode_seqs >= min(T, 64)
+        assert b.tiles >= (T + 3) // 4 and b.max_ctx == 2048
+        # every smaller step in the same bucket maps to the same bounds
+        if T > 16:
+            same = CudaRunner.bucket(fake, StepBounds(b.tokens // 2 + 1, 1, 1, 1, 1))
+            assert (same.tokens, same.rows, same.decode_seqs, same.tiles) == (b.tokens, b.rows, b.decode_seqs, b.tiles)
+
+
+def test_llama_workload_has_the_benchmark_shape():
+    """C4 requests: lognormal prompts of mean ~1024 clipped to [32, 8192] and
+    outputs of mean ~256 clipped to [16, 1024], tokens over the vocabulary,
+    deterministic per seed."""
+    from vllt.workloads import llama_lengths
+
+    a = llama_lengths(512, seed=0)
+    assert a == llama_lengths(512, seed=0)
+    plen = np.array([len(p) for p, _ in a])
+    olen = np.array([m for _, m in a])
+    assert plen.min() >= 32 and plen.max() <= 8192 and olen.min() >= 16 and olen.max() <= 1024
+    assert 900 < plen.mean() < 1150 and 220 < olen.mean() < 290
+    assert max(max(p) for p, _ in a) < 128256 and min(min(p) for p, _ in a) >= 0
