@@ -244,13 +244,25 @@ int vllt_sample_greedy(const float* logits, int32_t rows, int32_t vocab, int32_t
                        const uint8_t* eos_mask, int32_t eos_id, const float* penalty,
                        const uint32_t* seen_bits, int32_t* out_tokens, void* stream);
 
-/* Temperature / top-k / top-p sampling per row with a caller-provided uniform
- * u[r] in [0,1): the kept nucleus follows sampling.py:23-33 (descending
- * order, keep while the mass before a token is < p) and the token is the
- * inverse-CDF pick of u over the renormalised kept probabilities. */
-int vllt_sample_top_p(const float* logits, int32_t rows, int32_t vocab, int32_t ld,
-                      const float* temperature, const int32_t* top_k, const float* top_p,
-                      const float* u, int32_t* out_tokens, void* stream);
+/* The reference's whole sampler (vllmlite/sampling.py:41-64) for rows with a
+ * temperature > 0, one token per row. Row r of the call reads logits row
+ * row_index[r] (NULL: row r) of a buffer of logit_rows rows, and applies, in
+ * the reference's order: EOS -> -inf where eos_mask[r] != 0 (min_tokens not
+ * reached, :51-52), the repetition penalty on the tokens set in seen_bits[r]
+ * (ceil(vocab/32) words per row, may be NULL when penalty[r] == 1; :54),
+ * division by temperature[r] (:59), top-k (top_k[r] <= 0 or >= vocab keeps
+ * all, :16-20), top-p (the nucleus of sampling.py:23-33: descending order,
+ * keep while the mass before a token is < top_p[r]) and the draw (:63-64):
+ * numpy's Generator.choice given the float64 uniform u[r] it would draw from
+ * the request's generator, i.e. the first token whose cumulative kept
+ * probability (float64, divided by the total) exceeds u[r]. eos_mask,
+ * penalty, seen_bits, top_k and top_p may be NULL (no mask / no penalty /
+ * no top-k / top_p = 1). A row_index outside [0, logit_rows) yields -1. */
+int vllt_sample_top_p(const float* logits, int32_t rows, int32_t vocab, int32_t ld, int32_t logit_rows,
+                      const int32_t* row_index, const uint8_t* eos_mask, int32_t eos_id,
+                      const float* penalty, const uint32_t* seen_bits, const float* temperature,
+                      const int32_t* top_k, const float* top_p, const double* u, int32_t* out_tokens,
+                      void* stream);
 
 /* Speculative accept/reject for a batch of sequences. Sequence s owns logit
  * rows [cu_rows[s], cu_rows[s+1]) = n_drafts[s] + 1 rows (total_rows =

@@ -52,6 +52,36 @@ def greedy(logits: np.ndarray, eos_id=None, num_generated=0, min_tokens=0, seen=
     return int(np.argmax(x))
 
 
+def softmax(x: np.ndarray) -> np.ndarray:
+    """float32 softmax with the max subtracted. Follows vllmlite/sampling.py:35-38."""
+    z = x - x.max()
+    e = np.exp(z)
+    return e / e.sum()
+
+
+def sample_with_uniform(logits: np.ndarray, temperature: float, top_k: int, top_p: float, u: float,
+                        eos_id=None, num_generated=0, min_tokens=0, seen=(), penalty=1.0):
+    """The temperature branch of vllmlite/sampling.py:41-64 with the draw made
+    from a given uniform: EOS masked until min_tokens (:51-52), repetition
+    penalty (:54), division by the temperature (:59), top-k (:60), top-p
+    (:61), softmax (:63), then numpy's Generator.choice(size, p=probs) (:64),
+    which takes one rng.random() double u and returns the first index whose
+    float64 CDF (cumsum of probs divided by its last value) exceeds u.
+    Returns (token, keep mask, probs float32)."""
+    x = logits.astype(np.float32, copy=True)
+    if eos_id is not None and num_generated < min_tokens:
+        x[eos_id] = -np.inf
+    penalize(x, seen, penalty)
+    x /= np.float32(temperature)
+    top_k_mask(x, top_k)
+    x[~top_p_keep(x, top_p)] = -np.inf
+    probs = softmax(x)
+    cdf = np.cumsum(probs.astype(np.float64))
+    cdf /= cdf[-1]
+    tok = int(np.searchsorted(cdf, u, side="right"))
+    return tok, np.isfinite(x), probs
+
+
 def verify(logits: np.ndarray, drafts) -> tuple[list[int], int]:
     """Greedy speculative acceptance. Follows vllmlite/speculative.py:86-100:
     accept drafts while each equals the row's argmax; the first mismatch emits

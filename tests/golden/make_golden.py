@@ -13,6 +13,9 @@ given source tree; nothing here is needed at test time. Outputs:
                     plus wider cases; inputs are regenerated from the seeds
   rope.npz          build_rope tables (vllmlite/attention.py:21)
   sampling.npz      sample() greedy path, _top_p keep sets, verify() results
+  sampling_full.npz sample() temperature path with min_tokens EOS masks,
+                    repetition penalties, top-k and top-p: the reference's
+                    pick for a seeded generator, its uniform, keep set, probs
   workload.npz      make_workload requests (bench/bench.py:35-47) for the
                     mixed-length and shared-prefix benchmarks
   replay_*.npz      every ModelRunner.execute call of a reference LLMEngine run:
@@ -148,12 +151,65 @@ def streams_npz(streams):
     return dict(lens=lens, tokens=flat)
 
 
+def sampling_full():
+    """Temperature rows through the reference's whole sampler
+    (vllmlite/sampling.py:41-64): per row a logits vector, SamplingParams
+    (temperature, top_k, top_p, min_tokens, repetition_penalty), the tokens
+    seen so far, the number generated, and a seeded generator. Records the
+    reference's pick, the uniform choice() drew (the generator's first
+    random()), the keep set after mask / penalty / temperature / top-k /
+    top-p (the reference's own private steps) and the final probabilities."""
+    from vllmlite.sampling import _apply_repetition_penalty, _softmax, _top_k, _top_p, sample
+    from vllmlite.sequence import SamplingParams
+
+    rng = np.random.default_rng(11)
+    V, N, eos = 261, 96, 257
+    rows = (rng.standard_normal((N, V)) * 2.5).astype(np.float32)
+    rows[3, eos] = rows[3].max() + 4.0  # EOS would win if it were not masked
+    rows[7, 40] = rows[7, 41] = rows[7].max() + 0.5  # tie at the top
+    params, seen_all, picks, us, keep, probs = [], [], [], [], [], []
+    temps = (0.3, 0.7, 1.0, 1.6)
+    for i in range(N):
+        t = float(temps[i % 4])
+        k = int((0, 0, 5, 40, 260, 261, 1000)[i % 7])
+        p = float((1.0, 0.9, 0.5, 0.95, 0.2, 0.999)[i % 6])
+        mint, ngen = int(i % 3) * 2, int(i % 5)
+        pen = float((1.0, 1.3, 0.8, 2.0)[(i // 2) % 4])
+        seen = [int(x) for x in rng.integers(0, V, size=int(rng.integers(0, 60)))]
+        if i % 9 == 0:
+            seen += [eos, eos]
+        seed = 1000 + i
+        prm = SamplingParams(temperature=t, top_k=k, top_p=p, min_tokens=mint, repetition_penalty=pen)
+        picks.append(sample(rows[i], prm, seen, np.random.default_rng(seed), ngen, eos))
+        us.append(np.random.default_rng(seed).random())
+        x = rows[i].astype(np.float32, copy=True)
+        if ngen < mint:
+            x[eos] = -np.inf
+        _apply_repetition_penalty(x, seen, pen)
+        x /= t
+        _top_k(x, k)
+        _top_p(x, p)
+        keep.append(np.isfinite(x))
+        probs.append(_softmax(x).astype(np.float32))
+        params.append((t, k, p, mint, ngen, pen, seed, len(seen)))
+        seen_all += seen
+    np.savez_compressed(
+        os.path.join(HERE, "sampling_full.npz"), rows=rows, eos=np.int32(eos),
+        params=np.asarray(params, np.float64), seen=np.asarray(seen_all, np.int32),
+        picks=np.asarray(picks, np.int32), u=np.asarray(us, np.float64), keep=np.asarray(keep),
+        probs=np.asarray(probs))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="vllm-lite source checkout")
     ap.add_argument("--skip-slow", action="store_true")
+    ap.add_argument("--only", choices=["sampling_full"], help="write only this fixture")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
+    if args.only == "sampling_full":
+        sampling_full()
+        return
 
     from bench.bench import make_workload
     from vllmlite.attention import build_rope, gather_slots, paged_attention
@@ -245,6 +301,7 @@ def main():
         verify_tokens=np.asarray([t for c in vcases for t in c[2]], np.int32),
         verify_ntok=np.asarray([len(c[2]) for c in vcases], np.int32),
         verify_accepted=np.asarray([c[3] for c in vcases], np.int32))
+    sampling_full()
 
     # ---- workloads -------------------------------------------------------------
     wl = {}

@@ -230,6 +230,50 @@ def test_sampling_kernels_match_reference(dev):
                 assert out[i] == want, (i, p)
 
 
+def test_full_sampler_matches_reference(dev):
+    """vllt_sample_top_p on temperature rows with min_tokens EOS masks,
+    repetition penalties, top-k and top-p (sampling_full.npz, written by the
+    reference's sample()): given the uniform the reference's generator handed
+    numpy's choice(), every device pick lies in the reference's keep set and
+    equals the reference's pick unless u lies within 1e-5 of a CDF boundary
+    (the device sums the float32 probabilities in another order). Rows are
+    read through a shuffled row index; an index outside the buffer gives -1."""
+    from tests.test_oracle_golden import full_sampling_rows
+    from vllt.engine import seen_bitmaps
+    from vllt.ops import sample_top_p
+
+    items = list(full_sampling_rows())
+    n = len(items)
+    V = items[0][1].size
+    perm = np.random.default_rng(4).permutation(n)
+    logits = np.stack([items[j][1] for j in perm])  # row r of the buffer holds fixture row perm[r]
+    where = np.argsort(perm)  # fixture row i sits at buffer row where[i]
+    kw = [it[2] for it in items]
+    f32 = lambda a: torch.tensor(np.asarray(a, np.float32), device=dev)
+    temp = f32([k["temperature"] for k in kw])
+    top_k = torch.tensor([k["top_k"] for k in kw], dtype=torch.int32, device=dev)
+    top_p = f32([k["top_p"] for k in kw])
+    u = torch.tensor([k["u"] for k in kw], dtype=torch.float64, device=dev)
+    mask = torch.tensor([k["num_generated"] < k["min_tokens"] for k in kw], dtype=torch.uint8, device=dev)
+    pen = f32([k["penalty"] for k in kw])
+    seqs = [type("S", (), {"token_ids": list(k["seen"])})() for k in kw]
+    bits = torch.from_numpy(seen_bitmaps(seqs, V)).to(dev)
+    out = sample_top_p(torch.from_numpy(logits).to(dev), temp, top_k, top_p, u, row_index=where,
+                       eos_mask=mask, eos_id=kw[0]["eos_id"], penalty=pen, seen_bits=bits).cpu().numpy()
+    exact = 0
+    for i, row, k, pick, keep, probs in items:
+        assert keep[out[i]], (i, out[i])
+        cdf = np.cumsum(probs.astype(np.float64))
+        cdf /= cdf[-1]
+        if np.abs(cdf - k["u"]).min() > 1e-5:
+            assert out[i] == pick, (i, out[i], pick)
+            exact += 1
+    assert exact >= n - 2
+    bad = sample_top_p(torch.from_numpy(logits).to(dev), temp[:2], top_k[:2], top_p[:2], u[:2],
+                       row_index=np.asarray([0, n], np.int32)).cpu().numpy()
+    assert bad[1] == -1 and bad[0] >= 0
+
+
 def test_batch_meta_matches_reference_flatten(dev):
     """Device-built positions / slots / logit rows equal runner.py:66-90."""
     import ctypes

@@ -175,27 +175,43 @@ def test_pick_inputs_follow_the_reference_row_rules():
     rows (sequences with drafts) take plain argmax and contribute their drafts;
     temperature rows are sampled; EOS is masked while min_tokens is not reached
     (sampling.py:51-52, only with an EOS id); the repetition penalty lands on
-    the sequence's last row (sampling.py:54)."""
+    the sequence's last row (sampling.py:54); a chunk that leaves tokens of its
+    sequence uncomputed is neither masked, penalised nor sampled, since the
+    reference only samples once every token has KV (engine.py:131-149)."""
     from types import SimpleNamespace as NS
 
     from vllt.engine import pick_inputs
 
-    def item(drafts=(), greedy=True, min_tokens=0, out=0, pen=1.0):
+    def item(drafts=(), greedy=True, min_tokens=0, out=0, pen=1.0, final=True):
         p = NS(greedy=greedy, min_tokens=min_tokens, repetition_penalty=pen)
-        return NS(seq=NS(draft_token_ids=list(drafts), params=p, output_token_ids=[7] * out))
+        seq = NS(draft_token_ids=list(drafts), params=p, output_token_ids=[7] * out, num_tokens=10)
+        return NS(seq=seq, start_pos=10 - 1 - (0 if final else 3), num_tokens=1)
 
     sched = [item(), item(drafts=(11, 12, 13)), item(greedy=False), item(min_tokens=5, out=2),
-             item(min_tokens=5, out=5, pen=1.3)]
-    rows = [(0, 1), (1, 4), (5, 1), (6, 1), (7, 1)]
-    cu, doff, drafts, mask, pen, sampled = pick_inputs(sched, rows, 8, eos=257)
-    assert cu.tolist() == [0, 1, 5, 6, 7, 8] and cu.dtype == np.int32
-    assert doff.tolist() == [0, 0, 3, 3, 3]
+             item(min_tokens=5, out=5, pen=1.3), item(greedy=False, final=False),
+             item(min_tokens=5, out=1, pen=1.5, final=False)]
+    rows = [(0, 1), (1, 4), (5, 1), (6, 1), (7, 1), (8, 1), (9, 1)]
+    cu, doff, drafts, mask, pen, sampled = pick_inputs(sched, rows, 10, eos=257)
+    assert cu.tolist() == [0, 1, 5, 6, 7, 8, 9, 10] and cu.dtype == np.int32
+    assert doff.tolist() == [0, 0, 3, 3, 3, 3, 3]
     assert drafts == [11, 12, 13]
-    assert sampled == [(2, 5)]
-    assert mask.tolist() == [0, 0, 0, 0, 0, 0, 1, 0]
-    assert pen.dtype == np.float32 and pen[7] == np.float32(1.3) and (pen[:7] == 1).all()
+    assert sampled == [(2, 5)]  # the non-final temperature chunk draws nothing
+    assert mask.tolist() == [0, 0, 0, 0, 0, 0, 1, 0, 0, 0]
+    assert pen.dtype == np.float32 and pen[7] == np.float32(1.3)
+    assert (np.delete(pen, 7) == 1).all()  # nothing on the non-final chunk's row 9
     # no EOS id: min_tokens cannot mask anything
-    assert not pick_inputs(sched, rows, 8, eos=None)[3].any()
+    assert not pick_inputs(sched, rows, 10, eos=None)[3].any()
+
+
+def test_seen_bitmaps_mark_each_distinct_token_once():
+    from types import SimpleNamespace as NS
+
+    from vllt.engine import seen_bitmaps
+
+    b = seen_bitmaps([NS(token_ids=[0, 31, 32, 260, 31]), None, NS(token_ids=[])], 261)
+    assert b.shape == (3, 9) and b.dtype == np.uint32
+    assert b[0, 0] == (1 | (1 << 31)) and b[0, 1] == 1 and b[0, 8] == 1 << (260 - 256)
+    assert not b[1].any() and not b[2].any()
 
 
 def test_graph_bucket_bounds_cover_every_step_of_the_bucket():

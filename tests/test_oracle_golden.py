@@ -92,3 +92,35 @@ def test_sampling_fixtures():
         lo += k + 1
         do += k
         to += nt
+
+
+def full_sampling_rows():
+    """Yield (row index, logits, kwargs of oracle.sampling.sample_with_uniform,
+    the reference's pick, keep set, probs) for every row of sampling_full.npz."""
+    z = F.load("sampling_full.npz")
+    o = 0
+    eos = int(z["eos"])
+    for i, (t, k, p, mint, ngen, pen, seed, nseen) in enumerate(z["params"]):
+        seen = z["seen"][o:o + int(nseen)]
+        o += int(nseen)
+        kw = dict(temperature=float(t), top_k=int(k), top_p=float(p), u=float(z["u"][i]), eos_id=eos,
+                  num_generated=int(ngen), min_tokens=int(mint), seen=seen, penalty=float(pen))
+        yield i, z["rows"][i], kw, int(z["picks"][i]), z["keep"][i], z["probs"][i]
+
+
+def test_full_sampler_matches_the_reference():
+    """Temperature rows with EOS masks, repetition penalties, top-k and top-p:
+    the oracle's sampler, given the uniform the reference's generator handed
+    numpy's choice(), picks the reference's token and keeps its keep set."""
+    n = masked = penalised = 0
+    for i, row, kw, pick, keep, probs in full_sampling_rows():
+        assert kw["u"] == np.random.default_rng(int(1000 + i)).random()
+        tok, kept, pr = SP.sample_with_uniform(row, **kw)
+        assert tok == pick, i
+        np.testing.assert_array_equal(kept, keep)
+        np.testing.assert_allclose(pr, probs, rtol=1e-6, atol=1e-9)
+        assert keep[tok]
+        masked += kw["num_generated"] < kw["min_tokens"]
+        penalised += kw["penalty"] != 1.0 and len(kw["seen"]) > 0
+        n += 1
+    assert n == 96 and masked >= 10 and penalised >= 40

@@ -9,6 +9,10 @@ over gloo with CPU tensors and a recording stand-in for the forward:
     ends the worker loop with the right pass count;
   * the merged argmax equals np.argmax over the full (unsharded) logits,
     with planted ties inside a slice and across the slice boundary;
+  * a gather message (rows that need the whole vocabulary for their pick:
+    EOS mask, repetition penalty, temperature draw) reaches the worker's
+    gather handler with its row list, and the all-gather of every rank's
+    slice of those rows rebuilds the full rows in vocabulary order;
   * an oversize record is refused on rank 0 before anything is broadcast.
 """
 
@@ -44,6 +48,9 @@ def _messages():
     return out
 
 
+GATHER_ROWS = np.asarray([5, 0, 3], np.int32)
+
+
 def _logits(R, V):
     rng = np.random.default_rng(9)
     x = rng.standard_normal((R, V)).astype(np.float32)
@@ -59,7 +66,8 @@ def _rank(rank, world, port, result_dir):
     sys.path[:0] = [ROOT, os.path.join(ROOT, "vllm-lite_b200")]
     import torch.distributed as dist
 
-    from vllt.tp import CTRL_WORDS, OP_FORWARD, OP_MARK, OP_STOP, ControlPlane, merge_argmax, serve
+    from vllt.tp import (CTRL_WORDS, OP_FORWARD, OP_GATHER, OP_MARK, OP_STOP, ControlPlane, gather_vocab_rows,
+                         merge_argmax, serve)
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -70,22 +78,29 @@ def _rank(rank, world, port, result_dir):
             with pytest.raises(ValueError):
                 plane.send(OP_FORWARD, np.zeros(65, np.int32))
             plane.send(OP_MARK)
-            for rec, b, g in msgs:
+            for j, (rec, b, g) in enumerate(msgs):
                 plane.send(OP_FORWARD, rec, b, g)
+                if j == 2:
+                    plane.send(OP_GATHER, GATHER_ROWS)
             plane.send(OP_MARK)
             plane.send(OP_STOP)
         else:
-            seen, marks = [], []
+            seen, marks, gathers = [], [], []
 
             def forward(bounds, greedy):
                 n = int(plane.ctrl[7])
                 seen.append((plane.buf[:n].numpy().copy(), bounds, greedy))
 
-            assert serve(plane, forward, marks.append) == len(msgs)
+            def gather(n):
+                gathers.append((len(seen), plane.buf[:n].numpy().copy()))
+
+            assert serve(plane, forward, marks.append, gather) == len(msgs)
             assert marks == [0, 0]
             for (rec, b, g), (got, gb, gg) in zip(msgs, seen):
                 np.testing.assert_array_equal(got, rec)
                 assert [getattr(gb, f) for f in FIELDS] == [getattr(b, f) for f in FIELDS] and gg == g
+            assert len(gathers) == 1 and gathers[0][0] == 3
+            np.testing.assert_array_equal(gathers[0][1], GATHER_ROWS)
 
         # vocab-parallel greedy: rank r owns columns [r*V/2, (r+1)*V/2)
         R, V = 8, 40
@@ -100,6 +115,9 @@ def _rank(rank, world, port, result_dir):
         dist.all_gather(list(idxs.view(world, R)), idx)
         got = merge_argmax(vals.view(world, R), idxs.view(world, R)).numpy()
         np.testing.assert_array_equal(got, x.argmax(1))
+        # full rows of the gathered logit rows, from every rank's slice
+        full = gather_vocab_rows(torch.from_numpy(sl[GATHER_ROWS]), world).numpy()
+        np.testing.assert_array_equal(full, x[GATHER_ROWS])
         open(os.path.join(result_dir, f"ok{rank}"), "w").close()
     finally:
         dist.destroy_process_group()

@@ -4,6 +4,9 @@ Every rank builds its shard of a full-width 2-layer slice of the Llama-3-8B
 shape; rank 0 drives a fixed three-pass schedule through TPLlamaRunner
 (record broadcast, NCCL all-reduces in the forward, vocab-parallel greedy) and
 compares logits and picks with a 1-GPU LlamaRunner on the same weights.
+Rows whose pick needs the whole vocabulary (EOS mask, repetition penalty,
+temperature draw) are gathered from every rank: the gathered rows must hold
+rank 0's own slice bit for bit and match the 1-GPU logits like the slices do.
 Prints one line "TP_PARITY ok <max rel err> <agree>/<rows>" on success.
 """
 
@@ -54,6 +57,11 @@ def main():
             worst = max(worst, float(np.abs(local_logits - sl).max() / np.abs(want).max()))
             agree += int((picks == want.argmax(1)).sum())
             rows += R
+            g = sorted({0, R - 1})
+            full = run.gather_rows(g).cpu().numpy()
+            assert full.shape == (len(g), shape.vocab_size)
+            np.testing.assert_array_equal(full[:, :run.w.vocab_local], local_logits[g])
+            worst = max(worst, float(np.abs(full - want[g]).max() / np.abs(want).max()))
         run.stop_workers()
         ok = worst < 5e-2 and agree >= rows - 1
         print(f"TP_PARITY {'ok' if ok else 'FAIL'} {worst:.3e} {agree}/{rows}", flush=True)

@@ -334,15 +334,17 @@ int vllt_sample_greedy(const float* logits, int32_t rows, int32_t vocab, int32_t
                        out_tokens, as_stream(stream));
 }
 
-int vllt_sample_top_p(const float* logits, int32_t rows, int32_t vocab, int32_t ld,
-                      const float* temperature, const int32_t* top_k, const float* top_p,
-                      const float* u, int32_t* out_tokens, void* stream) {
+int vllt_sample_top_p(const float* logits, int32_t rows, int32_t vocab, int32_t ld, int32_t logit_rows,
+                      const int32_t* row_index, const uint8_t* eos_mask, int32_t eos_id, const float* penalty,
+                      const uint32_t* seen_bits, const float* temperature, const int32_t* top_k,
+                      const float* top_p, const double* u, int32_t* out_tokens, void* stream) {
   clear_error();
-  VLLT_REQUIRE(rows >= 0 && vocab > 0 && ld >= vocab, "sample_top_p: bad sizes");
+  VLLT_REQUIRE(rows >= 0 && vocab > 0 && ld >= vocab && logit_rows >= 0, "sample_top_p: bad sizes");
   if (rows == 0) return VLLT_OK;
+  VLLT_REQUIRE(logit_rows > 0 && (row_index || rows <= logit_rows), "sample_top_p: more rows than logit_rows");
   VLLT_REQUIRE(logits && temperature && u && out_tokens, "sample_top_p: null pointer");
-  return sample_top_p(logits, rows, vocab, ld, temperature, top_k, top_p, u, out_tokens,
-                      as_stream(stream));
+  return sample_top_p(logits, rows, vocab, ld, logit_rows, row_index, eos_mask, eos_id, penalty, seen_bits,
+                      temperature, top_k, top_p, u, out_tokens, as_stream(stream));
 }
 
 int vllt_spec_verify(const float* logits, int32_t ld, int32_t vocab, const int32_t* cu_rows,

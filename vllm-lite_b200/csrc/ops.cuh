@@ -29,9 +29,10 @@ int sample_greedy(const float* logits, int rows_cap, const int32_t* rows_dev, in
                   int32_t* out, cudaStream_t st);
 int spec_accept(const int32_t* cu_rows, const int32_t* drafts, const int32_t* draft_off,
                 int num_seqs, const int32_t* picks, int32_t* n_accepted, cudaStream_t st);
-int sample_top_p(const float* logits, int rows, int vocab, int ld, const float* temperature,
-                 const int32_t* top_k, const float* top_p, const float* u, int32_t* out,
-                 cudaStream_t st);
+int sample_top_p(const float* logits, int rows, int vocab, int ld, int logit_rows, const int32_t* row_index,
+                 const uint8_t* eos_mask, int eos_id, const float* penalty, const uint32_t* seen,
+                 const float* temperature, const int32_t* top_k, const float* top_p, const double* u,
+                 int32_t* out, cudaStream_t st);
 
 struct AttnCall {
   const void *q, *kc, *vc;

@@ -1,5 +1,6 @@
 // Device sampling: greedy argmax with the reference's pre-steps, speculative
-// accept/reject, and temperature / top-k / top-p sampling with a given uniform.
+// accept/reject, and temperature / top-k / top-p sampling with the same
+// pre-steps and a given uniform.
 
 #include <float.h>
 #include <math.h>
@@ -114,20 +115,43 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Temperature, top-k, top-p and the inverse-CDF draw; one CTA per row.
-// Follows sampling.py:59-64 and :16-33. The k-th largest value and the nucleus
-// threshold are found by bisection over order keys, so any vocab size works
-// with O(32 * vocab) work and no sort.
-__global__ void top_p_kernel(const float* __restrict__ logits, int vocab, int ld,
-                             const float* __restrict__ temperature, const int32_t* __restrict__ top_k,
-                             const float* __restrict__ top_p, const float* __restrict__ uni,
-                             int32_t* __restrict__ out) {
+// The full sampler of sampling.py:41-64 for temperature rows; one CTA per row.
+// The row's logits pass through the reference's pre-steps on the fly, in its
+// order: EOS masked to -inf while min_tokens is not reached (:51-52), the
+// repetition penalty on every token the row has seen (:54, :8-13), division by
+// the temperature (:59); then top-k (:16-20), top-p (:23-33) and the draw
+// (:63-64). The k-th largest value and the nucleus threshold are found by
+// bisection over order keys, so any vocab size works with O(32 * vocab) work
+// and no sort. The draw is numpy's Generator.choice with the uniform `uni[r]`
+// it would have taken from the request's generator: the first index whose
+// float64 CDF (cumulative sum of the kept probabilities, divided by the total)
+// exceeds u. Row r reads logits row row_index[r] (r when NULL); an index
+// outside [0, logit_rows) yields token -1 and nothing else is read.
+__global__ void top_p_kernel(const float* __restrict__ logits, int vocab, int ld, int logit_rows,
+                             const int32_t* __restrict__ row_index, const uint8_t* __restrict__ eos_mask,
+                             int eos_id, const float* __restrict__ penalty, const uint32_t* __restrict__ seen,
+                             int seen_words, const float* __restrict__ temperature,
+                             const int32_t* __restrict__ top_k, const float* __restrict__ top_p,
+                             const double* __restrict__ uni, int32_t* __restrict__ out) {
   const int r = blockIdx.x;
-  const float* x = logits + (int64_t)r * ld;
+  const int src = row_index ? row_index[r] : r;
+  if (src < 0 || src >= logit_rows) {  // uniform across the CTA
+    if (threadIdx.x == 0) out[r] = -1;
+    return;
+  }
+  const float* x = logits + (int64_t)src * ld;
+  const bool mask_eos = eos_mask && eos_mask[r] && eos_id >= 0 && eos_id < vocab;
+  const float pen = penalty ? penalty[r] : 1.f;
+  const uint32_t* sb = (seen && pen != 1.f) ? seen + (int64_t)r * seen_words : nullptr;
   const float temp = temperature[r];
   const int k = top_k ? top_k[r] : 0;
   const float p = top_p ? top_p[r] : 1.f;
-  auto val = [&](int c) { return __fdiv_rn(x[c], temp); };
+  auto val = [&](int c) {
+    float v = x[c];
+    if (mask_eos && c == eos_id) v = -INFINITY;
+    if (sb && ((sb[c >> 5] >> (c & 31)) & 1u)) v = v > 0.f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
+    return __fdiv_rn(v, temp);
+  };
 
   // top-k: the largest key v with count(x >= v) >= k
   uint32_t cut_key = 0;
@@ -196,7 +220,7 @@ __global__ void top_p_kernel(const float* __restrict__ logits, int vocab, int ld
     if (kept(v)) total += (double)__fdiv_rn(expf(v - mx), s2);
   }
   total = block_reduce<double>(total, [](double a, double b) { return a + b; }, 0.0);
-  const double u = (double)uni[r] * total;
+  const double u = uni[r] * total;
   for (int base = 0; base < vocab; base += kThreads) {
     const int c = base + threadIdx.x;
     double pc = 0.0;
@@ -252,12 +276,14 @@ int spec_accept(const int32_t* cu_rows, const int32_t* drafts, const int32_t* dr
   return check_launch("spec_accept");
 }
 
-int sample_top_p(const float* logits, int rows, int vocab, int ld, const float* temperature,
-                 const int32_t* top_k, const float* top_p, const float* u, int32_t* out,
-                 cudaStream_t st) {
+int sample_top_p(const float* logits, int rows, int vocab, int ld, int logit_rows, const int32_t* row_index,
+                 const uint8_t* eos_mask, int eos_id, const float* penalty, const uint32_t* seen,
+                 const float* temperature, const int32_t* top_k, const float* top_p, const double* u,
+                 int32_t* out, cudaStream_t st) {
   if (rows <= 0) return VLLT_OK;
-  VLLT_REQUIRE(vocab > 0 && ld >= vocab && temperature && u, "sample_top_p: bad arguments");
-  top_p_kernel<<<rows, kThreads, 0, st>>>(logits, vocab, ld, temperature, top_k, top_p, u, out);
+  VLLT_REQUIRE(vocab > 0 && ld >= vocab && logit_rows > 0 && temperature && u, "sample_top_p: bad arguments");
+  top_p_kernel<<<rows, kThreads, 0, st>>>(logits, vocab, ld, logit_rows, row_index, eos_mask, eos_id, penalty,
+                                          seen, (vocab + 31) / 32, temperature, top_k, top_p, u, out);
   return check_launch("sample_top_p");
 }
 

@@ -64,7 +64,7 @@ SIGNATURES = {
     "vllt_gemm_bf16_auto_splits": (i32, [i32, i32, i32]),
     "vllt_gemm_bf16_splitk": (C.c_int, [vp, vp, vp, i32, i32, i32, i32, vp, i64, vp, vp]),
     "vllt_sample_greedy": (C.c_int, [vp, i32, i32, i32, vp, i32, vp, vp, vp, vp]),
-    "vllt_sample_top_p": (C.c_int, [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp]),
+    "vllt_sample_top_p": (C.c_int, [vp, i32, i32, i32, i32, vp, vp, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
     "vllt_spec_verify": (C.c_int, [vp, i32, i32, vp, i32, vp, vp, i32, vp, vp, vp]),
     "vllt_spec_accept": (C.c_int, [vp, vp, vp, i32, vp, vp, vp]),
     "vllt_tp_unique_id": (C.c_int, [vp]),

@@ -8,10 +8,13 @@ Logits come back to the host every step, exactly as the reference expects.
 
 `GpuLLMEngine` keeps all of that but replaces the sampling half of
 LLMEngine.step (engine.py:113-148) by device kernels: one launch picks the
-argmax of every logit row and applies the speculative accept/reject rule
-(speculative.py:86-100); non-greedy rows draw on the device with the
-request's own generator supplying the uniform (sampling.py:59-64). Only the
-picked token ids cross back to the host.
+argmax of every logit row (with the min_tokens EOS mask and the repetition
+penalty, sampling.py:41-57) and one applies the speculative accept/reject rule
+(speculative.py:86-100); temperature rows go through the device sampler
+(mask, penalty, temperature, top-k, top-p, sampling.py:41-64) with the
+request's own generator supplying the uniform numpy's choice() would draw.
+Only the picked token ids cross back to the host; no row is sampled on the
+CPU.
 """
 
 from __future__ import annotations
@@ -47,13 +50,25 @@ def cuda_engine(cfg=None, tokenizer=None, speculative_tokens: int = 0, weights=N
         E.NumpyRunner = orig
 
 
+def completes(item) -> bool:
+    """Whether this pass computes the last token of the item's sequence: the
+    reference engine only picks a token for such sequences; chunked-prefill
+    and post-preemption chunks that leave tokens uncomputed pick nothing and
+    draw nothing from the request's generator (vllmlite/engine.py:131-149).
+    Evaluated before commit: the sequence then has num_computed == start_pos."""
+    return item.start_pos + item.num_tokens >= item.seq.num_tokens
+
+
 def pick_inputs(scheduled, rows, R: int, eos):
     """Host inputs of the device token picks for one step, following the
-    reference's per-row rules (vllmlite/engine.py:106-130, sampling.py:41-64):
+    reference's per-row rules (vllmlite/engine.py:106-149, sampling.py:41-64):
     cu_rows[S+1] and draft offsets[S] (int32), the flat draft tokens, eos_mask[R]
-    (min_tokens not reached), penalty[R] (repetition penalty of the row), and the
-    (sequence index, row) pairs that sample with temperature. Rows of sequences
-    that verify drafts take plain argmax (speculative.py:92)."""
+    (min_tokens not reached, greedy rows), penalty[R] (repetition penalty of a
+    greedy row), and the (sequence index, row) pairs that sample with
+    temperature. Rows of sequences that verify drafts take plain argmax
+    (speculative.py:92). Only the last row of a sequence that completes this
+    pass is masked, penalised or sampled: that is the only row the reference
+    hands to sample()."""
     S = len(scheduled)
     cu, doff, drafts = [0] * (S + 1), [0] * S, []
     mask_rows, pen_rows, pen_vals, sampled = [], [], [], []
@@ -65,6 +80,8 @@ def pick_inputs(scheduled, rows, R: int, eos):
         d = seq.draft_token_ids
         if d:
             drafts += d[:cnt - 1]
+            continue
+        if not completes(item):
             continue
         p = seq.params
         last = r0 + cnt - 1
@@ -83,6 +100,42 @@ def pick_inputs(scheduled, rows, R: int, eos):
     if pen_rows:
         penalty[pen_rows] = pen_vals
     return np.asarray(cu, np.int32), np.asarray(doff, np.int32), drafts, eos_mask, penalty, sampled
+
+
+def seen_bitmaps(seqs, vocab: int) -> np.ndarray:
+    """uint32 [len(seqs)][ceil(vocab/32)]: bit t of row j is set when token t
+    occurs in seqs[j].token_ids (the `seen_tokens` of sampling.py:54, which
+    penalises each distinct seen token once, :11)."""
+    b = np.zeros((len(seqs), (vocab + 31) // 32), np.uint32)
+    for j, seq in enumerate(seqs):
+        if seq is None:
+            continue
+        seen = np.unique(np.asarray(seq.token_ids, np.int64))
+        if seen.size:
+            np.bitwise_or.at(b[j], seen >> 5, np.uint32(1) << (seen & 31).astype(np.uint32))
+    return b
+
+
+def sample_inputs(seqs, eos, rngs):
+    """Per-row arrays of the device sampler for temperature rows, one row per
+    sequence: temperature, top_k, top_p, the float64 uniform numpy's choice()
+    would draw from the request's generator (one rng.random() per pick,
+    sampling.py:64), the min_tokens EOS mask and the repetition penalty."""
+    n = len(seqs)
+    temp = np.empty(n, np.float32)
+    top_k = np.empty(n, np.int32)
+    top_p = np.empty(n, np.float32)
+    u = np.empty(n, np.float64)
+    mask = np.zeros(n, np.uint8)
+    pen = np.ones(n, np.float32)
+    for j, seq in enumerate(seqs):
+        p = seq.params
+        temp[j], top_k[j], top_p[j] = p.temperature, p.top_k, p.top_p
+        u[j] = rngs[seq.request_id].random()
+        if eos is not None and p.min_tokens and len(seq.output_token_ids) < p.min_tokens:
+            mask[j] = 1
+        pen[j] = p.repetition_penalty
+    return temp, top_k, top_p, u, mask, pen
 
 
 def _engine_base():
@@ -118,91 +171,107 @@ def gpu_engine(cfg=None, tokenizer=None, speculative_tokens: int = 0, weights=No
 
 def _make_gpu_engine(Base):
     import torch
-    from vllmlite.sampling import sample
     from vllmlite.sequence import RequestOutput
 
     from . import _lib
     from ._lib import check
 
     class _GpuLLMEngine(Base):
+        def _h2d(self, a):
+            return torch.from_numpy(np.ascontiguousarray(a)).to(self.runner.dev, non_blocking=True)
+
+        def _greedy(self, logits, n_rows, ld, vocab, mask, pen, seqs, out, keep):
+            """Greedy kernel over logits rows [0, n_rows) with the EOS mask and
+            penalty arrays of those rows (seqs[j]: the sequence of a penalised
+            row j, else None)."""
+            L, eos = self.runner.L, self.tokenizer.eos_id
+            d_mask = self._h2d(mask) if mask.any() else None
+            d_pen = bits = None
+            if (pen != 1.0).any():
+                d_pen = self._h2d(pen)
+                bits = self._h2d(seen_bitmaps([s if pen[j] != 1.0 else None for j, s in enumerate(seqs)], vocab))
+            keep += [d_mask, d_pen, bits]
+            check(L.vllt_sample_greedy(logits.data_ptr(), n_rows, vocab, ld, _lib.ptr(d_mask),
+                                       eos if eos is not None else -1, _lib.ptr(d_pen), _lib.ptr(bits),
+                                       out.data_ptr(), _lib.stream_handle()))
+
+        def _sample(self, logits, n_logit_rows, ld, vocab, row_index, seqs, out, keep):
+            """Device sampler (vllt_sample_top_p) for temperature rows: row j
+            reads logits[row_index[j]] and belongs to seqs[j]."""
+            L, eos = self.runner.L, self.tokenizer.eos_id
+            temp, top_k, top_p, u, mask, pen = sample_inputs(seqs, eos, self.rngs)
+            d = [self._h2d(a) for a in (np.asarray(row_index, np.int32), temp, top_k, top_p, u)]
+            d_mask = self._h2d(mask) if mask.any() else None
+            d_pen = bits = None
+            if (pen != 1.0).any():
+                d_pen = self._h2d(pen)
+                bits = self._h2d(seen_bitmaps(seqs, vocab))
+            keep += d + [d_mask, d_pen, bits]
+            check(L.vllt_sample_top_p(logits.data_ptr(), len(seqs), vocab, ld, n_logit_rows, d[0].data_ptr(),
+                                      _lib.ptr(d_mask), eos if eos is not None else -1, _lib.ptr(d_pen),
+                                      _lib.ptr(bits), d[1].data_ptr(), d[2].data_ptr(), d[3].data_ptr(),
+                                      d[4].data_ptr(), out.data_ptr(), _lib.stream_handle()))
+
         def _device_picks(self, sched, rows, R):
             """Pick every row's token on the device; return host arrays
-            (picks[R], n_accepted[S], {seq index: sampled token})."""
+            (picks[R], n_accepted[S], {seq index: sampled token}).
+
+            One GPU: the greedy kernel over all R rows (EOS mask / penalty on
+            the rows that need them), the sampler over the temperature rows
+            (read in place through a row index), the accept rule over the
+            verify rows. Tensor parallel: the vocab-parallel argmax over all
+            rows; rows that need a mask, a penalty or a draw have their
+            full-vocabulary logits gathered from every rank first and go
+            through the same two kernels."""
             run = self.runner
-            dev = run.dev
             S = len(sched.scheduled)
             V = run.model_cfg.vocab_size
-            ld = run.w.vocab_padded
             eos = self.tokenizer.eos_id
             cu, doff, drafts, eos_mask, penalty, sampled = pick_inputs(sched.scheduled, rows, R, eos)
-            st = _lib.stream_handle()
-
-            def h2d(a):
-                return torch.from_numpy(np.ascontiguousarray(a)).to(dev, non_blocking=True)
-
-            acc = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
-            L = run.L
-            if getattr(run, "tp_size", 1) > 1:
-                # vocab-parallel greedy; rows needing masks or sampling are not supported across shards
-                if eos_mask.any() or (penalty != 1.0).any() or sampled:
-                    raise NotImplementedError("tensor-parallel engine: greedy rows without min_tokens / "
-                                              "repetition penalty only")
-                picks = run.greedy_picks(R)
-                if drafts:
-                    d_cu, d_dr, d_doff = h2d(cu), h2d(np.asarray(drafts, np.int32)), h2d(doff)
-                    check(L.vllt_spec_accept(d_cu.data_ptr(), d_dr.data_ptr(), d_doff.data_ptr(), S,
-                                             picks.data_ptr(), acc.data_ptr(), st))
-                acc_h = acc[:S].cpu().numpy() if drafts else np.zeros(S, np.int32)
-                return picks[:R].cpu().numpy(), acc_h, {}
-            picks = torch.empty(max(R, 1), dtype=torch.int32, device=dev)
-            d_mask = h2d(eos_mask) if eos_mask.any() else None
-            d_pen = bits = None
-            if (penalty != 1.0).any():
-                d_pen = h2d(penalty)
-                words = (V + 31) // 32
-                b = np.zeros((R, words), np.uint32)
-                for i, item in enumerate(sched.scheduled):
-                    last = rows[i][0] + rows[i][1] - 1
-                    if penalty[last] != 1.0:
-                        seen = np.unique(np.asarray(item.seq.token_ids, np.int64))
-                        np.bitwise_or.at(b[last], seen >> 5, (np.uint32(1) << (seen & 31).astype(np.uint32)))
-                bits = h2d(b)
-            check(L.vllt_sample_greedy(run.logits_dev.data_ptr(), R, V, ld, _lib.ptr(d_mask),
-                                       eos if eos is not None else -1, _lib.ptr(d_pen), _lib.ptr(bits),
-                                       picks.data_ptr(), st))
-            # device temporaries stay referenced until their kernels are enqueued:
+            keep = []  # device temporaries stay referenced until their kernels are enqueued:
             # a tensor freed earlier could be handed to the next copy by the
             # caching allocator and overwritten before the kernel reads it
-            if drafts:
-                d_cu, d_dr, d_doff = h2d(cu), h2d(np.asarray(drafts, np.int32)), h2d(doff)
-                check(L.vllt_spec_accept(d_cu.data_ptr(), d_dr.data_ptr(), d_doff.data_ptr(), S,
-                                         picks.data_ptr(), acc.data_ptr(), st))
+            seq_of_row = {}
+            for i, item in enumerate(sched.scheduled):
+                seq_of_row[rows[i][0] + rows[i][1] - 1] = item.seq
+            acc = torch.empty(max(S, 1), dtype=torch.int32, device=run.dev)
             sampled_tok = {}
-            plain = [(i, r) for i, r in sampled
-                     if sched.scheduled[i].seq.params.repetition_penalty == 1.0
-                     and len(sched.scheduled[i].seq.output_token_ids) >= sched.scheduled[i].seq.params.min_tokens]
-            other = [x for x in sampled if x not in plain]
-            if plain:
-                prm = [sched.scheduled[i].seq.params for i, _ in plain]
-                # the request's generator supplies the uniform numpy's choice() would draw
-                u = np.asarray([self.rngs[sched.scheduled[i].seq.request_id].random() for i, _ in plain], np.float32)
-                sel = h2d(np.asarray([r for _, r in plain], np.int64))
-                sub = run.logits_dev.index_select(0, sel).contiguous()
-                out = torch.empty(len(plain), dtype=torch.int32, device=dev)
-                d_t = h2d(np.asarray([q.temperature for q in prm], np.float32))
-                d_k = h2d(np.asarray([q.top_k for q in prm], np.int32))
-                d_p = h2d(np.asarray([q.top_p for q in prm], np.float32))
-                d_u = h2d(u)
-                check(L.vllt_sample_top_p(sub.data_ptr(), len(plain), V, ld, d_t.data_ptr(), d_k.data_ptr(),
-                                          d_p.data_ptr(), d_u.data_ptr(), out.data_ptr(), st))
-                for (i, _), t in zip(plain, out.cpu().numpy()):
-                    sampled_tok[i] = int(t)
-            for i, r in other:  # temperature with penalty / min_tokens: the reference sampler on that row
-                seq = sched.scheduled[i].seq
-                row = run.logits_dev[r, :V].cpu().numpy()
-                sampled_tok[i] = sample(row, seq.params, seq.token_ids, self.rngs[seq.request_id],
-                                        len(seq.output_token_ids), eos)
-            picks_h = picks[:R].cpu().numpy()
+            if getattr(run, "tp_size", 1) > 1:
+                picks = run.greedy_picks(R)
+            else:
+                picks = torch.empty(max(R, 1), dtype=torch.int32, device=run.dev)
+                self._greedy(run.logits_dev, R, run.w.vocab_padded, V, eos_mask, penalty,
+                             [seq_of_row.get(r) for r in range(R)], picks, keep)
+            if drafts:
+                d_cu, d_dr, d_doff = self._h2d(cu), self._h2d(np.asarray(drafts, np.int32)), self._h2d(doff)
+                keep += [d_cu, d_dr, d_doff]
+                check(run.L.vllt_spec_accept(d_cu.data_ptr(), d_dr.data_ptr(), d_doff.data_ptr(), S,
+                                             picks.data_ptr(), acc.data_ptr(), _lib.stream_handle()))
+            if getattr(run, "tp_size", 1) > 1:
+                special = [int(r) for r in np.flatnonzero(eos_mask | (penalty != 1.0))]
+                srows = [r for _, r in sampled]
+                picks_h = picks[:R].cpu().numpy()
+                if special or srows:
+                    full = run.gather_rows(special + srows)  # [n, V] fp32 on every rank
+                    out = torch.empty(len(special) + len(srows), dtype=torch.int32, device=run.dev)
+                    if special:
+                        self._greedy(full, len(special), V, V, eos_mask[special], penalty[special],
+                                     [seq_of_row[r] for r in special], out, keep)
+                    if srows:
+                        self._sample(full, full.shape[0], V, V, [len(special) + j for j in range(len(srows))],
+                                     [sched.scheduled[i].seq for i, _ in sampled], out[len(special):], keep)
+                    got = out.cpu().numpy()
+                    picks_h[special] = got[:len(special)]
+                    for j, (i, _) in enumerate(sampled):
+                        sampled_tok[i] = int(got[len(special) + j])
+            else:
+                if sampled:
+                    out = torch.empty(len(sampled), dtype=torch.int32, device=run.dev)
+                    self._sample(run.logits_dev, R, run.w.vocab_padded, V, [r for _, r in sampled],
+                                 [sched.scheduled[i].seq for i, _ in sampled], out, keep)
+                    for (i, _), t in zip(sampled, out.cpu().numpy()):
+                        sampled_tok[i] = int(t)
+                picks_h = picks[:R].cpu().numpy()
             acc_h = acc[:S].cpu().numpy() if drafts else np.zeros(S, np.int32)
             return picks_h, acc_h, sampled_tok
 

@@ -169,13 +169,24 @@ def greedy(logits, eos_mask=None, eos_id=257, penalty=None, seen_bits=None, voca
     return out
 
 
-def sample_top_p(logits, temperature, top_k, top_p, u, vocab=None):
+def sample_top_p(logits, temperature, top_k, top_p, u, vocab=None, row_index=None, eos_mask=None, eos_id=257,
+                 penalty=None, seen_bits=None):
+    """Temperature rows of vllmlite.sampling.sample (sampling.py:41-64) on the
+    device: EOS mask, repetition penalty, temperature, top-k, top-p, then the
+    inverse-CDF draw of the float64 uniform u[r] (what the request's generator
+    hands numpy's choice()). Row r reads logits[row_index[r]] (row r when
+    row_index is None). Returns int32 tokens [rows]."""
     import torch
 
-    rows, ld = logits.shape
+    n_logit_rows, ld = logits.shape
     vocab = vocab or ld
+    rows = row_index.shape[0] if row_index is not None else n_logit_rows
     out = torch.empty(rows, dtype=torch.int32, device=logits.device)
-    check(lib().vllt_sample_top_p(ptr(logits), rows, vocab, ld, ptr(temperature), ptr(top_k), ptr(top_p),
+    ri = _i32(row_index, logits.device) if row_index is not None else None
+    em = eos_mask.to(torch.uint8).contiguous() if eos_mask is not None else None
+    u = u.to(torch.float64).contiguous()
+    check(lib().vllt_sample_top_p(ptr(logits), rows, vocab, ld, n_logit_rows, ptr(ri), ptr(em), eos_id,
+                                  ptr(penalty), ptr(seen_bits), ptr(temperature), ptr(top_k), ptr(top_p),
                                   ptr(u), ptr(out), stream_handle()))
     return out
 

@@ -10,7 +10,11 @@ forward pass:
      every rank holds the same block ids for its own KV heads;
   3. greedy picks are vocab-parallel: each rank reduces its vocabulary slice to
      (max, first index) per row, the pairs are all-gathered and the lowest
-     global index among the maxima wins (np.argmax semantics).
+     global index among the maxima wins (np.argmax semantics);
+  4. rows whose pick needs the whole vocabulary at once (a min_tokens EOS mask,
+     a repetition penalty, or a temperature draw: sampling.py:41-64) are named
+     in a gather message; every rank contributes its slice of those rows and
+     rank 0 runs the single-GPU sampling kernels on the full rows.
 All ranks take the same collective steps in the same order; a stop record ends
 the workers.
 """
@@ -26,7 +30,7 @@ from ._lib import StepBounds, check, lib
 from .llama import LlamaRunner
 from .runner import CudaRunner
 
-OP_FORWARD, OP_STOP, OP_MARK = 1, 2, 3
+OP_FORWARD, OP_STOP, OP_MARK, OP_GATHER = 1, 2, 3, 4
 CTRL_WORDS = 8  # [op, tokens, rows, decode_seqs, tiles, max_ctx, greedy, record words]
 
 
@@ -72,14 +76,21 @@ class ControlPlane:
         self.host = buf if host is None else host
         self.capacity = buf.numel() - CTRL_WORDS
         self.ctrl = torch.zeros(CTRL_WORDS, dtype=torch.int32)
+        self._staged = None  # CUDA event after the last host->device copy out of `host`
 
     def send(self, op: int, rec=None, bounds=None, greedy: int = 0) -> int:
         """Rank 0: broadcast one message; returns the bytes staged host->device."""
+        import torch
         import torch.distributed as dist
 
         n = 0 if rec is None else int(rec.size)
         if n > self.capacity:
             raise ValueError(f"step record of {n} words exceeds the broadcast buffer ({self.capacity})")
+        if self._staged is not None:
+            # the previous message's copy out of the pinned staging buffer is
+            # asynchronous: let it finish before the buffer is overwritten
+            self._staged.synchronize()
+            self._staged = None
         if n:
             self.host[:n].numpy()[:] = rec
         b = bounds or StepBounds(0, 0, 0, 0, 1)
@@ -90,6 +101,9 @@ class ControlPlane:
                 self.buf[:n].copy_(self.host[:n], non_blocking=True)
             self.buf[-CTRL_WORDS:].copy_(self.host[-CTRL_WORDS:], non_blocking=True)
             staged = 4 * (n + CTRL_WORDS)
+            if self.buf.is_cuda:
+                self._staged = torch.cuda.Event()
+                self._staged.record()
         dist.broadcast(self.buf, src=0)
         return staged
 
@@ -104,13 +118,14 @@ class ControlPlane:
         return c[0], StepBounds(*c[1:6]), c[6], c[7]
 
 
-def serve(plane: ControlPlane, forward, mark) -> int:
+def serve(plane: ControlPlane, forward, mark, gather=None) -> int:
     """Worker dispatch loop: forward(bounds, greedy) for each OP_FORWARD,
-    mark(tag) for each OP_MARK, return the number of passes at OP_STOP.
-    An unknown op is a protocol error (rank 0 never sends one)."""
+    mark(tag) for each OP_MARK, gather(n) for each OP_GATHER (the n row
+    indices sit in the broadcast buffer), return the number of passes at
+    OP_STOP. An unknown op is a protocol error (rank 0 never sends one)."""
     passes = 0
     while True:
-        op, bounds, greedy, _ = plane.recv()
+        op, bounds, greedy, n = plane.recv()
         if op == OP_STOP:
             return passes
         if op == OP_MARK:
@@ -118,8 +133,24 @@ def serve(plane: ControlPlane, forward, mark) -> int:
         elif op == OP_FORWARD:
             forward(bounds, greedy)
             passes += 1
+        elif op == OP_GATHER and gather is not None:
+            gather(n)
         else:
             raise RuntimeError(f"tensor-parallel control: unknown op {op}")
+
+
+def gather_vocab_rows(local, world: int):
+    """Every rank's vocabulary slice of the same rows -> the full rows.
+    local: [n, V/world] on this rank; returns [n, V] with rank r's slice at
+    columns [r*V/world, (r+1)*V/world) (the lm_head row split of vllt.llama),
+    identical on every rank. One all-gather."""
+    import torch
+    import torch.distributed as dist
+
+    n, vl = local.shape
+    parts = torch.empty((world * n, vl), dtype=local.dtype, device=local.device)  # rank-major
+    dist.all_gather_into_tensor(parts, local.contiguous())
+    return parts.view(world, n, vl).permute(1, 0, 2).reshape(n, world * vl).contiguous()
 
 
 def merge_argmax(vals, idxs):
@@ -198,6 +229,25 @@ class TPLlamaRunner(LlamaRunner):
         dist.all_gather_into_tensor(idxs, self._idx[:R])
         return merge_argmax(vals.view(n, R), idxs.view(n, R))
 
+    def gather_rows(self, rows):
+        """Rank 0: full-vocabulary fp32 logits of the given logit rows of the
+        last pass, [len(rows), V] on this device. Every rank takes part (the
+        row list travels in one OP_GATHER message)."""
+        rows = np.asarray(rows, np.int32)
+        if rows.size == 0 or rows.min() < 0 or rows.max() >= self._pending_rows:
+            raise IndexError("gather_rows: row outside the last pass's logit rows")
+        self._broadcast(OP_GATHER, rows)
+        return self._gather(int(rows.size))
+
+    def _gather(self, n: int):
+        """This rank's slice of the n rows listed at the head of the broadcast
+        buffer, all-gathered into full rows."""
+        import torch
+
+        idx = self.rec_dev[:n].to(torch.int64)
+        local = self.logits_dev.index_select(0, idx)[:, :self.w.vocab_local]
+        return gather_vocab_rows(local, self.group.world)
+
     def stop_workers(self):
         self._broadcast(OP_STOP)
 
@@ -247,4 +297,8 @@ class TPLlamaRunner(LlamaRunner):
                 self.greedy_picks(bounds.rows)
             torch.cuda.current_stream(self.dev).synchronize()
 
-        return serve(self.plane, forward, self._record_mark)
+        def gather(n):
+            self._gather(n)
+            torch.cuda.current_stream(self.dev).synchronize()
+
+        return serve(self.plane, forward, self._record_mark, gather)
