@@ -248,3 +248,24 @@ def test_llama_workload_has_the_benchmark_shape():
     assert plen.min() >= 32 and plen.max() <= 8192 and olen.min() >= 16 and olen.max() <= 1024
     assert 900 < plen.mean() < 1150 and 220 < olen.mean() < 290
     assert max(max(p) for p, _ in a) < 128256 and min(min(p) for p, _ in a) >= 0
+
+
+def test_sources_hold_no_peer_memory_access():
+    """No kernel or host file of the product maps or dereferences another
+    GPU's memory: a fused all-reduce over CUDA IPC mappings faulted a GPU on
+    this pool with a cause that reading did not find, so cross-GPU data moves
+    through NCCL only. Every source that travels with the package is checked
+    for the calls and instructions such code needs."""
+    import glob
+
+    banned = ("cudaIpcOpenMemHandle", "cudaIpcGetMemHandle", "cuMemImportFromShareableHandle",
+              "multimem.", ".multicast::cluster", "ld.acquire.sys", "st.release.sys",
+              "cudaDeviceEnablePeerAccess", "cuMulticast")
+    files = (glob.glob(os.path.join(ROOT, "vllm-lite_b200", "csrc", "*")) +
+             glob.glob(os.path.join(ROOT, "vllm-lite_b200", "vllt", "*.py")) +
+             [os.path.join(ROOT, "include", "vllt.h"), os.path.join(ROOT, "bench.py")])
+    assert len(files) > 20
+    for f in files:
+        src = open(f, errors="replace").read()
+        for b in banned:
+            assert b not in src, f"{os.path.relpath(f, ROOT)} names {b}"
