@@ -162,12 +162,13 @@ int vllt_paged_attention_varlen(const void* q, const void* k_cache, const void* 
  *     rejected with VLLT_ERR_ARG.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress, with that device current); make that first call
- *     before any stream capture.
+ *     before any stream capture. The address is kept for the process: after
+ *     cudaDeviceReset on a device, do not call this entry point on it again.
  *   - Every call shares the one array and it keeps the last call's contents;
  *     the error word is cleared at the start of each call. Calls that overlap
  *     on the GPU (other streams, other threads) race on it: serialize them.
  *   - device_flags (optional device int32) receives the call's error flags
- *     (bit 2: a bounded wait on a TMA copy expired).
+ *     (bit 2: a bounded wait on a TMA copy expired); an empty batch writes 0.
  * Allocates nothing: no cudaMalloc / cudaFree, no allocating library call. */
 int vllt_paged_attention_varlen_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                         const int32_t* block_tables, int32_t table_width,

@@ -452,3 +452,46 @@ def test_attention_prefill_tensor_core(dev, H, KV):
                                              max(ctxs), H, KV, D, bs, tk.shape[0], float(scale), _lib.VLLT_BF16,
                                              out.data_ptr(), None, 0, _lib.stream_handle()))
     np.testing.assert_allclose(got, out.float().cpu().numpy(), rtol=2e-2, atol=2e-2)
+
+
+def test_decode_benchmark_setup_matches_oracle(dev):
+    """The paged-attention decode microbenchmark exactly as bench.py builds it
+    (256 sequences, contexts U[1, 4096] from seed 0, 32 / 8 heads, head_dim
+    128, bf16, block 16, tables a random permutation of the pool): one new
+    token per sequence written through reshape_and_cache, then the TMA decode
+    kernel with its 1024-token split-K and merge. Every sequence (all whose
+    context crosses a split boundary, and the short ones) is compared with
+    the float64 oracle on the same bf16 cache, within the bf16 bar of this
+    file (rtol 2e-2, atol 2e-2); the error flag must stay clear."""
+    import bench
+
+    s = bench.decode_setup(torch, dev)
+    from vllt import _lib
+
+    nbytes = _lib.lib().vllt_attention_workspace_bytes(s["seqs"], s["H"], s["D"], s["max_ctx"])
+    ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(s["q"])
+    bench.decode_write(s)
+    bench.decode_attend(s, ws, out)
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32).item()) == 0
+    ctx = s["ctx"].cpu().numpy()
+    tables = s["tables"].cpu().numpy()
+    q = s["q"].float().cpu().numpy()
+    got = out.float().cpu().numpy()
+    bs, KV, D = s["bs"], s["KV"], s["D"]
+    assert (ctx > 1024).sum() > 150 and (ctx <= 1024).sum() > 30  # split and unsplit sequences
+    for i in range(s["seqs"]):
+        n = (int(ctx[i]) + bs - 1) // bs
+        idx = torch.from_numpy(tables[i, :n].astype(np.int64)).to(dev)
+        # [n, KV, bs, D] -> token-major [n * bs, KV, D], first ctx tokens
+        k = s["kc"].index_select(0, idx).float().permute(0, 2, 1, 3).reshape(n * bs, KV, D)[:ctx[i]]
+        v = s["vc"].index_select(0, idx).float().permute(0, 2, 1, 3).reshape(n * bs, KV, D)[:ctx[i]]
+        want = A.dense_attention(q[i:i + 1], k.cpu().numpy(), v.cpu().numpy(), KV, 1.0 / np.sqrt(D))
+        np.testing.assert_allclose(got[i:i + 1], want, rtol=2e-2, atol=2e-2, err_msg=f"sequence {i}")
+    # the new token landed in the cache at position ctx - 1
+    last = ctx - 1
+    slot_blk = tables[np.arange(s["seqs"]), last // bs]
+    kc_new = s["kc"][torch.from_numpy(slot_blk.astype(np.int64)).to(dev), :, torch.from_numpy(
+        (last % bs).astype(np.int64)).to(dev)]
+    np.testing.assert_array_equal(kc_new.float().cpu().numpy(), s["knew"].float().cpu().numpy())

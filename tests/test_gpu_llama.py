@@ -4,10 +4,23 @@ The reference has no bf16 path and no checkpoint at this shape; the bf16 model
 is validated against the fp32 parity path (itself pinned to the reference's
 NumPy forward) running the SAME weights (the bf16 values, widened to fp32).
 
-Stated tolerance: max |logit_bf16 - logit_fp32| <= 5e-2 * max |logit_fp32| per
-step, and the greedy pick agrees on every row whose fp32 top-1 / top-2 gap is
-larger than twice that step's measured error (rows closer than that are
-near-ties that bf16 rounding of the activations may legitimately flip).
+Stated tolerances, each three times the worst error measured for the same
+schedule by oracle/llama_bf16.py (a CPU restatement of this forward's bf16
+rounding points run against its fp32 arithmetic, weights of the same
+N(0, 0.02) law; `python tests/bf16_bars.py` reprints the measurements):
+  * small model (2 layers, d 1024, 8 / 2 heads, vocab 1000): measured 6.3e-3
+    max |logit_bf16 - logit_fp32| / max |logit_fp32| (6.3e-3 per-row relative
+    norm) over five weight seeds -> bar 2e-2 on both;
+  * full-width 2-layer slice (d 4096, 32 / 8 heads, FFN 14336, vocab 128256):
+    measured 1.2e-2 (1.24e-2) -> bar 4e-2;
+  * the same slice with two sequences past 4096 tokens of context, each
+    prefilled in two chunks (the second over a cached prefix of 2100 / 4000
+    tokens), then decode and verify rows at contexts 4501 and 8104: measured
+    1.21e-2 (1.30e-2) -> bar 4e-2.
+A planted mistake shows the margin: zeroing one attention head in every layer
+moves the logits by 0.28-0.69 in both measures (oracle/llama_bf16.py,
+tests/test_bf16_error_model.py). The greedy pick must also agree on every row
+whose fp32 top-1 / top-2 gap is larger than twice that step's measured error.
 """
 
 import numpy as np
@@ -18,6 +31,10 @@ from tests import fixtures as F
 pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
+
+SMALL_BAR = 2e-2
+FULL_BAR = 4e-2
+LONG_BAR = 4e-2
 
 
 def schedule(vocab, rng):
@@ -39,24 +56,48 @@ def schedule(vocab, rng):
     ]
 
 
-def compare(shape):
+def long_schedule(vocab, rng):
+    """Contexts past 4096 with cached prefixes (the C4 workload's long
+    prompts, up to the 9216-token max_seq_len): sequence A is prefilled as
+    2100 + 2400 tokens, B as 4000 + 4100; then A decodes one token and B
+    verifies three drafts (rows at contexts 8101..8104). Block tables are
+    a shuffled pool of 800 blocks."""
+    def toks(n):
+        return [int(t) for t in rng.integers(0, vocab, size=n)]
+
+    pool = [int(x) for x in rng.permutation(800)]
+    A, B = pool[:282], pool[282:282 + 507]
+    a, b = toks(4501), toks(8104)
+    return [
+        [dict(start=0, n=2100, count=1, tokens=a[:2100], block_ids=A, drafts=[]),
+         dict(start=0, n=4000, count=1, tokens=b[:4000], block_ids=B, drafts=[])],
+        [dict(start=2100, n=2400, count=1, tokens=a[2100:4500], block_ids=A, drafts=[]),
+         dict(start=4000, n=4100, count=1, tokens=b[4000:8100], block_ids=B, drafts=[])],
+        [dict(start=4500, n=1, count=1, tokens=a[4500:], block_ids=A, drafts=[]),
+         dict(start=8100, n=4, count=4, tokens=b[8100:], block_ids=B, drafts=b[8101:])],
+    ]
+
+
+def compare(shape, passes=None, num_blocks=64, max_tokens=256):
     from types import SimpleNamespace
 
     from vllt.llama import LlamaRunner, fp32_reference_weights
     from vllt.runner import CudaRunner
 
-    cache = SimpleNamespace(block_size=16, num_blocks=64)
-    bf = LlamaRunner(shape, cache, max_seqs=8, max_tokens=256)
-    ref = CudaRunner(shape, cache, max_seqs=8, max_tokens=256, weights=fp32_reference_weights(shape, bf.dev))
-    rng = np.random.default_rng(3)
-    worst, agree, rows, decided = 0.0, 0, 0, 0
-    for seqs in schedule(shape.vocab_size, rng):
+    cache = SimpleNamespace(block_size=16, num_blocks=num_blocks)
+    bf = LlamaRunner(shape, cache, max_seqs=8, max_tokens=max_tokens)
+    ref = CudaRunner(shape, cache, max_seqs=8, max_tokens=max_tokens, weights=fp32_reference_weights(shape, bf.dev))
+    if passes is None:
+        passes = schedule(shape.vocab_size, np.random.default_rng(3))
+    worst, worst_row, agree, rows, decided = 0.0, 0.0, 0, 0, 0
+    for seqs in passes:
         out = F.as_scheduler_output(seqs)
         a, _ = bf.execute(out)
         b, _ = ref.execute(out)
         assert a.shape == b.shape and np.isfinite(a).all()
         err = np.abs(a - b).max()
         worst = max(worst, float(err / np.abs(b).max()))
+        worst_row = max(worst_row, float((np.linalg.norm(a - b, axis=1) / np.linalg.norm(b, axis=1)).max()))
         top2 = np.sort(b, axis=1)[:, -2:]
         clear = (top2[:, 1] - top2[:, 0]) > 2 * err
         same = a.argmax(1) == b.argmax(1)
@@ -64,7 +105,7 @@ def compare(shape):
         agree += int(same.sum())
         decided += int(clear.sum())
         rows += a.shape[0]
-    return worst, agree / rows, decided
+    return worst, worst_row, agree / rows, decided
 
 
 def test_bf16_small_llama_matches_fp32_rerun():
@@ -72,19 +113,34 @@ def test_bf16_small_llama_matches_fp32_rerun():
 
     shape = LlamaShape(n_layers=2, n_heads=8, n_kv_heads=2, d_model=1024, d_ff=2048, vocab_size=1000,
                        max_seq_len=2048, seed=1)
-    worst, agree, decided = compare(shape)
-    print(f"small llama: max rel logit err {worst:.3e}, greedy agreement {agree:.2%}, {decided} clear rows")
-    assert worst <= 5e-2
+    worst, worst_row, agree, decided = compare(shape)
+    print(f"small llama: max rel logit err {worst:.3e}, row rel {worst_row:.3e}, greedy agreement {agree:.2%}, "
+          f"{decided} clear rows")
+    assert worst <= SMALL_BAR and worst_row <= SMALL_BAR
 
 
 def test_bf16_llama8b_two_layer_slice_matches_fp32_rerun():
     from vllt.llama import LlamaShape
 
     shape = LlamaShape(n_layers=2, max_seq_len=2048)  # full width: d 4096, 32/8 heads, ffn 14336, vocab 128256
-    worst, agree, decided = compare(shape)
-    print(f"llama-8b 2-layer slice: max rel logit err {worst:.3e}, greedy agreement {agree:.2%}, "
-          f"{decided} clear rows")
-    assert worst <= 5e-2
+    worst, worst_row, agree, decided = compare(shape)
+    print(f"llama-8b 2-layer slice: max rel logit err {worst:.3e}, row rel {worst_row:.3e}, "
+          f"greedy agreement {agree:.2%}, {decided} clear rows")
+    assert worst <= FULL_BAR and worst_row <= FULL_BAR
+
+
+def test_bf16_llama8b_long_context_prefill_over_cached_prefix():
+    """Prefill chunks whose context passes 4096 tokens on top of a cached
+    prefix (tensor-core prefill tiles reading thousands of cached keys), then
+    decode and verify rows near the 9216-token max_seq_len."""
+    from vllt.llama import LlamaShape
+
+    shape = LlamaShape(n_layers=2, max_seq_len=9216)
+    passes = long_schedule(shape.vocab_size, np.random.default_rng(8))
+    worst, worst_row, agree, decided = compare(shape, passes, num_blocks=800, max_tokens=8192)
+    print(f"llama-8b long context: max rel logit err {worst:.3e}, row rel {worst_row:.3e}, "
+          f"greedy agreement {agree:.2%}, {decided} clear rows")
+    assert worst <= LONG_BAR and worst_row <= LONG_BAR
 
 
 def test_llama_engine_serves_requests_to_completion():

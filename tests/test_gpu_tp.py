@@ -2,8 +2,10 @@
 
 Runs tests/tp_parity.py under torchrun on two GPUs (one process each, NCCL,
 NVLS off as for every multi-rank test here). Skipped on a 1-GPU box.
-Tolerance: logits of this rank's vocabulary slice within 5e-2 of the 1-GPU
-logits' max magnitude (the bf16 all-reduce reorders the sums), greedy picks
+Tolerance: logits of this rank's vocabulary slice, and the full rows gathered
+from both ranks, within 3e-2 of the 1-GPU logits' max magnitude: three times the
+9.3e-3 that oracle/llama_bf16.py measures for two bf16 ranks against one on
+this schedule (the partials are rounded and summed in bf16); greedy picks
 equal on all rows but at most one near-tie.
 """
 

@@ -5,9 +5,11 @@ device memory (a framework allocator owns the GPU, a hard memory cap, or a hot
 loop where cudaMalloc's device synchronization is not acceptable). It keeps
 its split-K scratch in a static device array inside the library. Here it is
 called through the C ABI, twice in a row on different inputs (the array keeps
-the previous call's contents), and each output is compared with the
-workspace-taking entry point `vllt_paged_attention_varlen` within the
-tolerances the other attention tests use. The file sorts last so a run that
+the previous call's contents), and each output must equal, bit for bit, the
+workspace-taking entry point `vllt_paged_attention_varlen` on the same inputs
+(both run the same kernels with the same split-K decisions): the TMA decode
+kernel's splits, the generic kernel's single-query splits and a mixed batch of
+prefill tiles. An empty batch must still clear the caller's flag word. The file sorts last so a run that
 stops at the first failure has already run every other test; it also passes
 alone in a fresh process (the first call sets the scratch address up).
 """
@@ -67,8 +69,11 @@ def _no_alloc(L, c, flags):
     return out
 
 
-@pytest.mark.parametrize("kind", ["bf16-decode", "f32-mixed"])
+@pytest.mark.parametrize("kind", ["bf16-decode", "f32-decode", "f32-mixed"])
 def test_no_alloc_entry_matches_workspace_entry(kind):
+    """Both entry points run the same kernels with the same split decisions
+    (the static scratch and the caller's workspace both hold every split's
+    partials), so the outputs must be bit-identical, call after call."""
     from vllt import _lib
 
     assert torch.cuda.is_available(), "needs a CUDA device"
@@ -77,17 +82,29 @@ def test_no_alloc_entry_matches_workspace_entry(kind):
     rng = np.random.default_rng(21)
     flags = torch.full((1,), -1, dtype=torch.int32, device="cuda")
     for call in range(2):  # two calls in a row: the shared scratch must not leak between them
-        if kind == "bf16-decode":  # TMA decode kernel, split-K partials in the scratch
+        if kind == "bf16-decode":  # TMA decode kernel, its split-K partials in the scratch
             c = _case(rng, 32, 8, 128, 16, [1] * 6, [4096, 1, 17, 1500 + call, 2048, 333], torch.bfloat16)
-            tol = 2e-2
-        else:  # generic kernel: decode rows split-K, prefill tiles
+        elif kind == "f32-decode":  # generic kernel, single-query rows: 512-key split-K partials and merge
+            c = _case(rng, 8, 4, 48, 16, [1] * 5, [1300, 600, 2048 + call, 1, 513], torch.float32)
+        else:  # generic kernel, mixed query lengths (max_qlen 20): prefill tiles, no split
             c = _case(rng, 8, 4, 48, 16, [1, 7, 1, 20], [1300, 40, 900 + call, 20], torch.float32)
-            tol = 1e-4
-        want = _with_workspace(L, c).float()
-        got = _no_alloc(L, c, flags).float()
+        want = _with_workspace(L, c)
+        got = _no_alloc(L, c, flags)
         torch.cuda.synchronize()
-        np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), rtol=tol, atol=tol)
+        np.testing.assert_array_equal(got.float().cpu().numpy(), want.float().cpu().numpy())
         assert int(flags.item()) == 0
+
+
+def test_no_alloc_entry_clears_the_flag_word_of_an_empty_batch():
+    from vllt import _lib
+
+    L = _lib.lib()
+    flags = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    _lib.check(L.vllt_paged_attention_varlen_noalloc(None, None, None, None, 1, None, None, 0, 0, 0, 0,
+                                                     8, 4, 48, 16, 4, 0.1, 0, None, flags.data_ptr(),
+                                                     _lib.stream_handle()))
+    torch.cuda.synchronize()
+    assert int(flags.item()) == 0
 
 
 def test_no_alloc_entry_rejects_batches_beyond_its_scratch():

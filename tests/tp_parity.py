@@ -20,6 +20,12 @@ for p in (ROOT, os.path.join(ROOT, "vllm-lite_b200"), os.path.join(ROOT, "baseli
         sys.path.insert(0, p)
 
 import numpy as np  # noqa: E402
+
+# Three times the worst error of two bf16 ranks against one measured by
+# oracle/llama_bf16.py on this schedule and shape (9.3e-3 of the largest
+# |logit|: the partials are rounded to bf16 and summed in bf16 before they
+# join the residual); tests/bf16_bars.py --full reprints the measurement.
+TP_BAR = 3e-2
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
@@ -63,7 +69,7 @@ def main():
             np.testing.assert_array_equal(full[:, :run.w.vocab_local], local_logits[g])
             worst = max(worst, float(np.abs(full - want[g]).max() / np.abs(want).max()))
         run.stop_workers()
-        ok = worst < 5e-2 and agree >= rows - 1
+        ok = worst < TP_BAR and agree >= rows - 1
         print(f"TP_PARITY {'ok' if ok else 'FAIL'} {worst:.3e} {agree}/{rows}", flush=True)
     group.close()
     dist.destroy_process_group()

@@ -1,6 +1,11 @@
 // Paged attention whose scratch memory is a static array owned by the
 // library, for callers that cannot allocate device memory themselves.
 //
+// The device address is looked up once per device and kept for the life of
+// the process; it does not survive cudaDeviceReset (a reset context gets a
+// new module load), so a caller that resets a device must not call this
+// entry point on it again in the same process.
+//
 // Who needs this: code that runs under a device-memory budget owned by someone
 // else (a host framework whose allocator has already claimed the GPU, or a
 // process started with a hard memory cap), code that is not allowed to call
@@ -81,13 +86,19 @@ extern "C" int vllt_paged_attention_varlen_noalloc(
                "paged_attention_noalloc: this batch needs %lld bytes of scratch; the static scratch "
                "holds %lld (use vllt_paged_attention_varlen with a caller workspace)",
                (long long)need, (long long)kStaticScratchBytes);
-  if (num_seqs == 0 || num_tokens == 0) return VLLT_OK;
+  cudaStream_t st = as_stream(stream);
+  if (num_seqs == 0 || num_tokens == 0) {  // nothing to attend: report a clean call
+    if (device_flags && cudaMemsetAsync(device_flags, 0, sizeof(int32_t), st) != cudaSuccess) {
+      set_error("paged_attention_noalloc: clearing the error flags failed");
+      return VLLT_ERR_CUDA;
+    }
+    return VLLT_OK;
+  }
   VLLT_REQUIRE(q && k_cache && v_cache && block_tables && cu_seqlens_q && ctx_lens && out,
                "paged_attention_noalloc: null pointer");
   void* scratch = nullptr;
   int rc = scratch_address(&scratch);
   if (rc != VLLT_OK) return rc;
-  cudaStream_t st = as_stream(stream);
   // the array keeps the previous call's contents: the error word must start at zero
   if (cudaMemsetAsync(scratch, 0, kFlagHeaderBytes, st) != cudaSuccess) {
     set_error("paged_attention_noalloc: clearing the scratch flags failed");
