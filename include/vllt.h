@@ -82,7 +82,22 @@ int vllt_copy_blocks(void* k_cache, void* v_cache, const int32_t* pairs, int32_t
  *   seq_count[S]   logit rows wanted: min(1 + num_drafts, qlen) (runner.py:88)
  *   token_ids[T]   the pushed tokens, sequence after sequence
  *   block_tables[S][W]  physical block ids (BlockTable.block_ids), padded
- * Its length is 4 + 3*S + T + S*W int32 words. */
+ * Its length is 4 + 3*S + T + S*W int32 words.
+ *
+ * The pooled record leaves the block tables on the device. A persistent pool
+ * [pool_slots][max_table_width] int32 (allocated by the caller, contents
+ * initially irrelevant) holds one table per live sequence; each pass carries
+ * only what changed since the last (the blocks BlockManager.append_slots
+ * appended or replaced by copy-on-write, vllmlite/block_manager.py:65-93, or a
+ * whole table when a sequence first takes a slot):
+ *   [0]=S [1]=T [2]=R [3]=W [4]=U (updates)
+ *   seq_start[S], seq_qlen[S], seq_count[S], token_ids[T]   as above
+ *   table_slot[S]  the pool row of each sequence
+ *   updates[U][3]  (pool row, table index, block id), applied before the
+ *                  tables are read; U <= max_seqs * max_table_width
+ * Its length is 5 + 4*S + T + 3*U words. A pass reads entries
+ * [0, ceil(ctx/block_size)) of each sequence's row; the rest of a row is
+ * never read. */
 
 /* Capacities of the buffers one runner allocates once. */
 typedef struct vllt_caps {
@@ -104,6 +119,16 @@ int64_t vllt_meta_bytes(const vllt_caps* caps);
  * slot -1 and sets the device error flag (counter 7, below). */
 int vllt_build_batch_meta(const int32_t* step_record, const vllt_caps* caps, int32_t block_size,
                           int32_t num_blocks, int32_t n_rep, void* meta, void* stream);
+
+/* The same from a pooled record: applies its updates to table_pool
+ * ([pool_slots][caps->max_table_width] int32, device) and reads each
+ * sequence's table from its pool row. An update or a table slot outside the
+ * pool sets error bit 1. No reference counterpart beyond what
+ * vllt_build_batch_meta replaces: it moves the block-table upload of
+ * runner.py:66-90 from S*W words per pass to the changed entries. */
+int vllt_build_batch_meta_pooled(const int32_t* step_record, const vllt_caps* caps, int32_t block_size,
+                                 int32_t num_blocks, int32_t n_rep, int32_t* table_pool, int32_t pool_slots,
+                                 void* meta, void* stream);
 
 /* Device pointers into the meta buffer (for callers that launch their own
  * kernels on it): which = 0 counters[16], 1 cu_seqlens_q[S+1], 2 cu_rows[S+1],
@@ -325,6 +350,11 @@ typedef struct vllt_model_desc {
   /* KV cache base: [n_layers][num_blocks][n_kv][block_size][head_dim], dtype */
   void* k_cache;
   void* v_cache;
+  /* Optional persistent block-table pool [table_pool_slots][caps max_table_width]
+   * (device int32). NULL: step records carry their tables; else vllt_forward
+   * reads pooled records (see vllt_build_batch_meta_pooled). */
+  int32_t* table_pool;
+  int32_t table_pool_slots;
 } vllt_model_desc;
 
 /* Upper bounds of one step, used to size grids (exact counts are read on the

@@ -75,6 +75,27 @@ def test_runner_replay_logits(name, bs):
     assert worst < 1e-4, worst
 
 
+@pytest.mark.parametrize("name,bs", [("replay_bench.npz", 16), ("replay_spec.npz", 4)])
+def test_device_resident_tables_match_uploaded_tables(name, bs):
+    """The runner with its block tables in the device pool (pooled records,
+    the default) and with the whole tables uploaded every pass give
+    bit-identical logits on the reference's replays."""
+    from vllmlite.config import CacheConfig
+
+    from vllt.runner import CudaRunner
+
+    a = CudaRunner(model_cfg(F.BENCH), CacheConfig(block_size=bs, num_blocks=512))
+    b = CudaRunner(model_cfg(F.BENCH), CacheConfig(block_size=bs, num_blocks=512), pooled_tables=False)
+    for seqs, cow, _ in F.replay_steps(name):
+        out = F.as_scheduler_output(seqs, cow)
+        for item, s in zip(out.scheduled, seqs):
+            item.seq.request_id = f"b{s['block_ids'][0]}"
+        la, _ = a.execute(out)
+        lb, _ = b.execute(out)
+        np.testing.assert_array_equal(la, lb)
+    assert a.h2d_bytes < b.h2d_bytes
+
+
 def test_graph_replay_matches_eager():
     """CUDA-graph replays equal eager runs with the same (bucketed) bounds bit
     for bit; against eager runs with exact bounds they differ only by fp32

@@ -331,6 +331,87 @@ def test_batch_meta_flags_bad_tables_without_faulting(dev):
     assert meta[7].item() & 1
 
 
+def _meta_fields(L, meta, caps, S, T, R, W):
+    import ctypes
+
+    base = meta.data_ptr()
+
+    def field(i, n):
+        off = (L.vllt_meta_field(ctypes.c_void_p(base), ctypes.byref(caps), i) - base) // 4
+        return meta[off:off + n].cpu().numpy()
+
+    tabs = field(7, caps.max_seqs * caps.max_table_width).reshape(caps.max_seqs, caps.max_table_width)[:S, :W]
+    return dict(cnt=field(0, 16), cu_q=field(1, S + 1), cu_rows=field(2, S + 1), ctx=field(3, S), pos=field(4, T),
+                slot=field(5, T), rows=field(6, R), tables=tabs)
+
+
+def test_pooled_batch_meta_matches_the_classic_record(dev):
+    """vllt_build_batch_meta_pooled over a persistent device table pool,
+    pass after pass of the reference's replays, builds the same metadata as
+    vllt_build_batch_meta over the classic record (tables compared on the
+    entries each context uses; the pooled builder writes -1 past them)."""
+    import ctypes
+
+    from vllt import _lib
+    from vllt.runner import StepPacker, tile_positions
+
+    L = _lib.lib()
+    for name, bs in (("replay_bench.npz", 16), ("replay_spec.npz", 4)):
+        caps = _lib.Caps(16, 1024, 64, 128)
+        classic = StepPacker(bs, 512, 261, 512, tile_positions(2))
+        pooled = StepPacker(bs, 512, 261, 512, tile_positions(2), pool_slots=32, pool_width=caps.max_table_width)
+        pool = torch.full((32, caps.max_table_width), -1, dtype=torch.int32, device=dev)
+        n_meta = L.vllt_meta_bytes(ctypes.byref(caps)) // 4
+        for seqs, cow, _ in F.replay_steps(name):
+            out = F.as_scheduler_output(seqs, cow)
+            for seq, s in zip(out.scheduled, seqs):  # one request id per sequence, as the engine's
+                seq.seq.request_id = f"b{s['block_ids'][0]}"
+            rc, _, _, (S, T, R, W) = classic.pack(out)
+            rp, _, _, _ = pooled.pack(out)
+            m1 = torch.zeros(n_meta, dtype=torch.int32, device=dev)
+            m2 = torch.zeros(n_meta, dtype=torch.int32, device=dev)
+            d1, d2 = torch.from_numpy(rc).to(dev), torch.from_numpy(rp).to(dev)
+            _lib.check(L.vllt_build_batch_meta(d1.data_ptr(), ctypes.byref(caps), bs, 512, 2, m1.data_ptr(),
+                                               _lib.stream_handle()))
+            _lib.check(L.vllt_build_batch_meta_pooled(d2.data_ptr(), ctypes.byref(caps), bs, 512, 2,
+                                                      pool.data_ptr(), 32, m2.data_ptr(), _lib.stream_handle()))
+            a, b = _meta_fields(L, m1, caps, S, T, R, W), _meta_fields(L, m2, caps, S, T, R, W)
+            assert a["cnt"][7] == 0 and b["cnt"][7] == 0
+            for k in ("cnt", "cu_q", "cu_rows", "ctx", "pos", "slot", "rows"):
+                np.testing.assert_array_equal(a[k], b[k], err_msg=k)
+            used = -(-a["ctx"] // bs)
+            for i in range(S):
+                np.testing.assert_array_equal(a["tables"][i, :used[i]], b["tables"][i, :used[i]])
+                assert (b["tables"][i, used[i]:] == -1).all()
+
+
+def test_pooled_batch_meta_flags_bad_updates_without_faulting(dev):
+    """An update outside the pool, or a sequence whose row holds an id
+    outside [0, num_blocks), raises error bit 1; nothing is written out of
+    bounds (the pool's guard row past the 2 rows it is given stays intact)."""
+    import ctypes
+
+    from vllt import _lib
+
+    L = _lib.lib()
+    caps = _lib.Caps(4, 16, 16, 4)
+    pool = torch.full((3, 4), -7, dtype=torch.int32, device=dev)
+    meta = torch.zeros(L.vllt_meta_bytes(ctypes.byref(caps)) // 4, dtype=torch.int32, device=dev)
+
+    def build(words):
+        rec = torch.from_numpy(np.asarray(words, np.int32)).to(dev)
+        _lib.check(L.vllt_build_batch_meta_pooled(rec.data_ptr(), ctypes.byref(caps), 16, 64, 2, pool.data_ptr(), 2,
+                                                  meta.data_ptr(), _lib.stream_handle()))
+        return int(meta[7].item())
+
+    # S=1 T=3 R=1 W=1 U=1 | start 0 | qlen 3 | count 1 | tokens | slot 1 | update (2, 0, 5): row 2 is outside
+    assert build([1, 3, 1, 1, 1, 0, 3, 1, 256, 1, 2, 1, 2, 0, 5]) & 2
+    assert pool[2].tolist() == [-7] * 4
+    # a valid update, then a row whose entry is out of range
+    assert build([1, 3, 1, 1, 1, 0, 3, 1, 256, 1, 2, 1, 1, 0, 5]) == 0
+    assert build([1, 3, 1, 1, 1, 0, 3, 1, 256, 1, 2, 0, 0, 0, 99]) & 2
+
+
 @pytest.mark.parametrize("dtype,H,KV", [("f32", 32, 8), ("bf16", 32, 8), ("bf16", 8, 8), ("bf16", 16, 8),
                                         ("bf16", 64, 8), ("bf16", 12, 6)])
 def test_attention_decode_split_k(dev, dtype, H, KV):

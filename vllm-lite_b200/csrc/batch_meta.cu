@@ -60,16 +60,23 @@ __device__ __forceinline__ int upper_index(const int32_t* a, int n, int key) {
   return lo;
 }
 
+// `pool` (NULL: the record carries the tables) is the persistent block-table
+// pool [pool_slots][L.W_cap]: the record then carries, after the tokens, each
+// sequence's pool slot and a list of (slot, index, block id) updates that
+// this kernel applies to the pool before it reads the tables through the
+// slots (the record layout is in include/vllt.h).
 __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __restrict__ rec,
                                                               MetaLayout L, int bs, int num_blocks,
-                                                              int qp, int32_t* __restrict__ meta) {
+                                                              int qp, int32_t* __restrict__ meta,
+                                                              int32_t* __restrict__ pool, int pool_slots) {
   __shared__ int4 warp_tot[32];
   __shared__ int4 total;
   __shared__ int s_max_ctx, s_max_q, s_err;
   const int S = rec[0], T = rec[1], R = rec[2], W = rec[3];
+  const int U = pool ? rec[4] : 0;  // pool updates carried by this record
   int32_t* cnt = meta;
   const bool fits = S >= 0 && T >= 0 && R >= 0 && W >= 0 && S <= L.S_cap && T <= L.T_cap &&
-                    R <= L.R_cap && W <= L.W_cap;
+                    R <= L.R_cap && W <= L.W_cap && U >= 0 && (int64_t)U <= (int64_t)L.S_cap * L.W_cap;
   if (!fits) {  // uniform across the CTA: every thread takes this branch
     if (threadIdx.x == 0) {
       for (int i = 0; i < kCntWords; ++i) cnt[i] = 0;
@@ -77,17 +84,31 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
     }
     return;
   }
-  const int32_t* start = rec + 4;
+  const int32_t* start = rec + (pool ? 5 : 4);
   const int32_t* qlen = start + S;
   const int32_t* count = qlen + S;
   const int32_t* tokens = count + S;
-  const int32_t* tables = tokens + T;
+  const int32_t* tables = tokens + T;       // record tables [S][W] (no pool)
+  const int32_t* seq_slot = tokens + T;     // pool slot of each sequence (pool)
+  const int32_t* updates = seq_slot + S;    // [U][3] (slot, index, block) (pool)
   int32_t* cu_q = meta + L.cu_q;
   int32_t* cu_rows = meta + L.cu_rows;
   int32_t* ctx = meta + L.ctx;
   int32_t* mstart = meta + L.start;
   if (threadIdx.x == 0) { s_max_ctx = 0; s_max_q = 0; s_err = 0; }
   __syncthreads();
+
+  // Phase 0 (pool): apply this pass's block-table changes. An update outside
+  // the pool flags the step (bit 1) and is dropped.
+  for (int u = threadIdx.x; u < U; u += kThreads) {
+    const int sl = updates[3 * u], j = updates[3 * u + 1], blk = updates[3 * u + 2];
+    if (sl < 0 || sl >= pool_slots || j < 0 || j >= L.W_cap) {
+      atomicOr(&s_err, 2);
+      continue;
+    }
+    pool[(int64_t)sl * L.W_cap + j] = blk;
+  }
+  __syncthreads();  // the pool writes above are visible to every thread of the CTA below
 
   // Phase 1: exclusive scans over sequences of (qlen, count, is_decode, tiles).
   int32_t* cu_tiles = meta + L.cu_tiles;
@@ -129,12 +150,24 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
     return;
   }
 
-  // Phase 2: block tables into the fixed-width copy, validated.
+  // Phase 2: block tables into the fixed-width copy, validated. From the pool,
+  // only the entries a sequence's context uses are read (the rest of a pool
+  // row may hold a previous owner's ids); the others become -1.
   for (int i = threadIdx.x; i < S * W; i += kThreads) {
     const int s = i / W, b = i % W;
-    int blk = tables[i];
     const int used = ceil_div(ctx[s], bs);
-    if (b < used && (blk < 0 || blk >= num_blocks)) { atomicOr(&s_err, 2); blk = -1; }
+    int blk;
+    if (pool) {
+      blk = -1;
+      if (b < used) {
+        const int sl = seq_slot[s];
+        if (sl >= 0 && sl < pool_slots) blk = pool[(int64_t)sl * L.W_cap + b];
+        if (blk < 0 || blk >= num_blocks) { atomicOr(&s_err, 2); blk = -1; }
+      }
+    } else {
+      blk = tables[i];
+      if (b < used && (blk < 0 || blk >= num_blocks)) { atomicOr(&s_err, 2); blk = -1; }
+    }
     meta[L.tables + (int64_t)s * L.W_cap + b] = blk;
   }
   __syncthreads();
@@ -181,10 +214,11 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
 }  // namespace
 
 int build_batch_meta(const int32_t* rec, const MetaLayout& L, int bs, int num_blocks, int qp,
-                     int32_t* meta, cudaStream_t st) {
+                     int32_t* meta, cudaStream_t st, int32_t* pool, int pool_slots) {
   VLLT_REQUIRE(rec && meta, "build_batch_meta: null pointer");
   VLLT_REQUIRE(bs > 0 && num_blocks > 0 && qp > 0, "build_batch_meta: bad sizes");
-  build_meta_kernel<<<1, kThreads, 0, st>>>(rec, L, bs, num_blocks, qp, meta);
+  VLLT_REQUIRE(!pool || pool_slots > 0, "build_batch_meta: a table pool needs at least one slot");
+  build_meta_kernel<<<1, kThreads, 0, st>>>(rec, L, bs, num_blocks, qp, meta, pool, pool ? pool_slots : 0);
   return check_launch("build_batch_meta");
 }
 

@@ -94,6 +94,7 @@ int check_desc(const vllt_model_desc* m) {
   VLLT_REQUIRE(m->tp_size >= 1 && (m->tp_size == 1 || m->dtype == VLLT_BF16),
                "vllt_forward: tensor parallelism is built for the bf16 model only");
   VLLT_REQUIRE(m->embed_rows >= (m->tp_size == 1 ? m->vocab : 1), "vllt_forward: embed_rows too small");
+  VLLT_REQUIRE(!m->table_pool || m->table_pool_slots > 0, "vllt_forward: table_pool needs table_pool_slots > 0");
   VLLT_REQUIRE(m->n_layers > 0 && m->n_heads > 0 && m->n_kv_heads > 0 &&
                    m->n_heads % m->n_kv_heads == 0 && m->head_dim > 0 && m->d_model > 0 &&
                    m->d_ff > 0 && m->vocab > 0 && m->vocab_padded >= m->vocab &&
@@ -137,7 +138,8 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   const float eps = m->rms_eps;
 
   VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks,
-                            query_tile_positions(VLLT_F32, D, m->block_size, n_rep), meta, st));
+                            query_tile_positions(VLLT_F32, D, m->block_size, n_rep), meta, st, m->table_pool,
+                            m->table_pool_slots));
   VLLT_TRY(embed(reinterpret_cast<const float*>(m->tok_emb), meta + L.tokens, w.x, T_cap, T_dev, d, m->vocab, st));
 
   AttnCall ac{};
@@ -241,6 +243,17 @@ int vllt_build_batch_meta(const int32_t* step_record, const vllt_caps* caps, int
   VLLT_REQUIRE(n_rep > 0, "build_batch_meta: bad n_rep");
   return build_batch_meta(step_record, layout_of(caps), block_size, num_blocks, tile_positions(n_rep),
                           reinterpret_cast<int32_t*>(meta), as_stream(stream));
+}
+
+int vllt_build_batch_meta_pooled(const int32_t* step_record, const vllt_caps* caps, int32_t block_size,
+                                 int32_t num_blocks, int32_t n_rep, int32_t* table_pool, int32_t pool_slots,
+                                 void* meta, void* stream) {
+  clear_error();
+  VLLT_REQUIRE(caps_ok(caps), "build_batch_meta: bad capacities");
+  VLLT_REQUIRE(n_rep > 0, "build_batch_meta: bad n_rep");
+  VLLT_REQUIRE(table_pool && pool_slots > 0, "build_batch_meta: the pooled record needs a table pool");
+  return build_batch_meta(step_record, layout_of(caps), block_size, num_blocks, tile_positions(n_rep),
+                          reinterpret_cast<int32_t*>(meta), as_stream(stream), table_pool, pool_slots);
 }
 
 int32_t* vllt_meta_field(void* meta, const vllt_caps* caps, int32_t which) {

@@ -101,7 +101,8 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
   const bool tp = m->tp_size > 1;
 
   VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks,
-                            query_tile_positions(VLLT_BF16, D, m->block_size, n_rep), meta, st));
+                            query_tile_positions(VLLT_BF16, D, m->block_size, n_rep), meta, st, m->table_pool,
+                            m->table_pool_slots));
   VLLT_TRY(embed_bf16(m->tok_emb, meta + L.tokens, w.x, T_cap, T_dev, d, m->embed_rows, st));
 
   AttnCall ac{};

@@ -60,7 +60,9 @@ struct MetaLayout {
 __host__ __device__ inline int tile_positions(int n_rep) { return n_rep >= 16 ? 1 : 16 / n_rep; }
 
 // qp: query positions per multi-token attention tile (see query_tile_positions).
+// pool: persistent block-table pool [pool_slots][L.W_cap] for records in the
+// pooled layout (NULL for records that carry their tables).
 int build_batch_meta(const int32_t* rec, const MetaLayout& L, int bs, int num_blocks, int qp,
-                     int32_t* meta, cudaStream_t st);
+                     int32_t* meta, cudaStream_t st, int32_t* pool = nullptr, int pool_slots = 0);
 
 }  // namespace vllt

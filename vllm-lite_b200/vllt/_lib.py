@@ -37,7 +37,7 @@ class ModelDesc(C.Structure):
         ("rms_eps", f32), ("dtype", i32), ("tp_size", i32), ("embed_rows", i32), ("tp_comm", vp),
         ("tok_emb", vp), ("final_norm", vp), ("lm_head", vp), ("rope_cos", vp), ("rope_sin", vp),
         ("attn_norm", PP), ("wqkv", PP), ("wo", PP), ("ffn_norm", PP), ("w_gu", PP), ("w_down", PP),
-        ("k_cache", vp), ("v_cache", vp),
+        ("k_cache", vp), ("v_cache", vp), ("table_pool", vp), ("table_pool_slots", i32),
     ]
 
 
@@ -50,6 +50,7 @@ SIGNATURES = {
     "vllt_copy_blocks": (C.c_int, [vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp]),
     "vllt_meta_bytes": (i64, [C.POINTER(Caps)]),
     "vllt_build_batch_meta": (C.c_int, [vp, C.POINTER(Caps), i32, i32, i32, vp, vp]),
+    "vllt_build_batch_meta_pooled": (C.c_int, [vp, C.POINTER(Caps), i32, i32, i32, vp, i32, vp, vp]),
     "vllt_meta_field": (vp, [vp, C.POINTER(Caps), i32]),
     "vllt_attention_workspace_bytes": (i64, [i32, i32, i32, i32]),
     "vllt_paged_attention_varlen": (C.c_int, [vp, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, i32,

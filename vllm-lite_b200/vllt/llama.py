@@ -175,9 +175,10 @@ class LlamaRunner(CudaRunner):
         (weights + KV read/written) / HBM bandwidth and (GEMM + attention
         FLOPs) / tensor peak. Attention FLOPs count the causal pairs only."""
         cfg, n = self.model_cfg, self.tp_size
-        S, T, R = int(rec[0]), int(rec[1]), int(rec[2])
-        starts = rec[4:4 + S].astype(np.int64)
-        qlens = rec[4 + S:4 + 2 * S].astype(np.int64)
+        f = self.packer.fields(rec)
+        T, R = f["T"], f["R"]
+        starts = f["start"].astype(np.int64)
+        qlens = f["qlen"].astype(np.int64)
         ctx = starts + qlens
         d, f, D = cfg.d_model, cfg.d_ff, self.head_dim
         layer_params = d * (cfg.n_heads + 2 * cfg.n_kv_heads) * D + d * cfg.n_heads * D + 3 * d * f

@@ -6,9 +6,10 @@ constructor arguments (ModelConfig, CacheConfig), same
 `vocab_size` and `cache_bytes`. It
   * applies `out.cow` before any KV write (runner.py:63-64) with one copy kernel;
   * packs the step (per-sequence start / qlen / logit count, the pushed token
-    ids and the block tables) into one int32 record, uploads it with one
-    host-to-device copy, and lets the device build positions, slots and rows
-    (runner.py:66-90);
+    ids and the block-table entries that changed since the last pass; the
+    tables themselves stay in a persistent device pool) into one int32 record,
+    uploads it with one host-to-device copy, and lets the device build
+    positions, slots and rows (runner.py:66-90);
   * runs the whole TinyLlama forward (model.py:80-120) in libvllt with one call;
   * downloads only the logit rows.
 
@@ -67,26 +68,64 @@ def _tokens(seq, start: int, n: int) -> list:
     return out
 
 
+def record_fields(rec, pooled: bool) -> dict:
+    """Named views of a packed step record (layouts in include/vllt.h)."""
+    S, T, R, W = (int(x) for x in rec[:4])
+    U = int(rec[4]) if pooled else 0
+    o = 5 if pooled else 4
+    f = dict(S=S, T=T, R=R, W=W, U=U, start=rec[o:o + S], qlen=rec[o + S:o + 2 * S],
+             count=rec[o + 2 * S:o + 3 * S], tokens=rec[o + 3 * S:o + 3 * S + T])
+    o += 3 * S + T
+    if pooled:
+        f["slot"] = rec[o:o + S]
+        f["updates"] = rec[o + S:o + S + 3 * U].reshape(U, 3)
+    else:
+        f["tables"] = rec[o:o + S * W].reshape(S, W)
+    return f
+
+
 class StepPacker:
     """Host side of the batch flatten: SchedulerOutput -> (record int32 words,
     StepBounds, rows, (S, T, R, W)).
 
     Reads exactly what vllmlite/runner.py:72-90 reads: item.start_pos,
     item.num_tokens, seq.token_ids (via _tokens), seq.draft_token_ids,
-    seq.table.block_ids. The record layout is documented in include/vllt.h.
+    seq.table.block_ids. The record layouts are documented in include/vllt.h.
     Metadata the reference would fail on (NumPy IndexError) raises here, before
     anything reaches the device.
 
-    Block tables are cached per sequence as int32 arrays between passes: only
-    entries from the block being written onward can change (appended blocks, a
-    copy-on-write replacement, block_manager.py:77-93), so only those are
-    copied and validated; a table replaced after preemption or retirement
-    (a new BlockTable object) is reloaded whole.
-    """
+    Only entries from the block being written onward can change between two
+    passes of a sequence whose BlockTable object stays the same: blocks are
+    appended, or the block at num_filled // block_size (= start_pos //
+    block_size) is replaced by copy-on-write (block_manager.py:65-93); a table
+    replaced after preemption or retirement is a new object.
 
-    def __init__(self, block_size: int, num_blocks: int, vocab: int, max_pos: int, qp: int):
+    Classic record (pool_slots == 0): block tables are cached per sequence
+    between passes, only the changed suffix is copied and validated, and the
+    whole S x W table goes into the record.
+
+    Pooled record (pool_slots > 0): the tables stay on the device in a
+    persistent pool of pool_slots rows of pool_width ids. Each live sequence
+    holds a row (keyed by request id; the least recently scheduled sequence
+    gives its row up when none is free). The packer keeps a mirror of every
+    row as the device holds it (-1 where unknown, the pool's initial value)
+    and emits (row, index, block id) only for entries whose value differs:
+    per decode pass that is the new or copied-on-write block, if any."""
+
+    def __init__(self, block_size: int, num_blocks: int, vocab: int, max_pos: int, qp: int,
+                 pool_slots: int = 0, pool_width: int = 0):
         self.bs, self.nb, self.vocab, self.max_pos, self.qp = block_size, num_blocks, vocab, max_pos, qp
         self.cache = {}
+        self.pool_slots, self.pool_width = pool_slots, pool_width
+        if pool_slots:
+            if pool_width < 1:
+                raise ValueError("a table pool needs a positive width")
+            self.slot_of = {}  # sequence key -> pool row
+            self.owner = [None] * pool_slots  # pool row -> [key, BlockTable, entries in use]
+            self.mirror = np.full((pool_slots, pool_width), -1, np.int32)  # the device rows
+            self.free = list(range(pool_slots - 1, -1, -1))
+            self.last_used = np.full(pool_slots, -1, np.int64)
+            self.passes = 0
 
     def _table(self, key, seq, start: int, new_cache):
         """(int32 buffer, length) of the sequence's block table, validated."""
@@ -120,15 +159,71 @@ class StepPacker:
         new_cache[key] = (tbl, arr, n)
         return arr, n
 
+    def _take_row(self, in_step: set) -> int:
+        if self.free:
+            return self.free.pop()
+        best = -1
+        for r in range(self.pool_slots):  # least recently scheduled row not in this pass
+            if self.owner[r][0] not in in_step and (best < 0 or self.last_used[r] < self.last_used[best]):
+                best = r
+        if best < 0:
+            raise ValueError(f"more sequences in one pass than table pool rows ({self.pool_slots})")
+        del self.slot_of[self.owner[best][0]]
+        return best
+
+    def _pool_row(self, key, seq, start: int, in_step: set, updates: list) -> tuple:
+        """(pool row, table length) of the sequence; appends the (row, index,
+        block) entries the device row lacks to `updates`."""
+        tbl = seq.table
+        ids = tbl.block_ids
+        n = len(ids)
+        if n > self.pool_width:
+            raise ValueError(f"block table of {n} entries exceeds the pool width {self.pool_width}")
+        r = self.slot_of.get(key)
+        if r is None:
+            r = self._take_row(in_step)
+            self.slot_of[key] = r
+            self.owner[r] = [key, None, 0]
+        own = self.owner[r]
+        # entries before the written block keep their values while the table object is the same
+        first = min(own[2], start // self.bs) if own[1] is tbl and own[2] <= n else 0
+        row, nb = self.mirror[r], self.nb
+        if n - first <= 16:  # a decode pass: one or two entries, plain Python is cheaper
+            for j in range(first, n):
+                v = ids[j]
+                if v < 0 or v >= nb:
+                    raise IndexError("block id out of range")
+                if v != row[j]:
+                    row[j] = v
+                    updates += (r, j, v)
+        elif n > first:
+            seg = np.asarray(ids[first:n], dtype=np.int64)
+            if int(seg.min()) < 0 or int(seg.max()) >= nb:
+                raise IndexError("block id out of range")
+            diff = np.flatnonzero(seg != row[first:n]) + first
+            row[first:n] = seg
+            if diff.size:
+                trip = np.empty((diff.size, 3), np.int64)
+                trip[:, 0], trip[:, 1], trip[:, 2] = r, diff, row[diff]
+                updates += trip.ravel().tolist()
+        own[1], own[2] = tbl, n
+        self.last_used[r] = self.passes
+        in_step.add(key)
+        return r, n
+
     def pack(self, out):
         items = out.scheduled
         S = len(items)
+        pooled = self.pool_slots > 0
         starts, qlens, counts = [0] * S, [0] * S, [0] * S
         tabs, tab_n = [None] * S, [0] * S
         toks = []
         new_cache = {}
+        in_step, updates = set(), []
         bs, max_pos = self.bs, self.max_pos
         W, max_ctx = 1, 1
+        if pooled:
+            self.passes += 1
         for i, item in enumerate(items):
             seq = item.seq
             start, n = item.start_pos, item.num_tokens
@@ -138,7 +233,12 @@ class StepPacker:
             if ctx > max_pos:
                 raise IndexError(f"position {ctx - 1} beyond max_seq_len {max_pos}")
             key = getattr(seq, "request_id", None) or id(seq)
-            arr, tn = self._table(key, seq, start, new_cache)
+            if pooled:
+                if key in in_step:
+                    raise ValueError("a sequence is scheduled twice in one pass")
+                arr, tn = self._pool_row(key, seq, start, in_step, updates)
+            else:
+                arr, tn = self._table(key, seq, start, new_cache)
             if tn * bs < ctx:
                 raise IndexError(f"block table of sequence {i} too short for {ctx} positions")
             starts[i] = start
@@ -152,23 +252,36 @@ class StepPacker:
                 W = tn
             if ctx > max_ctx:
                 max_ctx = ctx
-        self.cache = new_cache
+        if not pooled:
+            self.cache = new_cache
         T = len(toks)
         R = sum(counts)
         tok = np.asarray(toks, dtype=np.int64)
         if T and (int(tok.min()) < 0 or int(tok.max()) >= self.vocab):
             raise IndexError("token id out of the vocabulary")
-        hdr = 4 + 3 * S
-        rec = np.zeros(hdr + T + S * W, np.int32)
-        rec[0], rec[1], rec[2], rec[3] = S, T, R, W
-        rec[4:4 + S] = starts
-        rec[4 + S:4 + 2 * S] = qlens
-        rec[4 + 2 * S:hdr] = counts
+        if pooled:
+            U = len(updates) // 3
+            hdr = 5 + 3 * S
+            rec = np.empty(hdr + T + S + 3 * U, np.int32)
+            rec[0], rec[1], rec[2], rec[3], rec[4] = S, T, R, W, U
+            o = 5
+        else:
+            hdr = 4 + 3 * S
+            rec = np.zeros(hdr + T + S * W, np.int32)
+            rec[0], rec[1], rec[2], rec[3] = S, T, R, W
+            o = 4
+        rec[o:o + S] = starts
+        rec[o + S:o + 2 * S] = qlens
+        rec[o + 2 * S:hdr] = counts
         rec[hdr:hdr + T] = tok
-        table = rec[hdr + T:].reshape(S, W)
-        for i in range(S):
-            tn = tab_n[i]
-            table[i, :tn] = tabs[i][:tn]
+        if pooled:
+            rec[hdr + T:hdr + T + S] = tabs
+            rec[hdr + T + S:] = updates
+        else:
+            table = rec[hdr + T:].reshape(S, W)
+            for i in range(S):
+                tn = tab_n[i]
+                table[i, :tn] = tabs[i][:tn]
         n_dec = qlens.count(1)
         qp = self.qp
         tiles = sum((q + qp - 1) // qp for q in qlens if q > 1)
@@ -179,10 +292,30 @@ class StepPacker:
             r0 += c
         return rec, bounds, rows, (S, T, R, W)
 
+    def fields(self, rec) -> dict:
+        return record_fields(rec, self.pool_slots > 0)
+
 
 def pack_step(out, block_size: int, num_blocks: int, vocab: int, max_pos: int, qp: int):
     """One-off packing (no table cache); see StepPacker."""
     return StepPacker(block_size, num_blocks, vocab, max_pos, qp).pack(out)
+
+
+def step_needs(out):
+    """(S, T, R, W) of a SchedulerOutput without packing it: sequences, tokens,
+    logit rows (runner.py:88) and the widest block table."""
+    S = len(out.scheduled)
+    T = R = 0
+    W = 1
+    for item in out.scheduled:
+        n = item.num_tokens
+        T += n
+        d = len(item.seq.draft_token_ids) + 1
+        R += d if d < n else n
+        w = len(item.seq.table.block_ids)
+        if w > W:
+            W = w
+    return S, T, R, W
 
 
 class CudaRunner(_Base):
@@ -190,9 +323,10 @@ class CudaRunner(_Base):
 
     def __init__(self, model_cfg, cache_cfg, sched_cfg=None, *, weights=None, device=None,
                  max_seqs: int | None = None, max_tokens: int | None = None, use_graphs: bool = True,
-                 bucket_bounds: bool = False):
+                 bucket_bounds: bool = False, pooled_tables: bool = True):
         import torch
 
+        self.pooled_tables = pooled_tables  # block tables resident on the device (pooled records)
         if not torch.cuda.is_available():
             raise RuntimeError("CudaRunner needs a CUDA device; there is no CPU fallback")
         self.torch = torch
@@ -269,7 +403,8 @@ class CudaRunner(_Base):
             return
         torch.cuda.current_stream(self.dev).synchronize()
         caps = Caps(max(S, c.max_seqs), max(T, c.max_tokens), max(R, c.max_rows), max(W, c.max_table_width))
-        rec_words = 4 + 3 * caps.max_seqs + caps.max_tokens + caps.max_seqs * caps.max_table_width
+        # words of the largest record: the classic one, or a pooled one whose every entry is new
+        rec_words = 5 + 4 * caps.max_seqs + caps.max_tokens + 3 * caps.max_seqs * caps.max_table_width
         meta_bytes = self.L.vllt_meta_bytes(C.byref(caps))
         ws_bytes = self.L.vllt_forward_workspace_bytes(C.byref(self.desc), C.byref(caps))
         if meta_bytes < 0 or ws_bytes < 0:
@@ -281,6 +416,14 @@ class CudaRunner(_Base):
         self.ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, **kw)  # split-K counters start at 0
         self.logits_dev = torch.empty((caps.max_rows, self.w.vocab_padded), dtype=torch.float32, **kw)
         self.logits_host = None  # pinned, allocated by the first execute()
+        if self.pooled_tables:
+            # the persistent block tables: one row per live sequence, twice the
+            # sequences of a pass so that finished sequences rarely have to be
+            # evicted before their rows are reused; -1 = unknown, as the packer's mirror
+            slots = 2 * caps.max_seqs
+            self.table_pool = torch.full((slots, caps.max_table_width), -1, dtype=torch.int32, **kw)
+            self.desc.table_pool, self.desc.table_pool_slots = self.table_pool.data_ptr(), slots
+        self.packer = None  # its mirror describes the old pool
         self._on_reserve(caps)
         self.counters_host = torch.empty(16, dtype=torch.int32, pin_memory=True)
         self.caps = caps
@@ -288,9 +431,14 @@ class CudaRunner(_Base):
 
     # ---- the step ------------------------------------------------------------------
     def pack(self, out):
+        """Reserve capacity for the step, then pack it (a grown table pool
+        starts a new packer, whose first record reloads every table)."""
+        self._reserve(*step_needs(out))
         if getattr(self, "packer", None) is None or self.packer.qp != self.qp:
+            pool = self.desc.table_pool_slots if self.pooled_tables else 0
             self.packer = StepPacker(self.block_size, self.num_blocks, self.model_cfg.vocab_size,
-                                     self.w.rope_len, self.qp)
+                                     self.w.rope_len, self.qp, pool_slots=pool,
+                                     pool_width=self.caps.max_table_width)
         return self.packer.pack(out)
 
     def copy_on_write(self, pairs) -> None:
@@ -315,7 +463,6 @@ class CudaRunner(_Base):
         torch = self.torch
         self.copy_on_write(out.cow)
         rec, bounds, rows, (S, T, R, W) = self.pack(out)
-        self._reserve(S, T, R, W)
         n = rec.size
         self._last_n = n
         self.rec_host[:n].numpy()[:] = rec

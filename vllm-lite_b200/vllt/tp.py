@@ -202,8 +202,7 @@ class TPLlamaRunner(LlamaRunner):
 
     # ---- rank 0 -------------------------------------------------------------------
     def launch(self, out):  # replaces LlamaRunner.launch (which is CudaRunner's plus the roofline)
-        rec, bounds, rows, (S, T, R, W) = self.pack(out)
-        self._reserve(S, T, R, W)
+        rec, bounds, rows, (S, T, R, W) = self.pack(out)  # every rank applies the record's table updates
         self._broadcast(OP_FORWARD, rec, bounds, greedy=1)
         self._last_n = rec.size
         self._timed_forward(bounds)
