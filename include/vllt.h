@@ -204,6 +204,17 @@ int vllt_paged_attention_varlen_noalloc(const void* q, const void* k_cache, cons
                                         float scale, int32_t dtype, void* out,
                                         int32_t* device_flags, void* stream);
 
+/* Test injection for the decode kernel's bounded waits (no reference
+ * counterpart). The next TMA-decode launch made by this thread (through
+ * vllt_paged_attention_varlen or vllt_forward) arms the mbarrier of the stage
+ * that would hold table index `table_index` for its bytes but issues no copy
+ * into it, and limits every wait of that launch to wait_ns (<= 1 s): each
+ * CTA reading that index sees its wait expire, sets error bit 2 in the
+ * workspace flags, waits for its other copies in flight and returns; the
+ * context stays usable. One-shot: later launches wait normally; a launch
+ * captured into a CUDA graph neither takes nor consumes the injection. */
+int vllt_test_decode_stall(int32_t table_index, int64_t wait_ns);
+
 /* ------------------------------------------------------------------------ */
 /* Layer pieces                                                             */
 /* ------------------------------------------------------------------------ */

@@ -576,3 +576,45 @@ def test_decode_benchmark_setup_matches_oracle(dev):
     kc_new = s["kc"][torch.from_numpy(slot_blk.astype(np.int64)).to(dev), :, torch.from_numpy(
         (last % bs).astype(np.int64)).to(dev)]
     np.testing.assert_array_equal(kc_new.float().cpu().numpy(), s["knew"].float().cpu().numpy())
+
+
+def test_decode_wait_expiry_reports_and_recovers(dev):
+    """Failure detection of the TMA decode kernel, without a fault: the
+    one-shot injection vllt_test_decode_stall arms the stage of table index 3
+    for its bytes but issues no copy, with a 2 ms wait limit. Every CTA that
+    reads index 3 gives up, sets bit 2 of the workspace flags, lets its other
+    copies land and returns: the call itself returns OK. The next call (no
+    injection) on the same context is correct with clean flags."""
+    from vllt import _lib
+    from vllt.ops import attention_flags, paged_attention_varlen
+
+    rng = np.random.default_rng(17)
+    S, H, KV, D, bs = 4, 32, 8, 128, 16
+    ctx = np.asarray([100, 700, 1500, 50], np.int32)
+    nblk = (ctx + bs - 1) // bs
+    pool = int(nblk.sum()) + 4
+    perm = rng.permutation(pool)
+    tab = np.zeros((S, nblk.max()), np.int32)
+    o = 0
+    for i, n in enumerate(nblk):
+        tab[i, :n] = perm[o:o + n]
+        o += n
+    kc = torch.randn((pool, KV, bs, D), device=dev).to(torch.bfloat16)
+    vc = torch.randn((pool, KV, bs, D), device=dev).to(torch.bfloat16)
+    q = torch.randn((S, H, D), device=dev).to(torch.bfloat16)
+    args = (q, kc, vc, tab, np.arange(S + 1, dtype=np.int32), ctx, 1.0 / np.sqrt(D))
+    L = _lib.lib()
+    _lib.check(L.vllt_test_decode_stall(3, 2_000_000))
+    paged_attention_varlen(*args)
+    torch.cuda.synchronize()
+    assert attention_flags(paged_attention_varlen.last_workspace) & 4
+    out = paged_attention_varlen(*args).float().cpu().numpy()
+    assert attention_flags(paged_attention_varlen.last_workspace) == 0
+    qh = q.float().cpu().numpy()
+    for i in range(S):
+        n = int(nblk[i])
+        idx = torch.from_numpy(tab[i, :n].astype(np.int64)).to(dev)
+        k = kc.index_select(0, idx).float().permute(0, 2, 1, 3).reshape(n * bs, KV, D)[:ctx[i]].cpu().numpy()
+        v = vc.index_select(0, idx).float().permute(0, 2, 1, 3).reshape(n * bs, KV, D)[:ctx[i]].cpu().numpy()
+        np.testing.assert_allclose(out[i:i + 1], A.dense_attention(qh[i:i + 1], k, v, KV, 1.0 / np.sqrt(D)),
+                                   rtol=2e-2, atol=2e-2)

@@ -51,7 +51,13 @@ def test_library_calls_reject_bad_arguments_without_a_gpu():
     assert rc == _lib.VLLT_ERR_ARG
     assert b"bad sizes" in L.vllt_last_error()
     assert L.vllt_sgemm(None, None, None, 4, 4, 4, None) == _lib.VLLT_ERR_ARG
+    # the decode wait injection is bounded: a positive index and at most 1 s
+    assert L.vllt_test_decode_stall(-1, 1000) == _lib.VLLT_ERR_ARG
+    assert L.vllt_test_decode_stall(3, 0) == _lib.VLLT_ERR_ARG
+    assert L.vllt_test_decode_stall(3, 2_000_000_000) == _lib.VLLT_ERR_ARG
+    # the pooled metadata builder refuses a missing pool before any launch
     caps = _lib.Caps(16, 1024, 1024, 32)
+    assert L.vllt_build_batch_meta_pooled(None, ctypes.byref(caps), 16, 64, 2, None, 0, None, None) == _lib.VLLT_ERR_ARG
     assert L.vllt_meta_bytes(ctypes.byref(caps)) > 0
     assert L.vllt_meta_bytes(ctypes.byref(_lib.Caps(0, 1, 1, 1))) == -1
 

@@ -128,3 +128,62 @@ def test_control_plane_and_vocab_parallel_greedy_over_gloo(tmp_path):
 
     mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
     assert sorted(os.listdir(tmp_path)) == ["ok0", "ok1"]
+
+
+def _silent_peer(rank, world, port, result_dir, who_stops):
+    """One rank stops taking part in the protocol; the other must get an error
+    from its next collective within the process group's timeout (2 s), not
+    hang. who_stops = 0: rank 0 sends one forward message, then nothing (a
+    driver that died or hung); the worker's receive fails. who_stops = 1: the
+    worker takes one message, then never joins another collective; rank 0's
+    vocab-parallel all-gather after its next forward fails."""
+    import datetime
+    import time
+
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "vllm-lite_b200")]
+    import torch.distributed as dist
+
+    from vllt.tp import CTRL_WORDS, OP_FORWARD, ControlPlane, serve
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=2))
+    plane = ControlPlane(torch.zeros(16 + CTRL_WORDS, dtype=torch.int32))
+    rec = np.arange(5, dtype=np.int32)
+    result = "none"
+    if rank == who_stops:
+        if rank == 0:
+            plane.send(OP_FORWARD, rec)
+        else:
+            plane.recv()
+        time.sleep(6)  # alive but silent: never joins another collective
+        result = "silent"
+    else:
+        t0 = time.monotonic()
+        try:
+            if rank == 0:
+                plane.send(OP_FORWARD, rec)  # the worker took this one
+                plane.send(OP_FORWARD, rec)  # a broadcast only sends: it may complete
+                vals = torch.empty(2 * 4)
+                dist.all_gather(list(vals.view(2, 4)), torch.zeros(4))  # needs the worker's slice
+            else:
+                serve(plane, lambda b, g: None, lambda t: None)
+            result = "no error"
+        except RuntimeError as e:
+            dt = time.monotonic() - t0
+            result = f"error {dt:.1f}" if dt < 5.0 else f"late error {dt:.1f}"
+            print(f"rank {rank} ({type(e).__name__}): {str(e)[:120]}", flush=True)
+    with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
+        f.write(result)
+    os._exit(0)  # the group cannot be torn down collectively with a silent peer
+
+
+@pytest.mark.parametrize("who_stops", [0, 1])
+def test_a_silent_rank_turns_into_an_error_within_the_timeout(tmp_path, who_stops):
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_silent_peer, args=(2, _free_port(), str(tmp_path), who_stops), nprocs=2, join=True,
+                       start_method="spawn")
+    got = {f: open(os.path.join(tmp_path, f)).read() for f in os.listdir(tmp_path)}
+    waiting = f"rank{1 - who_stops}"
+    assert got[f"rank{who_stops}"] == "silent"
+    assert got[waiting].startswith("error "), got

@@ -55,6 +55,8 @@ struct DecodeParams {
   float* ws_ml;       // [splits][P_cap][H][2] (max in natural-log units, sum)
   int P_cap;
   int* err;           // bit 2: a bounded wait expired
+  uint64_t wait_ns;   // limit of every mbarrier wait
+  int stall_block;    // test: table index whose stage is armed with no copy (-1: none)
 };
 
 __device__ __forceinline__ uint32_t saddr(const void* p) {
@@ -82,11 +84,11 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 // Wait for `parity` with a time limit; false if it expired.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(bar, parity))
-    if (global_ns() - t0 > kWaitNs) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   return true;
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
@@ -163,6 +165,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CU
     const int y = (blk * p.n_kv + kvh) * kBS;
     unsigned char* dst = my_ring + st * kStageBytes;
     mbar_expect_tx(bar, kStageBytes);
+    if (b == p.stall_block) return;  // test: bytes promised, no copy issued, the wait expires
     tma_load_2d(dst, &tk, bar, 0, y);
     tma_load_2d(dst + kBox, &tk, bar, 64, y);
     tma_load_2d(dst + 2 * kBox, &tv, bar, 0, y);
@@ -192,7 +195,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CU
   for (; j < my_n; ++j) {
     const int st = j % kStages;
     const int b = b_begin + warp + j * kWarps;
-    if (!mbar_wait(&my_bars[st], (j / kStages) & 1)) {
+    if (!mbar_wait(&my_bars[st], (j / kStages) & 1, p.wait_ns)) {
       failed = true;
       break;
     }
@@ -276,7 +279,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CU
   if (failed) {
     if (lane == 0) atomicOr(p.err, 4);
     // let the copies this warp still has in flight land before the CTA exits
-    for (int k = j; k < min(my_n, j + kStages); ++k) (void)mbar_wait(&my_bars[k % kStages], (k / kStages) & 1);
+    for (int k = j; k < min(my_n, j + kStages); ++k)
+      (void)mbar_wait(&my_bars[k % kStages], (k / kStages) & 1, p.wait_ns);
   }
 
   // ---- merge the four warps (reuse the ring) ---------------------------------------
@@ -391,6 +395,16 @@ int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const DecodePara
 
 constexpr int kDecodeSplitBlocks = 64;
 
+// Test injection for the bounded waits (vllt_test_decode_stall): the next
+// decode launch of this thread promises the bytes of table index `block` to
+// its stage's mbarrier without issuing the copies, and waits at most
+// `wait_ns`; every CTA reading that index reports bit 2 and returns.
+struct DecodeStall {
+  int block = -1;
+  uint64_t wait_ns = 0;
+};
+thread_local DecodeStall g_stall;
+
 int64_t decode_ws_bytes(int P_cap, int H, int max_ctx) {
   const int splits = ceil_div(ceil_div(max_ctx, kBS), kDecodeSplitBlocks);
   return splits <= 1 ? 0 : (int64_t)splits * P_cap * H * (kD + 2) * sizeof(float);
@@ -429,6 +443,15 @@ int decode_pass(const AttnCall& c, const int32_t* item_seq, const int32_t* n_ite
   p.qscale = c.scale * 1.4426950408889634f;
   p.P_cap = c.P_cap;
   p.err = err;
+  p.wait_ns = kWaitNs;
+  p.stall_block = -1;
+  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+  if (g_stall.block >= 0 && cudaStreamIsCapturing(st, &capturing) == cudaSuccess &&
+      capturing == cudaStreamCaptureStatusNone) {  // one-shot test injection of this thread, eager launches only
+    p.stall_block = g_stall.block;
+    p.wait_ns = g_stall.wait_ns;
+    g_stall.block = -1;
+  }
   int splits = ceil_div(ceil_div(max_ctx, kBS), kDecodeSplitBlocks);
   if (splits > 1) {
     const int64_t need = (int64_t)splits * c.P_cap * c.H * (kD + 2) * sizeof(float);
@@ -456,3 +479,12 @@ int decode_pass(const AttnCall& c, const int32_t* item_seq, const int32_t* n_ite
 }
 
 }  // namespace vllt
+
+extern "C" int vllt_test_decode_stall(int32_t table_index, int64_t wait_ns) {
+  vllt::clear_error();
+  VLLT_REQUIRE(table_index >= 0 && wait_ns > 0 && wait_ns <= 1000000000ll,
+               "test_decode_stall: table index >= 0 and 0 < wait_ns <= 1 s");
+  vllt::g_stall.block = table_index;
+  vllt::g_stall.wait_ns = (uint64_t)wait_ns;
+  return VLLT_OK;
+}

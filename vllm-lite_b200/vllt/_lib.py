@@ -57,6 +57,7 @@ SIGNATURES = {
                                               i32, i32, i32, i32, f32, i32, vp, vp, i64, vp]),
     "vllt_paged_attention_varlen_noalloc": (C.c_int, [vp, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, i32,
                                                       i32, i32, i32, i32, f32, i32, vp, vp, vp]),
+    "vllt_test_decode_stall": (C.c_int, [i32, i64]),
     "vllt_rmsnorm": (C.c_int, [vp, vp, vp, vp, i32, i32, f32, vp]),
     "vllt_rope": (C.c_int, [vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "vllt_sgemm": (C.c_int, [vp, vp, vp, i32, i32, i32, vp]),
