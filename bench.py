@@ -280,7 +280,9 @@ def main_ours(args):
         run_workload(eng, reqs, f"w{i}")
     run_workload(ref_eng, reqs, "w")
 
-    def timed(engine, tag):
+    window = tuple(int(x) for x in args.nvtx_passes.split(":")) if args.nvtx_passes else None
+
+    def timed(engine, tag, nvtx_window=None):
         flush_l2(torch, dev)
         if world > 1:
             torch.distributed.barrier()
@@ -293,7 +295,7 @@ def main_ours(args):
 
         l0 = launched()
         e0.record()
-        toks, ttft, steps = run_workload(engine, reqs, tag)
+        toks, ttft, steps = run_workload(engine, reqs, tag, nvtx_window)
         e1.record()
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / 1e3, toks, ttft, steps, launched() - l0
@@ -302,7 +304,7 @@ def main_ours(args):
     torch.cuda.nvtx.range_push("vllt_timed")  # ncu --nvtx --nvtx-include vllt_timed/
     with Clocks(local) as clk:
         for i in range(args.steps):
-            res.append(timed(eng, f"t{i}"))
+            res.append(timed(eng, f"t{i}", window if i == 0 else None))
     torch.cuda.nvtx.range_pop()
     e2e_res = [timed(ref_eng, f"e{i}") for i in range(max(1, min(args.steps, 3)))]
     # untimed extra run: per-pass GPU time (CUDA events around each forward) vs the rest of a step
@@ -378,7 +380,7 @@ def main_ours(args):
                      "launch_ms": round(decode_t * 1e3, 4), "traffic": None,
                      "traffic_note": "no ncu capture of the current decode kernel; the earlier version with "
                                      "the same access pattern read 2.254 GB + wrote 0.014 GB per launch "
-                                     "(= algorithmic), profiles/paged_attention_decode_c3.md"},
+                                     "(= algorithmic)"},
         "clocks": clk.summary(),
         "breakdown": breakdown,
     }
@@ -859,7 +861,7 @@ def main():
     ap.add_argument("--spec-k", type=int, default=4)
     ap.add_argument("--gemm-m", default="", help="token counts of the gemm workload (default 8192,512,256,64)")
     ap.add_argument("--gemm-shape", default="", help="projections of the gemm workload (qkv,o_proj,gate_up,down)")
-    ap.add_argument("--nvtx-passes", default="", help="a:b - mark engine steps a..b-1 of the timed llama8b run "
+    ap.add_argument("--nvtx-passes", default="", help="a:b - mark engine steps a..b-1 of the (first) timed run "
                                                       "with an NVTX range (profiling)")
     ap.add_argument("--llama-requests", type=int, default=512)
     ap.add_argument("--llama-blocks", type=int, default=45000)

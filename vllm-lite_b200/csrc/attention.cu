@@ -323,15 +323,11 @@ int launch_attention(const AttnParams& p, int grid_items, int splits, cudaStream
   const size_t smem = std::max(attention_smem<T, D, ROWS>(),
                                sizeof(float) * (2 * kWarps * ROWS + kWarps * ROWS * D) +
                                    sizeof(float) * ROWS * D);
-  // opt in to >48 KB of dynamic shared memory once per device
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 32 && !(configured & (1u << dev))) {
+  static PerDeviceOnce smem_opt_in;  // dynamic shared memory above 48 KB, once per device
+  smem_opt_in.run([&] {
     cudaFuncSetAttribute(attention_kernel<T, D, ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    configured |= 1u << dev;
-  }
+  });
   dim3 grid(p.n_kv, grid_items, splits);
   attention_kernel<T, D, ROWS><<<grid, kWarps * 32, smem, st>>>(p);
   return check_launch("attention");

@@ -379,13 +379,10 @@ template <int NREP>
 int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p, int items, int splits,
                   cudaStream_t st) {
   const size_t smem = decode_smem<NREP>();
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 32 && !(configured & (1u << dev))) {
+  static PerDeviceOnce smem_opt_in;  // dynamic shared memory above 48 KB, once per device
+  smem_opt_in.run([&] {
     cudaFuncSetAttribute(decode_kernel<NREP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    configured |= 1u << dev;
-  }
+  });
   dim3 grid(p.n_kv, items, splits);
   decode_kernel<NREP><<<grid, kWarps * 32, smem, st>>>(tk, tv, p);
   return check_launch("decode attention");

@@ -425,13 +425,10 @@ int encode(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, c
 template <int NREP>
 int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const PrefillParams& p,
                    int items, cudaStream_t st) {
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 32 && !(configured & (1u << dev))) {
+  static PerDeviceOnce smem_opt_in;  // dynamic shared memory above 48 KB, once per device
+  smem_opt_in.run([&] {
     cudaFuncSetAttribute(prefill_tc_kernel<NREP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    configured |= 1u << dev;
-  }
+  });
   prefill_tc_kernel<NREP><<<dim3(p.n_kv, items), 192, kSmemBytes, st>>>(tq, tk, tv, p);
   return check_launch("prefill attention (tcgen05)");
 }

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 #include "../../include/vllt.h"
@@ -31,6 +32,25 @@ int check_launch(const char* what);
   } while (0)
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// The devices on which one call site's one-time step (a kernel's dynamic
+// shared-memory opt-in) has run. Thread-safe: a device is recorded only after
+// its step has run, so a concurrent caller either finds it recorded or runs
+// the (idempotent) step again; devices from 64 on run it on every call.
+class PerDeviceOnce {
+ public:
+  template <class Fn> void run(Fn&& fn) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+    const bool tracked = dev >= 0 && dev < 64;
+    if (tracked && ((done_.load(std::memory_order_acquire) >> dev) & 1ull)) return;
+    fn();
+    if (tracked) done_.fetch_or(1ull << dev, std::memory_order_acq_rel);
+  }
+
+ private:
+  std::atomic<uint64_t> done_{0};
+};
 
 inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 

@@ -697,6 +697,11 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
+__device__ __forceinline__ int ld_dsmem_s32(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
 __device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -842,7 +847,15 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   __syncthreads();
   __syncwarp();
   cluster_sync();
-  if (warp < 4 && !abort_s) {  // ---- reduction of token rows [r*n/S, (r+1)*n/S) ----
+  // A CTA that gave up never wrote its staging buffer: then no CTA of the
+  // cluster reduces or runs the epilogue (which may write the KV cache). Each
+  // CTA set its own abort_s before the barrier above (release / acquire), so
+  // the peers' values read here are final.
+  bool cluster_ok = !abort_s;
+  if (warp < 4)
+    for (int src = 0; src < p.S && cluster_ok; ++src)
+      cluster_ok = ld_dsmem_s32(map_rank(saddr(const_cast<int*>(&abort_s)), src)) == 0;
+  if (warp < 4 && cluster_ok) {  // ---- reduction of token rows [r*n/S, (r+1)*n/S) ----
     const int n_tok = min(M, p.n_pad);
     const int r0 = rank * n_tok / p.S, r1 = (rank + 1) * n_tok / p.S;
     const uint32_t base = saddr(stage_acc);
@@ -1239,14 +1252,11 @@ inline int gemm_cluster_launch(const void* A, int M_cap, const int* M_dev, const
   rc = tc::kmajor_map(&tx, A, M_cap, K, p.n_pad);
   if (rc != VLLT_OK) return rc;
   const int smem = 1024 + p.stages * p.ksub * (tc::SK_W_BYTES + p.n_pad * 128);
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 32 && !(configured & (1u << dev))) {
+  static PerDeviceOnce smem_opt_in;  // dynamic shared memory above 48 KB, once per device
+  smem_opt_in.run([&] {
     cudaFuncSetAttribute(tc::gemm_cluster_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          1024 + tc::SK_RING_BYTES);
-    configured |= 1u << dev;
-  }
+  });
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.tiles * p.S);
   cfg.blockDim = dim3(tc::SK_THREADS);
@@ -1278,14 +1288,11 @@ inline int gemm_small_launch(const void* A, int M_cap, const int* M_dev, const v
   rc = tc::kmajor_map(&tx, A, M_cap, K, p.n_pad);
   if (rc != VLLT_OK) return rc;
   const int smem = 1024 + p.stages * p.ksub * (tc::SK_W_BYTES + p.n_pad * 128) + tc::SK_TBUF_BYTES;
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 32 && !(configured & (1u << dev))) {
+  static PerDeviceOnce smem_opt_in;  // dynamic shared memory above 48 KB, once per device
+  smem_opt_in.run([&] {
     cudaFuncSetAttribute(tc::gemm_small_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          1024 + tc::SK_RING_BYTES + tc::SK_TBUF_BYTES);
-    configured |= 1u << dev;
-  }
+  });
   // both kernels start under PDL: the main kernel's set-up and first weight
   // loads overlap the previous kernel, the reduce kernel waits in place
   cudaError_t e = launch_pdl(tc::gemm_small_kernel<Epi>, dim3(p.ctas), dim3(tc::SK_THREADS), (size_t)smem, st, tw,
@@ -1322,15 +1329,12 @@ inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const vo
   if (rc != VLLT_OK) return rc;
   rc = tc::kmajor_map(&tb, W, N, K, tc::BN);
   if (rc != VLLT_OK) return rc;
-  static unsigned configured = 0;  // per device: dynamic shared memory opted in for both kernels
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 32 && !(configured & (1u << dev))) {
+  static PerDeviceOnce smem_opt_in;  // dynamic shared memory above 48 KB, once per device
+  smem_opt_in.run([&] {
     cudaFuncSetAttribute(tc::gemm_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
     cudaFuncSetAttribute(tc::gemm_persistent_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          tc::SMEM_BYTES);
-    configured |= 1u << dev;
-  }
+  });
   if (splits <= 0) {
     tc::ClusterPlan cp;
     if (cluster_plan(M_cap, N, K, &cp)) return gemm_cluster_launch(A, M_cap, M_dev, W, N, K, epi, err, st, cp);
