@@ -143,6 +143,36 @@ def test_bf16_llama8b_long_context_prefill_over_cached_prefix():
     assert worst <= LONG_BAR and worst_row <= LONG_BAR
 
 
+def test_llama_checkpoint_reproduces_the_seeded_model(tmp_path):
+    """The seeded bf16 weights written to a checkpoint in the reference's
+    naming and orientation (bf16 as uint16 bits, lm_head present, norms fp32)
+    and loaded back through LlamaRunner(weights=path): bit-identical logits."""
+    from types import SimpleNamespace
+
+    from vllt.llama import NAMES, LlamaRunner, LlamaShape, full_matrix
+
+    shape = LlamaShape(n_layers=2, n_heads=8, n_kv_heads=2, d_model=1024, d_ff=2048, vocab_size=1000,
+                       max_seq_len=2048, seed=1)
+    dev = torch.device("cuda", 0)
+    bits = lambda t: t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+    arrays = {"tok_emb": bits(full_matrix(shape, -1, "tok_emb", dev)),
+              "lm_head": bits(full_matrix(shape, -1, "lm_head", dev).T), "final_norm": np.ones(1024, np.float32)}
+    for i in range(shape.n_layers):
+        for n in NAMES[:7]:
+            arrays[f"layers.{i}.{n}"] = bits(full_matrix(shape, i, n, dev).T)  # reference orientation [in][out]
+        arrays[f"layers.{i}.attn_norm"] = arrays[f"layers.{i}.ffn_norm"] = np.ones(1024, np.float32)
+    path = str(tmp_path / "llama_small.npz")
+    np.savez(path, **arrays)
+    cache = SimpleNamespace(block_size=16, num_blocks=64)
+    a = LlamaRunner(shape, cache, max_seqs=8, max_tokens=256)
+    b = LlamaRunner(shape, cache, max_seqs=8, max_tokens=256, weights=path)
+    for seqs in schedule(shape.vocab_size, np.random.default_rng(3)):
+        out = F.as_scheduler_output(seqs)
+        la, _ = a.execute(out)
+        lb, _ = b.execute(out)
+        np.testing.assert_array_equal(la, lb)
+
+
 def test_llama_engine_serves_requests_to_completion():
     """The bf16 runner behind the unmodified scheduler: chunked prefill, decode,
     every request reaches max_tokens, blocks all returned."""

@@ -3,9 +3,12 @@
 Shape (the north star's large config): 32 layers, d_model 4096, 32 query / 8 KV
 heads of 128, SwiGLU FFN 14336, vocabulary 128256, RoPE theta 10000 as in
 vllmlite/attention.py:21, bf16 weights drawn N(0, 0.02) from a seed. There is no
-reference checkpoint at this shape; every weight matrix is generated on the
-device from (seed, layer, name), so its values do not depend on the
-tensor-parallel split and a TP run computes the same model as a 1-GPU run.
+reference checkpoint at this shape; by default every weight matrix is
+generated on the device from (seed, layer, name), so its values do not depend
+on the tensor-parallel split and a TP run computes the same model as a 1-GPU
+run. A checkpoint in the reference's .npz naming (bf16 as uint16 bits, or any
+float type) loads instead (`load_llama_npz`, `LlamaRunner(weights=path)` or
+`ModelConfig.weights_path`).
 
 Layout for the tcgen05 GEMM (K-major, [out][in]); per rank r of N:
   wqkv   rows [q heads of r | k heads of r | v heads of r]      [(H+2KV)/N*128][4096]
@@ -65,10 +68,39 @@ def full_matrix(cfg, layer: int, name: str, device, std: float = 0.02):
     return _normal(shape, key, std, device)
 
 
-class LlamaWeights:
-    """This rank's bf16 shard on the device, in libvllt's layout."""
+def checkpoint_tensor(a, device, dtype):
+    """A checkpoint array as a torch tensor of `dtype` on `device`: floating
+    arrays (float16 / float32 / float64) are rounded to dtype; uint16 arrays
+    are bf16 bit patterns (NumPy has no bfloat16: that is how a bf16
+    checkpoint is stored in an .npz)."""
+    import torch
 
-    def __init__(self, cfg, device, tp_rank: int = 0, tp_size: int = 1):
+    a = np.asarray(a)
+    if a.dtype == np.uint16:
+        t = torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
+    elif a.dtype.kind == "f":
+        t = torch.from_numpy(np.ascontiguousarray(a))
+    else:
+        raise ValueError(f"checkpoint array of dtype {a.dtype}: expected float or uint16 (bf16 bits)")
+    return t.to(device=device, dtype=dtype)
+
+
+def load_llama_npz(path: str):
+    """A Llama-shaped checkpoint in the reference's .npz naming and
+    orientation (vllmlite/model.py:64-71): tok_emb [V][d], final_norm [d],
+    lm_head [d][V] (optional: tied to tok_emb), layers.{i}.{attn_norm, wq
+    [d][H*D], wk, wv [d][KV*D], wo [H*D][d], ffn_norm, w_gate, w_up [d][f],
+    w_down [f][d]}. Arrays are read when used."""
+    return np.load(path)
+
+
+class LlamaWeights:
+    """This rank's bf16 shard on the device, in libvllt's layout: drawn from
+    the seed (`source` None), or taken from a checkpoint mapping in the
+    reference's naming and [in][out] orientation (see load_llama_npz), each
+    array transposed to [out][in], rounded to bf16 and sliced to this rank."""
+
+    def __init__(self, cfg, device, tp_rank: int = 0, tp_size: int = 1, source=None):
         import torch
 
         D, H, KV, f, V = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.d_ff, cfg.vocab_size
@@ -76,28 +108,44 @@ class LlamaWeights:
             raise ValueError(f"heads, KV heads, d_ff and vocab must divide by tp_size={tp_size}")
         hl, kl, fl, vl = H // tp_size, KV // tp_size, f // tp_size, V // tp_size
         r = tp_rank
+        bf = torch.bfloat16
+
+        def mat(layer, name):  # [out][in] bf16
+            if source is None:
+                return full_matrix(cfg, layer, name, device)
+            key = name if layer < 0 else f"layers.{layer}.{name}"
+            if name == "lm_head" and key not in source:
+                return checkpoint_tensor(source["tok_emb"], device, bf)  # tied: lm_head = tok_emb.T
+            t = checkpoint_tensor(source[key], device, bf)
+            return t if name == "tok_emb" else t.T
+
+        def norm(key):
+            if source is None:
+                return torch.ones(cfg.d_model, dtype=torch.float32, device=device)
+            return checkpoint_tensor(source[key], device, torch.float32).contiguous()
+
         self.vocab_local, self.vocab_offset = vl, r * vl
         self.vocab_padded = (vl + 3) // 4 * 4
         self.layers = []
         for i in range(cfg.n_layers):
-            wq = full_matrix(cfg, i, "wq", device)[r * hl * D:(r + 1) * hl * D]
-            wk = full_matrix(cfg, i, "wk", device)[r * kl * D:(r + 1) * kl * D]
-            wv = full_matrix(cfg, i, "wv", device)[r * kl * D:(r + 1) * kl * D]
-            wo = full_matrix(cfg, i, "wo", device)[:, r * hl * D:(r + 1) * hl * D]
-            g = full_matrix(cfg, i, "w_gate", device)[r * fl:(r + 1) * fl]
-            u = full_matrix(cfg, i, "w_up", device)[r * fl:(r + 1) * fl]
-            gu = torch.empty((2 * fl, cfg.d_model), dtype=torch.bfloat16, device=device)
+            wq = mat(i, "wq")[r * hl * D:(r + 1) * hl * D]
+            wk = mat(i, "wk")[r * kl * D:(r + 1) * kl * D]
+            wv = mat(i, "wv")[r * kl * D:(r + 1) * kl * D]
+            wo = mat(i, "wo")[:, r * hl * D:(r + 1) * hl * D]
+            g = mat(i, "w_gate")[r * fl:(r + 1) * fl]
+            u = mat(i, "w_up")[r * fl:(r + 1) * fl]
+            gu = torch.empty((2 * fl, cfg.d_model), dtype=bf, device=device)
             gu[0::2], gu[1::2] = g, u
-            wd = full_matrix(cfg, i, "w_down", device)[:, r * fl:(r + 1) * fl]
+            wd = mat(i, "w_down")[:, r * fl:(r + 1) * fl]
             self.layers.append(dict(
-                attn_norm=torch.ones(cfg.d_model, dtype=torch.float32, device=device),
+                attn_norm=norm(f"layers.{i}.attn_norm"),
                 wqkv=torch.cat([wq, wk, wv], 0).contiguous(), wo=wo.contiguous(),
-                ffn_norm=torch.ones(cfg.d_model, dtype=torch.float32, device=device),
+                ffn_norm=norm(f"layers.{i}.ffn_norm"),
                 w_gu=gu, w_down=wd.contiguous()))
             del wq, wk, wv, g, u
-        self.tok_emb = full_matrix(cfg, -1, "tok_emb", device)
-        self.lm_head = full_matrix(cfg, -1, "lm_head", device)[r * vl:(r + 1) * vl].contiguous()
-        self.final_norm = torch.ones(cfg.d_model, dtype=torch.float32, device=device)
+        self.tok_emb = mat(-1, "tok_emb").contiguous()
+        self.lm_head = mat(-1, "lm_head")[r * vl:(r + 1) * vl].contiguous()
+        self.final_norm = norm("final_norm")
         cos, sin = rope_tables(D, cfg.max_seq_len)
         self.rope_cos = torch.from_numpy(cos).to(device)
         self.rope_sin = torch.from_numpy(sin).to(device)
@@ -140,10 +188,14 @@ class LlamaRunner(CudaRunner):
         super().__init__(model_cfg, cache_cfg, sched_cfg, **kw)
 
     def _init_model(self, weights) -> None:
+        """weights: None (seeded, or cfg.weights_path when set), a checkpoint
+        path, or a mapping in the reference's naming (see load_llama_npz)."""
         torch, cfg = self.torch, self.model_cfg
-        if weights is not None:
-            raise ValueError("LlamaRunner draws its own seeded weights")
-        self.w = LlamaWeights(cfg, self.dev, self.tp_rank, self.tp_size)
+        if weights is None and getattr(cfg, "weights_path", None):
+            weights = cfg.weights_path
+        if isinstance(weights, str):
+            weights = load_llama_npz(weights)
+        self.w = LlamaWeights(cfg, self.dev, self.tp_rank, self.tp_size, source=weights)
         kv_local = cfg.n_kv_heads // self.tp_size
         shape = (cfg.n_layers, self.num_blocks, kv_local, self.block_size, self.head_dim)
         self.cache_k = torch.zeros(shape, dtype=torch.bfloat16, device=self.dev)

@@ -5,7 +5,8 @@ Three sources, all in the reference's naming (vllmlite/model.py:26-71):
     (vllmlite/model.py:29-43, :47-55), so the same seed gives bit-identical
     arrays (pinned by tests/golden/weights.json);
   * `load_npz(path, cfg)`  - the reference's .npz checkpoint keys
-    (vllmlite/model.py:64-71);
+    (vllmlite/model.py:64-71), used when cfg.weights_path is set, as the
+    reference's constructor does (`initial_weights`);
   * `from_reference_model(m)` - the arrays of a live vllmlite TinyLlama.
 
 `DeviceWeights` lays them out for libvllt: [wq|wk|wv] fused per layer,
@@ -60,6 +61,13 @@ def load_npz(path: str, cfg) -> dict[str, np.ndarray]:
         for k in LAYER_KEYS:
             out[f"layers.{i}.{k}"] = z[f"layers.{i}.{k}"].astype(np.float32)
     return out
+
+
+def initial_weights(cfg) -> dict[str, np.ndarray]:
+    """The weights TinyLlama(cfg) ends up with: the seeded init, replaced by
+    the checkpoint at cfg.weights_path when one is set (vllmlite/model.py:61-62)."""
+    path = getattr(cfg, "weights_path", None)
+    return load_npz(path, cfg) if path else seeded_weights(cfg)
 
 
 def from_reference_model(model) -> dict[str, np.ndarray]:

@@ -26,7 +26,7 @@ import numpy as np
 
 from . import _lib
 from ._lib import Caps, ModelDesc, StepBounds, check, lib
-from .model import DeviceWeights, seeded_weights
+from .model import DeviceWeights, initial_weights
 
 try:  # the plug-in ABC of the host engine, when vllm-lite is importable
     from vllmlite.runner import ModelRunner as _Base
@@ -360,7 +360,7 @@ class CudaRunner(_Base):
     def _init_model(self, weights) -> None:
         """fp32 parity weights in libvllt's layout and the fp32 paged KV cache."""
         torch, cfg = self.torch, self.model_cfg
-        w = weights if weights is not None else seeded_weights(cfg)
+        w = weights if weights is not None else initial_weights(cfg)
         self.w = DeviceWeights(cfg, w, self.dev)
         shape = (cfg.n_layers, self.num_blocks, cfg.n_kv_heads, self.block_size, self.head_dim)
         self.cache_k = torch.zeros(shape, dtype=torch.float32, device=self.dev)
