@@ -402,6 +402,26 @@ int vllt_forward(const vllt_model_desc* m, const int32_t* step_record, const vll
                  int64_t workspace_bytes, float* logits, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Prefix-cache hashing                                                     */
+/* ------------------------------------------------------------------------ */
+
+/* Content hashes of full KV blocks, bit-identical to vllm-lite's hash_block
+ * (vllmlite/block.py:34-40: blake2b with a 16-byte digest over the previous
+ * block's hex digest, "|", and the block's token ids joined by commas,
+ * returned as 32 lowercase hex characters), chained block after block as
+ * BlockManager.commit and reuse_prefix chain them (block_manager.py:98-120).
+ * Chain c (all pointers device memory):
+ *   n_blocks[c] full blocks of block_size tokens at tokens + token_offsets[c];
+ *   prev_hex (NULL: no chain has one) + 32*c: the hex digest of the block
+ *     before the chain, or 32 zero bytes for none (the first block of a
+ *     sequence);
+ *   out_hex + 32 * (out_offsets[c] + b): the hex digest of block b.
+ * The caller keeps every offset inside its buffers. One thread per chain. */
+int vllt_prefix_hash_chains(const int32_t* tokens, const int64_t* token_offsets, const int32_t* n_blocks,
+                            const int64_t* out_offsets, const uint8_t* prev_hex, int32_t n_chains,
+                            int32_t block_size, uint8_t* out_hex, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Tensor parallelism (bf16 model): NCCL, loaded at run time                */
 /* ------------------------------------------------------------------------ */
 

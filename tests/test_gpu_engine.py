@@ -228,6 +228,21 @@ def test_bench_workload_shared_prefix_token_identical():
     assert eng.scheduler.blocks.stats()["prefix_hit_rate"] > 0.5
 
 
+def test_shared_prefix_benchmark_with_device_prefix_hashes():
+    """The shared-prefix benchmark with the prefix cache's block hashes
+    computed on the device: the reference's token streams, prefix-cache hits,
+    and every hash the BlockManager asked for planned ahead."""
+    from vllt.engine import gpu_engine
+    from vllt.workloads import mixed_workload
+
+    eng = gpu_engine(engine_cfg(F.BENCH, nb=768, max_seqs=16, budget=1024, prefix=True, maxlen=768),
+                     device_prefix_hash=True)
+    assert run_requests(eng, mixed_workload(48, 0, 256)) == F.streams("streams_shared.npz")
+    assert eng.scheduler.blocks.stats()["prefix_hit_rate"] > 0.5
+    h = eng.prefix_hasher
+    assert h.lookups > 0 and h.misses == 0
+
+
 @pytest.mark.parametrize("k", [2, 4, 8])
 def test_periodic_speculative_token_identical(k):
     from vllt.engine import gpu_engine

@@ -618,3 +618,35 @@ def test_decode_wait_expiry_reports_and_recovers(dev):
         v = vc.index_select(0, idx).float().permute(0, 2, 1, 3).reshape(n * bs, KV, D)[:ctx[i]].cpu().numpy()
         np.testing.assert_allclose(out[i:i + 1], A.dense_attention(qh[i:i + 1], k, v, KV, 1.0 / np.sqrt(D)),
                                    rtol=2e-2, atol=2e-2)
+
+
+def test_prefix_hash_kernel_matches_hash_block(dev):
+    """vllt_prefix_hash_chains: every digest equals the reference's
+    hash_block (vllmlite/block.py:34-40) chained as BlockManager chains them,
+    for 300 chains of 0 to 40 blocks of 16 tokens, with and without a
+    previous block, token ids over the Llama vocabulary."""
+    import hashlib
+
+    from vllt.prefix_hash import hash_chains
+
+    def hash_block(prev, toks):  # vllmlite/block.py:34-40
+        h = hashlib.blake2b(digest_size=16)
+        if prev:
+            h.update(prev.encode())
+        h.update(b"|")
+        h.update(",".join(map(str, toks)).encode())
+        return h.hexdigest()
+
+    rng = np.random.default_rng(12)
+    chains = []
+    for c in range(300):
+        n = int(rng.integers(0, 41))
+        prev = hash_block(None, [c]) if c % 3 == 0 else None
+        chains.append((prev, [int(t) for t in rng.integers(0, 128256, size=16 * n)]))
+    got = hash_chains(chains, 16, dev)
+    for (prev, toks), hs in zip(chains, got):
+        want, p = [], prev
+        for b in range(len(toks) // 16):
+            p = hash_block(p, toks[16 * b:16 * (b + 1)])
+            want.append(p)
+        assert hs == want

@@ -69,6 +69,7 @@ SIGNATURES = {
     "vllt_sample_top_p": (C.c_int, [vp, i32, i32, i32, i32, vp, vp, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
     "vllt_spec_verify": (C.c_int, [vp, i32, i32, vp, i32, vp, vp, i32, vp, vp, vp]),
     "vllt_spec_accept": (C.c_int, [vp, vp, vp, i32, vp, vp, vp]),
+    "vllt_prefix_hash_chains": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, vp, vp]),
     "vllt_tp_unique_id": (C.c_int, [vp]),
     "vllt_tp_init": (C.c_int, [vp, i32, i32, C.POINTER(vp)]),
     "vllt_tp_destroy": (C.c_int, [vp]),

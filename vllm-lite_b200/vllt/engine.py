@@ -164,9 +164,16 @@ class GpuLLMEngine(metaclass=_Lazy):
 
 
 def gpu_engine(cfg=None, tokenizer=None, speculative_tokens: int = 0, weights=None, device=None,
-               runner_cls=None, **runner_kw):
-    return cuda_engine(cfg, tokenizer, speculative_tokens, weights, device,
-                       engine_cls=GpuLLMEngine.resolve(), runner_cls=runner_cls, **runner_kw)
+               runner_cls=None, device_prefix_hash: bool = False, **runner_kw):
+    """A GpuLLMEngine (device token picks). device_prefix_hash: the prefix
+    cache's block hashes are computed on the device (vllt.prefix_hash)."""
+    eng = cuda_engine(cfg, tokenizer, speculative_tokens, weights, device,
+                      engine_cls=GpuLLMEngine.resolve(), runner_cls=runner_cls, **runner_kw)
+    if device_prefix_hash:
+        from .prefix_hash import DevicePrefixHasher
+
+        eng.prefix_hasher = DevicePrefixHasher(eng, lib=runner_kw.get("lib"))
+    return eng
 
 
 def _make_gpu_engine(Base):
@@ -276,14 +283,28 @@ def _make_gpu_engine(Base):
             return picks_h, acc_h, sampled_tok
 
         def step(self):
-            """engine.py:99-181 with device-side token picks."""
+            """engine.py:99-181 with device-side token picks (and, with a
+            prefix_hasher, device-side prefix-cache hashes)."""
+            hasher = getattr(self, "prefix_hasher", None)
+            if hasher is None:
+                return self._step(None)
+            with hasher.active():
+                return self._step(hasher)
+
+        def _step(self, hasher):
+            if hasher is not None:
+                hasher.prepare_prompts()
             sched = self.scheduler.schedule()
             dropped = [self._retired_output(s) for s in self.scheduler.drain_reports()]
             if sched.is_empty:
                 return dropped
             t0 = time.perf_counter()
             rows, R = self.runner.launch(sched)
+            if hasher is not None:
+                hasher.prepare_commits(sched)
             picks, accepted, sampled_tok = self._device_picks(sched, rows, R)
+            if hasher is not None:
+                hasher.collect()
             self.busy_time += time.perf_counter() - t0
             self.total_steps += 1
             results = list(dropped)
