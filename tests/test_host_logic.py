@@ -222,23 +222,29 @@ def test_seen_bitmaps_mark_each_distinct_token_once():
 
 def test_graph_bucket_bounds_cover_every_step_of_the_bucket():
     """A captured forward serves every step whose token count fits its bucket:
-    tokens round up to a power of two (>= 16, <= capacity) and the other bounds
-    are derived from that alone, so they hold for any step of the bucket."""
+    tokens round up to the next rung (multiples of 16 to 64, then four rungs
+    per doubling, capped at the capacity) and the other bounds are derived
+    from that alone, so they hold for any step of the bucket."""
     from types import SimpleNamespace as NS
 
     from vllt._lib import Caps, StepBounds
-    from vllt.runner import CudaRunner
+    from vllt.runner import CudaRunner, token_bucket
 
     fake = NS(caps=Caps(64, 1024, 1024, 32), qp=4, w=NS(rope_len=2048))
-    for T in (1, 15, 16, 17, 100, 512, 1000, 1024):
+    for T in (1, 15, 16, 17, 65, 100, 257, 512, 513, 1000, 1024):
         b = CudaRunner.bucket(fake, StepBounds(T, min(T, 64), min(T, 64), 1, 2048))
-        assert b.tokens >= max(T, 16) and b.tokens <= 1024 and (b.tokens & (b.tokens - 1)) == 0
+        assert b.tokens >= max(T, 16) and b.tokens <= 1024
         assert b.rows >= min(T, 64) and b.decode_seqs >= min(T, 64)
         assert b.tiles >= (T + 3) // 4 and b.max_ctx == 2048
         # every smaller step in the same bucket maps to the same bounds
-        if T > 16:
-            same = CudaRunner.bucket(fake, StepBounds(b.tokens // 2 + 1, 1, 1, 1, 1))
-            assert (same.tokens, same.rows, same.decode_seqs, same.tiles) == (b.tokens, b.rows, b.decode_seqs, b.tiles)
+        same = CudaRunner.bucket(fake, StepBounds(b.tokens, 1, 1, 1, 1))
+        assert (same.tokens, same.rows, same.decode_seqs, same.tiles) == (b.tokens, b.rows, b.decode_seqs, b.tiles)
+    rungs = sorted({token_bucket(t) for t in range(1, 8193)})
+    assert rungs[:8] == [16, 32, 48, 64, 80, 96, 112, 128] and rungs[-1] == 8192
+    assert len(rungs) <= 4 + 4 * 7  # at most four graphs per doubling
+    for t in range(1, 8193):  # at most 15 padded tokens up to 64, at most 25 % above
+        assert t <= token_bucket(t) <= (t + 15 if t <= 64 else t * 1.25)
+        assert token_bucket(token_bucket(t)) == token_bucket(t)
 
 
 def test_llama_workload_has_the_benchmark_shape():

@@ -301,6 +301,23 @@ def pack_step(out, block_size: int, num_blocks: int, vocab: int, max_pos: int, q
     return StepPacker(block_size, num_blocks, vocab, max_pos, qp).pack(out)
 
 
+def token_bucket(tokens: int) -> int:
+    """The token capacity of the CUDA graph that serves a pass of `tokens`
+    tokens: multiples of 16 up to 64, then four rungs per doubling
+    (80, 96, 112, 128, 160, ...). The forward's GEMMs, attention grids and
+    the tensor-parallel all-reduces (`rows x d_model` words) work on the
+    bucket's rows, so a pass of more than 64 tokens pays at most 25 % over
+    its tokens (at most 15 tokens below) instead of the up to 2x of
+    power-of-two buckets, with at most 4 graphs per doubling."""
+    if tokens <= 64:
+        return max(16, -(-tokens // 16) * 16)
+    top = 64
+    while top < tokens:
+        top *= 2
+    step = top // 8  # the rungs of (top/2, top]: top/2 + j * top/8
+    return -(-tokens // step) * step
+
+
 def step_needs(out):
     """(S, T, R, W) of a SchedulerOutput without packing it: sequences, tokens,
     logit rows (runner.py:88) and the widest block table."""
@@ -514,14 +531,11 @@ class CudaRunner(_Base):
                                   self.ws.numel(), self.logits_dev.data_ptr(), _lib.stream_handle()))
 
     def bucket(self, b) -> StepBounds:
-        """Bounds of the graph that serves a step: tokens rounded up to a power
-        of two (>= 16); everything else derived from that, so the graph is
-        valid for every step whose token count fits."""
+        """Bounds of the graph that serves a step: tokens rounded up to the
+        next rung of token_bucket's ladder; everything else derived from that,
+        so the graph is valid for every step whose token count fits."""
         c = self.caps
-        T = 16
-        while T < b.tokens:
-            T *= 2
-        T = min(T, c.max_tokens)
+        T = min(token_bucket(b.tokens), c.max_tokens)
         return StepBounds(T, min(T, c.max_rows), min(T, c.max_seqs), T // self.qp + c.max_seqs, self.w.rope_len)
 
     def _forward_graph(self, bounds) -> None:
