@@ -281,3 +281,61 @@ def test_sources_hold_no_peer_memory_access():
         src = open(f, errors="replace").read()
         for b in banned:
             assert b not in src, f"{os.path.relpath(f, ROOT)} names {b}"
+
+
+def _fake_desc(dtype=0, tp_size=1):
+    """A model descriptor whose pointers are placeholders: every check below
+    fails on the host, before any of them would be dereferenced."""
+    import ctypes as C
+
+    from vllt import _lib
+
+    d = _lib.ModelDesc()
+    d.n_layers, d.n_heads, d.n_kv_heads, d.head_dim = 2, 8, 4, 48
+    d.d_model, d.d_ff, d.vocab, d.vocab_padded = 384, 1024, 261, 264
+    d.max_seq_len, d.block_size, d.num_blocks, d.rms_eps = 512, 16, 64, 1e-5
+    d.dtype, d.tp_size, d.embed_rows = dtype, tp_size, 261
+    fake = 4096
+    for k in ("tok_emb", "final_norm", "lm_head", "rope_cos", "rope_sin", "k_cache", "v_cache"):
+        setattr(d, k, fake)
+    arr = (C.c_void_p * 2)(fake, fake)
+    for k in ("attn_norm", "wqkv", "wo", "ffn_norm", "w_gu", "w_down"):
+        setattr(d, k, C.cast(arr, C.POINTER(C.c_void_p)))
+    d._keep = arr
+    return d
+
+
+def test_c_abi_rejects_inconsistent_calls_before_any_launch():
+    """Inconsistent calls come back as VLLT_ERR_ARG with a message, decided
+    on the host from the arguments alone (no device is present here)."""
+    import ctypes as C
+
+    from vllt import _lib
+
+    L = _lib.lib()
+    caps = _lib.Caps(8, 64, 16, 32)
+    bounds = _lib.StepBounds(64, 16, 8, 8, 512)
+    fake = 4096
+
+    def forward(desc, ws_bytes=16):
+        return L.vllt_forward(C.byref(desc) if desc is not None else None, fake, C.byref(caps), C.byref(bounds),
+                              fake, fake, ws_bytes, fake, None)
+
+    assert forward(None) == _lib.VLLT_ERR_ARG and b"NULL" in L.vllt_last_error()
+    assert forward(_fake_desc(dtype=7)) == _lib.VLLT_ERR_ARG and b"dtype" in L.vllt_last_error()
+    assert forward(_fake_desc(tp_size=2)) == _lib.VLLT_ERR_ARG and b"tensor parallelism" in L.vllt_last_error()
+    d = _fake_desc()
+    d.table_pool, d.table_pool_slots = fake, 0
+    assert forward(d) == _lib.VLLT_ERR_ARG and b"table_pool" in L.vllt_last_error()
+    assert forward(_fake_desc()) == _lib.VLLT_ERR_ARG and b"workspace too small" in L.vllt_last_error()
+    need = L.vllt_forward_workspace_bytes(C.byref(_fake_desc()), C.byref(caps))
+    assert need > 16
+    # sampling: more rows than the logits buffer holds, and no row index to pick them
+    assert L.vllt_sample_top_p(fake, 5, 261, 264, 4, None, None, 257, None, None, fake, None, None, fake, fake,
+                               None) == _lib.VLLT_ERR_ARG
+    # prefix hash: no chains is a no-op, a zero block size is refused
+    assert L.vllt_prefix_hash_chains(None, None, None, None, None, 0, 16, None, None) == _lib.VLLT_OK
+    assert L.vllt_prefix_hash_chains(fake, fake, fake, fake, None, 3, 0, fake, None) == _lib.VLLT_ERR_ARG
+    # the allocation-free attention: unknown dtype
+    assert L.vllt_paged_attention_varlen_noalloc(fake, fake, fake, fake, 4, fake, fake, 1, 1, 1, 16, 8, 4, 48, 16, 64,
+                                                 0.1, 9, fake, None, None) == _lib.VLLT_ERR_ARG
