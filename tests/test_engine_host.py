@@ -108,6 +108,11 @@ class ReferenceLogitsRunner:
     def __init__(self, model_cfg, cache_cfg, sched_cfg=None, device=None, lib=None):
         from vllmlite.runner import NumpyRunner
 
+        from vllt.runner import CudaRunner
+
+        self.check_step_flags = CudaRunner.check_step_flags.__get__(self)
+        self.meta = torch.zeros(16, dtype=torch.int32)  # word 7: the metadata builder's error flags
+        self.packer = object()
         self.ref = NumpyRunner(model_cfg, cache_cfg)
         self.model_cfg = model_cfg
         self.dev = torch.device("cpu")
@@ -240,3 +245,19 @@ def test_generator_advances_only_on_completing_passes():
         assert completes(item) == final
         sampled = pick_inputs([item], [(0, 1)], 1, 257)[5]
         assert sampled == ([(0, 0)] if final else [])
+
+
+def test_a_pass_the_device_flagged_raises_and_reloads_the_tables():
+    """The metadata builder's error word comes back with the picks: a flagged
+    pass raises instead of committing tokens, and the runner drops its
+    packer so the next pass uploads whole tables."""
+    from vllmlite.sequence import SamplingParams
+
+    eng, lib = gpu_engine_on_host(ReferenceLogitsRunner, engine_cfg(1024))
+    eng.add_request(params=SamplingParams(max_tokens=4, temperature=0.0), request_id="x",
+                    prompt_token_ids=[256, 1, 2, 3])
+    eng.runner.meta[7] = 2
+    with pytest.raises(RuntimeError, match="flags 2"):
+        eng.step()
+    assert eng.runner.packer is None
+    assert eng.seqs["x"].output_token_ids == []

@@ -243,12 +243,14 @@ def _make_gpu_engine(Base):
                 seq_of_row[rows[i][0] + rows[i][1] - 1] = item.seq
             acc = torch.empty(max(S, 1), dtype=torch.int32, device=run.dev)
             sampled_tok = {}
+            # picks[R] holds the device metadata builder's error word: it comes back with the picks
+            picks = torch.empty(R + 1, dtype=torch.int32, device=run.dev)
             if getattr(run, "tp_size", 1) > 1:
-                picks = run.greedy_picks(R)
+                picks[:R] = run.greedy_picks(R)
             else:
-                picks = torch.empty(max(R, 1), dtype=torch.int32, device=run.dev)
                 self._greedy(run.logits_dev, R, run.w.vocab_padded, V, eos_mask, penalty,
                              [seq_of_row.get(r) for r in range(R)], picks, keep)
+            picks[R:R + 1] = run.meta[7:8]
             if drafts:
                 d_cu, d_dr, d_doff = self._h2d(cu), self._h2d(np.asarray(drafts, np.int32)), self._h2d(doff)
                 keep += [d_cu, d_dr, d_doff]
@@ -257,7 +259,8 @@ def _make_gpu_engine(Base):
             if getattr(run, "tp_size", 1) > 1:
                 special = [int(r) for r in np.flatnonzero(eos_mask | (penalty != 1.0))]
                 srows = [r for _, r in sampled]
-                picks_h = picks[:R].cpu().numpy()
+                picks_h = picks.cpu().numpy()
+                run.check_step_flags(int(picks_h[R]))
                 if special or srows:
                     full = run.gather_rows(special + srows)  # [n, V] fp32 on every rank
                     out = torch.empty(len(special) + len(srows), dtype=torch.int32, device=run.dev)
@@ -278,7 +281,8 @@ def _make_gpu_engine(Base):
                                  [sched.scheduled[i].seq for i, _ in sampled], out, keep)
                     for (i, _), t in zip(sampled, out.cpu().numpy()):
                         sampled_tok[i] = int(t)
-                picks_h = picks[:R].cpu().numpy()
+                picks_h = picks.cpu().numpy()
+                run.check_step_flags(int(picks_h[R]))
             acc_h = acc[:S].cpu().numpy() if drafts else np.zeros(S, np.int32)
             return picks_h, acc_h, sampled_tok
 

@@ -475,6 +475,15 @@ class CudaRunner(_Base):
     def _on_reserve(self, caps) -> None:
         """Hook for subclasses that size extra buffers by the capacities."""
 
+    def check_step_flags(self, err: int) -> None:
+        """Raise if the device's metadata builder flagged the last pass (bit 0
+        capacity, bit 1 block table / range). Its pool updates may not all
+        have landed, so the packer is dropped: the next pass uploads every
+        table it needs whole."""
+        if err:
+            self.packer = None
+            raise RuntimeError(f"libvllt rejected the step metadata on the device (flags {err})")
+
     def launch(self, out):
         """Enqueue CoW + H2D + forward for one SchedulerOutput; returns (rows, R)."""
         torch = self.torch
@@ -568,8 +577,6 @@ class CudaRunner(_Base):
             self.counters_host.copy_(self.meta[:16], non_blocking=True)
             self.d2h_bytes += R * self.w.vocab_padded * 4 + 64
             torch.cuda.current_stream(self.dev).synchronize()
-        err = int(self.counters_host[7])
-        if err:
-            raise RuntimeError(f"libvllt rejected the step metadata on the device (flags {err})")
+        self.check_step_flags(int(self.counters_host[7]))
         logits = self.logits_host[:R, :self.model_cfg.vocab_size].numpy().copy()
         return logits, rows
