@@ -5,10 +5,11 @@ and uploads per pass only the (row, index, block id) entries that changed
 (include/vllt.h, "pooled record"). Here the unmodified reference engine
 (Scheduler, BlockManager with prefix caching, copy-on-write, preemption, the
 n-gram proposer) drives a runner that packs every pass both ways; the pooled
-record's updates are applied to a host copy of the pool by a restatement of
-build_meta_kernel's phases 0 and 2 (csrc/batch_meta.cu), and the tables read
-back through each sequence's row must equal the classic record's tables bit
-for bit, on the 48-request mixed-length (C1) and shared-prefix (C2)
+record's updates are applied to a host copy of the pool twice: by a NumPy
+restatement of build_meta_kernel's phases 0 and 2, and by the kernel's own
+per-item code (csrc/table_pool.cuh, compiled for the host by g++). The tables
+read back through each sequence's row must equal the classic record's tables
+bit for bit, on the 48-request mixed-length (C1) and shared-prefix (C2)
 benchmarks, the 512-request Llama-shaped workload (C4), and small runs that
 force preemption and speculative rejections. The pooled record must also
 carry O(S + T + changed entries) words.
@@ -20,6 +21,34 @@ import pytest
 from tests.conftest import needs_vllmlite
 
 pytestmark = needs_vllmlite
+
+
+HOST = {}  # the host-compiled build_meta_kernel pool phases (tests/table_pool_host.cpp), when g++ exists
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _host_pool_phases(tmp_path_factory):
+    import ctypes
+
+    from tests.host_build import build_harness
+
+    lib = build_harness("table_pool_host", str(tmp_path_factory.mktemp("tp")))
+    if lib is not None:
+        lib.apply_pooled_host.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+        HOST["lib"] = lib
+    yield
+    HOST.clear()
+
+
+def apply_pooled_kernel_code(pool, rec, bs, num_blocks):
+    """The same phases with the kernel's own per-item code (pool_update /
+    pool_entry of csrc/table_pool.cuh) compiled for the host."""
+    S, W = int(rec[0]), int(rec[3])
+    rec = np.ascontiguousarray(rec, np.int32)
+    out = np.zeros((S, W), np.int32)
+    err = HOST["lib"].apply_pooled_host(rec.ctypes.data, pool.ctypes.data, pool.shape[0], pool.shape[1], bs,
+                                        num_blocks, out.ctypes.data)
+    return out, err
 
 
 def apply_pooled(pool, f, bs, num_blocks):
@@ -66,9 +95,10 @@ class PackingRunner:
         self.classic = StepPacker(*args)
         self.pooled = StepPacker(*args, pool_slots=2 * 512, pool_width=width)
         self.pool = np.full((2 * 512, width), -1, np.int32)
+        self.pool_k = self.pool.copy()  # the pool as the kernel's host-compiled code leaves it
         self.vocab_out = vocab_out
         self.words = {"classic": 0, "pooled": 0}
-        self.passes = self.updates = self.max_excess = 0
+        self.passes = self.updates = self.kernel_code_passes = 0
 
     @property
     def vocab_size(self):
@@ -87,6 +117,11 @@ class PackingRunner:
             np.testing.assert_array_equal(fc[k], fp[k])
         got, err = apply_pooled(self.pool, fp, self.bs, self.nb)
         assert err == 0
+        if "lib" in HOST:
+            got_k, err_k = apply_pooled_kernel_code(self.pool_k, rp, self.bs, self.nb)
+            assert err_k == 0
+            np.testing.assert_array_equal(got_k, got)
+            self.kernel_code_passes += 1
         ctx = fc["start"].astype(np.int64) + fc["qlen"]
         for s in range(S):
             used = -(-int(ctx[s]) // self.bs)
@@ -140,6 +175,7 @@ def engine_cfg(n_layers=6, vocab=261, max_len=512, bs=16, nb=512, max_seqs=16, b
 def check(eng, ratio):
     run = eng.runner
     assert run.passes > 10 and run.updates > 0
+    assert run.kernel_code_passes == (run.passes if "lib" in HOST else 0)
     assert run.words["pooled"] * ratio < run.words["classic"], run.words
     return run
 

@@ -16,28 +16,22 @@ kernel runs:
 """
 
 import ctypes
-import os
-import shutil
-import subprocess
 
 import numpy as np
 import pytest
 
-from tests.conftest import ROOT, needs_vllmlite
+from tests.conftest import needs_vllmlite
 
 torch = pytest.importorskip("torch")
 
 
 @pytest.fixture(scope="module")
 def host_hash(tmp_path_factory):
-    gxx = shutil.which("g++")
-    if gxx is None:
+    from tests.host_build import build_harness
+
+    lib = build_harness("prefix_hash_host", str(tmp_path_factory.mktemp("ph")))
+    if lib is None:
         pytest.skip("g++ is not available")
-    out = str(tmp_path_factory.mktemp("ph") / "libprefixhash.so")
-    subprocess.run([gxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-I",
-                    os.path.join(ROOT, "vllm-lite_b200", "csrc"), os.path.join(ROOT, "tests", "prefix_hash_host.cpp"),
-                    "-o", out], check=True)
-    lib = ctypes.CDLL(out)
     lib.hash_chain_host.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
     return lib
 

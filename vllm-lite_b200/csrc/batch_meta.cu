@@ -5,6 +5,7 @@
 // CTA (no grid sync, no second launch) has the lowest latency.
 
 #include "meta.cuh"
+#include "table_pool.cuh"
 
 namespace vllt {
 
@@ -100,14 +101,8 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
 
   // Phase 0 (pool): apply this pass's block-table changes. An update outside
   // the pool flags the step (bit 1) and is dropped.
-  for (int u = threadIdx.x; u < U; u += kThreads) {
-    const int sl = updates[3 * u], j = updates[3 * u + 1], blk = updates[3 * u + 2];
-    if (sl < 0 || sl >= pool_slots || j < 0 || j >= L.W_cap) {
-      atomicOr(&s_err, 2);
-      continue;
-    }
-    pool[(int64_t)sl * L.W_cap + j] = blk;
-  }
+  for (int u = threadIdx.x; u < U; u += kThreads)
+    if (!pool_update(pool, pool_slots, L.W_cap, updates + 3 * u)) atomicOr(&s_err, 2);
   __syncthreads();  // the pool writes above are visible to every thread of the CTA below
 
   // Phase 1: exclusive scans over sequences of (qlen, count, is_decode, tiles).
@@ -158,12 +153,9 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
     const int used = ceil_div(ctx[s], bs);
     int blk;
     if (pool) {
-      blk = -1;
-      if (b < used) {
-        const int sl = seq_slot[s];
-        if (sl >= 0 && sl < pool_slots) blk = pool[(int64_t)sl * L.W_cap + b];
-        if (blk < 0 || blk >= num_blocks) { atomicOr(&s_err, 2); blk = -1; }
-      }
+      bool bad = false;
+      blk = pool_entry(pool, pool_slots, L.W_cap, seq_slot[s], b, used, num_blocks, &bad);
+      if (bad) atomicOr(&s_err, 2);
     } else {
       blk = tables[i];
       if (b < used && (blk < 0 || blk >= num_blocks)) { atomicOr(&s_err, 2); blk = -1; }
