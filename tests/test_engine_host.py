@@ -77,6 +77,9 @@ class OracleLib:
         b = view(bits, np.uint32, rows * words)
         for r in range(rows):
             src = int(ri[r]) if ri is not None else r
+            if not 0 <= src < n_logit_rows:  # the kernel's answer to a row outside the buffer
+                o[r] = -1
+                continue
             masked = m is not None and m[r]
             o[r], _, _ = SP.sample_with_uniform(
                 x[src, :vocab], float(t[r]), int(k[r]), float(tp[r]), float(uu[r]),
