@@ -229,11 +229,15 @@ def _make_gpu_engine(Base):
             verify rows. Tensor parallel: the vocab-parallel argmax over all
             rows; rows that need a mask, a penalty or a draw have their
             full-vocabulary logits gathered from every rank first and go
-            through the same two kernels."""
+            through the same two kernels. Every result lands in one device
+            buffer, read back with one copy per step:
+              [0, R) row picks | R: the metadata builder's error word |
+              [R+1, R+1+S) accepted drafts | then the sampled / masked picks."""
             run = self.runner
             S = len(sched.scheduled)
             V = run.model_cfg.vocab_size
             eos = self.tokenizer.eos_id
+            tp = getattr(run, "tp_size", 1) > 1
             cu, doff, drafts, eos_mask, penalty, sampled = pick_inputs(sched.scheduled, rows, R, eos)
             keep = []  # device temporaries stay referenced until their kernels are enqueued:
             # a tensor freed earlier could be handed to the next copy by the
@@ -241,49 +245,38 @@ def _make_gpu_engine(Base):
             seq_of_row = {}
             for i, item in enumerate(sched.scheduled):
                 seq_of_row[rows[i][0] + rows[i][1] - 1] = item.seq
-            acc = torch.empty(max(S, 1), dtype=torch.int32, device=run.dev)
-            sampled_tok = {}
-            # picks[R] holds the device metadata builder's error word: it comes back with the picks
-            picks = torch.empty(R + 1, dtype=torch.int32, device=run.dev)
-            if getattr(run, "tp_size", 1) > 1:
-                picks[:R] = run.greedy_picks(R)
+            special = [int(r) for r in np.flatnonzero(eos_mask | (penalty != 1.0))] if tp else []
+            tail = R + 1 + S  # first word of the sampled / masked picks
+            res = torch.empty(tail + len(special) + len(sampled), dtype=torch.int32, device=run.dev)
+            if tp:
+                res[:R] = run.greedy_picks(R)
             else:
                 self._greedy(run.logits_dev, R, run.w.vocab_padded, V, eos_mask, penalty,
-                             [seq_of_row.get(r) for r in range(R)], picks, keep)
-            picks[R:R + 1] = run.meta[7:8]
+                             [seq_of_row.get(r) for r in range(R)], res, keep)
+            res[R:R + 1] = run.meta[7:8]
             if drafts:
                 d_cu, d_dr, d_doff = self._h2d(cu), self._h2d(np.asarray(drafts, np.int32)), self._h2d(doff)
                 keep += [d_cu, d_dr, d_doff]
                 check(run.L.vllt_spec_accept(d_cu.data_ptr(), d_dr.data_ptr(), d_doff.data_ptr(), S,
-                                             picks.data_ptr(), acc.data_ptr(), _lib.stream_handle()))
-            if getattr(run, "tp_size", 1) > 1:
-                special = [int(r) for r in np.flatnonzero(eos_mask | (penalty != 1.0))]
-                srows = [r for _, r in sampled]
-                picks_h = picks.cpu().numpy()
-                run.check_step_flags(int(picks_h[R]))
-                if special or srows:
-                    full = run.gather_rows(special + srows)  # [n, V] fp32 on every rank
-                    out = torch.empty(len(special) + len(srows), dtype=torch.int32, device=run.dev)
-                    if special:
-                        self._greedy(full, len(special), V, V, eos_mask[special], penalty[special],
-                                     [seq_of_row[r] for r in special], out, keep)
-                    if srows:
-                        self._sample(full, full.shape[0], V, V, [len(special) + j for j in range(len(srows))],
-                                     [sched.scheduled[i].seq for i, _ in sampled], out[len(special):], keep)
-                    got = out.cpu().numpy()
-                    picks_h[special] = got[:len(special)]
-                    for j, (i, _) in enumerate(sampled):
-                        sampled_tok[i] = int(got[len(special) + j])
-            else:
+                                             res.data_ptr(), res[R + 1:].data_ptr(), _lib.stream_handle()))
+            seqs = [sched.scheduled[i].seq for i, _ in sampled]
+            if tp and (special or sampled):
+                full = run.gather_rows(special + [r for _, r in sampled])  # [n, V] fp32 on every rank
+                if special:
+                    self._greedy(full, len(special), V, V, eos_mask[special], penalty[special],
+                                 [seq_of_row[r] for r in special], res[tail:], keep)
                 if sampled:
-                    out = torch.empty(len(sampled), dtype=torch.int32, device=run.dev)
-                    self._sample(run.logits_dev, R, run.w.vocab_padded, V, [r for _, r in sampled],
-                                 [sched.scheduled[i].seq for i, _ in sampled], out, keep)
-                    for (i, _), t in zip(sampled, out.cpu().numpy()):
-                        sampled_tok[i] = int(t)
-                picks_h = picks.cpu().numpy()
-                run.check_step_flags(int(picks_h[R]))
-            acc_h = acc[:S].cpu().numpy() if drafts else np.zeros(S, np.int32)
+                    self._sample(full, full.shape[0], V, V, [len(special) + j for j in range(len(sampled))], seqs,
+                                 res[tail + len(special):], keep)
+            elif sampled:
+                self._sample(run.logits_dev, R, run.w.vocab_padded, V, [r for _, r in sampled], seqs, res[tail:], keep)
+            res_h = res.cpu().numpy()
+            run.check_step_flags(int(res_h[R]))
+            picks_h = res_h[:R].copy()
+            if special:
+                picks_h[special] = res_h[tail:tail + len(special)]
+            sampled_tok = {i: int(res_h[tail + len(special) + j]) for j, (i, _) in enumerate(sampled)}
+            acc_h = res_h[R + 1:R + 1 + S].copy() if drafts else np.zeros(S, np.int32)
             return picks_h, acc_h, sampled_tok
 
         def step(self):
