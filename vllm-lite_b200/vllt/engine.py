@@ -254,10 +254,10 @@ def _make_gpu_engine(Base):
                 self._greedy(run.logits_dev, R, run.w.vocab_padded, V, eos_mask, penalty,
                              [seq_of_row.get(r) for r in range(R)], res, keep)
             res[R:R + 1] = run.meta[7:8]
-            if drafts:
-                d_cu, d_dr, d_doff = self._h2d(cu), self._h2d(np.asarray(drafts, np.int32)), self._h2d(doff)
-                keep += [d_cu, d_dr, d_doff]
-                check(run.L.vllt_spec_accept(d_cu.data_ptr(), d_dr.data_ptr(), d_doff.data_ptr(), S,
+            if drafts:  # cu_rows[S+1] | draft offsets[S] | drafts, one upload
+                d = self._h2d(np.concatenate([cu, doff, np.asarray(drafts, np.int32)]))
+                keep.append(d)
+                check(run.L.vllt_spec_accept(d.data_ptr(), d[2 * S + 1:].data_ptr(), d[S + 1:].data_ptr(), S,
                                              res.data_ptr(), res[R + 1:].data_ptr(), _lib.stream_handle()))
             seqs = [sched.scheduled[i].seq for i, _ in sampled]
             if tp and (special or sampled):
