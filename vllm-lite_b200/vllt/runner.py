@@ -463,9 +463,11 @@ class CudaRunner(_Base):
         if not pairs:
             return
         torch = self.torch
-        p = torch.tensor(np.asarray(pairs, np.int32).reshape(-1, 2), device=self.dev)
-        if int(p.min()) < 0 or int(p.max()) >= self.num_blocks:
+        a = np.asarray(pairs, np.int64).reshape(-1, 2)
+        if int(a.min()) < 0 or int(a.max()) >= self.num_blocks:  # checked on the host: no device read
             raise IndexError("copy-on-write block id out of range")
+        p = torch.from_numpy(a.astype(np.int32)).to(self.dev, non_blocking=True)
+        self._cow_pairs = p  # referenced until the copy kernel has been enqueued
         cfg = self.model_cfg
         check(self.L.vllt_copy_blocks(self.cache_k.data_ptr(), self.cache_v.data_ptr(), p.data_ptr(),
                                       len(pairs), cfg.n_layers, self.num_blocks, cfg.n_kv_heads,
