@@ -264,3 +264,53 @@ def test_a_pass_the_device_flagged_raises_and_reloads_the_tables():
         eng.step()
     assert eng.runner.packer is None
     assert eng.seqs["x"].output_token_ids == []
+
+
+@pytest.mark.parametrize("workload", ["mixed", "shared"])
+def test_benchmark_streams_through_the_device_pick_path(workload, tmp_path):
+    """The reference's 48-request benchmarks (C1; C2 with the prefix cache,
+    its block hashes planned and computed by the device hash code compiled
+    for the host) through GpuLLMEngine's host path: every greedy token and
+    the number of engine steps equal the reference run's golden streams."""
+    import ctypes
+
+    from tests.host_build import build_harness
+    from tests.test_prefix_hash import chain_host
+    from vllt.engine import GpuLLMEngine, cuda_engine
+    from vllt.prefix_hash import DevicePrefixHasher
+    from vllt.workloads import mixed_workload
+
+    from vllmlite.config import CacheConfig, EngineConfig, ModelConfig, SchedulerConfig
+
+    shared = workload == "shared"
+    host = build_harness("prefix_hash_host", str(tmp_path)) if shared else None
+    if shared and host is None:
+        pytest.skip("g++ is not available")
+
+    class Lib(OracleLib):
+        def vllt_prefix_hash_chains(self, tokens, tok_off, nblk, out_off, prev, n, bs, out, stream):
+            nb = view(nblk, np.int32, n)
+            to, oo = view(tok_off, np.int64, n), view(out_off, np.int64, n)
+            o = view(out, np.uint8, 32 * max(int(oo[-1] + nb[-1]) if n else 0, 1))
+            for c in range(n):
+                toks = view(tokens + 4 * int(to[c]), np.int32, max(int(nb[c]) * bs, 1))[:int(nb[c]) * bs]
+                p = bytes(view(prev + 32 * c, np.uint8, 32)) if prev else b"\0"
+                for b, h in enumerate(chain_host(host, p.decode() if p[0] else None, toks, bs)):
+                    o[32 * (int(oo[c]) + b):32 * (int(oo[c]) + b + 1)] = np.frombuffer(h.encode(), np.uint8)
+            return 0
+
+    if shared:
+        host.hash_chain_host.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int] * 2 + [ctypes.c_void_p]
+    maxlen = 768 if shared else 512
+    cfg = EngineConfig(model=ModelConfig(vocab_size=261, **dict(F.BENCH, max_seq_len=maxlen)),
+                       cache=CacheConfig(block_size=16, num_blocks=maxlen, enable_prefix_caching=shared),
+                       scheduler=SchedulerConfig(max_seqs=16, max_batched_tokens=1024))
+    lib = Lib()
+    eng = cuda_engine(cfg, engine_cls=GpuLLMEngine.resolve(), runner_cls=ReferenceLogitsRunner, lib=lib)
+    if shared:
+        eng.prefix_hasher = DevicePrefixHasher(eng, lib=lib)
+    got = run(eng, mixed_workload(48, 0, 256 if shared else 0))
+    assert got == F.streams(f"streams_{workload}.npz")
+    assert eng.total_steps == int(F.load(f"streams_{workload}.npz")["steps"])
+    if shared:
+        assert eng.prefix_hasher.misses == 0 and eng.prefix_hasher.lookups > 0
