@@ -726,6 +726,10 @@ def main_llama(args, torch, dev, rank, world):
     for i in range(args.warmup):  # short requests: every graph bucket and kernel warmed
         run_workload(eng, llama_workload(16, seed=100 + i, out_mean=24), f"w{i}")
         _progress(f"warm-up {i} done")
+    # as many short sequences as the timed run holds, with spread-out lengths: decode passes
+    # shrink through every token bucket (graph) of the ladder before the timed region
+    run_workload(eng, llama_workload(args.llama_requests, seed=99, prompt_mean=48, out_mean=40), "wd")
+    _progress("decode warm-up done")
     reqs = llama_workload(args.llama_requests, seed=0)
     run.roofline_peaks = (hbm, tfl)
     run.roofline_s = 0.0
@@ -764,7 +768,8 @@ def main_llama(args, torch, dev, rank, world):
                                "(32-8192) output mean 256 (16-1024), budget 8192, block 16, greedy",
                    "model": "Llama-3-8B shape (random init)", "global_batch": len(reqs), "seq_len": 9216,
                    "parallelism": f"tp{world}", "forward_passes": steps, "num_blocks": args.llama_blocks,
-                   "warmup": f"{args.warmup} short 16-request workloads", "l2": "flushed before the timed workload"},
+                   "warmup": f"{args.warmup} short 16-request workloads and one {args.llama_requests}-request "
+                             "short workload (every decode bucket)", "l2": "flushed before the timed workload"},
         "ttft_p50_ms": round(1e3 * statistics.median(ttft), 1) if ttft else None,
         "wall_s": round(t_wall, 3),
         "gpu_launches": int(launches),
