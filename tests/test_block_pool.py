@@ -319,3 +319,67 @@ def test_pooled_packing_rejects_what_the_reference_cannot_index():
         pack([1], n=20, rid="w")  # table too short for the context
     with pytest.raises(ValueError):
         pack([1, 2, 3, 4, 5], rid="v")  # wider than the pool
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_pooled_tables_under_random_table_histories(seed):
+    """Random pass sequences without the reference scheduler: sequences grow
+    block by block, have the block being written replaced (copy-on-write),
+    get a new empty table and are rebuilt (preemption), retire, and new ones
+    arrive, with fewer pool rows than sequences over time. After every pass
+    the tables read through the pool (both restatements of the kernel's
+    phases) equal the classic record's."""
+    from types import SimpleNamespace as NS
+
+    from vllt.runner import StepPacker
+
+    rng = np.random.default_rng(seed)
+    bs, nb, width, rows = 4, 4096, 40, 12
+    classic = StepPacker(bs, nb, 100, 160, 8)
+    pooled = StepPacker(bs, nb, 100, 160, 8, pool_slots=rows, pool_width=width)
+    pool = np.full((rows, width), -1, np.int32)
+    pool_k = pool.copy()
+    live, next_id = [], 0
+    for step in range(120):
+        while len(live) < 8 and rng.random() < 0.5:  # arrivals
+            live.append(NS(request_id=f"q{next_id}", table=NS(block_ids=[]), filled=0, draft_token_ids=[]))
+            next_id += 1
+        sched = []
+        for seq in list(live):
+            r = rng.random()
+            if r < 0.05:  # retire
+                live.remove(seq)
+                continue
+            if r < 0.12:  # preempted: a new empty table, recomputed from position 0
+                seq.table, seq.filled = NS(block_ids=[]), 0
+            if rng.random() < 0.3:
+                continue  # not scheduled this pass
+            n = int(rng.integers(1, 9))
+            if seq.filled + n > 150:
+                live.remove(seq)
+                continue
+            ids = seq.table.block_ids
+            if seq.filled % bs and ids and rng.random() < 0.3:  # copy-on-write of the block being written
+                ids[seq.filled // bs] = int(rng.integers(0, nb))
+            while len(ids) * bs < seq.filled + n:
+                ids.append(int(rng.integers(0, nb)))
+            seq.token_ids = [1] * (seq.filled + n)
+            sched.append(NS(seq=seq, start_pos=seq.filled, num_tokens=n))
+            seq.filled += n
+        if not sched:
+            continue
+        out = NS(scheduled=sched, cow=[])
+        rc = classic.pack(out)[0]
+        rp = pooled.pack(out)[0]
+        fc, fp = classic.fields(rc), pooled.fields(rp)
+        got, err = apply_pooled(pool, fp, bs, nb)
+        assert err == 0
+        if "lib" in HOST:
+            got_k, err_k = apply_pooled_kernel_code(pool_k, rp, bs, nb)
+            assert err_k == 0
+            np.testing.assert_array_equal(got_k, got)
+        ctx = fc["start"].astype(np.int64) + fc["qlen"]
+        for s in range(fc["S"]):
+            used = -(-int(ctx[s]) // bs)
+            np.testing.assert_array_equal(got[s, :used], fc["tables"][s, :used])
+    assert next_id > rows  # more sequences than pool rows over the run: rows were reused
