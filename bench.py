@@ -692,6 +692,46 @@ def _progress(what: str) -> None:
     print(f"[rank {os.environ.get('RANK', '0')}] {what} {time.strftime('%H:%M:%S')}", file=sys.stderr, flush=True)
 
 
+def allreduce_profile(torch, dev, comm, d_model, reps=20):
+    """Device time (us, max over ranks) of one libvllt all-reduce
+    (vllt_tp_allreduce_bf16: bf16, in place, the forward's collective after
+    o_proj and down_proj) of `rows x d_model` for every token bucket the
+    forward's graphs use. Every rank calls it with the same sizes, before the
+    engine starts, so the ranks take the same collectives in the same order."""
+    import torch.distributed as dist
+
+    from vllt import _lib
+    from vllt.runner import token_bucket
+
+    L = _lib.lib()
+    sizes = sorted({token_bucket(t) for t in range(1, 8193)})
+    buf = torch.zeros(sizes[-1] * d_model, dtype=torch.bfloat16, device=dev)
+    st = _lib.stream_handle()
+    times = []
+    for rows in sizes:
+        n = rows * d_model
+        for _ in range(3):
+            _lib.check(L.vllt_tp_allreduce_bf16(buf.data_ptr(), n, comm, st))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            _lib.check(L.vllt_tp_allreduce_bf16(buf.data_ptr(), n, comm, st))
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3 / reps)
+    t = torch.tensor(times, dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return dict(zip(sizes, (round(float(x), 2) for x in t.cpu())))
+
+
+def allreduce_share(pass_log, ar_us: dict, n_layers: int, max_tokens: int) -> float:
+    """Seconds of all-reduce in the logged passes: two per layer, each of the
+    pass's graph bucket (the rows the forward reduces)."""
+    from vllt.runner import token_bucket
+
+    return sum(2 * n_layers * ar_us[min(token_bucket(tokens), max_tokens)] for tokens, _, _, _ in pass_log) / 1e6
+
+
 def main_llama(args, torch, dev, rank, world):
     """Llama-3-8B-shaped continuous batching, tensor parallel over all ranks:
     512 requests (prompt mean 1024, output mean 256), greedy, bf16."""
@@ -702,6 +742,7 @@ def main_llama(args, torch, dev, rank, world):
 
     cfg = llama_config(args.llama_blocks)
     group = TPGroup() if world > 1 else None
+    ar_us = allreduce_profile(torch, dev, group.comm, cfg.model.d_model) if world > 1 else None
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             pk = json.load(f)
@@ -782,6 +823,11 @@ def main_llama(args, torch, dev, rank, world):
     }
     ps = run.pass_summary()
     line["breakdown"] = dict(ps, host_and_other_s=round(elapsed - ps["gpu_s"], 3))
+    if ar_us is not None:  # the tensor-parallel collectives' share of the forward passes
+        ar_s = allreduce_share(run.pass_log, ar_us, cfg.model.n_layers, run.caps.max_tokens)
+        line["breakdown"].update(allreduce_s_est=round(ar_s, 3),
+                                 allreduce_share_of_pass_gpu=round(ar_s / max(ps["gpu_s"], 1e-9), 3),
+                                 allreduce_us_by_rows={str(k): v for k, v in ar_us.items() if k in (16, 64, 256, 512, 1024, 8192)})
     print(json.dumps(line), flush=True)
     if world > 1:  # after the result line: graphs holding NCCL calls go before the communicators
         _progress("teardown")

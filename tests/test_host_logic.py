@@ -339,3 +339,14 @@ def test_c_abi_rejects_inconsistent_calls_before_any_launch():
     # the allocation-free attention: unknown dtype
     assert L.vllt_paged_attention_varlen_noalloc(fake, fake, fake, fake, 4, fake, fake, 1, 1, 1, 16, 8, 4, 48, 16, 64,
                                                  0.1, 9, fake, None, None) == _lib.VLLT_ERR_ARG
+
+
+def test_allreduce_share_counts_two_bucket_reductions_per_layer():
+    """bench.py's estimate of the tensor-parallel collectives per pass: two
+    all-reduces per layer of the pass's graph bucket of rows."""
+    import bench
+
+    ar_us = {16: 10.0, 32: 12.0, 512: 40.0, 640: 50.0}
+    log = [(1, 1, None, None), (20, 20, None, None), (512, 512, None, None), (513, 10, None, None)]
+    got = bench.allreduce_share(log, ar_us, n_layers=32, max_tokens=8192)
+    assert abs(got - 2 * 32 * (10 + 12 + 40 + 50) / 1e6) < 1e-12
