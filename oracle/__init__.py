@@ -13,6 +13,10 @@ CUDA library replaces:
   sampling.py   greedy / temperature / top-k / top-p sampling and the
                 speculative accept/reject rule     (vllmlite/sampling.py:16-64,
                                                     vllmlite/speculative.py:86-100)
+  llama_bf16.py the same forward with the bf16 Llama-shaped path's rounding
+                points (torch on the CPU), to measure the bf16 error the GPU
+                tests' tolerances are derived from; with rounding off it is
+                pinned to model.py's forward
 
 Who may use it: only `tests/`, `__graft_entry__.smoke()` and the CPU-baseline
 leg of `bench.py`, and only as the checker. The shipped library

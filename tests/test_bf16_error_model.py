@@ -28,3 +28,31 @@ def test_bars_are_three_times_the_measured_bf16_error():
         assert 1e-3 < max(r["bf16"]) and 3 * max(r["bf16"]) <= SMALL_BAR, r
         assert 3 * max(r["tp"]) <= TP_BAR, r
         assert min(r["dropped"]) > 5 * SMALL_BAR, r
+
+
+def test_error_model_computes_the_reference_forward_without_rounding():
+    """With rounding off, oracle/llama_bf16.py is the reference's forward
+    (vllmlite/model.py:80-120, as oracle/model.py restates it and the golden
+    replays pin it): same RoPE pairs, GQA head grouping, SwiGLU and norms, on
+    the reference's seeded weights of a small model; logits at every position
+    agree within fp32 reassociation."""
+    from oracle import model as OM
+    from oracle.llama_bf16 import forward_sequence
+    from tests import fixtures as F
+
+    cfg = OM.Shape(vocab_size=261, **F.TINY)
+    w = OM.seeded_weights(cfg)
+    emu = {"tok_emb": torch.from_numpy(w["tok_emb"]), "lm_head": torch.from_numpy(w["lm_head"].T.copy())}
+    for i in range(cfg.n_layers):
+        for k in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"):
+            emu[f"{i}.{k}"] = torch.from_numpy(w[f"layers.{i}.{k}"].T.copy())  # reference [in][out] -> [out][in]
+    T = 37
+    toks = np.random.default_rng(2).integers(0, 261, size=T)
+    hd, KV = cfg.head_dim, cfg.n_kv_heads
+    ck = np.zeros((cfg.n_layers, T, KV, hd), np.float32)
+    cv = np.zeros_like(ck)
+    slots = np.arange(T)
+    want = OM.forward(cfg, w, toks, np.arange(T), ck, cv, [(0, T, slots, slots)], np.arange(T))
+    with torch.no_grad():
+        got = forward_sequence(cfg, emu, toks.tolist(), [(0, T)], bf16=False).numpy()
+    np.testing.assert_allclose(got, want, rtol=0, atol=2e-5 * np.abs(want).max())
