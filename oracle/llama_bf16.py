@@ -77,7 +77,8 @@ def _rope(x, pos, cos, sin):
     return y
 
 
-def forward_sequence(shape, w: dict, tokens, chunks, bf16: bool = True, tp: int = 1, drop_head=None):
+def forward_sequence(shape, w: dict, tokens, chunks, bf16: bool = True, tp: int = 1, drop_head=None,
+                     wide: bool = False):
     """fp32 logits [len(tokens), V] of one sequence at every position.
 
     chunks: list of (start, n) in which the sequence's prompt went through the
@@ -85,8 +86,17 @@ def forward_sequence(shape, w: dict, tokens, chunks, bf16: bool = True, tp: int 
     probabilities when bf16). tp: tensor-parallel ranks whose row-parallel
     partials are rounded and summed in bf16. drop_head: a query head whose
     attention output is zeroed in every layer (a planted kernel mistake, to
-    show what the tolerances catch)."""
+    show what the tolerances catch). wide: every contraction (projections,
+    scores, P.V) accumulates in float64 before it is rounded to fp32, to
+    measure how much the order of fp32 accumulation alone moves the result
+    (the GPU accumulates in another order than the CPU)."""
     import torch
+
+    def mm(a, b):
+        return (a.double() @ b.double()).float() if wide else a @ b
+
+    def es(eq, a, b):
+        return torch.einsum(eq, a.double(), b.double()).float() if wide else torch.einsum(eq, a, b)
 
     D, H, KV = shape.head_dim, shape.n_heads, shape.n_kv_heads
     T = len(tokens)
@@ -102,42 +112,42 @@ def forward_sequence(shape, w: dict, tokens, chunks, bf16: bool = True, tp: int 
     def rowpar(a, wm, parts):
         """a . wm^T, in `parts` column slices of `a` (rows of wm^T) when bf16 TP."""
         if not bf16 or parts == 1:
-            return a @ wm.T
+            return mm(a, wm.T)
         k = a.shape[1] // parts
         acc = None
         for r in range(parts):
-            p = _bf(a[:, r * k:(r + 1) * k] @ wm[:, r * k:(r + 1) * k].T, True)
+            p = _bf(mm(a[:, r * k:(r + 1) * k], wm[:, r * k:(r + 1) * k].T), True)
             acc = p if acc is None else _bf(acc + p, True)
         return acc
 
     x = w["tok_emb"][torch.as_tensor(tokens)]
     for i in range(shape.n_layers):
         h = _bf(_rmsnorm(x), bf16)
-        q = _bf(_rope((h @ w[f"{i}.wq"].T).view(T, H, D), pos, cos, sin), bf16)
-        k = _bf(_rope((h @ w[f"{i}.wk"].T).view(T, KV, D), pos, cos, sin), bf16)
-        v = _bf((h @ w[f"{i}.wv"].T).view(T, KV, D), bf16)
+        q = _bf(_rope(mm(h, w[f"{i}.wq"].T).view(T, H, D), pos, cos, sin), bf16)
+        k = _bf(_rope(mm(h, w[f"{i}.wk"].T).view(T, KV, D), pos, cos, sin), bf16)
+        v = _bf(mm(h, w[f"{i}.wv"].T).view(T, KV, D), bf16)
         kk = k.repeat_interleave(rep, dim=1)
         vv = v.repeat_interleave(rep, dim=1)
         o = torch.empty(T, H, D)
         for q0 in range(0, T, 512):  # query blocks: bounded memory at long contexts
             q1 = min(T, q0 + 512)
-            s = torch.einsum("thd,shd->hts", q[q0:q1], kk[:q1]) / np.float32(np.sqrt(D))
+            s = es("thd,shd->hts", q[q0:q1], kk[:q1]) / np.float32(np.sqrt(D))
             s = s.masked_fill(~causal[None, q0:q1, :q1], float("-inf"))
             m = s.max(-1, keepdim=True).values
             p = torch.exp(s - m)
             l = p.sum(-1, keepdim=True)
             if bf16:
                 p = torch.where(multi[None, q0:q1, None], _bf(p, True), p)
-            o[q0:q1] = torch.einsum("hts,shd->thd", p, vv[:q1]) / l.permute(1, 0, 2)
+            o[q0:q1] = es("hts,shd->thd", p, vv[:q1]) / l.permute(1, 0, 2)
         if drop_head is not None:
             o[:, drop_head] = 0
         a = _bf(o.reshape(T, H * D), bf16)
         x = x + rowpar(a, w[f"{i}.wo"], tp)
         h = _bf(_rmsnorm(x), bf16)
-        g, u = h @ w[f"{i}.w_gate"].T, h @ w[f"{i}.w_up"].T
+        g, u = mm(h, w[f"{i}.w_gate"].T), mm(h, w[f"{i}.w_up"].T)
         act = _bf(g / (1 + torch.exp(-g)) * u, bf16)
         x = x + rowpar(act, w[f"{i}.w_down"], tp)
-    return _bf(_rmsnorm(x), bf16) @ w["lm_head"].T
+    return mm(_bf(_rmsnorm(x), bf16), w["lm_head"].T)
 
 
 def schedule_sequences(passes):
@@ -168,13 +178,14 @@ def _errors(got, ref):
     return mx, rms
 
 
-def schedule_error(shape, passes, seed: int = 0, tp: int = 1, drop_head=None):
+def schedule_error(shape, passes, seed: int = 0, tp: int = 1, drop_head=None, order: bool = False):
     """The errors the GPU tests bound, worst over the passes of a schedule:
     {"bf16": (max-rel, row-rel) of bf16 against fp32, "tp": the same of bf16
     with `tp` ranks against bf16 on one rank (when tp > 1), "dropped": bf16
-    with `drop_head` zeroed against fp32 (when given)}. max-rel is
-    max |a - b| / max |b| over a pass's rows; row-rel is the largest
-    ||a_r - b_r|| / ||b_r|| of a row."""
+    with `drop_head` zeroed against fp32 (when given), "order": bf16 with
+    float64 accumulation against bf16 with fp32 accumulation (when order)}.
+    max-rel is max |a - b| / max |b| over a pass's rows; row-rel is the
+    largest ||a_r - b_r|| / ||b_r|| of a row."""
     import torch
 
     w = llama_weights(shape, seed)
@@ -188,6 +199,8 @@ def schedule_error(shape, passes, seed: int = 0, tp: int = 1, drop_head=None):
                 r["tp"] = forward_sequence(shape, w, toks, chunks, bf16=True, tp=tp)
             if drop_head is not None:
                 r["dropped"] = forward_sequence(shape, w, toks, chunks, bf16=True, drop_head=drop_head)
+            if order:
+                r["wide"] = forward_sequence(shape, w, toks, chunks, bf16=True, wide=True)
             out[key] = r
     worst = {}
     for step in rows:
@@ -197,6 +210,8 @@ def schedule_error(shape, passes, seed: int = 0, tp: int = 1, drop_head=None):
             pairs["tp"] = ("tp", "bf16")
         if drop_head is not None:
             pairs["dropped"] = ("dropped", "fp32")
+        if order:
+            pairs["order"] = ("wide", "bf16")
         for name, (a, b) in pairs.items():
             e = _errors(pick(a), pick(b))
             old = worst.get(name, (0.0, 0.0))

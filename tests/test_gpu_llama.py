@@ -17,6 +17,11 @@ N(0, 0.02) law; `python tests/bf16_bars.py` reprints the measurements):
     prefilled in two chunks (the second over a cached prefix of 2100 / 4000
     tokens), then decode and verify rows at contexts 4501 and 8104: measured
     1.21e-2 (1.30e-2) -> bar 4e-2.
+The comparison is with the fp32 re-run (anchored to the reference by the fp32
+replays) rather than with the CPU model of the bf16 rounding: the order of fp32
+accumulation alone moves the bf16 result by 2.6-4.1e-3 on the small model (the
+model run with float64 against fp32 contractions), so a bf16-to-bf16 bar could
+not be much tighter.
 A planted mistake shows the margin: zeroing one attention head in every layer
 moves the logits by 0.28-0.69 in both measures (oracle/llama_bf16.py,
 tests/test_bf16_error_model.py). The greedy pick must also agree on every row
