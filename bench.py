@@ -875,6 +875,14 @@ def main_reference(args):
     except Exception as e:
         print(json.dumps({"impl": "reference", "unavailable": f"vllm-lite not importable: {e}"}))
         return
+    if args.workload not in ("mixed", "shared", "decode"):
+        why = {"llama8b": "the reference runs the Llama-3-8B shape only in NumPy on the host, impractical at "
+                          "this size (a 2-layer slice is its CPU parity check)",
+               "spec": "run the reference's speculative engine through --workload spec's own cpu_baseline",
+               "gemm": "the reference has no separate projection kernels (NumPy matmul inside its forward)",
+               "prefill": "the reference has no separate prefill attention (NumPy inside its forward)"}
+        print(json.dumps({"impl": "reference", "unavailable": why[args.workload]}), flush=True)
+        return
     wl = "mixed" if args.workload == "decode" else args.workload
     for _ in range(args.warmup):
         reference_run(wl)
