@@ -1,7 +1,7 @@
 """Build the host-compiled test harnesses (tests/*_host.cpp).
 
 Some kernels keep their per-item arithmetic in CUDA-free headers under
-vllm-lite_b200/csrc (prefix_hash.cuh, table_pool.cuh) so that the same code
+vllm-lite_b200/csrc (prefix_hash.cuh, meta_items.cuh) so that the same code
 compiles for the host; a harness wraps it in extern "C" functions that the CPU
 tests call through ctypes. Built with g++ into a temporary directory per test
 session (nothing is written into the repository).

@@ -7,7 +7,7 @@ and uploads per pass only the (row, index, block id) entries that changed
 n-gram proposer) drives a runner that packs every pass both ways; the pooled
 record's updates are applied to a host copy of the pool twice: by a NumPy
 restatement of build_meta_kernel's phases 0 and 2, and by the kernel's own
-per-item code (csrc/table_pool.cuh, compiled for the host by g++). The tables
+per-item code (csrc/meta_items.cuh, compiled for the host by g++). The tables
 read back through each sequence's row must equal the classic record's tables
 bit for bit, on the 48-request mixed-length (C1) and shared-prefix (C2)
 benchmarks, the 512-request Llama-shaped workload (C4), and small runs that
@@ -23,7 +23,7 @@ from tests.conftest import needs_vllmlite
 pytestmark = needs_vllmlite
 
 
-HOST = {}  # the host-compiled build_meta_kernel pool phases (tests/table_pool_host.cpp), when g++ exists
+HOST = {}  # the host-compiled build_meta_kernel pool phases (tests/meta_host.cpp), when g++ exists
 
 
 @pytest.fixture(autouse=True, scope="module")
@@ -32,7 +32,7 @@ def _host_pool_phases(tmp_path_factory):
 
     from tests.host_build import build_harness
 
-    lib = build_harness("table_pool_host", str(tmp_path_factory.mktemp("tp")))
+    lib = build_harness("meta_host", str(tmp_path_factory.mktemp("tp")))
     if lib is not None:
         lib.apply_pooled_host.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
         HOST["lib"] = lib
@@ -42,7 +42,7 @@ def _host_pool_phases(tmp_path_factory):
 
 def apply_pooled_kernel_code(pool, rec, bs, num_blocks):
     """The same phases with the kernel's own per-item code (pool_update /
-    pool_entry of csrc/table_pool.cuh) compiled for the host."""
+    pool_entry of csrc/meta_items.cuh) compiled for the host."""
     S, W = int(rec[0]), int(rec[3])
     rec = np.ascontiguousarray(rec, np.int32)
     out = np.zeros((S, W), np.int32)

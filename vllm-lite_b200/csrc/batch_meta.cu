@@ -5,7 +5,6 @@
 // CTA (no grid sync, no second launch) has the lowest latency.
 
 #include "meta.cuh"
-#include "table_pool.cuh"
 
 namespace vllt {
 
@@ -49,16 +48,6 @@ __device__ int4 block_exclusive_scan(int4 v, int4* warp_tot, int4* total) {
                      base.w + incl.w - v.w);
   __syncthreads();
   return r;
-}
-
-// Largest i in [0, n) with a[i] <= key (a ascending, a[0] == 0 <= key).
-__device__ __forceinline__ int upper_index(const int32_t* a, int n, int key) {
-  int lo = 0, hi = n - 1;
-  while (lo < hi) {
-    int mid = (lo + hi + 1) >> 1;
-    if (a[mid] <= key) lo = mid; else hi = mid - 1;
-  }
-  return lo;
 }
 
 // `pool` (NULL: the record carries the tables) is the persistent block-table
@@ -113,11 +102,10 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
     int4 v = make_int4(0, 0, 0, 0);
     if (s < S) {
       const int q = qlen[s];
-      v = make_int4(q, count[s], q == 1 ? 1 : 0, q > 1 ? ceil_div(q, qp) : 0);
-      const int c = start[s] + q;
-      atomicMax(&s_max_ctx, c);
+      v = make_int4(q, count[s], q == 1 ? 1 : 0, seq_tiles(q, qp));
+      atomicMax(&s_max_ctx, start[s] + q);
       atomicMax(&s_max_q, q);
-      if (q < 1 || count[s] < 1 || count[s] > q || start[s] < 0 || c > W * bs) atomicOr(&s_err, 2);
+      if (seq_fields_bad(start[s], q, count[s], W, bs)) atomicOr(&s_err, 2);
     }
     int4 ex = block_exclusive_scan(v, warp_tot, &total);
     if (s < S) {
@@ -157,8 +145,9 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
       blk = pool_entry(pool, pool_slots, L.W_cap, seq_slot[s], b, used, num_blocks, &bad);
       if (bad) atomicOr(&s_err, 2);
     } else {
-      blk = tables[i];
-      if (b < used && (blk < 0 || blk >= num_blocks)) { atomicOr(&s_err, 2); blk = -1; }
+      bool bad = false;
+      blk = record_entry(tables[i], b, used, num_blocks, &bad);
+      if (bad) atomicOr(&s_err, 2);
     }
     meta[L.tables + (int64_t)s * L.W_cap + b] = blk;
   }
@@ -167,21 +156,15 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
   // Phase 3: per token -> sequence, position, flat slot (runner.py:75, :83-84).
   const int Tv = min(T, cu_q[S]);
   for (int t = threadIdx.x; t < Tv; t += kThreads) {
-    const int s = upper_index(cu_q, S + 1, t);
-    const int p = start[s] + (t - cu_q[s]);
-    const int b = p / bs;  // p >= 0 and p < W * bs were validated in phase 1
-    const int blk = b < W ? meta[L.tables + (int64_t)s * L.W_cap + b] : -1;
-    meta[L.pos + t] = p;
-    meta[L.tok_seq + t] = s;
+    const TokenMeta m = token_meta(cu_q, S, start, meta + L.tables, L.W_cap, W, bs, t);
+    meta[L.pos + t] = m.pos;
+    meta[L.tok_seq + t] = m.seq;
     meta[L.tokens + t] = tokens[t];
-    meta[L.slot + t] = blk < 0 ? -1 : blk * bs + p % bs;
+    meta[L.slot + t] = m.slot;
   }
   // Phase 4: logit rows = the last `count` tokens of each sequence (runner.py:86-90).
   const int Rv = min(R, cu_rows[S]);
-  for (int r = threadIdx.x; r < Rv; r += kThreads) {
-    const int s = upper_index(cu_rows, S + 1, r);
-    meta[L.rows + r] = cu_q[s] + qlen[s] - count[s] + (r - cu_rows[s]);
-  }
+  for (int r = threadIdx.x; r < Rv; r += kThreads) meta[L.rows + r] = row_token(cu_rows, cu_q, qlen, count, S, r);
   // Phase 5: multi-token query tiles (seq, first query index).
   const int n_tiles = cu_tiles[S];
   for (int i = threadIdx.x; i < n_tiles; i += kThreads) {
