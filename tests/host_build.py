@@ -1,7 +1,7 @@
 """Build the host-compiled test harnesses (tests/*_host.cpp).
 
 Some kernels keep their per-item arithmetic in CUDA-free headers under
-vllm-lite_b200/csrc (prefix_hash.cuh, meta_items.cuh) so that the same code
+vllm-lite_b200/csrc (prefix_hash.cuh, meta_items.cuh, sampler_row.cuh) so that the same code
 compiles for the host; a harness wraps it in extern "C" functions that the CPU
 tests call through ctypes. Built with g++ into a temporary directory per test
 session (nothing is written into the repository).
@@ -21,6 +21,8 @@ def build_harness(name: str, out_dir: str):
     if gxx is None:
         return None
     out = os.path.join(out_dir, f"lib{name}.so")
-    subprocess.run([gxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-I", os.path.join(ROOT, "vllm-lite_b200", "csrc"),
+    # no FMA contraction: the device code rounds every product and quotient (__fmul_rn, __fdiv_rn)
+    subprocess.run([gxx, "-O2", "-std=c++20", "-ffp-contract=off", "-shared", "-fPIC", "-I",
+                    os.path.join(ROOT, "vllm-lite_b200", "csrc"),
                     os.path.join(ROOT, "tests", f"{name}.cpp"), "-o", out], check=True)
     return ctypes.CDLL(out)

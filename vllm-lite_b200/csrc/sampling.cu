@@ -6,6 +6,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "sampler_row.cuh"
 
 namespace vllt {
 
@@ -109,24 +110,67 @@ __global__ void accept_kernel(const int32_t* __restrict__ cu_rows, const int32_t
   n_accepted[s] = acc;
 }
 
-// Map a float to an unsigned key with the same order (for bisection).
-__device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
+// The CTA of one row as sampler_row.cuh's execution policy: every thread
+// takes c = threadIdx.x, + kThreads, ...; reductions are block_reduce; the
+// CDF search scans kThreads entries at a time in shared memory (float64),
+// carrying the running sum, and stops at the first chunk that holds the
+// crossing (the lowest such index wins).
+struct BlockPolicy {
+  __device__ int tid() const { return threadIdx.x; }
+  __device__ int stride() const { return kThreads; }
+  __device__ int reduce_sum(int v) { return block_reduce<int>(v, [](int a, int b) { return a + b; }, 0); }
+  __device__ float reduce_sum(float v) { return block_reduce<float>(v, [](float a, float b) { return a + b; }, 0.f); }
+  __device__ double reduce_sum(double v) {
+    return block_reduce<double>(v, [](double a, double b) { return a + b; }, 0.0);
+  }
+  __device__ float reduce_max(float v) {
+    return block_reduce<float>(v, [](float a, float b) { return fmaxf(a, b); }, -INFINITY);
+  }
+  template <class F>
+  __device__ int first_crossing(int n, F pc_of, double u) {
+    __shared__ double carry_s;
+    __shared__ int pick_s;
+    __shared__ double scan[kThreads];
+    if (threadIdx.x == 0) {
+      carry_s = 0.0;
+      pick_s = INT32_MAX;
+    }
+    __syncthreads();
+    for (int base = 0; base < n; base += kThreads) {
+      const int c = base + threadIdx.x;
+      const double pc = c < n ? pc_of(c) : 0.0;
+      scan[threadIdx.x] = pc;  // inclusive scan of pc across the CTA
+      __syncthreads();
+      for (int o = 1; o < kThreads; o <<= 1) {
+        const double add = threadIdx.x >= o ? scan[threadIdx.x - o] : 0.0;
+        __syncthreads();
+        scan[threadIdx.x] += add;
+        __syncthreads();
+      }
+      const double cdf = carry_s + scan[threadIdx.x];
+      const double prev = cdf - pc;
+      if (c < n && pc > 0.0 && prev <= u && u < cdf) atomicMin(&pick_s, c);
+      __syncthreads();
+      if (threadIdx.x == 0) carry_s += scan[kThreads - 1];
+      __syncthreads();
+      if (pick_s != INT32_MAX) break;  // uniform: every thread reads it after the barrier
+    }
+    const int pick = pick_s;
+    __syncthreads();
+    return pick == INT32_MAX ? -1 : pick;
+  }
+  template <class F>
+  __device__ int last(int n, F pred) {
+    int best = -1;
+    for (int c = threadIdx.x; c < n; c += kThreads)
+      if (pred(c)) best = c;
+    return block_reduce<int>(best, [](int a, int b) { return a > b ? a : b; }, -1);
+  }
+};
 
-// The full sampler of sampling.py:41-64 for temperature rows; one CTA per row.
-// The row's logits pass through the reference's pre-steps on the fly, in its
-// order: EOS masked to -inf while min_tokens is not reached (:51-52), the
-// repetition penalty on every token the row has seen (:54, :8-13), division by
-// the temperature (:59); then top-k (:16-20), top-p (:23-33) and the draw
-// (:63-64). The k-th largest value and the nucleus threshold are found by
-// bisection over order keys, so any vocab size works with O(32 * vocab) work
-// and no sort. The draw is numpy's Generator.choice with the uniform `uni[r]`
-// it would have taken from the request's generator: the first index whose
-// float64 CDF (cumulative sum of the kept probabilities, divided by the total)
-// exceeds u. Row r reads logits row row_index[r] (r when NULL); an index
-// outside [0, logit_rows) yields token -1 and nothing else is read.
+// The temperature sampler of sampling.py:41-64 (sampler_row.cuh); one CTA per
+// row. Row r reads logits row row_index[r] (r when NULL); an index outside
+// [0, logit_rows) yields token -1 and nothing else is read.
 __global__ void top_p_kernel(const float* __restrict__ logits, int vocab, int ld, int logit_rows,
                              const int32_t* __restrict__ row_index, const uint8_t* __restrict__ eos_mask,
                              int eos_id, const float* __restrict__ penalty, const uint32_t* __restrict__ seen,
@@ -139,122 +183,17 @@ __global__ void top_p_kernel(const float* __restrict__ logits, int vocab, int ld
     if (threadIdx.x == 0) out[r] = -1;
     return;
   }
-  const float* x = logits + (int64_t)src * ld;
-  const bool mask_eos = eos_mask && eos_mask[r] && eos_id >= 0 && eos_id < vocab;
-  const float pen = penalty ? penalty[r] : 1.f;
-  const uint32_t* sb = (seen && pen != 1.f) ? seen + (int64_t)r * seen_words : nullptr;
-  const float temp = temperature[r];
-  const int k = top_k ? top_k[r] : 0;
-  const float p = top_p ? top_p[r] : 1.f;
-  auto val = [&](int c) {
-    float v = x[c];
-    if (mask_eos && c == eos_id) v = -INFINITY;
-    if (sb && ((sb[c >> 5] >> (c & 31)) & 1u)) v = v > 0.f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
-    return __fdiv_rn(v, temp);
-  };
-
-  // top-k: the largest key v with count(x >= v) >= k
-  uint32_t cut_key = 0;
-  if (k > 0 && k < vocab) {
-    uint32_t lo = 0, hi = 0xffffffffu;
-    while (lo < hi) {
-      const uint32_t mid = lo + (hi - lo + 1) / 2;
-      int cnt = 0;
-      for (int c = threadIdx.x; c < vocab; c += kThreads) cnt += order_key(val(c)) >= mid;
-      cnt = block_reduce<int>(cnt, [](int a, int b) { return a + b; }, 0);
-      if (cnt >= k) lo = mid; else hi = mid - 1;
-    }
-    cut_key = lo;
-  }
-  auto kept_k = [&](float v) { return order_key(v) >= cut_key; };
-  float mx = -INFINITY;
-  for (int c = threadIdx.x; c < vocab; c += kThreads) {
-    const float v = val(c);
-    if (kept_k(v)) mx = fmaxf(mx, v);
-  }
-  mx = block_reduce<float>(mx, [](float a, float b) { return fmaxf(a, b); }, -INFINITY);
-  float sum = 0.f;
-  for (int c = threadIdx.x; c < vocab; c += kThreads) {
-    const float v = val(c);
-    if (kept_k(v)) sum += expf(v - mx);
-  }
-  sum = block_reduce<float>(sum, [](float a, float b) { return a + b; }, 0.f);
-  // top-p: smallest probability b with G(b) = sum_{p_j > b} p_j < p; keep p_i >= b
-  float pmin = 0.f;
-  if (p < 1.f) {
-    uint32_t lo = __float_as_uint(0.f), hi = __float_as_uint(1.f);
-    while (lo < hi) {
-      const uint32_t mid = lo + (hi - lo) / 2;
-      const float b = __uint_as_float(mid);
-      float g = 0.f;
-      for (int c = threadIdx.x; c < vocab; c += kThreads) {
-        const float v = val(c);
-        if (kept_k(v)) {
-          const float pc = __fdiv_rn(expf(v - mx), sum);
-          if (pc > b) g += pc;
-        }
-      }
-      g = block_reduce<float>(g, [](float a, float b2) { return a + b2; }, 0.f);
-      if (g < p) hi = mid; else lo = mid + 1;
-    }
-    pmin = __uint_as_float(lo);
-  }
-  auto kept = [&](float v) {
-    return kept_k(v) && (p >= 1.f || __fdiv_rn(expf(v - mx), sum) >= pmin);
-  };
-  // renormalised probabilities, CDF in vocab order (numpy's choice: cumsum in
-  // float64, divided by the total, first index with cdf > u)
-  float s2 = 0.f;
-  for (int c = threadIdx.x; c < vocab; c += kThreads) {
-    const float v = val(c);
-    if (kept(v)) s2 += expf(v - mx);
-  }
-  s2 = block_reduce<float>(s2, [](float a, float b) { return a + b; }, 0.f);
-  __shared__ double carry_s;
-  __shared__ int pick_s;
-  if (threadIdx.x == 0) { carry_s = 0.0; pick_s = -1; }
-  __syncthreads();
-  double total = 0.0;
-  for (int c = threadIdx.x; c < vocab; c += kThreads) {
-    const float v = val(c);
-    if (kept(v)) total += (double)__fdiv_rn(expf(v - mx), s2);
-  }
-  total = block_reduce<double>(total, [](double a, double b) { return a + b; }, 0.0);
-  const double u = uni[r] * total;
-  for (int base = 0; base < vocab; base += kThreads) {
-    const int c = base + threadIdx.x;
-    double pc = 0.0;
-    if (c < vocab) {
-      const float v = val(c);
-      if (kept(v)) pc = (double)__fdiv_rn(expf(v - mx), s2);
-    }
-    // inclusive scan of pc across the CTA
-    __shared__ double scan[kThreads];
-    scan[threadIdx.x] = pc;
-    __syncthreads();
-    for (int o = 1; o < kThreads; o <<= 1) {
-      const double add = threadIdx.x >= o ? scan[threadIdx.x - o] : 0.0;
-      __syncthreads();
-      scan[threadIdx.x] += add;
-      __syncthreads();
-    }
-    const double cdf = carry_s + scan[threadIdx.x];
-    const double prev = cdf - pc;
-    if (c < vocab && pc > 0.0 && prev <= u && u < cdf) atomicCAS(&pick_s, -1, c);
-    __syncthreads();
-    if (threadIdx.x == 0) carry_s += scan[kThreads - 1];
-    __syncthreads();
-    if (pick_s >= 0) break;
-  }
-  if (threadIdx.x == 0) {
-    int pk = pick_s;
-    if (pk < 0) {  // u at the very top after rounding: the last kept token
-      pk = 0;
-      for (int c = vocab - 1; c >= 0; --c)
-        if (kept(val(c))) { pk = c; break; }
-    }
-    out[r] = pk;
-  }
+  sampler::RowInput row;
+  row.x = logits + (int64_t)src * ld;
+  row.vocab = vocab;
+  row.mask_eos = eos_mask && eos_mask[r] && eos_id >= 0 && eos_id < vocab;
+  row.eos_id = eos_id;
+  row.pen = penalty ? penalty[r] : 1.f;
+  row.seen = (seen && row.pen != 1.f) ? seen + (int64_t)r * seen_words : nullptr;
+  row.temp = temperature[r];
+  BlockPolicy pol;
+  const int pick = sampler::sample_row(pol, row, top_k ? top_k[r] : 0, top_p ? top_p[r] : 1.f, uni[r]);
+  if (threadIdx.x == 0) out[r] = pick;
 }
 
 }  // namespace
