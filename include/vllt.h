@@ -84,6 +84,13 @@ int vllt_copy_blocks(void* k_cache, void* v_cache, const int32_t* pairs, int32_t
  *   block_tables[S][W]  physical block ids (BlockTable.block_ids), padded
  * Its length is 4 + 3*S + T + S*W int32 words.
  *
+ * A token id t < 0 stands for entry -t - 1 of the forward's token source
+ * (vllt_model_desc.token_source): a token the previous pass picked on the
+ * device and the host has not read yet. The metadata builder resolves it; an
+ * id outside [0, embed_rows) after that, or a reference outside the source,
+ * embeds token 0 and sets error bit 1. Without a token source (and in the
+ * vllt_build_batch_meta* entries) a negative id is such an error.
+ *
  * The pooled record leaves the block tables on the device. A persistent pool
  * [pool_slots][max_table_width] int32 (allocated by the caller, contents
  * initially irrelevant) holds one table per live sequence; each pass carries
@@ -133,7 +140,9 @@ int vllt_build_batch_meta_pooled(const int32_t* step_record, const vllt_caps* ca
 /* Device pointers into the meta buffer (for callers that launch their own
  * kernels on it): which = 0 counters[16], 1 cu_seqlens_q[S+1], 2 cu_rows[S+1],
  * 3 ctx_lens[S], 4 positions[T], 5 slot_mapping[T], 6 logit-row token
- * indices[R], 7 block tables [max_seqs][max_table_width]. NULL if unknown. */
+ * indices[R], 7 block tables [max_seqs][max_table_width], 8 token ids[T] (as
+ * resolved: references to the token source replaced by the tokens). NULL if
+ * unknown. */
 int32_t* vllt_meta_field(void* meta, const vllt_caps* caps, int32_t which);
 
 /* Counters: 0 S, 1 T, 2 R, 3 W, 4 single-query sequences, 5 query tiles,
@@ -366,6 +375,13 @@ typedef struct vllt_model_desc {
    * reads pooled records (see vllt_build_batch_meta_pooled). */
   int32_t* table_pool;
   int32_t table_pool_slots;
+  /* Optional token source (device int32 [token_source_len]): the buffer the
+   * previous pass's pick kernels wrote; step-record token ids t < 0 read entry
+   * -t - 1 of it (see the record layout). The pointer is read when the
+   * forward is enqueued, so a CUDA graph keeps it: keep the buffer at one
+   * address. NULL: negative ids are errors. */
+  const int32_t* token_source;
+  int32_t token_source_len;
 } vllt_model_desc;
 
 /* Upper bounds of one step, used to size grids (exact counts are read on the

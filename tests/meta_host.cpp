@@ -31,9 +31,11 @@ extern "C" int apply_pooled_host(const int32_t* rec, int32_t* pool, int pool_slo
 }
 
 // The whole metadata buffer (MetaLayout of the capacities) of one step
-// record, classic (pool == NULL) or pooled; returns the error word.
+// record, classic (pool == NULL) or pooled, with record token ids resolved
+// against tsrc (may be NULL) and checked against vocab; returns the error word.
 extern "C" int build_meta_host(const int32_t* rec, int32_t* pool, int pool_slots, int S_cap, int T_cap, int R_cap,
-                               int W_cap, int bs, int num_blocks, int qp, int32_t* meta) {
+                               int W_cap, int bs, int num_blocks, int qp, int32_t* meta, const int32_t* tsrc,
+                               int tsrc_len, int vocab) {
   const MetaLayout L = MetaLayout::make(S_cap, T_cap, R_cap, W_cap);
   const int S = rec[0], T = rec[1], R = rec[2], W = rec[3];
   const int U = pool ? rec[4] : 0;
@@ -93,7 +95,9 @@ extern "C" int build_meta_host(const int32_t* rec, int32_t* pool, int pool_slots
     const TokenMeta m = token_meta(cu_q, S, start, meta + L.tables, L.W_cap, W, bs, t);
     meta[L.pos + t] = m.pos;
     meta[L.tok_seq + t] = m.seq;
-    meta[L.tokens + t] = tokens[t];
+    bool bad = false;
+    meta[L.tokens + t] = resolve_token(tokens[t], tsrc, tsrc_len, vocab, &bad);
+    if (bad) err |= 2;
     meta[L.slot + t] = m.slot;
   }
   for (int r = 0; r < R && r < cu_rows[S]; ++r) meta[L.rows + r] = row_token(cu_rows, cu_q, qlen, count, S, r);

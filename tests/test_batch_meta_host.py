@@ -28,11 +28,12 @@ def meta_host(tmp_path_factory):
     lib = build_harness("meta_host", str(tmp_path_factory.mktemp("meta")))
     if lib is None:
         pytest.skip("g++ is not available")
-    lib.build_meta_host.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 8 + [ctypes.c_void_p]
+    lib.build_meta_host.argtypes = ([ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 8 +
+                                    [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int])
     return lib
 
 
-def build(host, rec, caps, bs, nb, qp, pool=None):
+def build(host, rec, caps, bs, nb, qp, pool=None, tsrc=None, vocab=261):
     from vllt import _lib
 
     L = _lib.lib()
@@ -41,7 +42,9 @@ def build(host, rec, caps, bs, nb, qp, pool=None):
     rec = np.ascontiguousarray(rec, np.int32)
     err = host.build_meta_host(rec.ctypes.data, pool.ctypes.data if pool is not None else None,
                                pool.shape[0] if pool is not None else 0, caps.max_seqs, caps.max_tokens,
-                               caps.max_rows, caps.max_table_width, bs, nb, qp, meta.ctypes.data)
+                               caps.max_rows, caps.max_table_width, bs, nb, qp, meta.ctypes.data,
+                               tsrc.ctypes.data if tsrc is not None else None,
+                               tsrc.size if tsrc is not None else 0, vocab)
     base = meta.ctypes.data
 
     def field(i, n):  # offsets from the library's own layout function (host arithmetic only)
@@ -108,3 +111,24 @@ def test_kernel_arithmetic_flags_bad_records(meta_host):
     pooled_bad = [1, 3, 1, 1, 1, 0, 3, 1, 256, 1, 2, 1, 2, 0, 5]  # update (2, 0, 5): row 2 of a 2-row pool
     err, meta, f = build(meta_host, pooled_bad, caps, 16, 64, 8, pool[:2])
     assert err & 2 and pool[2].tolist() == [-7] * 4
+
+
+def test_kernel_arithmetic_resolves_token_references(meta_host):
+    """Record token ids t < 0 read entry -t - 1 of the previous pass's picks
+    (the token source); a reference outside the source, a resolved id outside
+    the vocabulary, or a negative id without a source embeds token 0 and sets
+    bit 1 (the step stays runnable); ids >= vocab are flagged the same way."""
+    from vllt import _lib
+
+    caps = _lib.Caps(4, 16, 16, 4)
+    picks = np.array([7, 250, 3, 300, -1], np.int32)  # entries 3 and 4 are not tokens of a 261 vocabulary
+    # two decode sequences: tokens -(1 + 1) -> picks[1] = 250, 5 -> 5
+    rec = [2, 2, 2, 1, 0, 4, 1, 1, 1, 1, -2, 5, 1, 2]
+    err, meta, f = build(meta_host, rec, caps, 16, 64, 8, tsrc=picks)
+    assert err == 0 and f(8, 2).tolist() == [250, 5]
+    for bad_tok in (-4, -5, -6, 261):  # picks[3] = 300, picks[4] = -1, beyond the source, beyond the vocabulary
+        err, meta, f = build(meta_host, [2, 2, 2, 1, 0, 4, 1, 1, 1, 1, bad_tok, 5, 1, 2], caps, 16, 64, 8,
+                             tsrc=picks)
+        assert err == 2 and f(8, 2).tolist() == [0, 5] and f(0, 16)[0] == 2
+    err, meta, f = build(meta_host, rec, caps, 16, 64, 8)  # no source
+    assert err == 2 and f(8, 2).tolist() == [0, 5]

@@ -207,7 +207,9 @@ def test_gpu_engine_matches_on_prompts_and_frees_blocks():
 
 
 def test_bench_workload_mixed_lengths_token_identical():
-    """The 48-request mixed-length benchmark: every greedy token equal."""
+    """The 48-request mixed-length benchmark: every greedy token equal, with
+    the drop-in runner and with device picks (which run ahead: the next
+    pass's tokens are resolved on the device from the pick buffer)."""
     from vllt.engine import cuda_engine, gpu_engine
     from vllt.workloads import mixed_workload
 
@@ -217,6 +219,8 @@ def test_bench_workload_mixed_lengths_token_identical():
         got = run_requests(eng, mixed_workload(48, 0, 0))
         assert got == want
         assert eng.total_steps == int(F.load("streams_mixed.npz")["steps"])
+        if make is gpu_engine:  # greedy ignore_eos: passes launch before the previous tokens are read
+            assert eng.passes_ahead >= eng.total_steps // 2
 
 
 def test_bench_workload_shared_prefix_token_identical():

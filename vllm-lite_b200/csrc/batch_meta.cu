@@ -54,11 +54,15 @@ __device__ int4 block_exclusive_scan(int4 v, int4* warp_tot, int4* total) {
 // pool [pool_slots][L.W_cap]: the record then carries, after the tokens, each
 // sequence's pool slot and a list of (slot, index, block id) updates that
 // this kernel applies to the pool before it reads the tables through the
-// slots (the record layout is in include/vllt.h).
+// slots (the record layout is in include/vllt.h). Token ids are resolved
+// against `tsrc` (the previous pass's picks, tsrc_len entries; may be NULL)
+// and checked against the embedding's `vocab` rows.
 __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __restrict__ rec,
                                                               MetaLayout L, int bs, int num_blocks,
                                                               int qp, int32_t* __restrict__ meta,
-                                                              int32_t* __restrict__ pool, int pool_slots) {
+                                                              int32_t* __restrict__ pool, int pool_slots,
+                                                              const int32_t* __restrict__ tsrc, int tsrc_len,
+                                                              int vocab) {
   __shared__ int4 warp_tot[32];
   __shared__ int4 total;
   __shared__ int s_max_ctx, s_max_q, s_err;
@@ -159,7 +163,9 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
     const TokenMeta m = token_meta(cu_q, S, start, meta + L.tables, L.W_cap, W, bs, t);
     meta[L.pos + t] = m.pos;
     meta[L.tok_seq + t] = m.seq;
-    meta[L.tokens + t] = tokens[t];
+    bool bad = false;
+    meta[L.tokens + t] = resolve_token(tokens[t], tsrc, tsrc_len, vocab, &bad);
+    if (bad) atomicOr(&s_err, 2);
     meta[L.slot + t] = m.slot;
   }
   // Phase 4: logit rows = the last `count` tokens of each sequence (runner.py:86-90).
@@ -189,11 +195,14 @@ __global__ void __launch_bounds__(kThreads) build_meta_kernel(const int32_t* __r
 }  // namespace
 
 int build_batch_meta(const int32_t* rec, const MetaLayout& L, int bs, int num_blocks, int qp,
-                     int32_t* meta, cudaStream_t st, int32_t* pool, int pool_slots) {
+                     int32_t* meta, cudaStream_t st, int32_t* pool, int pool_slots, const int32_t* token_src,
+                     int token_src_len, int vocab) {
   VLLT_REQUIRE(rec && meta, "build_batch_meta: null pointer");
-  VLLT_REQUIRE(bs > 0 && num_blocks > 0 && qp > 0, "build_batch_meta: bad sizes");
+  VLLT_REQUIRE(bs > 0 && num_blocks > 0 && qp > 0 && vocab > 0, "build_batch_meta: bad sizes");
   VLLT_REQUIRE(!pool || pool_slots > 0, "build_batch_meta: a table pool needs at least one slot");
-  build_meta_kernel<<<1, kThreads, 0, st>>>(rec, L, bs, num_blocks, qp, meta, pool, pool ? pool_slots : 0);
+  VLLT_REQUIRE(!token_src || token_src_len > 0, "build_batch_meta: a token source needs at least one entry");
+  build_meta_kernel<<<1, kThreads, 0, st>>>(rec, L, bs, num_blocks, qp, meta, pool, pool ? pool_slots : 0,
+                                            token_src, token_src ? token_src_len : 0, vocab);
   return check_launch("build_batch_meta");
 }
 

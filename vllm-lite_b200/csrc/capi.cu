@@ -95,6 +95,7 @@ int check_desc(const vllt_model_desc* m) {
                "vllt_forward: tensor parallelism is built for the bf16 model only");
   VLLT_REQUIRE(m->embed_rows >= (m->tp_size == 1 ? m->vocab : 1), "vllt_forward: embed_rows too small");
   VLLT_REQUIRE(!m->table_pool || m->table_pool_slots > 0, "vllt_forward: table_pool needs table_pool_slots > 0");
+  VLLT_REQUIRE(!m->token_source || m->token_source_len > 0, "vllt_forward: token_source needs token_source_len > 0");
   VLLT_REQUIRE(m->n_layers > 0 && m->n_heads > 0 && m->n_kv_heads > 0 &&
                    m->n_heads % m->n_kv_heads == 0 && m->head_dim > 0 && m->d_model > 0 &&
                    m->d_ff > 0 && m->vocab > 0 && m->vocab_padded >= m->vocab &&
@@ -139,7 +140,7 @@ int forward_impl(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
 
   VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks,
                             query_tile_positions(VLLT_F32, D, m->block_size, n_rep), meta, st, m->table_pool,
-                            m->table_pool_slots));
+                            m->table_pool_slots, m->token_source, m->token_source_len, m->vocab));
   VLLT_TRY(embed(reinterpret_cast<const float*>(m->tok_emb), meta + L.tokens, w.x, T_cap, T_dev, d, m->vocab, st));
 
   AttnCall ac{};
@@ -269,6 +270,7 @@ int32_t* vllt_meta_field(void* meta, const vllt_caps* caps, int32_t which) {
     case 5: return m + L.slot;
     case 6: return m + L.rows;
     case 7: return m + L.tables;
+    case 8: return m + L.tokens;
     default: return nullptr;
   }
 }

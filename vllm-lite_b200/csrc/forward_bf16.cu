@@ -102,7 +102,7 @@ int forward_bf16(const vllt_model_desc* m, const int32_t* rec, const vllt_caps* 
 
   VLLT_TRY(build_batch_meta(rec, L, m->block_size, m->num_blocks,
                             query_tile_positions(VLLT_BF16, D, m->block_size, n_rep), meta, st, m->table_pool,
-                            m->table_pool_slots));
+                            m->table_pool_slots, m->token_source, m->token_source_len, m->embed_rows));
   VLLT_TRY(embed_bf16(m->tok_emb, meta + L.tokens, w.x, T_cap, T_dev, d, m->embed_rows, st));
 
   AttnCall ac{};

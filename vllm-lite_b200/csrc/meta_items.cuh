@@ -139,6 +139,26 @@ __host__ __device__ inline TokenMeta token_meta(const int32_t* cu_q, int S, cons
   return m;
 }
 
+// Phase 3: the token id a record entry stands for. t >= 0 is the id; t < 0
+// is entry -t - 1 of the previous pass's picks (src, src_len entries). An id
+// outside [0, vocab) after that, or a reference outside src, is flagged
+// (*bad) and yields token 0, so the embedding never reads outside its table.
+__host__ __device__ inline int resolve_token(int32_t t, const int32_t* src, int src_len, int vocab, bool* bad) {
+  if (t < 0) {
+    const int64_t i = -(int64_t)t - 1;
+    if (!src || i >= src_len) {
+      *bad = true;
+      return 0;
+    }
+    t = src[i];
+  }
+  if (t < 0 || t >= vocab) {
+    *bad = true;
+    return 0;
+  }
+  return t;
+}
+
 // Phase 4: logit row r -> its query token: the last `count` tokens of each
 // sequence (runner.py:86-90).
 __host__ __device__ inline int row_token(const int32_t* cu_rows, const int32_t* cu_q, const int32_t* qlen,

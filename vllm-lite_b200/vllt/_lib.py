@@ -38,6 +38,7 @@ class ModelDesc(C.Structure):
         ("tok_emb", vp), ("final_norm", vp), ("lm_head", vp), ("rope_cos", vp), ("rope_sin", vp),
         ("attn_norm", PP), ("wqkv", PP), ("wo", PP), ("ffn_norm", PP), ("w_gu", PP), ("w_down", PP),
         ("k_cache", vp), ("v_cache", vp), ("table_pool", vp), ("table_pool_slots", i32),
+        ("token_source", vp), ("token_source_len", i32),
     ]
 
 

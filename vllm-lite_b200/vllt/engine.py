@@ -15,6 +15,18 @@ penalty, sampling.py:41-57) and one applies the speculative accept/reject rule
 request's own generator supplying the uniform numpy's choice() would draw.
 Only the picked token ids cross back to the host; no row is sampled on the
 CPU.
+
+Run-ahead: the reference's step is strictly serial (schedule, forward, read
+the tokens, bookkeeping, schedule again), so the GPU idles during the host's
+bookkeeping and the host idles during the forward. When no sequence that
+completes a pass can stop on the value of its new token (stops_on_length),
+the scheduler's next decisions do not depend on those values: the step
+commits the pass, appends a stand-in for each new token (a reference to
+where the token lands in the device pick buffer, resolved by the next
+forward's metadata builder on the device), runs the length stop checks,
+schedules and launches the next pass, and only then waits for this pass's
+tokens and writes them over the stand-ins. The schedule, the token streams,
+the per-call outputs and the step count are the reference's.
 """
 
 from __future__ import annotations
@@ -102,6 +114,27 @@ def pick_inputs(scheduled, rows, R: int, eos):
     return np.asarray(cu, np.int32), np.asarray(doff, np.int32), drafts, eos_mask, penalty, sampled
 
 
+def stops_on_length(params, eos) -> bool:
+    """Whether the reference's stop checks for a new token of a request with
+    these SamplingParams depend only on lengths (vllmlite/engine.py:218-234):
+    EOS and stop_token_ids are ignored (ignore_eos, or no EOS id and no stop
+    ids) and there are no stop strings; max_tokens and max_seq_len remain."""
+    return not params.stop and (params.ignore_eos or (eos is None and not params.stop_token_ids))
+
+
+class PendingPicks:
+    """One pass's device picks on their way to the host: the layout of the
+    pick buffer (R rows, S sequences, tail, special rows, sampled (seq, row)
+    pairs, whether drafts were verified), token_at {seq index: buffer entry
+    of the sequence's new token}, the host copy and the event after it."""
+
+    __slots__ = ("R", "S", "tail", "special", "sampled", "drafts", "token_at", "host", "event")
+
+    def __init__(self, R, S, tail, special, sampled, drafts, token_at, host, event):
+        self.R, self.S, self.tail, self.special, self.sampled = R, S, tail, special, sampled
+        self.drafts, self.token_at, self.host, self.event = drafts, token_at, host, event
+
+
 def seen_bitmaps(seqs, vocab: int) -> np.ndarray:
     """uint32 [len(seqs)][ceil(vocab/32)]: bit t of row j is set when token t
     occurs in seqs[j].token_ids (the `seen_tokens` of sampling.py:54, which
@@ -164,11 +197,16 @@ class GpuLLMEngine(metaclass=_Lazy):
 
 
 def gpu_engine(cfg=None, tokenizer=None, speculative_tokens: int = 0, weights=None, device=None,
-               runner_cls=None, device_prefix_hash: bool = False, **runner_kw):
+               runner_cls=None, device_prefix_hash: bool = False, run_ahead: bool = True, **runner_kw):
     """A GpuLLMEngine (device token picks). device_prefix_hash: the prefix
-    cache's block hashes are computed on the device (vllt.prefix_hash)."""
+    cache's block hashes are computed on the device (vllt.prefix_hash).
+    run_ahead: schedule and launch the next pass while the current one runs
+    when its tokens cannot stop a sequence (GpuLLMEngine.can_run_ahead); a
+    request added or aborted between two step() calls then takes effect one
+    pass later than in the reference engine."""
     eng = cuda_engine(cfg, tokenizer, speculative_tokens, weights, device,
                       engine_cls=GpuLLMEngine.resolve(), runner_cls=runner_cls, **runner_kw)
+    eng.run_ahead = run_ahead
     if device_prefix_hash:
         from .prefix_hash import DevicePrefixHasher
 
@@ -184,8 +222,18 @@ def _make_gpu_engine(Base):
     from ._lib import check
 
     class _GpuLLMEngine(Base):
+        run_ahead = True  # see gpu_engine
+        passes_ahead = 0  # passes launched before the previous pass's tokens were on the host
+        _next = None  # (SchedulerOutput, dropped reports, (rows, R, launch time) or None) for the next call
+
         def _h2d(self, a):
-            return torch.from_numpy(np.ascontiguousarray(a)).to(self.runner.dev, non_blocking=True)
+            """Upload through a pinned staging block: a copy from pageable
+            memory may wait for the stream, which would stall the host behind
+            a pass that is still running."""
+            t = torch.from_numpy(np.ascontiguousarray(a))
+            if self.runner.dev.type == "cuda":
+                t = t.pin_memory()
+            return t.to(self.runner.dev, non_blocking=True)
 
         def _greedy(self, logits, n_rows, ld, vocab, mask, pen, seqs, out, keep):
             """Greedy kernel over logits rows [0, n_rows) with the EOS mask and
@@ -219,9 +267,9 @@ def _make_gpu_engine(Base):
                                       _lib.ptr(bits), d[1].data_ptr(), d[2].data_ptr(), d[3].data_ptr(),
                                       d[4].data_ptr(), out.data_ptr(), _lib.stream_handle()))
 
-        def _device_picks(self, sched, rows, R):
-            """Pick every row's token on the device; return host arrays
-            (picks[R], n_accepted[S], {seq index: sampled token}).
+        def _enqueue_picks(self, sched, rows, R):
+            """Enqueue the device picks of one pass and their copy to the
+            host; returns a PendingPicks (read it with _collect_picks).
 
             One GPU: the greedy kernel over all R rows (EOS mask / penalty on
             the rows that need them), the sampler over the temperature rows
@@ -230,7 +278,8 @@ def _make_gpu_engine(Base):
             rows; rows that need a mask, a penalty or a draw have their
             full-vocabulary logits gathered from every rank first and go
             through the same two kernels. Every result lands in one device
-            buffer, read back with one copy per step:
+            buffer (the runner's pick buffer, which the next forward can read
+            tokens from), copied back with one copy per pass:
               [0, R) row picks | R: the metadata builder's error word |
               [R+1, R+1+S) accepted drafts | then the sampled / masked picks."""
             run = self.runner
@@ -247,7 +296,9 @@ def _make_gpu_engine(Base):
                 seq_of_row[rows[i][0] + rows[i][1] - 1] = item.seq
             special = [int(r) for r in np.flatnonzero(eos_mask | (penalty != 1.0))] if tp else []
             tail = R + 1 + S  # first word of the sampled / masked picks
-            res = torch.empty(tail + len(special) + len(sampled), dtype=torch.int32, device=run.dev)
+            n = tail + len(special) + len(sampled)
+            buf = getattr(run, "pick_buffer", None)
+            res = buf(n) if buf is not None else torch.empty(n, dtype=torch.int32, device=run.dev)
             if tp:
                 res[:R] = run.greedy_picks(R)
             else:
@@ -270,18 +321,81 @@ def _make_gpu_engine(Base):
                                  res[tail + len(special):], keep)
             elif sampled:
                 self._sample(run.logits_dev, R, run.w.vocab_padded, V, [r for _, r in sampled], seqs, res[tail:], keep)
-            res_h = res.cpu().numpy()
-            run.check_step_flags(int(res_h[R]))
+            # where the token of each completing sequence without drafts lands
+            token_at = {}
+            sampled_at = {i: tail + len(special) + j for j, (i, _) in enumerate(sampled)}
+            special_at = {r: tail + j for j, r in enumerate(special)}
+            for i, item in enumerate(sched.scheduled):
+                if item.seq.draft_token_ids or not completes(item):
+                    continue
+                last = rows[i][0] + rows[i][1] - 1
+                token_at[i] = sampled_at.get(i, special_at.get(last, last))
+            host = torch.empty(n, dtype=torch.int32, pin_memory=res.is_cuda)
+            host.copy_(res, non_blocking=True)
+            ev = None
+            if res.is_cuda:
+                ev = torch.cuda.Event()
+                ev.record()
+            return PendingPicks(R, S, tail, special, sampled, bool(drafts), token_at, host, ev)
+
+        def _collect_picks(self, pend):
+            """Wait for a pass's picks; (picks[R], n_accepted[S], {seq index:
+            sampled token}, the whole host copy)."""
+            if pend.event is not None:
+                pend.event.synchronize()
+            res_h = pend.host.numpy()
+            R, S, tail, special = pend.R, pend.S, pend.tail, pend.special
+            self.runner.check_step_flags(int(res_h[R]))
             picks_h = res_h[:R].copy()
             if special:
                 picks_h[special] = res_h[tail:tail + len(special)]
-            sampled_tok = {i: int(res_h[tail + len(special) + j]) for j, (i, _) in enumerate(sampled)}
-            acc_h = res_h[R + 1:R + 1 + S].copy() if drafts else np.zeros(S, np.int32)
-            return picks_h, acc_h, sampled_tok
+            sampled_tok = {i: int(res_h[tail + len(special) + j]) for j, (i, _) in enumerate(pend.sampled)}
+            acc_h = res_h[R + 1:R + 1 + S].copy() if pend.drafts else np.zeros(S, np.int32)
+            return picks_h, acc_h, sampled_tok, res_h
+
+        def _device_picks(self, sched, rows, R):
+            """Picks of one pass, waited for: (picks[R], n_accepted[S],
+            {seq index: sampled token})."""
+            return self._collect_picks(self._enqueue_picks(sched, rows, R))[:3]
+
+        @property
+        def has_work(self) -> bool:
+            return self.scheduler.has_work or self._next is not None
+
+        def can_run_ahead(self, sched) -> bool:
+            """Whether the pass after `sched` can be scheduled before this
+            pass's tokens reach the host: one GPU, no speculation, no device
+            prefix hashes, and every sequence that completes this pass stops
+            only on its length (see stops_on_length)."""
+            if not self.run_ahead or self.proposer is not None:
+                return False
+            run = self.runner
+            if getattr(self, "prefix_hasher", None) is not None or getattr(run, "tp_size", 1) > 1:
+                return False
+            if getattr(run, "pick_buffer", None) is None:
+                return False
+            eos = self.tokenizer.eos_id
+            for item in sched.scheduled:
+                if item.seq.draft_token_ids:
+                    return False
+                if completes(item) and not stops_on_length(item.seq.params, eos):
+                    return False
+            return True
+
+        def _mark_busy(self, t_launch):
+            """busy_time as the reference counts it (time spent in forward
+            passes), without counting the overlap of two passes twice."""
+            now = time.perf_counter()
+            self.busy_time += now - max(t_launch, getattr(self, "_busy_until", 0.0))
+            self._busy_until = now
 
         def step(self):
             """engine.py:99-181 with device-side token picks (and, with a
-            prefix_hasher, device-side prefix-cache hashes)."""
+            prefix_hasher, device-side prefix-cache hashes). With run_ahead,
+            the next pass is scheduled and launched while this one runs
+            whenever this pass's tokens cannot stop a sequence (can_run_ahead):
+            every call still returns its own pass's outputs, and the
+            scheduler sees the state the reference's would."""
             hasher = getattr(self, "prefix_hasher", None)
             if hasher is None:
                 return self._step(None)
@@ -289,25 +403,50 @@ def _make_gpu_engine(Base):
                 return self._step(hasher)
 
         def _step(self, hasher):
-            if hasher is not None:
-                hasher.prepare_prompts()
-            sched = self.scheduler.schedule()
-            dropped = [self._retired_output(s) for s in self.scheduler.drain_reports()]
+            nxt, self._next = self._next, None
+            if nxt is None:
+                if hasher is not None:
+                    hasher.prepare_prompts()
+                sched = self.scheduler.schedule()
+                dropped = self.scheduler.drain_reports()
+                launched = None
+            else:  # scheduled (and launched) by the previous call
+                sched, dropped, launched = nxt
+            results = [self._retired_output(s) for s in dropped]
             if sched.is_empty:
-                return dropped
-            t0 = time.perf_counter()
-            rows, R = self.runner.launch(sched)
+                return results
+            if launched is None:
+                t0 = time.perf_counter()
+                rows, R = self.runner.launch(sched)
+            else:
+                rows, R, t0 = launched
             if hasher is not None:
                 hasher.prepare_commits(sched)
-            picks, accepted, sampled_tok = self._device_picks(sched, rows, R)
+            pend = self._enqueue_picks(sched, rows, R)
+            if self.can_run_ahead(sched):
+                waiting = self._commit_ahead(sched, pend)
+                sched2 = self.scheduler.schedule()
+                dropped2 = self.scheduler.drain_reports()
+                if not sched2.is_empty:
+                    t2 = time.perf_counter()
+                    self._next = (sched2, dropped2, (*self.runner.launch(sched2), t2))
+                    self.passes_ahead += 1
+                elif dropped2:
+                    self._next = (sched2, dropped2, None)
+                res_h = self._collect_picks(pend)[3]
+                self._mark_busy(t0)
+                self.total_steps += 1
+                return results + self._patch_ahead(waiting, res_h)
+            picks, accepted, sampled_tok, _ = self._collect_picks(pend)
             if hasher is not None:
                 hasher.collect()
-            self.busy_time += time.perf_counter() - t0
+            self._mark_busy(t0)
             self.total_steps += 1
-            results = list(dropped)
             eos = self.tokenizer.eos_id
             for i, item in enumerate(sched.scheduled):
                 seq = item.seq
+                if seq.status.finished:  # aborted while its pass was in flight
+                    continue
                 row0, count = rows[i]
                 drafts = list(seq.draft_token_ids)
                 if drafts:
@@ -336,18 +475,71 @@ def _make_gpu_engine(Base):
                     self._check_stop(seq, tok, eos)
                     if seq.status.finished:
                         break
-                delta = self._advance_detok(seq)
-                if seq.status.finished:
-                    self.scheduler.finish(seq)
-                results.append(RequestOutput(
-                    request_id=seq.request_id, token_ids=list(seq.output_token_ids),
-                    new_token_ids=emitted, text_delta=delta, finished=seq.status.finished,
-                    finish_reason=self._reason(seq), num_prompt_tokens=seq.num_prompt_tokens,
-                    num_output_tokens=len(seq.output_token_ids),
-                    cached_prefix_tokens=seq.cached_prefix_tokens))
+                results.append(self._output(seq, emitted))
             if self.proposer is not None:
                 self.spec.rounds += 1
                 self._make_proposals()
             return results
+
+        def _output(self, seq, emitted):
+            delta = self._advance_detok(seq)
+            if seq.status.finished:
+                self.scheduler.finish(seq)
+            return RequestOutput(
+                request_id=seq.request_id, token_ids=list(seq.output_token_ids),
+                new_token_ids=emitted, text_delta=delta, finished=seq.status.finished,
+                finish_reason=self._reason(seq), num_prompt_tokens=seq.num_prompt_tokens,
+                num_output_tokens=len(seq.output_token_ids),
+                cached_prefix_tokens=seq.cached_prefix_tokens)
+
+        def _commit_ahead(self, sched, pend):
+            """engine.py:113-160 for a pass whose tokens are still on the
+            device: commit and num_computed as the reference, then each
+            completing sequence takes a stand-in token -1 - j (j: where its
+            token lands in the pick buffer, which the next forward resolves on
+            the device), the length stop checks run (can_run_ahead guarantees
+            no other check applies) and finished sequences free their blocks.
+            Returns what _patch_ahead needs."""
+            eos = self.tokenizer.eos_id
+            waiting = []
+            for i, item in enumerate(sched.scheduled):
+                seq = item.seq
+                if seq.status.finished:  # aborted while its pass was in flight
+                    continue
+                self.scheduler.blocks.commit(seq, item.num_tokens)
+                seq.num_computed += item.num_tokens
+                if seq.num_computed < seq.num_tokens:
+                    continue
+                j = pend.token_at[i]
+                first = seq.first_token_at is None
+                seq.append_token(-1 - j)
+                self.total_output_tokens += 1
+                self._check_stop(seq, -1 - j, eos)
+                if seq.status.finished:
+                    self.scheduler.finish(seq)
+                waiting.append((seq, len(seq.output_token_ids) - 1, j, first))
+            return waiting
+
+        def _patch_ahead(self, waiting, res_h):
+            """The picked tokens replace the stand-ins; first-token and finish
+            times are taken now (when the token is on the host, as the
+            reference's); detokenise and report in the reference's order."""
+            now = time.perf_counter()
+            out = []
+            for seq, k, j, first in waiting:
+                tok = int(res_h[j])
+                seq.output_token_ids[k] = tok
+                if first:
+                    seq.first_token_at = now
+                if seq.status.finished:
+                    seq.finished_at = now
+                delta = self._advance_detok(seq)
+                out.append(RequestOutput(
+                    request_id=seq.request_id, token_ids=list(seq.output_token_ids),
+                    new_token_ids=[tok], text_delta=delta, finished=seq.status.finished,
+                    finish_reason=self._reason(seq), num_prompt_tokens=seq.num_prompt_tokens,
+                    num_output_tokens=len(seq.output_token_ids),
+                    cached_prefix_tokens=seq.cached_prefix_tokens))
+            return out
 
     return _GpuLLMEngine

@@ -246,7 +246,7 @@ class LlamaRunner(CudaRunner):
     def launch(self, out):
         rows, R = super().launch(out)
         if getattr(self, "roofline_peaks", None):
-            self.roofline_s += self.step_roofline(self.rec_host[:self._last_n].numpy(), None, *self.roofline_peaks)
+            self.roofline_s += self.step_roofline(self._last_rec, None, *self.roofline_peaks)
         return rows, R
 
     def execute(self, out):

@@ -113,8 +113,11 @@ class StepPacker:
     per decode pass that is the new or copied-on-write block, if any."""
 
     def __init__(self, block_size: int, num_blocks: int, vocab: int, max_pos: int, qp: int,
-                 pool_slots: int = 0, pool_width: int = 0):
+                 pool_slots: int = 0, pool_width: int = 0, token_refs: int = 0):
         self.bs, self.nb, self.vocab, self.max_pos, self.qp = block_size, num_blocks, vocab, max_pos, qp
+        # token ids t in [-token_refs, -1] are references to entry -t - 1 of
+        # the forward's token source (a token picked on the device, not yet read)
+        self.token_refs = token_refs
         self.cache = {}
         self.pool_slots, self.pool_width = pool_slots, pool_width
         if pool_slots:
@@ -257,7 +260,7 @@ class StepPacker:
         T = len(toks)
         R = sum(counts)
         tok = np.asarray(toks, dtype=np.int64)
-        if T and (int(tok.min()) < 0 or int(tok.max()) >= self.vocab):
+        if T and (int(tok.min()) < -self.token_refs or int(tok.max()) >= self.vocab):
             raise IndexError("token id out of the vocabulary")
         if pooled:
             U = len(updates) // 3
@@ -427,7 +430,13 @@ class CudaRunner(_Base):
         if meta_bytes < 0 or ws_bytes < 0:
             raise ValueError("bad runner capacities")
         kw = dict(device=self.dev)
-        self.rec_host = torch.empty(rec_words, dtype=torch.int32, pin_memory=True)
+        # two pinned staging buffers for the record, used in turn: with the
+        # engine running ahead, the previous record's copy may still be queued
+        # behind a running pass when the next record is packed
+        self._rec_bufs = [torch.empty(rec_words, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._rec_copied = [None, None]  # event after the copy that last read each buffer
+        self._rec_i = 0
+        self.rec_host = self._rec_bufs[0]
         self.rec_dev = torch.empty(rec_words, dtype=torch.int32, **kw)
         self.meta = torch.empty((meta_bytes + 3) // 4, dtype=torch.int32, **kw)
         self.ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, **kw)  # split-K counters start at 0
@@ -440,6 +449,16 @@ class CudaRunner(_Base):
             slots = 2 * caps.max_seqs
             self.table_pool = torch.full((slots, caps.max_table_width), -1, dtype=torch.int32, **kw)
             self.desc.table_pool, self.desc.table_pool_slots = self.table_pool.data_ptr(), slots
+        # the pick buffer of the engine's token picks (row picks, flag word,
+        # accepted drafts, masked / sampled picks: 2 (R + S) + 1 words at most);
+        # the forward reads tokens it has not handed to the host yet from it
+        # (record ids < 0), so it keeps its contents when it grows
+        words = 2 * (caps.max_rows + caps.max_seqs) + 1
+        old = getattr(self, "picks_dev", None)
+        self.picks_dev = torch.zeros(words, dtype=torch.int32, **kw)
+        if old is not None:
+            self.picks_dev[:old.numel()].copy_(old)
+        self.desc.token_source, self.desc.token_source_len = self.picks_dev.data_ptr(), words
         self.packer = None  # its mirror describes the old pool
         self._on_reserve(caps)
         self.counters_host = torch.empty(16, dtype=torch.int32, pin_memory=True)
@@ -455,8 +474,16 @@ class CudaRunner(_Base):
             pool = self.desc.table_pool_slots if self.pooled_tables else 0
             self.packer = StepPacker(self.block_size, self.num_blocks, self.model_cfg.vocab_size,
                                      self.w.rope_len, self.qp, pool_slots=pool,
-                                     pool_width=self.caps.max_table_width)
+                                     pool_width=self.caps.max_table_width, token_refs=self.picks_dev.numel())
         return self.packer.pack(out)
+
+    def pick_buffer(self, n: int):
+        """The first n words of the pick buffer (device int32), where the
+        engine's pick kernels write and the next forward resolves record
+        token ids < 0 from."""
+        if n > self.picks_dev.numel():
+            raise ValueError("pick buffer smaller than the step's picks")
+        return self.picks_dev[:n]
 
     def copy_on_write(self, pairs) -> None:
         """Apply (src_block, dst_block) copies in every layer (runner.py:54-60)."""
@@ -466,7 +493,7 @@ class CudaRunner(_Base):
         a = np.asarray(pairs, np.int64).reshape(-1, 2)
         if int(a.min()) < 0 or int(a.max()) >= self.num_blocks:  # checked on the host: no device read
             raise IndexError("copy-on-write block id out of range")
-        p = torch.from_numpy(a.astype(np.int32)).to(self.dev, non_blocking=True)
+        p = torch.from_numpy(a.astype(np.int32)).pin_memory().to(self.dev, non_blocking=True)  # no wait on the stream
         self._cow_pairs = p  # referenced until the copy kernel has been enqueued
         cfg = self.model_cfg
         check(self.L.vllt_copy_blocks(self.cache_k.data_ptr(), self.cache_v.data_ptr(), p.data_ptr(),
@@ -493,8 +520,17 @@ class CudaRunner(_Base):
         rec, bounds, rows, (S, T, R, W) = self.pack(out)
         n = rec.size
         self._last_n = n
-        self.rec_host[:n].numpy()[:] = rec
-        self.rec_dev[:n].copy_(self.rec_host[:n], non_blocking=True)
+        self._last_rec = rec
+        i = self._rec_i
+        if self._rec_copied[i] is not None:
+            self._rec_copied[i].synchronize()  # the copy that last read this buffer has run
+        buf = self._rec_bufs[i]
+        buf[:n].numpy()[:] = rec
+        self.rec_dev[:n].copy_(buf[:n], non_blocking=True)
+        ev = self._rec_copied[i] = torch.cuda.Event()
+        ev.record()
+        self._rec_i = i ^ 1
+        self.rec_host = buf
         self.h2d_bytes += 4 * n + 8 * len(out.cow)
         self._timed_forward(bounds)
         self.steps += 1
