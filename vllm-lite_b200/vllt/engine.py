@@ -362,24 +362,29 @@ def _make_gpu_engine(Base):
         def has_work(self) -> bool:
             return self.scheduler.has_work or self._next is not None
 
-        def can_run_ahead(self, sched) -> bool:
+        def can_run_ahead(self, sched, pend) -> bool:
             """Whether the pass after `sched` can be scheduled before this
-            pass's tokens reach the host: one GPU, no speculation, no device
-            prefix hashes, and every sequence that completes this pass stops
-            only on its length (see stops_on_length)."""
+            pass's tokens (enqueued as `pend`) reach the host: no speculation,
+            no device prefix hashes, and every sequence that completes this
+            pass stops only on its length (see stops_on_length). Under tensor
+            parallelism their tokens must also be plain greedy picks (entries
+            below R of the pick buffer, which every rank holds); masked,
+            penalised and sampled rows are picked on rank 0 only."""
             if not self.run_ahead or self.proposer is not None:
                 return False
             run = self.runner
-            if getattr(self, "prefix_hasher", None) is not None or getattr(run, "tp_size", 1) > 1:
+            if getattr(self, "prefix_hasher", None) is not None or getattr(run, "pick_buffer", None) is None:
                 return False
-            if getattr(run, "pick_buffer", None) is None:
-                return False
+            tp = getattr(run, "tp_size", 1) > 1
             eos = self.tokenizer.eos_id
-            for item in sched.scheduled:
+            for i, item in enumerate(sched.scheduled):
                 if item.seq.draft_token_ids:
                     return False
-                if completes(item) and not stops_on_length(item.seq.params, eos):
-                    return False
+                if completes(item):
+                    if not stops_on_length(item.seq.params, eos):
+                        return False
+                    if tp and pend.token_at[i] >= pend.R:
+                        return False
             return True
 
         def _mark_busy(self, t_launch):
@@ -423,7 +428,7 @@ def _make_gpu_engine(Base):
             if hasher is not None:
                 hasher.prepare_commits(sched)
             pend = self._enqueue_picks(sched, rows, R)
-            if self.can_run_ahead(sched):
+            if self.can_run_ahead(sched, pend):
                 waiting = self._commit_ahead(sched, pend)
                 sched2 = self.scheduler.schedule()
                 dropped2 = self.scheduler.drain_reports()

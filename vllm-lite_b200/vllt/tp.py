@@ -10,7 +10,9 @@ forward pass:
      every rank holds the same block ids for its own KV heads;
   3. greedy picks are vocab-parallel: each rank reduces its vocabulary slice to
      (max, first index) per row, the pairs are all-gathered and the lowest
-     global index among the maxima wins (np.argmax semantics);
+     global index among the maxima wins (np.argmax semantics); every rank
+     keeps the merged picks in its pick buffer, so a record that refers to
+     them (rank 0's engine running ahead) resolves the same on every rank;
   4. rows whose pick needs the whole vocabulary at once (a min_tokens EOS mask,
      a repetition penalty, or a temperature draw: sampling.py:41-64) are named
      in a gather message; every rank contributes its slice of those rows and
@@ -292,8 +294,9 @@ class TPLlamaRunner(LlamaRunner):
 
         def forward(bounds, greedy):
             self._dispatch(bounds)
-            if greedy:
-                self.greedy_picks(bounds.rows)
+            if greedy:  # the merged picks at the entries rank 0's engine uses: the next
+                # record may refer to them (a pass launched before rank 0 read them)
+                self.picks_dev[:bounds.rows].copy_(self.greedy_picks(bounds.rows))
             torch.cuda.current_stream(self.dev).synchronize()
 
         def gather(n):
