@@ -67,8 +67,8 @@ class AheadRunner(ReferenceLogitsRunner):
 
         super().__init__(model_cfg, cache_cfg, sched_cfg, device, lib)
         self.picks_dev = torch.zeros(self.PICK_WORDS, dtype=torch.int32)
-        self.caps = _lib.Caps(64, 2048, 256, 64)
         self.bs, self.nb = cache_cfg.block_size, cache_cfg.num_blocks
+        self.caps = _lib.Caps(64, 4096, 256, -(-model_cfg.max_seq_len // self.bs))
         self.qp = tile_positions(model_cfg.n_heads // model_cfg.n_kv_heads)
         self.packer = StepPacker(self.bs, self.nb, model_cfg.vocab_size, model_cfg.max_seq_len, self.qp,
                                  pool_slots=128, pool_width=self.caps.max_table_width, token_refs=self.PICK_WORDS)
@@ -132,12 +132,13 @@ def drive(eng, reqs):
     return calls, [eng.seqs[i].output_token_ids for i in ids]
 
 
-def config(budget=64, max_seqs=8, bs=16, nb=512, prefix=False, max_len=512):
+def config(budget=64, max_seqs=8, bs=16, nb=512, prefix=False, max_len=512, chunked=True):
     from vllmlite.config import CacheConfig, EngineConfig, ModelConfig, SchedulerConfig
 
     return EngineConfig(model=ModelConfig(vocab_size=261, **dict(F.TINY, max_seq_len=max_len)),
                         cache=CacheConfig(block_size=bs, num_blocks=nb, enable_prefix_caching=prefix),
-                        scheduler=SchedulerConfig(max_seqs=max_seqs, max_batched_tokens=budget))
+                        scheduler=SchedulerConfig(max_seqs=max_seqs, max_batched_tokens=budget,
+                                                  chunked_prefill=chunked))
 
 
 def bench_requests(n=12, shared=0, max_tokens=None):
@@ -253,3 +254,28 @@ def test_first_token_time_is_taken_when_the_token_is_on_the_host(meta_host):
             assert min(seq.output_token_ids) >= 0  # no stand-in is ever visible in an output
             assert seq.first_token_at is not None and seq.first_token_at >= seq.arrival
     assert eng.passes_ahead > 0 and all(eng.seqs[i].finished_at >= eng.seqs[i].first_token_at for i in ids)
+
+
+def prompt_requests(max_tokens=20):
+    """The fixture prompts, greedy with ignore_eos (the reference's invariance tests' requests)."""
+    from vllmlite.sequence import SamplingParams
+    from vllmlite.tokenizer import ByteTokenizer
+
+    tok = ByteTokenizer()
+    return [(f"p{i}", tok.encode(t), SamplingParams(max_tokens=max_tokens, temperature=0.0, ignore_eos=True))
+            for i, t in enumerate(F.PROMPTS)]
+
+
+# the reference's invariance grid (tests/test_engine.py:57-110), with run-ahead on
+@pytest.mark.parametrize("kw", [dict(bs=1), dict(bs=4), dict(bs=64), dict(prefix=True),
+                                dict(budget=8), dict(budget=33), dict(budget=4096),
+                                dict(budget=4096, chunked=False), dict(max_seqs=1), dict(max_seqs=2),
+                                dict(max_seqs=3), dict(bs=4, nb=24), dict(bs=4, nb=24, prefix=True)],
+                         ids=lambda kw: ",".join(f"{k}={v}" for k, v in kw.items()))
+def test_reference_invariance_grid(meta_host, kw):
+    cfg = dict(budget=1024, max_seqs=8, bs=16, nb=512)
+    cfg.update(kw)
+    eng, ref = compare(config(**cfg), prompt_requests(), meta_host)
+    assert eng.passes_ahead > 0
+    if cfg["nb"] == 24:
+        assert ref.scheduler.total_preemptions > 0
