@@ -2,7 +2,9 @@
 
 Some kernels keep their per-item arithmetic in CUDA-free headers under
 vllm-lite_b200/csrc (prefix_hash.cuh, meta_items.cuh, sampler_row.cuh) so that the same code
-compiles for the host; a harness wraps it in extern "C" functions that the CPU
+compiles for the host, and the SIMT kernels' device code sits in *_kernels.cuh
+headers that compile for the host under the fiber emulation of
+tests/simt_host.h; a harness wraps them in extern "C" functions that the CPU
 tests call through ctypes. Built with g++ into a temporary directory per test
 session (nothing is written into the repository).
 """
@@ -23,6 +25,6 @@ def build_harness(name: str, out_dir: str):
     out = os.path.join(out_dir, f"lib{name}.so")
     # no FMA contraction: the device code rounds every product and quotient (__fmul_rn, __fdiv_rn)
     subprocess.run([gxx, "-O2", "-std=c++20", "-ffp-contract=off", "-shared", "-fPIC", "-I",
-                    os.path.join(ROOT, "vllm-lite_b200", "csrc"),
+                    os.path.join(ROOT, "vllm-lite_b200", "csrc"), "-I", os.path.join(ROOT, "tests"),
                     os.path.join(ROOT, "tests", f"{name}.cpp"), "-o", out], check=True)
     return ctypes.CDLL(out)

@@ -1,0 +1,335 @@
+// Test infrastructure: runs the library's SIMT kernels (plain CUDA C++, no
+// inline PTX, no tensor-memory or TMA instructions) on the host, so CPU
+// tests can execute the kernels' own code against the oracle.
+//
+// Each CTA runs as blockDim cooperative fibers (ucontext) on one OS thread.
+// A fiber runs until it reaches a barrier, then hands over to the next
+// runnable fiber of the CTA:
+//   * __syncthreads() waits for every thread of the CTA that has not exited
+//     (threads that returned early no longer count, as on sm_70 and later);
+//   * __syncwarp() and the warp shuffles wait for the lanes of the warp that
+//     have not exited; a shuffle writes the lane's value to a per-warp slot,
+//     waits, reads its source lane's slot and waits again before the slot can
+//     be reused;
+//   * a barrier that can never complete (threads waiting on different
+//     barriers) stops the launch with an error instead of hanging.
+// Fibers never preempt each other, so plain loads and stores are coherent
+// and atomics are ordinary read-modify-writes. __shared__ becomes a static
+// (one instance per CTA run; CTAs run one after another). Math intrinsics map
+// to the host's IEEE operations (the _rn forms are exact; approximate ones
+// such as __expf or rsqrtf map to the host's expf / 1 / sqrtf, so results
+// agree with the device within their stated error, not bit for bit).
+//
+// Include this before any library header; it defines VLLT_SIMT_HOST, which
+// makes the library's device helpers (device_common.cuh) use these shims.
+#pragma once
+
+#define VLLT_SIMT_HOST 1
+
+#include <ucontext.h>
+
+#include <climits>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <type_traits>
+#include <vector>
+
+#define __global__
+#define __device__
+#define __host__
+#define __forceinline__ inline
+#define __noinline__
+#define __launch_bounds__(...)
+#define __shared__ static
+#define __align__(n) alignas(n)
+#define __grid_constant__
+
+// ---- vector types ------------------------------------------------------------
+struct int2 { int x, y; };
+struct alignas(16) int4 { int x, y, z, w; };
+struct uint2 { unsigned x, y; };
+struct alignas(16) uint4 { unsigned x, y, z, w; };
+struct alignas(8) float2 { float x, y; };
+struct alignas(16) float4 { float x, y, z, w; };
+struct dim3 {
+  unsigned x = 1, y = 1, z = 1;
+  dim3() = default;
+  dim3(unsigned a, unsigned b = 1, unsigned c = 1) : x(a), y(b), z(c) {}
+};
+inline int2 make_int2(int x, int y) { return {x, y}; }
+inline int4 make_int4(int x, int y, int z, int w) { return {x, y, z, w}; }
+inline uint2 make_uint2(unsigned x, unsigned y) { return {x, y}; }
+inline float2 make_float2(float x, float y) { return {x, y}; }
+inline float4 make_float4(float x, float y, float z, float w) { return {x, y, z, w}; }
+
+// ---- bf16 (storage type and the round-to-nearest-even conversion) ------------
+struct __nv_bfloat16 {
+  uint16_t bits;
+};
+inline float __bfloat162float(__nv_bfloat16 h) {
+  uint32_t u = (uint32_t)h.bits << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+inline __nv_bfloat16 __float2bfloat16_rn(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return {(uint16_t)((u >> 16) | 0x40)};  // NaN stays NaN
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return {(uint16_t)(u >> 16)};
+}
+
+// ---- scalar intrinsics ---------------------------------------------------------
+template <class A, class B> inline typename std::common_type<A, B>::type min(A a, B b) { return b < a ? b : a; }
+template <class A, class B> inline typename std::common_type<A, B>::type max(A a, B b) { return a < b ? b : a; }
+inline float __fdiv_rn(float a, float b) { return a / b; }
+inline float __fmul_rn(float a, float b) { return a * b; }
+inline float __fadd_rn(float a, float b) { return a + b; }
+inline float __fsub_rn(float a, float b) { return a - b; }
+inline float __fmaf_rn(float a, float b, float c) { return std::fmaf(a, b, c); }
+inline float __frcp_rn(float a) { return 1.f / a; }
+inline float __fsqrt_rn(float a) { return std::sqrt(a); }
+inline double __dadd_rn(double a, double b) { return a + b; }
+inline float rsqrtf(float a) { return 1.f / std::sqrt(a); }
+inline float __expf(float a) { return std::exp(a); }
+inline float __logf(float a) { return std::log(a); }
+inline float __saturatef(float a) { return a < 0.f ? 0.f : (a > 1.f ? 1.f : a); }
+inline uint32_t __float_as_uint(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
+inline float __uint_as_float(uint32_t u) { float f; std::memcpy(&f, &u, 4); return f; }
+inline int __float_as_int(float f) { int u; std::memcpy(&u, &f, 4); return u; }
+inline float __int_as_float(int u) { float f; std::memcpy(&f, &u, 4); return f; }
+inline int __clz(int x) { return x == 0 ? 32 : __builtin_clz((unsigned)x); }
+inline int __popc(unsigned x) { return __builtin_popcount(x); }
+inline int __ffs(int x) { return __builtin_ffs(x); }
+template <class T> inline T __ldg(const T* p) { return *p; }
+template <class T> inline T __ldcg(const T* p) { return *p; }
+template <class T> inline void __stcg(T* p, T v) { *p = v; }
+inline void __threadfence() {}
+inline void __threadfence_block() {}
+inline void __nanosleep(unsigned) {}
+
+// ---- atomics (cooperative fibers: plain read-modify-write) ---------------------
+template <class T> inline T atomicAdd(T* p, T v) { T o = *p; *p = o + v; return o; }
+template <class T> inline T atomicSub(T* p, T v) { T o = *p; *p = o - v; return o; }
+template <class T> inline T atomicMax(T* p, T v) { T o = *p; if (v > o) *p = v; return o; }
+template <class T> inline T atomicMin(T* p, T v) { T o = *p; if (v < o) *p = v; return o; }
+template <class T> inline T atomicOr(T* p, T v) { T o = *p; *p = o | v; return o; }
+template <class T> inline T atomicAnd(T* p, T v) { T o = *p; *p = o & v; return o; }
+template <class T> inline T atomicExch(T* p, T v) { T o = *p; *p = v; return o; }
+template <class T> inline T atomicCAS(T* p, T c, T v) { T o = *p; if (o == c) *p = v; return o; }
+
+// ---- the CTA scheduler ---------------------------------------------------------
+namespace simt {
+
+constexpr int kMaxThreads = 1024;
+constexpr size_t kStack = 1 << 17;
+
+struct Fiber {
+  ucontext_t ctx;
+  dim3 tid;
+  int waiting = -2;  // -2 running / runnable, -1 CTA barrier, w >= 0 warp w's barrier
+  bool done = false;
+};
+
+struct Cta {
+  std::vector<Fiber> f;
+  std::vector<char> stacks;
+  ucontext_t main_ctx;
+  int cur = 0, n = 0, done = 0;
+  int live_cta = 0;                  // threads not exited
+  int live_warp[kMaxThreads / 32];   // lanes not exited per warp
+  int arrived_cta = 0;
+  int arrived_warp[kMaxThreads / 32];
+  uint64_t slot[kMaxThreads / 32][32];  // shuffle exchange
+  const std::function<void()>* body = nullptr;
+  bool deadlock = false;
+};
+
+inline Cta& cta() {
+  static Cta c;
+  return c;
+}
+inline dim3& block_idx() { static dim3 d; return d; }
+inline dim3& block_dim() { static dim3 d; return d; }
+inline dim3& grid_dim() { static dim3 d; return d; }
+inline std::vector<unsigned char>& dyn_smem() { static std::vector<unsigned char> m; return m; }
+inline const dim3& thread_idx() { return cta().f[cta().cur].tid; }
+
+inline void switch_next() {
+  Cta& c = cta();
+  const int from = c.cur;
+  for (int k = 1; k <= c.n; ++k) {
+    const int i = (from + k) % c.n;
+    if (!c.f[i].done && c.f[i].waiting == -2) {
+      if (i == from) return;
+      c.cur = i;
+      swapcontext(&c.f[from].ctx, &c.f[i].ctx);
+      return;
+    }
+  }
+  // nobody can run: every live thread waits on a barrier that cannot complete
+  c.deadlock = true;
+  swapcontext(&c.f[from].ctx, &c.main_ctx);
+}
+
+inline void release(int group) {
+  Cta& c = cta();
+  for (auto& fb : c.f)
+    if (!fb.done && fb.waiting == group) fb.waiting = -2;
+  if (group < 0) c.arrived_cta = 0; else c.arrived_warp[group] = 0;
+}
+
+inline void arrive(int group) {  // -1: the CTA; w: warp w
+  Cta& c = cta();
+  int& arrived = group < 0 ? c.arrived_cta : c.arrived_warp[group];
+  const int size = group < 0 ? c.live_cta : c.live_warp[group];
+  if (++arrived >= size) {
+    release(group);
+    return;
+  }
+  c.f[c.cur].waiting = group;
+  switch_next();
+}
+
+inline void exit_thread() {
+  Cta& c = cta();
+  Fiber& me = c.f[c.cur];
+  me.done = true;
+  ++c.done;
+  const int w = (int)((me.tid.z * block_dim().y + me.tid.y) * block_dim().x + me.tid.x) / 32;
+  --c.live_cta;
+  --c.live_warp[w];
+  if (c.arrived_cta > 0 && c.arrived_cta >= c.live_cta) release(-1);
+  if (c.arrived_warp[w] > 0 && c.arrived_warp[w] >= c.live_warp[w]) release(w);
+  if (c.done == c.n) {
+    setcontext(&c.main_ctx);
+  }
+  switch_next();
+  setcontext(&c.main_ctx);  // not reached unless stopped
+}
+
+inline void trampoline() {
+  (*cta().body)();
+  exit_thread();
+}
+
+inline int flat_tid() {
+  const dim3& t = thread_idx();
+  return (int)((t.z * block_dim().y + t.y) * block_dim().x + t.x);
+}
+
+// Runs body() as every thread of every CTA of the grid; returns false if a
+// CTA's threads waited on barriers that could never complete.
+inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<void()>& body) {
+  const int n = (int)(block.x * block.y * block.z);
+  if (n < 1 || n > kMaxThreads) return false;
+  grid_dim() = grid;
+  block_dim() = block;
+  dyn_smem().assign(smem + 16, 0);
+  Cta& c = cta();
+  c.stacks.assign(kStack * n, 0);
+  for (unsigned bz = 0; bz < grid.z; ++bz)
+    for (unsigned by = 0; by < grid.y; ++by)
+      for (unsigned bx = 0; bx < grid.x; ++bx) {
+        block_idx() = dim3(bx, by, bz);
+        c.f.assign(n, Fiber{});
+        c.n = n;
+        c.cur = c.done = 0;
+        c.live_cta = n;
+        c.arrived_cta = 0;
+        for (int w = 0; w < kMaxThreads / 32; ++w) {
+          c.live_warp[w] = std::max(0, std::min(32, n - 32 * w));
+          c.arrived_warp[w] = 0;
+        }
+        c.body = &body;
+        c.deadlock = false;
+        for (int i = 0; i < n; ++i) {
+          c.f[i].tid = dim3(i % block.x, (i / block.x) % block.y, i / (block.x * block.y));
+          getcontext(&c.f[i].ctx);
+          c.f[i].ctx.uc_stack.ss_sp = c.stacks.data() + kStack * i;
+          c.f[i].ctx.uc_stack.ss_size = kStack;
+          c.f[i].ctx.uc_link = nullptr;
+          makecontext(&c.f[i].ctx, trampoline, 0);
+        }
+        swapcontext(&c.main_ctx, &c.f[0].ctx);
+        if (c.deadlock) {
+          std::fprintf(stderr, "simt: block (%u,%u,%u): threads wait on barriers that cannot complete\n", bx, by,
+                       bz);
+          return false;
+        }
+      }
+  return true;
+}
+
+template <class... KArgs, class... Args>
+inline bool launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+  std::function<void()> body = [&] { kernel(args...); };
+  return run_grid(grid, block, smem, body);
+}
+
+template <class T>
+inline T shfl(T v, int src_lane, bool in_range) {
+  static_assert(sizeof(T) <= 8, "shuffle of more than 8 bytes");
+  Cta& c = cta();
+  const int t = flat_tid(), w = t / 32, lane = t % 32;
+  uint64_t u = 0;
+  std::memcpy(&u, &v, sizeof(T));
+  c.slot[w][lane] = u;
+  arrive(w);
+  T r = v;
+  if (in_range) std::memcpy(&r, &c.slot[w][src_lane], sizeof(T));
+  arrive(w);
+  return r;
+}
+
+}  // namespace simt
+
+#define threadIdx (::simt::thread_idx())
+#define blockIdx (::simt::block_idx())
+#define blockDim (::simt::block_dim())
+#define gridDim (::simt::grid_dim())
+
+inline void __syncthreads() { simt::arrive(-1); }
+inline int __syncthreads_or(int p) {
+  static int acc;
+  simt::arrive(-1);
+  acc = 0;
+  simt::arrive(-1);
+  if (p) acc = 1;
+  simt::arrive(-1);
+  const int r = acc;
+  simt::arrive(-1);
+  return r;
+}
+inline void __syncwarp(unsigned = 0xffffffffu) { simt::arrive(simt::flat_tid() / 32); }
+template <class T> inline T __shfl_xor_sync(unsigned, T v, int o, int = 32) {
+  const int lane = simt::flat_tid() % 32;
+  return simt::shfl(v, lane ^ o, true);
+}
+template <class T> inline T __shfl_sync(unsigned, T v, int src, int = 32) { return simt::shfl(v, src & 31, true); }
+template <class T> inline T __shfl_down_sync(unsigned, T v, unsigned d, int = 32) {
+  const int lane = simt::flat_tid() % 32;
+  return simt::shfl(v, lane + (int)d, lane + (int)d < 32);
+}
+template <class T> inline T __shfl_up_sync(unsigned, T v, unsigned d, int = 32) {
+  const int lane = simt::flat_tid() % 32;
+  return simt::shfl(v, lane - (int)d, lane - (int)d >= 0);
+}
+inline unsigned __ballot_sync(unsigned, int p) {
+  simt::Cta& c = simt::cta();
+  const int t = simt::flat_tid(), w = t / 32, lane = t % 32;
+  c.slot[w][lane] = p ? 1 : 0;
+  simt::arrive(w);
+  unsigned r = 0;
+  for (int o = 0; o < c.live_warp[w] && o < 32; ++o)
+    if (c.slot[w][o]) r |= 1u << o;
+  simt::arrive(w);
+  return r;
+}
+inline int __all_sync(unsigned m, int p) { return __ballot_sync(m, !p) == 0; }
+inline int __any_sync(unsigned m, int p) { return __ballot_sync(m, p) != 0; }
