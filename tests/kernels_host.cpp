@@ -5,6 +5,7 @@
 // could never complete. Built by the CPU tests with g++ (tests/host_build.py).
 #include "simt_host.h"
 
+#include "batch_meta_kernels.cuh"
 #include "sampling_kernels.cuh"
 
 using namespace vllt;
@@ -28,4 +29,12 @@ extern "C" int run_accept(const int32_t* cu_rows, const int32_t* drafts, const i
                           const int32_t* picks, int32_t* n_accepted) {
   return simt::launch(smp::accept_kernel, dim3((num_seqs + 127) / 128), dim3(128), 0, cu_rows, drafts, draft_off,
                       num_seqs, picks, n_accepted) ? 0 : -1;
+}
+
+extern "C" int run_build_meta(const int32_t* rec, int32_t* pool, int pool_slots, int S_cap, int T_cap, int R_cap,
+                              int W_cap, int bs, int num_blocks, int qp, int32_t* meta, const int32_t* tsrc,
+                              int tsrc_len, int vocab) {
+  const MetaLayout L = MetaLayout::make(S_cap, T_cap, R_cap, W_cap);
+  return simt::launch(bmk::build_meta_kernel, dim3(1), dim3(bmk::kThreads), 0, rec, L, bs, num_blocks, qp, meta,
+                      pool, pool ? pool_slots : 0, tsrc, tsrc ? tsrc_len : 0, vocab) ? 0 : -1;
 }

@@ -127,7 +127,7 @@ template <class T> inline T atomicCAS(T* p, T c, T v) { T o = *p; if (o == c) *p
 namespace simt {
 
 constexpr int kMaxThreads = 1024;
-constexpr size_t kStack = 1 << 17;
+constexpr size_t kStack = 1 << 16;  // per fiber
 
 struct Fiber {
   ucontext_t ctx;
@@ -232,7 +232,7 @@ inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<voi
   block_dim() = block;
   dyn_smem().assign(smem + 16, 0);
   Cta& c = cta();
-  c.stacks.assign(kStack * n, 0);
+  if (c.stacks.size() < kStack * n) c.stacks.resize(kStack * n);
   for (unsigned bz = 0; bz < grid.z; ++bz)
     for (unsigned by = 0; by < grid.y; ++by)
       for (unsigned bx = 0; bx < grid.x; ++bx) {

@@ -1,8 +1,10 @@
 """CPU: the device batch flatten's arithmetic against the reference.
 
-build_meta_kernel (csrc/batch_meta.cu) keeps its per-item arithmetic in
-csrc/meta_items.cuh; tests/meta_host.cpp runs the kernel's phases one after
-another with those functions, compiled for the host. On every pass of the
+build_meta_kernel (csrc/batch_meta_kernels.cuh) keeps its per-item
+arithmetic in csrc/meta_items.cuh. Every test runs twice: on
+tests/meta_host.cpp, which runs the kernel's phases one after another with
+those functions compiled for the host, and on the kernel's own code under the
+host SIMT emulation (one CTA of 1024 fibers, tests/kernels_host.cpp). On every pass of the
 reference's replays (the bench model with chunked prefill; speculative k = 4
 with the prefix cache, block 4) the metadata it builds from the packed step
 record (classic, and pooled with a persistent table pool) must equal the
@@ -21,16 +23,44 @@ from oracle import runner as OR
 from tests import fixtures as F
 
 
-@pytest.fixture(scope="module")
-def meta_host(tmp_path_factory):
+ARGS = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 8 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                                                 ctypes.c_int]
+
+
+class _Kernel:
+    """build_meta_kernel's own code on the host SIMT emulation (one CTA of
+    1024 fibers), behind the phase harness's entry point."""
+
+    def __init__(self, lib):
+        self.lib = lib
+
+    def build_meta_host(self, *a):
+        guard = [a[0], a[1]]  # keep the ctypes call's buffers as given
+        rc = self.lib.run_build_meta(*a)
+        assert rc == 0, "the CTA's threads waited on barriers that cannot complete"
+        del guard
+        # the kernel reports through the counters' error word, as on the device
+        meta_ptr = a[10]
+        return int(np.ctypeslib.as_array((ctypes.c_int32 * 16).from_address(meta_ptr))[7])
+
+
+@pytest.fixture(scope="module", params=["phases", "kernel"])
+def meta_host(request, tmp_path_factory):
+    """The builder run as its phases one after another (tests/meta_host.cpp),
+    or as the kernel itself on the host SIMT emulation (tests/kernels_host.cpp)."""
     from tests.host_build import build_harness
 
-    lib = build_harness("meta_host", str(tmp_path_factory.mktemp("meta")))
+    if request.param == "phases":
+        lib = build_harness("meta_host", str(tmp_path_factory.mktemp("meta")))
+        if lib is None:
+            pytest.skip("g++ is not available")
+        lib.build_meta_host.argtypes = ARGS
+        return lib
+    lib = build_harness("kernels_host", str(tmp_path_factory.mktemp("meta_kernel")))
     if lib is None:
         pytest.skip("g++ is not available")
-    lib.build_meta_host.argtypes = ([ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 8 +
-                                    [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int])
-    return lib
+    lib.run_build_meta.argtypes = ARGS
+    return _Kernel(lib)
 
 
 def build(host, rec, caps, bs, nb, qp, pool=None, tsrc=None, vocab=261):
@@ -132,3 +162,24 @@ def test_kernel_arithmetic_resolves_token_references(meta_host):
         assert err == 2 and f(8, 2).tolist() == [0, 5] and f(0, 16)[0] == 2
     err, meta, f = build(meta_host, rec, caps, 16, 64, 8)  # no source
     assert err == 2 and f(8, 2).tolist() == [0, 5]
+
+
+def test_a_runnable_error_leaves_every_token_built(meta_host):
+    """A bad block id is flagged in phase 2 while the step stays runnable:
+    every one of the step's tokens (here 100, spread over four warps) still
+    gets its position, token and slot. The stop flag that every thread reads
+    after phase 1 is a separate word from the phase-2/3 flags, so a warp
+    that reads it late cannot see a later phase's error and leave early."""
+    from vllt import _lib
+
+    caps = _lib.Caps(4, 128, 16, 8)
+    toks = list(range(100))
+    rec = [1, 100, 1, 7, 0, 100, 1] + toks + [3, 4, 5, 777, 6, 7, 8]  # block 3 of 7 is unknown
+    err, meta, f = build(meta_host, rec, caps, 16, 64, 8)
+    assert err == 2 and f(0, 16)[0] == 1
+    assert f(4, 100).tolist() == list(range(100)) and f(8, 100).tolist() == toks
+    slots = f(5, 100)
+    assert slots[48:64].tolist() == [-1] * 16 and slots[:48].tolist() == [3 * 16 + i for i in range(16)] + \
+        [4 * 16 + i for i in range(16)] + [5 * 16 + i for i in range(16)]
+    assert slots[64:].tolist() == [6 * 16 + i for i in range(16)] + [7 * 16 + i for i in range(16)] + \
+        [8 * 16 + i for i in range(4)]
