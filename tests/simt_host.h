@@ -84,6 +84,11 @@ inline __nv_bfloat16 __float2bfloat16_rn(float f) {
   return {(uint16_t)(u >> 16)};
 }
 
+struct __nv_bfloat162 {
+  __nv_bfloat16 x, y;
+};
+inline __nv_bfloat162 __floats2bfloat162_rn(float a, float b) { return {__float2bfloat16_rn(a), __float2bfloat16_rn(b)}; }
+
 // ---- scalar intrinsics ---------------------------------------------------------
 template <class A, class B> inline typename std::common_type<A, B>::type min(A a, B b) { return b < a ? b : a; }
 template <class A, class B> inline typename std::common_type<A, B>::type max(A a, B b) { return a < b ? b : a; }

@@ -1,8 +1,8 @@
-"""CPU: the library's sampling kernels, their own code, on the host.
+"""CPU: the library's SIMT kernels, their own code, on the host.
 
-csrc/sampling_kernels.cuh holds the device code of greedy_kernel,
-top_p_kernel and accept_kernel. tests/kernels_host.cpp compiles it for the
-host, where each CTA runs as 256 cooperative fibers with CUDA's barrier and
+csrc/sampling_kernels.cuh, norm_kernels.cuh and cache_kernels.cuh hold the
+device code of the sampling, row-wise and KV-cache kernels.
+tests/kernels_host.cpp compiles it for the host, where each CTA runs as 256 cooperative fibers with CUDA's barrier and
 warp-shuffle semantics (tests/simt_host.h). The kernels run with the grids
 their launchers use, against the reference's fixtures. Every buffer sits
 against a PROT_NONE guard page (tests/guarded.py), alternately after and
@@ -16,7 +16,13 @@ before it, so an out-of-bounds read or write stops the test:
     a CDF boundary) inside the reference's keep set; an index outside the
     logits yields -1. At the Llama-3 vocabulary with top-k and top-p it
     matches the oracle;
-  * accept_kernel, on the reference's verify cases: the accepted counts.
+  * accept_kernel, on the reference's verify cases: the accepted counts;
+  * rmsnorm_kernel against the oracle's rms_norm over gathered rows; the
+    embedding (ids outside the vocabulary give zeros) and RoPE bit-identical
+    to the oracle; the bf16 model's embedding and fused add + RMSNorm;
+    argmax_rows with ties and padding;
+  * reshape_and_cache (fp32 and bf16) and copy_blocks against the oracle's
+    flat-slot cache, with slots and pairs outside the cache skipped.
 """
 
 import ctypes
@@ -152,3 +158,157 @@ def test_accept_kernel_on_reference_verify_cases(k):
     g = [guarded(a) for a in (cu, z["verify_drafts"].astype(np.int32), doff, picks)]
     assert k.run_accept(ptr(g[0]), ptr(g[1]), ptr(g[2]), S, ptr(g[3]), ptr(acc)) == 0
     assert acc.tolist() == z["verify_accepted"].tolist()
+
+
+# ---- row-wise kernels (csrc/norm_kernels.cuh) ---------------------------------------
+
+def _bf16_bits(x):
+    """float32 -> bf16 bit patterns (round to nearest even), as uint16."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def _bf16_float(b):
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+@pytest.mark.parametrize("dim", [64, 384])
+def test_rmsnorm_kernel_against_the_oracle(k, dim):
+    """fp32 RMSNorm (vllmlite/model.py:17-19) over gathered rows: within
+    2 ulp-scale of the oracle (the sum of squares is reduced in another
+    order), rows past the device row count untouched."""
+    from oracle.model import rms_norm
+
+    f = k.run_rmsnorm
+    f.argtypes = [P, P, P, P, I, P, I, ctypes.c_float]
+    rng = np.random.default_rng(dim)
+    x = guarded(rng.standard_normal((50, dim)).astype(np.float32))
+    w = guarded((1 + 0.1 * rng.standard_normal(dim)).astype(np.float32))
+    idx = guarded(rng.permutation(50)[:40].astype(np.int32), "start")
+    out = guarded(np.full((40, dim), -7, np.float32))
+    rows = guarded(np.array([37], np.int32))
+    assert f(ptr(x), ptr(idx), ptr(w), ptr(out), 40, ptr(rows), dim, 1e-5) == 0
+    want = rms_norm(x[idx[:37]], w)
+    np.testing.assert_allclose(out[:37], want, rtol=2e-6, atol=1e-7)
+    assert (out[37:] == -7).all()
+
+
+def test_embed_and_rope_kernels_against_the_oracle(k):
+    """Embedding rows by token id (out-of-range ids give zeros), then RoPE on
+    interleaved pairs (vllmlite/attention.py:28-37): bit-identical to the
+    oracle, whose products and sums round the same way."""
+    from oracle.attention import rope_tables, rotate
+
+    emb_f = k.run_embed
+    emb_f.argtypes = [P, P, P, I, P, I, I]
+    rope_f = k.run_rope
+    rope_f.argtypes = [P, P, P, P, I, I, I, I]
+    rng = np.random.default_rng(3)
+    V, H, D = 261, 8, 48
+    dim = H * D
+    emb = guarded(rng.standard_normal((V, dim)).astype(np.float32))
+    tok = rng.integers(0, V, 30).astype(np.int32)
+    tok[[4, 9]] = [-1, V]
+    tok = guarded(tok, "start")
+    x = guarded(np.full((30, dim), -7, np.float32))
+    assert emb_f(ptr(emb), ptr(tok), ptr(x), 30, None, dim, V) == 0
+    want = emb[np.clip(tok, 0, V - 1)]
+    want[[4, 9]] = 0
+    np.testing.assert_array_equal(x, want)
+    cos, sin = rope_tables(D, 512)
+    cos_g, sin_g = guarded(cos.astype(np.float32)), guarded(sin.astype(np.float32))
+    pos = guarded(rng.integers(0, 512, 30).astype(np.int32), "start")
+    before = x.copy().reshape(30, H, D)
+    assert rope_f(ptr(x), ptr(pos), ptr(cos_g), ptr(sin_g), 30, H, D, 512) == 0
+    np.testing.assert_array_equal(x.reshape(30, H, D), rotate(before, pos, cos, sin))
+
+
+def test_bf16_embed_and_fused_add_rmsnorm(k):
+    """The bf16 model's embedding (bf16 rows widened to fp32) and the fused
+    x += add; out = bf16(x / rms * w) over gathered rows: x exact, out within
+    one bf16 rounding of a float64 restatement."""
+    emb_f = k.run_embed_bf16
+    emb_f.argtypes = [P, P, P, I, P, I, I]
+    f = k.run_rmsnorm_bf16
+    f.argtypes = [P, P, P, P, P, I, P, I, ctypes.c_float]
+    rng = np.random.default_rng(5)
+    V, dim, T = 100, 256, 12
+    table = _bf16_bits(rng.standard_normal((V, dim)))
+    tok = guarded(rng.integers(0, V, T).astype(np.int32))
+    x = guarded(np.full((T, dim), -7, np.float32))
+    assert emb_f(ptr(guarded(table)), ptr(tok), ptr(x), T, None, dim, V) == 0
+    np.testing.assert_array_equal(x, _bf16_float(table[tok]))
+    add = _bf16_bits(rng.standard_normal((T, dim)))
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    idx = rng.permutation(T)[:8].astype(np.int32)
+    x0 = x.copy()
+    out = guarded(np.zeros((8, dim), np.uint16))
+    assert f(ptr(x), ptr(guarded(add)), ptr(guarded(idx)), ptr(guarded(w)), ptr(out), 8, None, dim, 1e-5) == 0
+    summed = x0 + _bf16_float(add)
+    np.testing.assert_array_equal(x[idx], summed[idx])  # the gathered rows take the all-reduced partial
+    xs = summed[idx].astype(np.float64)
+    want = xs / np.sqrt((xs * xs).mean(1, keepdims=True) + 1e-5) * w
+    np.testing.assert_allclose(_bf16_float(out), want, rtol=2 ** -8, atol=1e-6)
+
+
+@pytest.mark.parametrize("ld", [264, 263])
+def test_argmax_rows_kernel(k, ld):
+    """(max, first index of the max) + offset per row, vector or scalar path."""
+    f = k.run_argmax_rows
+    f.argtypes = [P, I, P, I, I, I, P, P]
+    rng = np.random.default_rng(ld)
+    V, R = 261, 9
+    x = rng.standard_normal((R, ld)).astype(np.float32)
+    x[0, [5, 200]] = 9.0      # tie: the first index wins
+    x[1, :] = 1.0             # all equal: index 0
+    x[2, V:] = 100.0          # padding past the vocabulary is not read as a candidate
+    val = guarded(np.zeros(R, np.float32))
+    idx = guarded(np.zeros(R, np.int32))
+    assert f(ptr(guarded(x)), R, None, V, ld, 1000, ptr(val), ptr(idx)) == 0
+    np.testing.assert_array_equal(idx, x[:, :V].argmax(1) + 1000)
+    np.testing.assert_array_equal(val, x[:, :V].max(1))
+
+
+# ---- KV-cache kernels (csrc/cache_kernels.cuh) -------------------------------------
+
+@pytest.mark.parametrize("f32", [1, 0])
+def test_reshape_and_cache_and_copy_blocks(k, f32):
+    """write_kv (vllmlite/attention.py:47-49) into the [block][kv head][offset][D]
+    layout, skipping slots outside the cache, then copy-on-write block copies
+    (vllmlite/runner.py:54-60) in every layer, skipping out-of-range pairs:
+    the oracle's flat-slot cache, entry for entry."""
+    from oracle.attention import scatter_kv
+    from oracle.runner import copy_blocks
+
+    w = k.run_reshape_and_cache
+    w.argtypes = [P, P, P, P, P, I, I, I, I, I, I]
+    c = k.run_copy_blocks
+    c.argtypes = [P, P, P, I, I, I, I, I, I, I]
+    rng = np.random.default_rng(f32)
+    L, nb, n_kv, bs, D, T = 3, 10, 2, 4, 48 if f32 else 64, 13
+    dt = np.float32 if f32 else np.uint16
+    kv = [rng.standard_normal((T, n_kv, D)).astype(np.float32) for _ in range(2)]
+    if not f32:
+        kv = [_bf16_bits(a) for a in kv]
+    slots = rng.choice(nb * bs, T, replace=False).astype(np.int32)
+    slots[[2, 7]] = [-1, nb * bs]
+    caches = [np.zeros((L, nb, n_kv, bs, D), dt) for _ in range(2)]
+    gk, gv = guarded(caches[0]), guarded(caches[1], "start")
+    layer = 1  # write into one layer's slice, as the forward does
+    lk, lv = gk[layer], gv[layer]
+    assert w(ptr(guarded(kv[0])), ptr(guarded(kv[1])), ptr(lk), ptr(lv), ptr(guarded(slots, "start")), T, n_kv, D,
+             bs, nb, f32) == 0
+    flat = [np.zeros((L, nb * bs, n_kv, D), dt) for _ in range(2)]
+    ok = (slots >= 0) & (slots < nb * bs)
+    scatter_kv(flat[0][layer], flat[1][layer], kv[0][ok], kv[1][ok], slots[ok])
+
+    def as_flat(g):
+        return g.transpose(0, 1, 3, 2, 4).reshape(L, nb * bs, n_kv, D)
+
+    np.testing.assert_array_equal(as_flat(gk), flat[0])
+    np.testing.assert_array_equal(as_flat(gv), flat[1])
+    pairs = np.array([[slots[0] // bs, 9], [3, 0], [-1, 2], [4, nb]], np.int32)
+    assert c(ptr(gk), ptr(gv), ptr(guarded(pairs)), len(pairs), L, nb, n_kv, bs, D, f32) == 0
+    copy_blocks(flat[0], flat[1], [tuple(p) for p in pairs[:2]], bs)
+    np.testing.assert_array_equal(as_flat(gk), flat[0])
+    np.testing.assert_array_equal(as_flat(gv), flat[1])
