@@ -7,6 +7,7 @@
 
 #include <algorithm>
 
+#include "attention_kernels.cuh"
 #include "batch_meta_kernels.cuh"
 #include "cache_kernels.cuh"
 #include "norm_kernels.cuh"
@@ -102,4 +103,73 @@ extern "C" int run_copy_blocks(void* kc, void* vc, const int32_t* pairs, int n_p
   const int64_t block_bytes = (int64_t)n_kv * bs * D * (f32 ? 4 : 2);
   return simt::launch(ck::copy_blocks_kernel, dim3(n_pairs, n_layers, 2), dim3(256), 0, (uint4*)kc, (uint4*)vc,
                       pairs, num_blocks, block_bytes / 16) ? 0 : -1;
+}
+
+// ---- generic paged attention (as attention_pass's generic branch, standalone) ----
+// Items are (sequence, tile) pairs from num_seqs and max_qlen; a single-query
+// pass over more than 512 keys splits the context when `ws` holds the
+// partials (split_len 512), then merges. Returns -1 on a barrier error, -2 for
+// a head_dim the library does not build.
+namespace {
+
+template <typename T, int D, int ROWS>
+bool launch_rows(const ak::AttnParams& p, int items, int splits) {
+  return simt::launch(ak::attention_kernel<T, D, ROWS>, dim3(p.n_kv, items, splits), dim3(ak::kWarps * 32),
+                      ak::attention_smem_bytes<T, D, ROWS>(), p);
+}
+
+template <typename T, int D>
+int launch_dim(const ak::AttnParams& p, int rows, int items, int splits) {
+  bool ok;
+  if (rows <= 2) ok = launch_rows<T, D, 2>(p, items, splits);
+  else if (rows <= 4) ok = launch_rows<T, D, 4>(p, items, splits);
+  else if (rows <= 8) ok = launch_rows<T, D, 8>(p, items, splits);
+  else ok = launch_rows<T, D, 16>(p, items, splits);
+  if (!ok) return -1;
+  if (splits == 1) return 0;
+  const int blocks = (items * p.H * 32 + 255) / 256;
+  return simt::launch(ak::merge_splits_kernel<T, D>, dim3(blocks), dim3(256), 0, p, splits) ? 0 : -1;
+}
+
+template <typename T>
+int launch_any(const ak::AttnParams& p, int D, int rows, int items, int splits) {
+  switch (D) {
+    case 8: return launch_dim<T, 8>(p, rows, items, splits);
+    case 16: return launch_dim<T, 16>(p, rows, items, splits);
+    case 32: return launch_dim<T, 32>(p, rows, items, splits);
+    case 48: return launch_dim<T, 48>(p, rows, items, splits);
+    case 64: return launch_dim<T, 64>(p, rows, items, splits);
+    case 128: return launch_dim<T, 128>(p, rows, items, splits);
+    default: return -2;
+  }
+}
+
+}  // namespace
+
+extern "C" int run_attention(int f32, const void* q, const void* kc, const void* vc, void* out, const int32_t* tables,
+                             int W, const int32_t* cu_q, const int32_t* ctx, int num_seqs, int max_qlen,
+                             int single_query, int max_ctx, int H, int n_kv, int D, int bs, int num_blocks,
+                             float scale, float* ws, int64_t ws_bytes) {
+  ak::AttnParams p{};
+  p.q = q; p.kc = kc; p.vc = vc; p.out = out;
+  p.tables = tables; p.W = W; p.cu_q = cu_q; p.ctx = ctx;
+  p.H = H; p.n_kv = n_kv; p.n_rep = H / n_kv; p.bs = bs; p.num_blocks = num_blocks;
+  p.scale = scale; p.P_cap = num_seqs; p.num_seqs = num_seqs;
+  p.qp = single_query ? 1 : vllt::tile_positions(p.n_rep);
+  p.items_per_seq = single_query ? 1 : (std::max(max_qlen, 1) + p.qp - 1) / p.qp;
+  const int items = p.items_per_seq * num_seqs;
+  const int rows = p.qp * p.n_rep;
+  int splits = 1;
+  if (single_query && max_ctx > 512) {
+    splits = (max_ctx + 511) / 512;
+    const int64_t need = (int64_t)splits * num_seqs * H * (D + 2) * (int64_t)sizeof(float);
+    if (ws && ws_bytes >= need) {
+      p.split_len = 512;
+      p.ws_o = ws;
+      p.ws_ml = ws + (int64_t)splits * num_seqs * H * D;
+    } else {
+      splits = 1;
+    }
+  }
+  return f32 ? launch_any<float>(p, D, rows, items, splits) : launch_any<__nv_bfloat16>(p, D, rows, items, splits);
 }

@@ -164,6 +164,10 @@ inline dim3& block_dim() { static dim3 d; return d; }
 inline dim3& grid_dim() { static dim3 d; return d; }
 inline std::vector<unsigned char>& dyn_smem() { static std::vector<unsigned char> m; return m; }
 inline const dim3& thread_idx() { return cta().f[cta().cur].tid; }
+inline unsigned char* dynamic_smem() {  // 16-byte aligned
+  auto& m = dyn_smem();
+  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(m.data()) + 15) & ~uintptr_t(15));
+}
 
 inline void switch_next() {
   Cta& c = cta();

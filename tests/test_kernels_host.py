@@ -1,7 +1,8 @@
 """CPU: the library's SIMT kernels, their own code, on the host.
 
-csrc/sampling_kernels.cuh, norm_kernels.cuh and cache_kernels.cuh hold the
-device code of the sampling, row-wise and KV-cache kernels.
+csrc/sampling_kernels.cuh, norm_kernels.cuh, cache_kernels.cuh and
+attention_kernels.cuh hold the device code of the sampling, row-wise,
+KV-cache and generic attention kernels.
 tests/kernels_host.cpp compiles it for the host, where each CTA runs as 256 cooperative fibers with CUDA's barrier and
 warp-shuffle semantics (tests/simt_host.h). The kernels run with the grids
 their launchers use, against the reference's fixtures. Every buffer sits
@@ -22,7 +23,12 @@ before it, so an out-of-bounds read or write stops the test:
     to the oracle; the bf16 model's embedding and fused add + RMSNorm;
     argmax_rows with ties and padding;
   * reshape_and_cache (fp32 and bf16) and copy_blocks against the oracle's
-    flat-slot cache, with slots and pairs outside the cache skipped.
+    flat-slot cache, with slots and pairs outside the cache skipped;
+  * the generic varlen attention kernel (and its split-K merge) against a
+    float64 restatement of the reference's attention: C1 decode rows up to
+    1300 keys, chunked-prefill tiles mixed with decode rows, the C3 shape
+    (32 heads / 8 KV heads / D 128, 4096 keys), GQA 1 to 8, block sizes 1 to
+    64, fp32 and bf16.
 """
 
 import ctypes
@@ -312,3 +318,78 @@ def test_reshape_and_cache_and_copy_blocks(k, f32):
     copy_blocks(flat[0], flat[1], [tuple(p) for p in pairs[:2]], bs)
     np.testing.assert_array_equal(as_flat(gk), flat[0])
     np.testing.assert_array_equal(as_flat(gv), flat[1])
+
+
+# ---- generic paged attention (csrc/attention_kernels.cuh) --------------------------
+
+def _attention_case(rng, qlens, ctxs, H, n_kv, D, bs, f32, spare=7):
+    """Random q / K / V per sequence, K and V scattered into the
+    [block][kv head][offset][D] cache through shuffled block tables."""
+    S = len(qlens)
+    W = max(-(-c // bs) for c in ctxs)
+    nb = sum(-(-c // bs) for c in ctxs) + spare
+    perm = rng.permutation(nb)
+    tables = np.full((S, W), -1, np.int32)
+    o = 0
+    kc = np.zeros((nb, n_kv, bs, D), np.float32)
+    vc = np.zeros_like(kc)
+    dense = []
+    for s, c in enumerate(ctxs):
+        n = -(-c // bs)
+        tables[s, :n] = perm[o:o + n]
+        o += n
+        k = rng.standard_normal((c, n_kv, D)).astype(np.float32)
+        v = rng.standard_normal((c, n_kv, D)).astype(np.float32)
+        if not f32:
+            k, v = _bf16_float(_bf16_bits(k)), _bf16_float(_bf16_bits(v))
+        for p in range(c):
+            kc[tables[s, p // bs], :, p % bs] = k[p]
+            vc[tables[s, p // bs], :, p % bs] = v[p]
+        dense.append((k, v))
+    T = sum(qlens)
+    q = rng.standard_normal((T, H, D)).astype(np.float32)
+    if not f32:
+        q = _bf16_float(_bf16_bits(q))
+    cu = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+    return q, kc, vc, tables, cu, np.asarray(ctxs, np.int32), dense, nb, W
+
+
+@pytest.mark.parametrize("f32", [1, 0])
+@pytest.mark.parametrize("H,n_kv,D,bs,qlens,ctxs,single", [
+    (8, 4, 48, 16, [1] * 6, [1, 15, 16, 17, 300, 1300], 1),     # C1 decode rows, split-K past 512 keys
+    (8, 4, 48, 16, [40, 1, 7, 16], [40, 200, 7, 33], 0),       # chunked prefill tiles mixed with decode rows
+    (32, 8, 128, 16, [1] * 3, [4096, 517, 1], 1),              # C3 shape, 8 splits
+    (6, 1, 64, 4, [9, 3], [30, 3], 0),                         # GQA 6, block 4
+    (4, 4, 8, 1, [3, 1], [3, 9], 0),                           # MHA, block 1, head_dim 8
+    (16, 2, 32, 64, [5, 1], [70, 64], 0),                      # n_rep 8, block 64
+])
+def test_generic_attention_kernel_against_float64(k, f32, H, n_kv, D, bs, qlens, ctxs, single):
+    """The generic varlen kernel (vllmlite/attention.py:59-98 for a ragged
+    batch: causal, GQA, online softmax, split-K with the merge kernel) against
+    a float64 restatement of the reference's attention. Tolerance: fp32 paths
+    2e-5 of the output scale, bf16 outputs one bf16 rounding (2^-8)."""
+    from oracle.attention import dense_attention
+
+    f = k.run_attention
+    f.argtypes = [I, P, P, P, P, P, I, P, P, I, I, I, I, I, I, I, I, I, ctypes.c_float, P, ctypes.c_int64]
+    rng = np.random.default_rng(D * 7 + len(qlens) + f32)
+    q, kc, vc, tables, cu, ctx, dense, nb, W = _attention_case(rng, qlens, ctxs, H, n_kv, D, bs, f32)
+    scale = 1.0 / np.sqrt(D)
+    S, T = len(qlens), int(cu[-1])
+    if f32:
+        bufs = [guarded(a) for a in (q, kc, vc)]
+        out = guarded(np.full((T, H, D), np.nan, np.float32))
+    else:
+        bufs = [guarded(_bf16_bits(a)) for a in (q, kc, vc)]
+        out = guarded(np.zeros((T, H, D), np.uint16))
+    splits = -(-max(ctxs) // 512)
+    ws = guarded(np.zeros(splits * S * H * (D + 2), np.float32), "start")
+    assert f(f32, ptr(bufs[0]), ptr(bufs[1]), ptr(bufs[2]), ptr(out), ptr(guarded(tables, "start")), W,
+             ptr(guarded(cu)), ptr(guarded(ctx, "start")), S, max(qlens), single, max(ctxs), H, n_kv, D, bs, nb,
+             scale, ptr(ws), ws.nbytes) == 0
+    got = out if f32 else _bf16_float(out)
+    for s in range(S):
+        kk, vv = dense[s]
+        want = dense_attention(q[cu[s]:cu[s + 1]], kk, vv, n_kv, scale)
+        tol = 2e-5 if f32 else 2.0 ** -8
+        np.testing.assert_allclose(got[cu[s]:cu[s + 1]], want, rtol=tol, atol=tol)

@@ -12,6 +12,15 @@
 #include <stdint.h>
 #include <string.h>
 
+// A kernel's dynamic shared memory: `VLLT_DYNAMIC_SMEM(name);` declares
+// `name` as the 16-byte aligned unsigned char array of the launch's dynamic
+// shared memory (under the host emulation, the emulation's buffer for it).
+#ifdef VLLT_SIMT_HOST
+#define VLLT_DYNAMIC_SMEM(name) unsigned char* name = ::simt::dynamic_smem()
+#else
+#define VLLT_DYNAMIC_SMEM(name) extern __shared__ __align__(16) unsigned char name[]
+#endif
+
 namespace vllt {
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }

@@ -8,10 +8,6 @@
 
 namespace vllt {
 
-// Query positions per multi-token attention tile for a GQA group of n_rep:
-// a tile holds up to 16 (position, head) rows.
-__host__ __device__ inline int tile_positions(int n_rep) { return n_rep >= 16 ? 1 : 16 / n_rep; }
-
 // qp: query positions per multi-token attention tile (see query_tile_positions).
 // pool: persistent block-table pool [pool_slots][L.W_cap] for records in the
 // pooled layout (NULL for records that carry their tables). token_src: the

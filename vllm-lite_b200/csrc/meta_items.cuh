@@ -66,6 +66,10 @@ struct MetaLayout {
   }
 };
 
+// Query positions per multi-token attention tile for a GQA group of n_rep:
+// a tile holds up to 16 (position, head) rows.
+__host__ __device__ inline int tile_positions(int n_rep) { return n_rep >= 16 ? 1 : 16 / n_rep; }
+
 // Largest i in [0, n) with a[i] <= key (a ascending, a[0] == 0 <= key).
 __host__ __device__ inline int upper_index(const int32_t* a, int n, int key) {
   int lo = 0, hi = n - 1;
