@@ -283,7 +283,7 @@ def test_sources_hold_no_peer_memory_access():
             assert b not in src, f"{os.path.relpath(f, ROOT)} names {b}"
 
 
-def _fake_desc(dtype=0, tp_size=1):
+def _fake_desc(dtype=0, tp_size=1, head_dim=48):
     """A model descriptor whose pointers are placeholders: every check below
     fails on the host, before any of them would be dereferenced."""
     import ctypes as C
@@ -291,7 +291,7 @@ def _fake_desc(dtype=0, tp_size=1):
     from vllt import _lib
 
     d = _lib.ModelDesc()
-    d.n_layers, d.n_heads, d.n_kv_heads, d.head_dim = 2, 8, 4, 48
+    d.n_layers, d.n_heads, d.n_kv_heads, d.head_dim = 2, 8, 4, head_dim
     d.d_model, d.d_ff, d.vocab, d.vocab_padded = 384, 1024, 261, 264
     d.max_seq_len, d.block_size, d.num_blocks, d.rms_eps = 512, 16, 64, 1e-5
     d.dtype, d.tp_size, d.embed_rows = dtype, tp_size, 261
@@ -327,6 +327,8 @@ def test_c_abi_rejects_inconsistent_calls_before_any_launch():
     d = _fake_desc()
     d.table_pool, d.table_pool_slots = fake, 0
     assert forward(d) == _lib.VLLT_ERR_ARG and b"table_pool" in L.vllt_last_error()
+    for hd in (6, 24, 256):  # a head size the attention kernels are not built for fails before any launch
+        assert forward(_fake_desc(head_dim=hd)) == _lib.VLLT_ERR_ARG and b"head_dim" in L.vllt_last_error()
     assert forward(_fake_desc()) == _lib.VLLT_ERR_ARG and b"workspace too small" in L.vllt_last_error()
     need = L.vllt_forward_workspace_bytes(C.byref(_fake_desc()), C.byref(caps))
     assert need > 16

@@ -102,6 +102,13 @@ int check_desc(const vllt_model_desc* m) {
                    m->vocab_padded % 4 == 0 && m->block_size > 0 && m->num_blocks > 0 &&
                    m->max_seq_len > 0,
                "vllt_forward: bad model shape");
+  // the attention kernels are built for these head sizes; checked before any
+  // launch (each layer's QKV epilogue rotates and routes 4-column chunks, which
+  // needs head_dim % 4 == 0, and runs before its attention)
+  VLLT_REQUIRE(m->head_dim == 8 || m->head_dim == 16 || m->head_dim == 32 || m->head_dim == 48 ||
+                   m->head_dim == 64 || m->head_dim == 128,
+               "vllt_forward: head_dim %d not built (8, 16, 32, 48, 64, 128)", m->head_dim);
+  VLLT_REQUIRE(m->d_model % 8 == 0 && m->d_ff % 4 == 0, "vllt_forward: d_model must be a multiple of 8 and d_ff of 4");
   VLLT_REQUIRE(m->tok_emb && m->final_norm && m->lm_head && m->rope_cos && m->rope_sin &&
                    m->attn_norm && m->wqkv && m->wo && m->ffn_norm && m->w_gu && m->w_down &&
                    m->k_cache && m->v_cache,
