@@ -28,3 +28,32 @@ def build_harness(name: str, out_dir: str):
                     os.path.join(ROOT, "vllm-lite_b200", "csrc"), "-I", os.path.join(ROOT, "tests"),
                     os.path.join(ROOT, "tests", f"{name}.cpp"), "-o", out], check=True)
     return ctypes.CDLL(out)
+
+
+# the fp32 path of libvllt: the C ABI, its launchers and their kernels
+LIBRARY_SOURCES = ("capi.cu", "norm.cu", "cache_ops.cu", "sampling.cu", "batch_meta.cu", "attention.cu")
+
+
+def build_library_host(out_dir: str):
+    """libvllt's fp32 path compiled for the host: the library's own sources
+    (LIBRARY_SOURCES, unchanged) against the stub CUDA headers of
+    tests/simt_include, every launch running on the SIMT emulation of
+    tests/simt_host.h, plus tests/simt_stubs.cpp for the device-only paths.
+    Returns the CDLL with the C ABI's signatures set, or None without g++."""
+    gxx = shutil.which("g++")
+    if gxx is None:
+        return None
+    csrc = os.path.join(ROOT, "vllm-lite_b200", "csrc")
+    out = os.path.join(out_dir, "libvllt_host.so")
+    subprocess.run([gxx, "-O2", "-std=c++20", "-ffp-contract=off", "-shared", "-fPIC",
+                    "-I", os.path.join(ROOT, "tests", "simt_include"), "-I", os.path.join(ROOT, "tests"), "-I", csrc,
+                    "-x", "c++", *[os.path.join(csrc, f) for f in LIBRARY_SOURCES],
+                    "-x", "none", os.path.join(ROOT, "tests", "simt_stubs.cpp"), "-o", out], check=True)
+    lib = ctypes.CDLL(out)
+    from vllt import _lib
+
+    for name, (res, args) in _lib.SIGNATURES.items():
+        f = getattr(lib, name, None)
+        if f is not None:
+            f.restype, f.argtypes = res, args
+    return lib

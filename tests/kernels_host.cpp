@@ -10,6 +10,7 @@
 #include "attention_kernels.cuh"
 #include "batch_meta_kernels.cuh"
 #include "cache_kernels.cuh"
+#include "gemm_f32_kernels.cuh"
 #include "norm_kernels.cuh"
 #include "sampling_kernels.cuh"
 
@@ -172,4 +173,54 @@ extern "C" int run_attention(int f32, const void* q, const void* kc, const void*
     }
   }
   return f32 ? launch_any<float>(p, D, rows, items, splits) : launch_any<__nv_bfloat16>(p, D, rows, items, splits);
+}
+
+// ---- fp32 SIMT GEMM (tiles and split-K slices as sgemm_launch / sgemm_go) -------
+namespace {
+
+template <int BM, int BN, int BK, int TM, int TN, int THREADS, class Epi>
+int sgemm_go_host(const float* A, int lda, const float* B, int ldb, int M_cap, const int* M_dev, int N, int K,
+                  const Epi& epi, const GemmScratch* sc) {
+  const int k_slice = gemm_k_slice(M_cap, N, K, BM, BN, BK, sc);
+  const int ks = ceil_div(K, k_slice);
+  return simt::launch(sgemm_kernel<BM, BN, BK, TM, TN, THREADS, Epi>,
+                      dim3(ceil_div(N, BN), ceil_div(M_cap, BM), ks), dim3(THREADS), 0, A, lda, B, ldb, M_cap, M_dev,
+                      N, K, k_slice, ks > 1 ? sc->partials : nullptr, ks > 1 ? sc->counters : nullptr, epi) ? 0 : -1;
+}
+
+template <class Epi>
+int sgemm_host(const float* A, int lda, const float* B, int ldb, int M_cap, const int* M_dev, int N, int K,
+               const Epi& epi, float* partials, int* counters, int64_t partial_floats, int n_counters) {
+  GemmScratch scratch{partials, counters, partial_floats, n_counters};
+  const GemmScratch* sc = partials ? &scratch : nullptr;
+  if (M_cap <= 16) return sgemm_go_host<16, 64, 32, 2, 4, 128>(A, lda, B, ldb, M_cap, M_dev, N, K, epi, sc);
+  if (M_cap <= 32) return sgemm_go_host<32, 64, 32, 4, 4, 128>(A, lda, B, ldb, M_cap, M_dev, N, K, epi, sc);
+  if (M_cap <= 64) return sgemm_go_host<64, 64, 16, 4, 4, 256>(A, lda, B, ldb, M_cap, M_dev, N, K, epi, sc);
+  return sgemm_go_host<128, 64, 16, 8, 4, 256>(A, lda, B, ldb, M_cap, M_dev, N, K, epi, sc);
+}
+
+}  // namespace
+
+#define VLLT_GEMM_ARGS                                                                                           \
+  const float *A, int lda, const float *B, int ldb, int M_cap, const int *M_dev, int N, int K, float *partials, \
+      int *counters, int64_t partial_floats, int n_counters
+#define VLLT_GEMM_PASS A, lda, B, ldb, M_cap, M_dev, N, K
+
+extern "C" int run_sgemm_store(VLLT_GEMM_ARGS, float* C, int ldc, int n_valid) {
+  return sgemm_host(VLLT_GEMM_PASS, EpiStore{C, ldc, n_valid}, partials, counters, partial_floats, n_counters);
+}
+
+extern "C" int run_sgemm_residual(VLLT_GEMM_ARGS, float* C, int ldc) {
+  return sgemm_host(VLLT_GEMM_PASS, EpiResidual{C, ldc}, partials, counters, partial_floats, n_counters);
+}
+
+extern "C" int run_sgemm_swiglu(VLLT_GEMM_ARGS, float* out, int ldo) {
+  return sgemm_host(VLLT_GEMM_PASS, EpiSwiGLU{out, ldo}, partials, counters, partial_floats, n_counters);
+}
+
+extern "C" int run_sgemm_qkv(VLLT_GEMM_ARGS, float* q_out, float* kc, float* vc, const int32_t* pos,
+                             const int32_t* slot, const float* cos_t, const float* sin_t, int H, int n_kv, int D,
+                             int bs, int max_pos, int64_t num_slots) {
+  EpiQKV e{q_out, kc, vc, pos, slot, cos_t, sin_t, H, n_kv, D, bs, max_pos, num_slots};
+  return sgemm_host(VLLT_GEMM_PASS, e, partials, counters, partial_floats, n_counters);
 }

@@ -2,7 +2,9 @@
 // inline PTX, no tensor-memory or TMA instructions) on the host, so CPU
 // tests can execute the kernels' own code against the oracle.
 //
-// Each CTA runs as blockDim cooperative fibers (ucontext) on one OS thread.
+// Each CTA runs as blockDim cooperative fibers on one OS thread (a stack
+// switch that saves the callee-saved registers and the FP control words; no
+// system call, so a barrier over 256 threads costs microseconds).
 // A fiber runs until it reaches a barrier, then hands over to the next
 // runnable fiber of the CTA:
 //   * __syncthreads() waits for every thread of the CTA that has not exited
@@ -26,8 +28,6 @@
 
 #define VLLT_SIMT_HOST 1
 
-#include <ucontext.h>
-
 #include <climits>
 #include <cmath>
 #include <cstdint>
@@ -45,7 +45,7 @@
 #define __noinline__
 #define __launch_bounds__(...)
 #define __shared__ static
-#define __align__(n) alignas(n)
+#define __align__(n) __attribute__((aligned(n)))
 #define __grid_constant__
 
 // ---- vector types ------------------------------------------------------------
@@ -128,14 +128,65 @@ template <class T> inline T atomicAnd(T* p, T v) { T o = *p; *p = o & v; return 
 template <class T> inline T atomicExch(T* p, T v) { T o = *p; *p = v; return o; }
 template <class T> inline T atomicCAS(T* p, T c, T v) { T o = *p; if (o == c) *p = v; return o; }
 
+// ---- built-in variables: set by the scheduler (threadIdx whenever a fiber resumes) --
+inline dim3 threadIdx, blockIdx, blockDim, gridDim;
+
 // ---- the CTA scheduler ---------------------------------------------------------
 namespace simt {
+
+#if !defined(__x86_64__)
+#error "the SIMT emulation's context switch is written for x86-64"
+#endif
+
+// Saves the callee-saved registers, MXCSR and the x87 control word on the
+// current stack, stores the stack pointer in *from, switches to `to` and
+// restores the same from there (System V x86-64 ABI).
+__attribute__((naked, noinline)) inline void stack_switch(void** /*from*/, void* /*to*/) {
+  asm volatile(
+      "pushq %rbp\n"
+      "pushq %rbx\n"
+      "pushq %r12\n"
+      "pushq %r13\n"
+      "pushq %r14\n"
+      "pushq %r15\n"
+      "subq $8, %rsp\n"
+      "stmxcsr (%rsp)\n"
+      "fnstcw 4(%rsp)\n"
+      "movq %rsp, (%rdi)\n"
+      "movq %rsi, %rsp\n"
+      "ldmxcsr (%rsp)\n"
+      "fldcw 4(%rsp)\n"
+      "addq $8, %rsp\n"
+      "popq %r15\n"
+      "popq %r14\n"
+      "popq %r13\n"
+      "popq %r12\n"
+      "popq %rbx\n"
+      "popq %rbp\n"
+      "ret\n");
+}
+
+// A fresh stack whose first stack_switch "returns" into entry(), with the
+// stack aligned as at a function's entry.
+inline void* prepare_stack(char* base, size_t size, void (*entry)()) {
+  uintptr_t top = (reinterpret_cast<uintptr_t>(base) + size) & ~uintptr_t(15);
+  uint64_t* sp = reinterpret_cast<uint64_t*>(top);
+  *--sp = 0;                                    // padding: entry sees rsp % 16 == 8
+  *--sp = reinterpret_cast<uint64_t>(entry);    // return address of the first switch
+  for (int i = 0; i < 6; ++i) *--sp = 0;        // rbp rbx r12 r13 r14 r15
+  uint32_t mxcsr;
+  uint16_t fpcw;
+  asm volatile("stmxcsr %0" : "=m"(mxcsr));
+  asm volatile("fnstcw %0" : "=m"(fpcw));
+  *--sp = (uint64_t)mxcsr | ((uint64_t)fpcw << 32);
+  return sp;
+}
 
 constexpr int kMaxThreads = 1024;
 constexpr size_t kStack = 1 << 16;  // per fiber
 
 struct Fiber {
-  ucontext_t ctx;
+  void* sp = nullptr;
   dim3 tid;
   int waiting = -2;  // -2 running / runnable, -1 CTA barrier, w >= 0 warp w's barrier
   bool done = false;
@@ -144,7 +195,7 @@ struct Fiber {
 struct Cta {
   std::vector<Fiber> f;
   std::vector<char> stacks;
-  ucontext_t main_ctx;
+  void* main_sp = nullptr;
   int cur = 0, n = 0, done = 0;
   int live_cta = 0;                  // threads not exited
   int live_warp[kMaxThreads / 32];   // lanes not exited per warp
@@ -159,11 +210,8 @@ inline Cta& cta() {
   static Cta c;
   return c;
 }
-inline dim3& block_idx() { static dim3 d; return d; }
-inline dim3& block_dim() { static dim3 d; return d; }
-inline dim3& grid_dim() { static dim3 d; return d; }
 inline std::vector<unsigned char>& dyn_smem() { static std::vector<unsigned char> m; return m; }
-inline const dim3& thread_idx() { return cta().f[cta().cur].tid; }
+inline const dim3& thread_idx() { return ::threadIdx; }
 inline unsigned char* dynamic_smem() {  // 16-byte aligned
   auto& m = dyn_smem();
   return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(m.data()) + 15) & ~uintptr_t(15));
@@ -177,13 +225,14 @@ inline void switch_next() {
     if (!c.f[i].done && c.f[i].waiting == -2) {
       if (i == from) return;
       c.cur = i;
-      swapcontext(&c.f[from].ctx, &c.f[i].ctx);
+      stack_switch(&c.f[from].sp, c.f[i].sp);
+      ::threadIdx = c.f[c.cur].tid;  // resumed: this fiber's index again
       return;
     }
   }
   // nobody can run: every live thread waits on a barrier that cannot complete
   c.deadlock = true;
-  swapcontext(&c.f[from].ctx, &c.main_ctx);
+  stack_switch(&c.f[from].sp, c.main_sp);
 }
 
 inline void release(int group) {
@@ -210,26 +259,25 @@ inline void exit_thread() {
   Fiber& me = c.f[c.cur];
   me.done = true;
   ++c.done;
-  const int w = (int)((me.tid.z * block_dim().y + me.tid.y) * block_dim().x + me.tid.x) / 32;
+  const int w = (int)((me.tid.z * ::blockDim.y + me.tid.y) * ::blockDim.x + me.tid.x) / 32;
   --c.live_cta;
   --c.live_warp[w];
   if (c.arrived_cta > 0 && c.arrived_cta >= c.live_cta) release(-1);
   if (c.arrived_warp[w] > 0 && c.arrived_warp[w] >= c.live_warp[w]) release(w);
-  if (c.done == c.n) {
-    setcontext(&c.main_ctx);
-  }
+  if (c.done == c.n) stack_switch(&me.sp, c.main_sp);  // the last thread: back to the launch
   switch_next();
-  setcontext(&c.main_ctx);  // not reached unless stopped
+  stack_switch(&me.sp, c.main_sp);  // not reached unless stopped
 }
 
 inline void trampoline() {
+  ::threadIdx = cta().f[cta().cur].tid;
   (*cta().body)();
   exit_thread();
 }
 
 inline int flat_tid() {
   const dim3& t = thread_idx();
-  return (int)((t.z * block_dim().y + t.y) * block_dim().x + t.x);
+  return (int)((t.z * ::blockDim.y + t.y) * ::blockDim.x + t.x);
 }
 
 // Runs body() as every thread of every CTA of the grid; returns false if a
@@ -237,15 +285,15 @@ inline int flat_tid() {
 inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<void()>& body) {
   const int n = (int)(block.x * block.y * block.z);
   if (n < 1 || n > kMaxThreads) return false;
-  grid_dim() = grid;
-  block_dim() = block;
+  ::gridDim = grid;
+  ::blockDim = block;
   dyn_smem().assign(smem + 16, 0);
   Cta& c = cta();
   if (c.stacks.size() < kStack * n) c.stacks.resize(kStack * n);
   for (unsigned bz = 0; bz < grid.z; ++bz)
     for (unsigned by = 0; by < grid.y; ++by)
       for (unsigned bx = 0; bx < grid.x; ++bx) {
-        block_idx() = dim3(bx, by, bz);
+        ::blockIdx = dim3(bx, by, bz);
         c.f.assign(n, Fiber{});
         c.n = n;
         c.cur = c.done = 0;
@@ -259,13 +307,9 @@ inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<voi
         c.deadlock = false;
         for (int i = 0; i < n; ++i) {
           c.f[i].tid = dim3(i % block.x, (i / block.x) % block.y, i / (block.x * block.y));
-          getcontext(&c.f[i].ctx);
-          c.f[i].ctx.uc_stack.ss_sp = c.stacks.data() + kStack * i;
-          c.f[i].ctx.uc_stack.ss_size = kStack;
-          c.f[i].ctx.uc_link = nullptr;
-          makecontext(&c.f[i].ctx, trampoline, 0);
+          c.f[i].sp = prepare_stack(c.stacks.data() + kStack * i, kStack, trampoline);
         }
-        swapcontext(&c.main_ctx, &c.f[0].ctx);
+        stack_switch(&c.main_sp, c.f[0].sp);
         if (c.deadlock) {
           std::fprintf(stderr, "simt: block (%u,%u,%u): threads wait on barriers that cannot complete\n", bx, by,
                        bz);
@@ -279,6 +323,29 @@ template <class... KArgs, class... Args>
 inline bool launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
   std::function<void()> body = [&] { kernel(args...); };
   return run_grid(grid, block, smem, body);
+}
+
+// Sticky launch error (a barrier that could not complete), read and cleared
+// by the emulated cudaGetLastError.
+inline bool& launch_failed() {
+  static bool f = false;
+  return f;
+}
+
+// VLLT_LAUNCH(grid, block, smem, stream, kernel)(args...) under the emulation.
+template <class... KArgs>
+struct Launcher {
+  void (*kernel)(KArgs...);
+  dim3 grid, block;
+  size_t smem;
+  template <class... Args>
+  void operator()(Args&&... args) const {
+    if (!launch(kernel, grid, block, smem, static_cast<KArgs>(args)...)) launch_failed() = true;
+  }
+};
+template <class... KArgs>
+inline Launcher<KArgs...> launcher(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem) {
+  return {kernel, grid, block, smem};
 }
 
 template <class T>
@@ -298,10 +365,6 @@ inline T shfl(T v, int src_lane, bool in_range) {
 
 }  // namespace simt
 
-#define threadIdx (::simt::thread_idx())
-#define blockIdx (::simt::block_idx())
-#define blockDim (::simt::block_dim())
-#define gridDim (::simt::grid_dim())
 
 inline void __syncthreads() { simt::arrive(-1); }
 inline int __syncthreads_or(int p) {

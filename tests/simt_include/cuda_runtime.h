@@ -1,0 +1,53 @@
+// Test infrastructure: the part of the CUDA runtime API the library's fp32
+// launchers use, for building them for the host on the SIMT emulation
+// (tests/simt_host.h). Streams are opaque handles; launches run to completion
+// when they are made; a launch whose threads waited on barriers that could not
+// complete is reported by cudaGetLastError as a launch failure.
+#pragma once
+
+#include "simt_host.h"
+
+typedef void* cudaStream_t;
+enum cudaError_t { cudaSuccess = 0, cudaErrorInvalidValue = 1, cudaErrorLaunchFailure = 719 };
+
+inline cudaError_t cudaGetLastError() {
+  const bool f = simt::launch_failed();
+  simt::launch_failed() = false;
+  return f ? cudaErrorLaunchFailure : cudaSuccess;
+}
+inline cudaError_t cudaPeekAtLastError() { return simt::launch_failed() ? cudaErrorLaunchFailure : cudaSuccess; }
+inline const char* cudaGetErrorString(cudaError_t e) {
+  return e == cudaSuccess ? "no error" : "host emulation: threads waited on barriers that could not complete";
+}
+inline cudaError_t cudaGetDevice(int* d) {
+  *d = 0;
+  return cudaSuccess;
+}
+
+enum cudaFuncAttribute { cudaFuncAttributeMaxDynamicSharedMemorySize = 8 };
+template <class F>
+inline cudaError_t cudaFuncSetAttribute(F, cudaFuncAttribute, int) {
+  return cudaSuccess;
+}
+
+enum cudaLaunchAttributeID { cudaLaunchAttributeProgrammaticStreamSerialization = 1 };
+struct cudaLaunchAttributeValue {
+  int programmaticStreamSerializationAllowed;
+};
+struct cudaLaunchAttribute {
+  cudaLaunchAttributeID id;
+  cudaLaunchAttributeValue val;
+};
+struct cudaLaunchConfig_t {
+  dim3 gridDim, blockDim;
+  size_t dynamicSmemBytes;
+  cudaStream_t stream;
+  cudaLaunchAttribute* attrs;
+  unsigned numAttrs;
+};
+template <class... KArgs, class... Args>
+inline cudaError_t cudaLaunchKernelEx(const cudaLaunchConfig_t* c, void (*kernel)(KArgs...), Args&&... args) {
+  return simt::launch(kernel, c->gridDim, c->blockDim, c->dynamicSmemBytes, static_cast<KArgs>(args)...)
+             ? cudaSuccess
+             : cudaErrorLaunchFailure;
+}

@@ -393,3 +393,118 @@ def test_generic_attention_kernel_against_float64(k, f32, H, n_kv, D, bs, qlens,
         want = dense_attention(q[cu[s]:cu[s + 1]], kk, vv, n_kv, scale)
         tol = 2e-5 if f32 else 2.0 ** -8
         np.testing.assert_allclose(got[cu[s]:cu[s + 1]], want, rtol=tol, atol=tol)
+
+
+# ---- fp32 SIMT GEMM and its epilogues (csrc/gemm_f32_kernels.cuh) -----------------
+
+GEMM_ARGS = [P, I, P, I, I, P, I, I, P, P, ctypes.c_int64, I]
+
+
+def _gemm(k, name, extra):
+    f = getattr(k, name)
+    f.argtypes = GEMM_ARGS + extra
+    return f
+
+
+def _scratch(N):
+    """The forward's split-K scratch for N columns (gemm_scratch_floats / counters)."""
+    floats = -(-N // 64) * 64 * 64 * 8
+    return guarded(np.zeros(floats, np.float32)), guarded(np.zeros(-(-N // 64) * 4, np.int32), "start")
+
+
+def _gemm_tol(A, B):
+    """fp32 accumulation bound against float64: K * eps * |A| |B|."""
+    return A.shape[1] * 2.0 ** -23 * (np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64))
+
+
+@pytest.mark.parametrize("M", [1, 5, 16, 17, 40, 64, 65, 130])
+@pytest.mark.parametrize("split", [True, False])
+def test_sgemm_store_and_residual(k, M, split):
+    """C = A @ B (lm_head rows, columns past n_valid untouched) and C += A @ B
+    (o_proj / down_proj residual) against float64, with the split-K path for
+    small M when scratch is given (its counters end at zero for the next
+    launch or graph replay), and rows past the device row count untouched."""
+    store = _gemm(k, "run_sgemm_store", [P, I, I])
+    resid = _gemm(k, "run_sgemm_residual", [P, I])
+    rng = np.random.default_rng(M + 100 * split)
+    K, N = 384, 264
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = (rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float32)
+    Mv = max(1, M - 2)  # rows on the device counter
+    part, cnt = _scratch(N) if split else (None, None)
+    args = lambda: [ptr(guarded(A)), K, ptr(guarded(B, "start")), N, M, ptr(guarded(np.array([Mv], np.int32))), N, K,
+                    ptr(part), ptr(cnt), part.size if split else 0, cnt.size if split else 0]
+    C = guarded(np.full((M, N), 7.0, np.float32))
+    assert store(*args(), ptr(C), N, 261) == 0
+    want = A.astype(np.float64) @ B.astype(np.float64)
+    tol = _gemm_tol(A, B)
+    assert (np.abs(C[:Mv, :261] - want[:Mv, :261]) <= tol[:Mv, :261] + 1e-7).all()
+    assert (C[:Mv, 261:] == 7.0).all() and (C[Mv:] == 7.0).all()
+    R = guarded(np.ones((M, N), np.float32))
+    assert resid(*args(), ptr(R), N) == 0
+    assert (np.abs(R[:Mv] - (1.0 + want[:Mv])) <= tol[:Mv] + 1e-6).all() and (R[Mv:] == 1.0).all()
+    if split:
+        assert (cnt == 0).all()
+
+
+@pytest.mark.parametrize("M", [3, 33, 100])
+def test_sgemm_swiglu(k, M):
+    """Gate/up columns interleaved (gate_j, up_j): out_j = silu(gate_j) * up_j
+    (vllmlite/model.py:22-23, :117)."""
+    from oracle.model import silu
+
+    f = _gemm(k, "run_sgemm_swiglu", [P, I])
+    rng = np.random.default_rng(M)
+    K, F = 384, 256
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = (rng.standard_normal((K, 2 * F)) / np.sqrt(K)).astype(np.float32)
+    part, cnt = _scratch(2 * F)
+    out = guarded(np.zeros((M, F), np.float32))
+    assert f(ptr(guarded(A)), K, ptr(guarded(B)), 2 * F, M, None, 2 * F, K, ptr(part), ptr(cnt), part.size, cnt.size,
+             ptr(out), F) == 0
+    y = A.astype(np.float64) @ B.astype(np.float64)
+    want = silu(y[:, 0::2]) * y[:, 1::2]
+    np.testing.assert_allclose(out, want, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("H,n_kv,D,bs", [(8, 4, 48, 16), (4, 2, 64, 4), (32, 8, 128, 16)])
+def test_sgemm_qkv_epilogue(k, H, n_kv, D, bs):
+    """The QKV projection's epilogue: RoPE on the q and k columns at each
+    token's position (interleaved pairs, vllmlite/attention.py:28-37), q to its
+    buffer, k and v into the paged cache at the token's slot (write_kv,
+    attention.py:47-49); tokens with slot -1 write no K/V."""
+    from oracle.attention import rope_tables, rotate
+
+    f = _gemm(k, "run_sgemm_qkv", [P, P, P, P, P, P, P, I, I, I, I, I, ctypes.c_int64])
+    rng = np.random.default_rng(D)
+    T, d, nb, max_pos = 21, 128, 12, 256
+    N = (H + 2 * n_kv) * D
+    A = rng.standard_normal((T, d)).astype(np.float32)
+    B = (rng.standard_normal((d, N)) / np.sqrt(d)).astype(np.float32)
+    pos = rng.integers(0, max_pos, T).astype(np.int32)
+    slot = rng.choice(nb * bs, T, replace=False).astype(np.int32)
+    slot[3] = -1
+    cos, sin = rope_tables(D, max_pos)
+    part, cnt = _scratch(N)
+    q_out = guarded(np.zeros((T, H * D), np.float32))
+    kc = guarded(np.zeros((nb, n_kv, bs, D), np.float32))
+    vc = guarded(np.zeros((nb, n_kv, bs, D), np.float32), "start")
+    assert f(ptr(guarded(A)), d, ptr(guarded(B)), N, T, None, N, d, ptr(part), ptr(cnt), part.size, cnt.size,
+             ptr(q_out), ptr(kc), ptr(vc), ptr(guarded(pos)), ptr(guarded(slot)), ptr(guarded(cos.astype(np.float32))),
+             ptr(guarded(sin.astype(np.float32))), H, n_kv, D, bs, max_pos, nb * bs) == 0
+    y = (A.astype(np.float64) @ B.astype(np.float64)).astype(np.float32)
+    q = rotate(y[:, :H * D].reshape(T, H, D), pos, cos, sin)
+    kk = rotate(y[:, H * D:(H + n_kv) * D].reshape(T, n_kv, D), pos, cos, sin)
+    vv = y[:, (H + n_kv) * D:].reshape(T, n_kv, D)
+    np.testing.assert_allclose(q_out.reshape(T, H, D), q, rtol=1e-4, atol=1e-5)
+    for t in range(T):
+        if slot[t] < 0:
+            continue
+        b, o = divmod(int(slot[t]), bs)
+        np.testing.assert_allclose(kc[b, :, o], kk[t], rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(vc[b, :, o], vv[t], rtol=1e-4, atol=1e-5)
+    written = {divmod(int(s), bs) for s in slot if s >= 0}
+    for b in range(nb):
+        for o in range(bs):
+            if (b, o) not in written:
+                assert not kc[b, :, o].any() and not vc[b, :, o].any()

@@ -47,7 +47,7 @@ int launch_attention(const AttnParams& p, int grid_items, int splits, cudaStream
                          (int)smem);
   });
   dim3 grid(p.n_kv, grid_items, splits);
-  attention_kernel<T, D, ROWS><<<grid, kWarps * 32, smem, st>>>(p);
+  VLLT_LAUNCH(grid, kWarps * 32, smem, st, attention_kernel<T, D, ROWS>)(p);
   return check_launch("attention");
 }
 
@@ -78,12 +78,12 @@ int merge_dim(const AttnParams& p, int D, int items, int splits, cudaStream_t st
   const int warps = items * p.H;
   const int blocks = ceil_div(warps * 32, 256);
   switch (D) {
-    case 8: merge_splits_kernel<T, 8><<<blocks, 256, 0, st>>>(p, splits); break;
-    case 16: merge_splits_kernel<T, 16><<<blocks, 256, 0, st>>>(p, splits); break;
-    case 32: merge_splits_kernel<T, 32><<<blocks, 256, 0, st>>>(p, splits); break;
-    case 48: merge_splits_kernel<T, 48><<<blocks, 256, 0, st>>>(p, splits); break;
-    case 64: merge_splits_kernel<T, 64><<<blocks, 256, 0, st>>>(p, splits); break;
-    case 128: merge_splits_kernel<T, 128><<<blocks, 256, 0, st>>>(p, splits); break;
+    case 8: VLLT_LAUNCH(blocks, 256, 0, st, merge_splits_kernel<T, 8>)(p, splits); break;
+    case 16: VLLT_LAUNCH(blocks, 256, 0, st, merge_splits_kernel<T, 16>)(p, splits); break;
+    case 32: VLLT_LAUNCH(blocks, 256, 0, st, merge_splits_kernel<T, 32>)(p, splits); break;
+    case 48: VLLT_LAUNCH(blocks, 256, 0, st, merge_splits_kernel<T, 48>)(p, splits); break;
+    case 64: VLLT_LAUNCH(blocks, 256, 0, st, merge_splits_kernel<T, 64>)(p, splits); break;
+    case 128: VLLT_LAUNCH(blocks, 256, 0, st, merge_splits_kernel<T, 128>)(p, splits); break;
     default: return VLLT_ERR_UNSUPPORTED;
   }
   return check_launch("attention merge");

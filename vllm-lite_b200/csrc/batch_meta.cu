@@ -18,7 +18,7 @@ int build_batch_meta(const int32_t* rec, const MetaLayout& L, int bs, int num_bl
   VLLT_REQUIRE(bs > 0 && num_blocks > 0 && qp > 0 && vocab > 0, "build_batch_meta: bad sizes");
   VLLT_REQUIRE(!pool || pool_slots > 0, "build_batch_meta: a table pool needs at least one slot");
   VLLT_REQUIRE(!token_src || token_src_len > 0, "build_batch_meta: a token source needs at least one entry");
-  build_meta_kernel<<<1, kThreads, 0, st>>>(rec, L, bs, num_blocks, qp, meta, pool, pool ? pool_slots : 0,
+  VLLT_LAUNCH(1, kThreads, 0, st, build_meta_kernel)(rec, L, bs, num_blocks, qp, meta, pool, pool ? pool_slots : 0,
                                             token_src, token_src ? token_src_len : 0, vocab);
   return check_launch("build_batch_meta");
 }

@@ -22,10 +22,10 @@ int reshape_and_cache(const void* k, const void* v, void* kc, void* vc, const in
   const int blocks = (int)std::min<int64_t>((vecs + threads - 1) / threads, 148 * 16);
   const int64_t nslots = (int64_t)num_blocks * bs;
   if (dtype == VLLT_F32)
-    reshape_and_cache_kernel<float><<<blocks, threads, 0, st>>>(
+    VLLT_LAUNCH(blocks, threads, 0, st, reshape_and_cache_kernel<float>)(
         (const float*)k, (const float*)v, (float*)kc, (float*)vc, slots, num_tokens, n_kv, D, bs, nslots);
   else
-    reshape_and_cache_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(
+    VLLT_LAUNCH(blocks, threads, 0, st, reshape_and_cache_kernel<__nv_bfloat16>)(
         (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc,
         slots, num_tokens, n_kv, D, bs, nslots);
   return check_launch("reshape_and_cache");
@@ -38,7 +38,7 @@ int copy_blocks(void* kc, void* vc, const int32_t* pairs, int n_pairs, int n_lay
   const int64_t block_bytes = (int64_t)n_kv * bs * D * esize;
   VLLT_REQUIRE(block_bytes % 16 == 0, "copy_blocks: block bytes must be a multiple of 16");
   dim3 grid(n_pairs, n_layers, 2);
-  copy_blocks_kernel<<<grid, 256, 0, st>>>((uint4*)kc, (uint4*)vc, pairs, num_blocks, block_bytes / 16);
+  VLLT_LAUNCH(grid, 256, 0, st, copy_blocks_kernel)((uint4*)kc, (uint4*)vc, pairs, num_blocks, block_bytes / 16);
   return check_launch("copy_blocks");
 }
 

@@ -21,6 +21,16 @@
 #define VLLT_DYNAMIC_SMEM(name) extern __shared__ __align__(16) unsigned char name[]
 #endif
 
+// A kernel launch: `VLLT_LAUNCH(grid, block, smem, stream, kernel)(args...)`
+// is `kernel<<<grid, block, smem, stream>>>(args...)` (the kernel last, so a
+// template argument list may hold commas); under the host emulation it runs
+// the grid there.
+#ifdef VLLT_SIMT_HOST
+#define VLLT_LAUNCH(grid, block, smem, stream, ...) ::simt::launcher(__VA_ARGS__, grid, block, smem)
+#else
+#define VLLT_LAUNCH(grid, block, smem, stream, ...) __VA_ARGS__<<<grid, block, smem, stream>>>
+#endif
+
 namespace vllt {
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }

@@ -14,7 +14,7 @@ int embed_bf16(const void* emb, const int32_t* tok, float* x, int T_cap, const i
   VLLT_REQUIRE(dim % 8 == 0, "embed_bf16: dim must be a multiple of 8");
   const int64_t vecs = (int64_t)T_cap * dim / 8;
   const int blocks = (int)std::min<int64_t>((vecs + 255) / 256, 148 * 8);
-  embed_bf16_kernel<<<blocks, 256, 0, st>>>((const __nv_bfloat16*)emb, tok, x, T_cap, T_dev, dim, vocab);
+  VLLT_LAUNCH(blocks, 256, 0, st, embed_bf16_kernel)((const __nv_bfloat16*)emb, tok, x, T_cap, T_dev, dim, vocab);
   return check_launch("embed_bf16");
 }
 
@@ -22,7 +22,7 @@ int rmsnorm_bf16(float* x, const void* add, const int32_t* idx, const float* w, 
                  const int32_t* rows_dev, int dim, float eps, cudaStream_t st) {
   if (rows_cap <= 0) return VLLT_OK;
   VLLT_REQUIRE(dim % 4 == 0, "rmsnorm_bf16: dim must be a multiple of 4");
-  rmsnorm_bf16_kernel<<<rows_cap, 256, 0, st>>>(x, (const __nv_bfloat16*)add, idx, w, (__nv_bfloat16*)out, rows_cap,
+  VLLT_LAUNCH(rows_cap, 256, 0, st, rmsnorm_bf16_kernel)(x, (const __nv_bfloat16*)add, idx, w, (__nv_bfloat16*)out, rows_cap,
                                                 rows_dev, dim, eps);
   return check_launch("rmsnorm_bf16");
 }
@@ -30,7 +30,7 @@ int rmsnorm_bf16(float* x, const void* add, const int32_t* idx, const float* w, 
 int argmax_rows(const float* logits, int rows_cap, const int32_t* rows_dev, int vocab, int ld, int offset,
                 float* val, int32_t* idx, cudaStream_t st) {
   if (rows_cap <= 0) return VLLT_OK;
-  argmax_rows_kernel<<<rows_cap, 256, 0, st>>>(logits, vocab, ld, offset, rows_cap, rows_dev, val, idx);
+  VLLT_LAUNCH(rows_cap, 256, 0, st, argmax_rows_kernel)(logits, vocab, ld, offset, rows_cap, rows_dev, val, idx);
   return check_launch("argmax_rows");
 }
 
@@ -40,7 +40,7 @@ int rmsnorm(const float* x, const int32_t* idx, const float* w, float* out, int 
   VLLT_REQUIRE(dim % 4 == 0, "rmsnorm: dim must be a multiple of 4");
   const int threads = 256;
   const int blocks = ceil_div(rows_cap * 32, threads);
-  rmsnorm_kernel<<<blocks, threads, 0, st>>>(x, idx, w, out, rows_cap, rows_dev, dim, eps);
+  VLLT_LAUNCH(blocks, threads, 0, st, rmsnorm_kernel)(x, idx, w, out, rows_cap, rows_dev, dim, eps);
   return check_launch("rmsnorm");
 }
 
@@ -50,7 +50,7 @@ int embed(const float* emb, const int32_t* tok, float* x, int T_cap, const int32
   VLLT_REQUIRE(dim % 4 == 0, "embed: dim must be a multiple of 4");
   const int64_t vecs = (int64_t)T_cap * dim / 4;
   const int blocks = (int)std::min<int64_t>((vecs + 255) / 256, 148 * 8);
-  embed_kernel<<<blocks, 256, 0, st>>>(emb, tok, x, T_cap, T_dev, dim, vocab);
+  VLLT_LAUNCH(blocks, 256, 0, st, embed_kernel)(emb, tok, x, T_cap, T_dev, dim, vocab);
   return check_launch("embed");
 }
 
@@ -60,7 +60,7 @@ int rope(float* x, const int32_t* positions, const float* cos_t, const float* si
   VLLT_REQUIRE(D % 2 == 0, "rope: head_dim must be even");
   const int64_t total = (int64_t)T * heads * (D / 2);
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
-  rope_kernel<<<blocks, 256, 0, st>>>(x, positions, cos_t, sin_t, T, heads, D, max_pos);
+  VLLT_LAUNCH(blocks, 256, 0, st, rope_kernel)(x, positions, cos_t, sin_t, T, heads, D, max_pos);
   return check_launch("rope");
 }
 

@@ -14,7 +14,7 @@ int sample_greedy(const float* logits, int rows_cap, const int32_t* rows_dev, in
                   int32_t* out, cudaStream_t st) {
   if (rows_cap <= 0) return VLLT_OK;
   VLLT_REQUIRE(vocab > 0 && ld >= vocab, "sample_greedy: bad vocab/ld");
-  greedy_kernel<<<rows_cap, kThreads, 0, st>>>(logits, vocab, ld, eos_mask, eos_id, penalty, seen,
+  VLLT_LAUNCH(rows_cap, kThreads, 0, st, greedy_kernel)(logits, vocab, ld, eos_mask, eos_id, penalty, seen,
                                                (vocab + 31) / 32, rows_cap, rows_dev, out);
   return check_launch("sample_greedy");
 }
@@ -22,7 +22,7 @@ int sample_greedy(const float* logits, int rows_cap, const int32_t* rows_dev, in
 int spec_accept(const int32_t* cu_rows, const int32_t* drafts, const int32_t* draft_off,
                 int num_seqs, const int32_t* picks, int32_t* n_accepted, cudaStream_t st) {
   if (num_seqs <= 0) return VLLT_OK;
-  accept_kernel<<<ceil_div(num_seqs, 128), 128, 0, st>>>(cu_rows, drafts, draft_off, num_seqs, picks, n_accepted);
+  VLLT_LAUNCH(ceil_div(num_seqs, 128), 128, 0, st, accept_kernel)(cu_rows, drafts, draft_off, num_seqs, picks, n_accepted);
   return check_launch("spec_accept");
 }
 
@@ -32,7 +32,7 @@ int sample_top_p(const float* logits, int rows, int vocab, int ld, int logit_row
                  int32_t* out, cudaStream_t st) {
   if (rows <= 0) return VLLT_OK;
   VLLT_REQUIRE(vocab > 0 && ld >= vocab && logit_rows > 0 && temperature && u, "sample_top_p: bad arguments");
-  top_p_kernel<<<rows, kThreads, 0, st>>>(logits, vocab, ld, logit_rows, row_index, eos_mask, eos_id, penalty,
+  VLLT_LAUNCH(rows, kThreads, 0, st, top_p_kernel)(logits, vocab, ld, logit_rows, row_index, eos_mask, eos_id, penalty,
                                           seen, (vocab + 31) / 32, temperature, top_k, top_p, u, out);
   return check_launch("sample_top_p");
 }
