@@ -33,3 +33,14 @@ def have_vllmlite() -> bool:
 
 
 needs_vllmlite = pytest.mark.skipif(not have_vllmlite(), reason="vllm-lite (the host engine) is not importable")
+
+
+@pytest.fixture(scope="session")
+def host_library(tmp_path_factory):
+    """libvllt's fp32 path built for the host (tests/host_build.py), once per session."""
+    from tests.host_build import build_library_host
+
+    lib = build_library_host(str(tmp_path_factory.mktemp("libvllt_host")))
+    if lib is None:
+        pytest.skip("g++ is not available")
+    return lib

@@ -23,8 +23,9 @@ def build_harness(name: str, out_dir: str):
     if gxx is None:
         return None
     out = os.path.join(out_dir, f"lib{name}.so")
-    # no FMA contraction: the device code rounds every product and quotient (__fmul_rn, __fdiv_rn)
-    subprocess.run([gxx, "-O2", "-std=c++20", "-ffp-contract=off", "-shared", "-fPIC", "-I",
+    # no FMA contraction: the device code rounds every product and quotient (__fmul_rn, __fdiv_rn);
+    # -march=native: the harness runs where it is built, and fmaf becomes one instruction
+    subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-shared", "-fPIC", "-I",
                     os.path.join(ROOT, "vllm-lite_b200", "csrc"), "-I", os.path.join(ROOT, "tests"),
                     os.path.join(ROOT, "tests", f"{name}.cpp"), "-o", out], check=True)
     return ctypes.CDLL(out)
@@ -45,7 +46,7 @@ def build_library_host(out_dir: str):
         return None
     csrc = os.path.join(ROOT, "vllm-lite_b200", "csrc")
     out = os.path.join(out_dir, "libvllt_host.so")
-    subprocess.run([gxx, "-O2", "-std=c++20", "-ffp-contract=off", "-shared", "-fPIC",
+    subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-shared", "-fPIC",
                     "-I", os.path.join(ROOT, "tests", "simt_include"), "-I", os.path.join(ROOT, "tests"), "-I", csrc,
                     "-x", "c++", *[os.path.join(csrc, f) for f in LIBRARY_SOURCES],
                     "-x", "none", os.path.join(ROOT, "tests", "simt_stubs.cpp"), "-o", out], check=True)

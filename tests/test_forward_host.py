@@ -31,14 +31,9 @@ torch = pytest.importorskip("torch")
 pytestmark = needs_vllmlite
 
 
-@pytest.fixture(scope="module")
-def host_lib(tmp_path_factory):
-    from tests.host_build import build_library_host
-
-    lib = build_library_host(str(tmp_path_factory.mktemp("libvllt_host")))
-    if lib is None:
-        pytest.skip("g++ is not available")
-    return lib
+@pytest.fixture
+def host_lib(host_library):
+    return host_library
 
 
 class HostForward:
