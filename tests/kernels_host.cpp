@@ -16,6 +16,9 @@
 
 using namespace vllt;
 
+// 0: the default schedule; otherwise the seed of the schedule variation.
+extern "C" void set_schedule_seed(uint64_t seed) { simt::schedule_seed() = seed; }
+
 extern "C" int run_greedy(const float* logits, int rows, int vocab, int ld, const uint8_t* eos_mask, int eos_id,
                           const float* penalty, const uint32_t* seen, const int32_t* rows_dev, int32_t* out) {
   return simt::launch(smp::greedy_kernel, dim3(rows), dim3(smp::kThreads), 0, logits, vocab, ld, eos_mask, eos_id,

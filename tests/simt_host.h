@@ -235,6 +235,24 @@ inline void switch_next() {
   stack_switch(&c.f[from].sp, c.main_sp);
 }
 
+// Schedule variation: with a nonzero seed, a released barrier and the start
+// of a CTA hand over to a pseudo-random runnable thread instead of letting
+// the releasing one continue, so reads that race with another thread's writes
+// between two barriers see different orders from run to run of the seed.
+inline uint64_t& schedule_seed() {
+  static uint64_t s = 0;
+  return s;
+}
+inline uint32_t next_random() {
+  uint64_t& x = schedule_seed();
+  x ^= x << 13;
+  x ^= x >> 7;
+  x ^= x << 17;
+  return (uint32_t)(x >> 32);
+}
+
+inline void switch_to(int i);
+
 inline void release(int group) {
   Cta& c = cta();
   for (auto& fb : c.f)
@@ -248,10 +266,30 @@ inline void arrive(int group) {  // -1: the CTA; w: warp w
   const int size = group < 0 ? c.live_cta : c.live_warp[group];
   if (++arrived >= size) {
     release(group);
+    if (schedule_seed()) {  // hand over to a random runnable thread (possibly this one)
+      const int pick = (int)(next_random() % (uint32_t)c.n);
+      for (int k = 0; k < c.n; ++k) {
+        const int i = (pick + k) % c.n;
+        if (!c.f[i].done && c.f[i].waiting == -2) {
+          switch_to(i);
+          break;
+        }
+      }
+    }
     return;
   }
   c.f[c.cur].waiting = group;
   switch_next();
+}
+
+// Run thread i now; the current thread stays runnable and resumes later.
+inline void switch_to(int i) {
+  Cta& c = cta();
+  const int from = c.cur;
+  if (i == from) return;
+  c.cur = i;
+  stack_switch(&c.f[from].sp, c.f[i].sp);
+  ::threadIdx = c.f[c.cur].tid;
 }
 
 inline void exit_thread() {
@@ -309,7 +347,8 @@ inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<voi
           c.f[i].tid = dim3(i % block.x, (i / block.x) % block.y, i / (block.x * block.y));
           c.f[i].sp = prepare_stack(c.stacks.data() + kStack * i, kStack, trampoline);
         }
-        stack_switch(&c.main_sp, c.f[0].sp);
+        c.cur = schedule_seed() ? (int)(next_random() % (uint32_t)n) : 0;
+        stack_switch(&c.main_sp, c.f[c.cur].sp);
         if (c.deadlock) {
           std::fprintf(stderr, "simt: block (%u,%u,%u): threads wait on barriers that cannot complete\n", bx, by,
                        bz);

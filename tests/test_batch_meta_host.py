@@ -4,7 +4,9 @@ build_meta_kernel (csrc/batch_meta_kernels.cuh) keeps its per-item
 arithmetic in csrc/meta_items.cuh. Every test runs twice: on
 tests/meta_host.cpp, which runs the kernel's phases one after another with
 those functions compiled for the host, and on the kernel's own code under the
-host SIMT emulation (one CTA of 1024 fibers, tests/kernels_host.cpp). On every pass of the
+host SIMT emulation (one CTA of 1024 fibers, tests/kernels_host.cpp), with
+the emulation's default schedule and with a seeded shuffle after every
+barrier. On every pass of the
 reference's replays (the bench model with chunked prefill; speculative k = 4
 with the prefix cache, block 4) the metadata it builds from the packed step
 record (classic, and pooled with a persistent table pool) must equal the
@@ -44,7 +46,7 @@ class _Kernel:
         return int(np.ctypeslib.as_array((ctypes.c_int32 * 16).from_address(meta_ptr))[7])
 
 
-@pytest.fixture(scope="module", params=["phases", "kernel"])
+@pytest.fixture(scope="module", params=["phases", "kernel", "kernel-shuffled"])
 def meta_host(request, tmp_path_factory):
     """The builder run as its phases one after another (tests/meta_host.cpp),
     or as the kernel itself on the host SIMT emulation (tests/kernels_host.cpp)."""
@@ -60,6 +62,8 @@ def meta_host(request, tmp_path_factory):
     if lib is None:
         pytest.skip("g++ is not available")
     lib.run_build_meta.argtypes = ARGS
+    lib.set_schedule_seed.argtypes = [ctypes.c_uint64]
+    lib.set_schedule_seed(0x5DEECE66D if request.param == "kernel-shuffled" else 0)
     return _Kernel(lib)
 
 

@@ -7,7 +7,9 @@ tests/kernels_host.cpp compiles it for the host, where each CTA runs as 256 coop
 warp-shuffle semantics (tests/simt_host.h). The kernels run with the grids
 their launchers use, against the reference's fixtures. Every buffer sits
 against a PROT_NONE guard page (tests/guarded.py), alternately after and
-before it, so an out-of-bounds read or write stops the test:
+before it, so an out-of-bounds read or write stops the test; and every test
+runs under two thread schedules (the default, and a seeded shuffle after
+every barrier) to expose order-dependent reads:
   * greedy_kernel, on the reference's greedy cases (EOS mask under
     min_tokens, repetition penalty): its pick is the reference's, with
     aligned rows (vector path) and unaligned rows (scalar path); rows past the
@@ -46,7 +48,7 @@ I = ctypes.c_int
 
 
 @pytest.fixture(scope="module")
-def k(tmp_path_factory):
+def _harness(tmp_path_factory):
     from tests.host_build import build_harness
 
     lib = build_harness("kernels_host", str(tmp_path_factory.mktemp("kernels")))
@@ -55,7 +57,19 @@ def k(tmp_path_factory):
     lib.run_greedy.argtypes = [P, I, I, I, P, I, P, P, P, P]
     lib.run_top_p.argtypes = [P, I, I, I, I, P, P, I, P, P, P, P, P, P, P]
     lib.run_accept.argtypes = [P, P, P, I, P, P]
+    lib.set_schedule_seed.argtypes = [ctypes.c_uint64]
     return lib
+
+
+@pytest.fixture(scope="module", params=[0, 0x9E3779B97F4A7C15], ids=["schedule-default", "schedule-shuffled"])
+def k(_harness, request):
+    """Every kernel test runs twice: with the emulation's default schedule and
+    with its seeded variation (a random thread continues after each barrier),
+    so a read that races with another thread's write between two barriers
+    meets two different orders."""
+    _harness.set_schedule_seed(request.param)
+    yield _harness
+    _harness.set_schedule_seed(0)
 
 
 def bitmaps(seen_lists, vocab):
