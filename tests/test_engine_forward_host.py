@@ -12,10 +12,12 @@ code as on the GPU:
     stand-ins), RMSNorm, SGEMM epilogues and attention;
   * vllt_sample_greedy's compiled kernel, the pick buffer and the error word.
 
-The benchmark's requests (C1: 6 layers, d 384, greedy with ignore_eos,
-budget 1024, block 16) must give the streams the reference engine gave
-(tests/golden/streams_mixed.npz). Greedy streams do not depend on which
-requests share a batch, so a subset of the 48 requests is run.
+The benchmarks' requests must give the token streams the reference engine
+gave (tests/golden/streams_*.npz): C1 (mixed lengths), C2 (a 256-token shared
+prefix with the prefix cache, so copy-on-write runs through the compiled
+copy kernel) and C5 (periodic prompts with speculative k = 4, verified by
+the compiled accept kernel against the k = 0 streams). Greedy streams do not
+depend on which requests share a batch, so a subset of each is run.
 """
 
 import ctypes as C
@@ -112,29 +114,46 @@ class HostRunner:
         return rows, R
 
 
-def test_engine_streams_through_the_compiled_device_path(host_lib):
+def fixture_streams(name):
+    z = F.load(name)
+    out, o = [], 0
+    for n in z["lens"]:
+        out.append(z["tokens"][o:o + int(n)].tolist())
+        o += int(n)
+    return out
+
+
+@pytest.mark.parametrize("workload,pick,maxlen,nb,prefix,spec,seqs,budget", [
+    ("mixed", [1, 9, 30, 46], 512, 512, False, 0, 16, 1024),           # C1, run-ahead
+    ("shared", [0, 7, 15, 33], 768, 768, True, 0, 16, 384),            # C2: prefix cache hits, run-ahead
+    ("periodic", [0, 5], 1024, 4096, False, 4, 64, 2048),             # C5: speculative k = 4
+])
+def test_engine_streams_through_the_compiled_device_path(host_lib, workload, pick, maxlen, nb, prefix, spec, seqs,
+                                                          budget):
     from vllmlite.config import CacheConfig, EngineConfig, ModelConfig, SchedulerConfig
 
     from vllt.engine import GpuLLMEngine, cuda_engine
-    from vllt.workloads import mixed_workload
+    from vllt.workloads import mixed_workload, periodic_workload
 
-    z = F.load("streams_mixed.npz")
-    lens, toks = z["lens"], z["tokens"]
-    want_all, o = [], 0
-    for n in lens:
-        want_all.append(toks[o:o + int(n)].tolist())
-        o += int(n)
-    reqs = mixed_workload(48, 0, 0)
-    pick = [1, 4, 9, 17, 23, 30, 38, 46]  # a subset of the 48 requests
+    if workload == "periodic":
+        reqs, want_all = periodic_workload(128, seed=0), fixture_streams("streams_periodic.npz")
+    else:
+        reqs = mixed_workload(48, 0, 256 if workload == "shared" else 0)
+        want_all = fixture_streams(f"streams_{workload}.npz")
     HostRunner.lib = host_lib
-    cfg = EngineConfig(model=ModelConfig(vocab_size=261, max_seq_len=512, **{k: v for k, v in F.BENCH.items()
-                                                                           if k != "max_seq_len"}),
-                       cache=CacheConfig(block_size=16, num_blocks=512),
-                       scheduler=SchedulerConfig(max_seqs=16, max_batched_tokens=1024))
-    eng = cuda_engine(cfg, engine_cls=GpuLLMEngine.resolve(), runner_cls=HostRunner)
+    shape = {k: v for k, v in F.BENCH.items() if k != "max_seq_len"}
+    cfg = EngineConfig(model=ModelConfig(vocab_size=261, max_seq_len=maxlen, **shape),
+                       cache=CacheConfig(block_size=16, num_blocks=nb, enable_prefix_caching=prefix),
+                       scheduler=SchedulerConfig(max_seqs=seqs, max_batched_tokens=budget))
+    eng = cuda_engine(cfg, speculative_tokens=spec, engine_cls=GpuLLMEngine.resolve(), runner_cls=HostRunner)
     ids = [eng.add_request(params=reqs[i][2], request_id=reqs[i][0], prompt_token_ids=reqs[i][1]) for i in pick]
     while eng.has_work:
         eng.step()
     got = [eng.seqs[i].output_token_ids for i in ids]
     assert got == [want_all[i] for i in pick]
-    assert eng.passes_ahead >= eng.total_steps // 2 and eng.runner.stand_ins > 0
+    if spec:  # proposals read the new tokens: no pass runs ahead; drafts were verified on the device
+        assert eng.passes_ahead == 0 and eng.spec.accepted > 0
+    else:
+        assert eng.passes_ahead >= eng.total_steps // 2 and eng.runner.stand_ins > 0
+    if prefix:
+        assert eng.scheduler.blocks.allocator.hits > 0
