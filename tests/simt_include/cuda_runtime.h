@@ -24,6 +24,23 @@ inline cudaError_t cudaGetDevice(int* d) {
   return cudaSuccess;
 }
 
+enum cudaMemcpyKind { cudaMemcpyHostToHost = 0, cudaMemcpyHostToDevice = 1, cudaMemcpyDeviceToHost = 2,
+                      cudaMemcpyDeviceToDevice = 3, cudaMemcpyDefault = 4 };
+inline cudaError_t cudaMemsetAsync(void* p, int v, size_t n, cudaStream_t = nullptr) {
+  std::memset(p, v, n);
+  return cudaSuccess;
+}
+inline cudaError_t cudaMemcpyAsync(void* d, const void* s, size_t n, cudaMemcpyKind, cudaStream_t = nullptr) {
+  std::memmove(d, s, n);
+  return cudaSuccess;
+}
+// A __device__ variable is a host global here: its address is the host address.
+template <class T>
+inline cudaError_t cudaGetSymbolAddress(void** p, T& symbol) {
+  *p = (void*)&symbol;
+  return cudaSuccess;
+}
+
 enum cudaFuncAttribute { cudaFuncAttributeMaxDynamicSharedMemorySize = 8 };
 template <class F>
 inline cudaError_t cudaFuncSetAttribute(F, cudaFuncAttribute, int) {
