@@ -8,11 +8,12 @@ kernel runs:
     for chained blocks of 1 to 64 tokens, token ids up to int32's range, with
     and without a previous block (messages of one and several BLAKE2b blocks);
   * chains packed by vllt.prefix_hash.pack_chains come back in order;
-  * GpuLLMEngine with device_prefix_hash=True (the kernel stood in for by the
-    compiled header, through the pointers the C ABI receives) gives the
-    reference engine's token streams and prefix-cache hits on a
-    shared-prefix workload (with and without speculation), with every hash the BlockManager asks for
-    planned ahead (no on-the-spot launches).
+  * GpuLLMEngine with device_prefix_hash=True gives the reference engine's
+    token streams and prefix-cache hits on a shared-prefix workload (with and
+    without speculation). Its hashes come from vllt_prefix_hash_chains itself
+    (the library's entry point and kernel, built for the host on the SIMT
+    emulation, tests/host_build.py), and every hash the BlockManager asks
+    for is planned ahead (no on-the-spot launches).
 """
 
 import ctypes
@@ -79,13 +80,13 @@ def test_pack_chains_layout():
 
 @needs_vllmlite
 @pytest.mark.parametrize("spec_k", [0, 4])
-def test_engine_with_device_prefix_hash_matches_reference(host_hash, spec_k, monkeypatch):
+def test_engine_with_device_prefix_hash_matches_reference(host_library, spec_k, monkeypatch):
     from vllmlite.engine import LLMEngine
     from vllmlite.sequence import SamplingParams
 
     import vllt._lib as _lib
     from tests import fixtures as F
-    from tests.test_engine_host import OracleLib, ReferenceLogitsRunner, run, view
+    from tests.test_engine_host import OracleLib, ReferenceLogitsRunner, run
     from vllt.engine import GpuLLMEngine, cuda_engine
     from vllt.prefix_hash import DevicePrefixHasher
     from vllt.workloads import mixed_lengths
@@ -93,18 +94,8 @@ def test_engine_with_device_prefix_hash_matches_reference(host_hash, spec_k, mon
     monkeypatch.setattr(_lib, "stream_handle", lambda stream=None: 0)
 
     class Lib(OracleLib):
-        def vllt_prefix_hash_chains(self, tokens, tok_off, nblk, out_off, prev, n, bs, out, stream):
-            nb = view(nblk, np.int32, n)
-            to, oo = view(tok_off, np.int64, n), view(out_off, np.int64, n)
-            total = int(oo[-1] + nb[-1]) if n else 0
-            o = view(out, np.uint8, 32 * max(total, 1))
-            for c in range(n):
-                toks = view(tokens + 4 * int(to[c]), np.int32, int(nb[c]) * bs)
-                p = bytes(view(prev + 32 * c, np.uint8, 32)) if prev else b"\0"
-                hs = chain_host(host_hash, p.decode() if p[0] else None, toks, bs)
-                for b, h in enumerate(hs):
-                    o[32 * (int(oo[c]) + b):32 * (int(oo[c]) + b + 1)] = np.frombuffer(h.encode(), np.uint8)
-            return 0
+        def vllt_prefix_hash_chains(self, *args):  # the library's own entry point, built for the host
+            return host_library.vllt_prefix_hash_chains(*args)
 
     from vllmlite.config import CacheConfig, EngineConfig, ModelConfig, SchedulerConfig
 

@@ -36,7 +36,7 @@ extern "C" int vllt_prefix_hash_chains(const int32_t* tokens, const int64_t* tok
   if (n_chains == 0) return VLLT_OK;
   VLLT_REQUIRE(tokens && token_offsets && n_blocks && out_offsets && out_hex, "prefix_hash: null pointer");
   const int threads = 128;
-  prefix_hash_kernel<<<ceil_div(n_chains, threads), threads, 0, as_stream(stream)>>>(
+  VLLT_LAUNCH(ceil_div(n_chains, threads), threads, 0, as_stream(stream), prefix_hash_kernel)(
       tokens, token_offsets, n_blocks, out_offsets, prev_hex, n_chains, block_size, out_hex);
   return check_launch("prefix_hash");
 }
