@@ -33,7 +33,7 @@ def build_harness(name: str, out_dir: str):
 
 # the fp32 path of libvllt: the C ABI, its launchers and their kernels
 LIBRARY_SOURCES = ("capi.cu", "norm.cu", "cache_ops.cu", "sampling.cu", "batch_meta.cu", "attention.cu",
-                   "attention_static.cu", "prefix_hash.cu")
+                   "attention_static.cu", "prefix_hash.cu", "attention_decode.cu")
 
 
 def build_library_host(out_dir: str):

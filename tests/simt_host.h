@@ -34,6 +34,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <ctime>
 #include <functional>
 #include <type_traits>
 #include <vector>
@@ -117,6 +118,11 @@ template <class T> inline void __stcg(T* p, T v) { *p = v; }
 inline void __threadfence() {}
 inline void __threadfence_block() {}
 inline void __nanosleep(unsigned) {}
+
+// packed fp32 pairs (sm_100): element-wise, each rounded once
+inline float2 __ffma2_rn(float2 a, float2 b, float2 c) { return {std::fmaf(a.x, b.x, c.x), std::fmaf(a.y, b.y, c.y)}; }
+inline float2 __fmul2_rn(float2 a, float2 b) { return {a.x * b.x, a.y * b.y}; }
+inline float2 __fadd2_rn(float2 a, float2 b) { return {a.x + b.x, a.y + b.y}; }
 
 // ---- atomics (cooperative fibers: plain read-modify-write) ---------------------
 template <class T> inline T atomicAdd(T* p, T v) { T o = *p; *p = o + v; return o; }
@@ -209,6 +215,11 @@ struct Cta {
 inline Cta& cta() {
   static Cta c;
   return c;
+}
+inline uint64_t host_ns() {  // the device's %globaltimer
+  timespec t;
+  clock_gettime(CLOCK_MONOTONIC, &t);
+  return (uint64_t)t.tv_sec * 1000000000ull + (uint64_t)t.tv_nsec;
 }
 inline std::vector<unsigned char>& dyn_smem() { static std::vector<unsigned char> m; return m; }
 inline const dim3& thread_idx() { return ::threadIdx; }

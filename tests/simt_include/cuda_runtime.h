@@ -5,6 +5,9 @@
 // complete is reported by cudaGetLastError as a launch failure.
 #pragma once
 
+#include <chrono>
+
+#include "cuda.h"
 #include "simt_host.h"
 
 typedef void* cudaStream_t;
@@ -67,4 +70,23 @@ inline cudaError_t cudaLaunchKernelEx(const cudaLaunchConfig_t* c, void (*kernel
   return simt::launch(kernel, c->gridDim, c->blockDim, c->dynamicSmemBytes, static_cast<KArgs>(args)...)
              ? cudaSuccess
              : cudaErrorLaunchFailure;
+}
+
+enum cudaStreamCaptureStatus { cudaStreamCaptureStatusNone = 0, cudaStreamCaptureStatusActive = 1 };
+inline cudaError_t cudaStreamIsCapturing(cudaStream_t, cudaStreamCaptureStatus* s) {
+  *s = cudaStreamCaptureStatusNone;
+  return cudaSuccess;
+}
+enum cudaDriverEntryPointQueryResult { cudaDriverEntryPointSuccess = 0, cudaDriverEntryPointSymbolNotFound = 1 };
+enum { cudaEnableDefault = 0 };
+// The driver entry points the library looks up: cuTensorMapEncodeTiled only.
+inline cudaError_t cudaGetDriverEntryPoint(const char* name, void** fn, unsigned long long,
+                                           cudaDriverEntryPointQueryResult* q) {
+  if (strcmp(name, "cuTensorMapEncodeTiled") != 0) {
+    *q = cudaDriverEntryPointSymbolNotFound;
+    return cudaErrorInvalidValue;
+  }
+  *fn = reinterpret_cast<void*>(&simt::encode_tiled);
+  *q = cudaDriverEntryPointSuccess;
+  return cudaSuccess;
 }

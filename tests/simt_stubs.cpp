@@ -1,7 +1,7 @@
-// Test infrastructure: the device-only paths of libvllt (bf16 forward, TMA
-// decode attention, tensor-core prefill attention) for the host build of the
-// fp32 path (tests/host_build.py build_library_host). They report themselves
-// unsupported; the fp32 forward never selects them.
+// Test infrastructure: the tensor-core paths of libvllt (bf16 forward,
+// tensor-core prefill attention) for the host build (tests/host_build.py
+// build_library_host). They report themselves unsupported; the fp32 forward
+// and the CUDA-core attention kernels never select them.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -18,14 +18,6 @@ int forward_bf16(const vllt_model_desc*, const int32_t*, const vllt_caps*, const
   return VLLT_ERR_UNSUPPORTED;
 }
 int64_t forward_bf16_ws_bytes(const vllt_model_desc*, const vllt_caps*) { return 0; }
-
-int64_t decode_ws_bytes(int, int, int) { return 0; }
-bool decode_supported(const AttnCall&) { return false; }
-int decode_pass(const AttnCall&, const int32_t*, const int32_t*, int, int, int, int*, cudaStream_t,
-                int (*)(const AttnCall&, const int32_t*, const int32_t*, int, int, int, cudaStream_t)) {
-  set_error("decode attention: not in the host build");
-  return VLLT_ERR_UNSUPPORTED;
-}
 
 bool prefill_tc_supported(const AttnCall&) { return false; }
 int prefill_tc_positions(int n_rep) { return n_rep >= 16 ? 1 : 16 / n_rep; }

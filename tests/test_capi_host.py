@@ -12,7 +12,13 @@ the same C signatures a reference-side binding uses (vllt/_lib.py SIGNATURES):
     split-K decode rows and prefill tiles (fp32 and bf16); its device error
     word reads 0, also for an empty batch;
   * vllt_spec_verify on the reference's verify cases: emitted tokens and
-    accepted counts.
+    accepted counts;
+  * bf16 decode rows (head_dim 128, block 16), which the same entry gives to
+    the TMA decode kernel (csrc/decode_kernels.cuh; its tensor-map box loads,
+    128-byte swizzle and mbarriers on the emulation's host equivalents):
+    against float64 at C3's shape with split-K, and GQA 1 to 8; and the test
+    injection of vllt_test_decode_stall, whose armed barrier makes the bounded
+    waits expire, set bit 2 and leave the next call clean.
 """
 
 import ctypes as C
@@ -145,3 +151,90 @@ def test_spec_verify_entry_on_the_reference_cases(L):
         nt = int(z["verify_ntok"][s])
         assert out[cu[s]:cu[s] + nt].tolist() == z["verify_tokens"][to:to + nt].tolist()
         to += nt
+
+
+# ---- the TMA decode kernel (csrc/decode_kernels.cuh) through the same entry ---------
+
+def _decode_case(rng, ctxs, H, n_kv, spare=5):
+    """bf16 single-query batch over the [block][kv head][16][128] cache."""
+    D, bs = 128, 16
+    S, W = len(ctxs), max(-(-c // bs) for c in ctxs)
+    nb = sum(-(-c // bs) for c in ctxs) + spare
+    perm = rng.permutation(nb).astype(np.int32)
+    tables = np.full((S, W), -1, np.int32)
+    o = 0
+    for s, c in enumerate(ctxs):
+        n = -(-c // bs)
+        tables[s, :n] = perm[o:o + n]
+        o += n
+    q = _bf16(rng.standard_normal((S, H, D)))
+    kc = _bf16(rng.standard_normal((nb, n_kv, bs, D)))
+    vc = _bf16(rng.standard_normal((nb, n_kv, bs, D)))
+    return q, kc, vc, tables, nb
+
+
+def _f(b):
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def _decode_want(q, kc, vc, tables, ctxs, n_kv, scale):
+    from oracle.attention import dense_attention
+
+    out = []
+    for s, c in enumerate(ctxs):
+        blocks = tables[s, :-(-c // 16)]
+        k = _f(kc[blocks]).transpose(0, 2, 1, 3).reshape(-1, n_kv, 128)[:c]
+        v = _f(vc[blocks]).transpose(0, 2, 1, 3).reshape(-1, n_kv, 128)[:c]
+        out.append(dense_attention(_f(q[s:s + 1]), k, v, n_kv, scale)[0])
+    return np.stack(out)
+
+
+@pytest.mark.parametrize("H,n_kv,ctxs", [
+    (32, 8, [4096, 1, 2047, 16, 17, 1025, 3000, 100, 4000, 63, 640, 2500]),   # C3's shape, 4 splits
+    (8, 8, [33, 700]), (16, 8, [1300, 5]), (64, 8, [260, 1100]),             # GQA 1, 2, 8
+])
+def test_tma_decode_kernel_against_float64(L, H, n_kv, ctxs):
+    """bf16 decode rows (head_dim 128, block 16) go to the TMA decode kernel:
+    tensor-map box loads with the 128-byte swizzle into per-warp rings guarded
+    by mbarriers, split-K over 64-block chunks with the merge kernel. Against a
+    float64 restatement of the reference's attention, within one bf16
+    rounding of the output; the error word stays 0."""
+    from vllt import _lib
+
+    rng = np.random.default_rng(sum(ctxs) + H)
+    q, kc, vc, tables, nb = _decode_case(rng, ctxs, H, n_kv)
+    S = len(ctxs)
+    cu = np.arange(S + 1, dtype=np.int32)
+    ctx = np.asarray(ctxs, np.int32)
+    scale = 1 / np.sqrt(128)
+    out = attend(L, q, kc, vc, tables, cu, ctx, 1, max(ctxs), n_kv, 16, scale, _lib.VLLT_BF16)
+    want = _decode_want(q, kc, vc, tables, ctxs, n_kv, scale)
+    np.testing.assert_allclose(_f(out), want, rtol=2.0 ** -7, atol=2e-3)
+
+
+def test_decode_stall_injection_reports_and_recovers(L):
+    """vllt_test_decode_stall arms one stage's mbarrier for its bytes without
+    issuing the copies: every CTA reading that table index sees its bounded
+    wait expire, sets bit 2 of the error word, drains its other copies and
+    returns; the next call is clean and equals a normal run."""
+    from vllt import _lib
+
+    rng = np.random.default_rng(11)
+    ctxs = [300, 90]
+    q, kc, vc, tables, nb = _decode_case(rng, ctxs, 32, 8)
+    S = len(ctxs)
+    cu = np.arange(S + 1, dtype=np.int32)
+    ctx = np.asarray(ctxs, np.int32)
+    args = (q, kc, vc, tables, cu, ctx, 1, max(ctxs), 8, 16, 1 / np.sqrt(128), _lib.VLLT_BF16)
+    clean = attend(L, *args)
+    assert L.vllt_test_decode_stall(3, 2_000_000) == 0  # table index 3, 2 ms waits
+    T, H, D = q.shape
+    W = tables.shape[1]
+    out = guarded(np.zeros(q.shape, q.dtype))
+    ws = guarded(np.zeros(max(L.vllt_attention_workspace_bytes(S, H, D, max(ctxs)), 256), np.uint8))
+    assert L.vllt_paged_attention_varlen(ptr(guarded(q)), ptr(guarded(kc)), ptr(guarded(vc)), ptr(guarded(tables)), W,
+                                         ptr(guarded(cu)), ptr(guarded(ctx)), S, T, 1, max(ctxs), H, 8, D, 16, nb,
+                                         1 / np.sqrt(128), _lib.VLLT_BF16, ptr(out), ptr(ws), ws.size, None) == 0
+    assert ws[:4].view(np.int32)[0] & 4
+    again = attend(L, *args)  # asserts a clean error word
+    np.testing.assert_array_equal(again, clean)
