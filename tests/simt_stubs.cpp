@@ -28,3 +28,7 @@ int prefill_tc_pass(const AttnCall&, int, const int32_t*, const int32_t*, const 
 }
 
 }  // namespace vllt
+
+// The emulation's schedule for every launch of the host build: 0 is the
+// default, any other value seeds the shuffled schedule (tests/simt_host.h).
+extern "C" void vllt_host_schedule_seed(uint64_t seed) { simt::schedule_seed() = seed; }

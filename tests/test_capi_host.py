@@ -193,7 +193,8 @@ def _decode_want(q, kc, vc, tables, ctxs, n_kv, scale):
     (32, 8, [4096, 1, 2047, 16, 17, 1025, 3000, 100, 4000, 63, 640, 2500]),   # C3's shape, 4 splits
     (8, 8, [33, 700]), (16, 8, [1300, 5]), (64, 8, [260, 1100]),             # GQA 1, 2, 8
 ])
-def test_tma_decode_kernel_against_float64(L, H, n_kv, ctxs):
+@pytest.mark.parametrize("seed", [0, 0x5EED])
+def test_tma_decode_kernel_against_float64(L, H, n_kv, ctxs, seed):
     """bf16 decode rows (head_dim 128, block 16) go to the TMA decode kernel:
     tensor-map box loads with the 128-byte swizzle into per-warp rings guarded
     by mbarriers, split-K over 64-block chunks with the merge kernel. Against a
@@ -207,7 +208,12 @@ def test_tma_decode_kernel_against_float64(L, H, n_kv, ctxs):
     cu = np.arange(S + 1, dtype=np.int32)
     ctx = np.asarray(ctxs, np.int32)
     scale = 1 / np.sqrt(128)
-    out = attend(L, q, kc, vc, tables, cu, ctx, 1, max(ctxs), n_kv, 16, scale, _lib.VLLT_BF16)
+    L.vllt_host_schedule_seed.argtypes = [C.c_uint64]
+    L.vllt_host_schedule_seed(seed)  # nonzero: the shuffled schedule
+    try:
+        out = attend(L, q, kc, vc, tables, cu, ctx, 1, max(ctxs), n_kv, 16, scale, _lib.VLLT_BF16)
+    finally:
+        L.vllt_host_schedule_seed(0)
     want = _decode_want(q, kc, vc, tables, ctxs, n_kv, scale)
     np.testing.assert_allclose(_f(out), want, rtol=2.0 ** -7, atol=2e-3)
 

@@ -87,11 +87,16 @@ class HostForward:
         return self.logits[:R, :self.cfg.vocab_size].copy(), rows
 
 
-@pytest.mark.parametrize("name,bs,pooled,bucketed", [("replay_bench.npz", 16, True, False),
-                                                     ("replay_spec.npz", 4, False, True)])
-def test_host_forward_reproduces_the_reference_logits(host_lib, name, bs, pooled, bucketed):
+@pytest.mark.parametrize("name,bs,pooled,bucketed,seed", [("replay_bench.npz", 16, True, False, 0),
+                                                          ("replay_spec.npz", 4, False, True, 0),
+                                                          ("replay_bench.npz", 16, False, False, 0xC0FFEE)])
+def test_host_forward_reproduces_the_reference_logits(host_lib, name, bs, pooled, bucketed, seed):
+    """seed != 0: every kernel of the forward runs under the emulation's
+    shuffled schedule (a random thread continues after each barrier)."""
     from vllmlite.config import ModelConfig
 
+    host_lib.vllt_host_schedule_seed.argtypes = [C.c_uint64]
+    host_lib.vllt_host_schedule_seed(seed)
     run = HostForward(host_lib, ModelConfig(vocab_size=261, **F.BENCH), bs, 512, pooled, bucketed)
     worst, n = 0.0, 0
     for seqs, cow, want in F.replay_steps(name):
@@ -104,4 +109,5 @@ def test_host_forward_reproduces_the_reference_logits(host_lib, name, bs, pooled
         worst = max(worst, rel)
         assert (got.argmax(1) == want.argmax(1)).all(), n
         n += 1
+    host_lib.vllt_host_schedule_seed(0)
     assert n > 10 and worst < 1e-4, worst
