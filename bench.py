@@ -32,6 +32,8 @@ import subprocess
 import sys
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 for p in (ROOT, os.path.join(ROOT, "vllm-lite_b200"), os.path.join(ROOT, "baseline", "_ref")):
     if os.path.isdir(p) and p not in sys.path:
@@ -83,10 +85,26 @@ def run_workload(eng, reqs, tag, nvtx_window=None):
             torch.cuda.nvtx.range_pop()
     seqs = [eng.seqs[f"{tag}-{rid}"] for rid, _, _ in reqs]
     out_tokens = sum(len(s.output_token_ids) for s in seqs)
-    ttft = [s.ttft for s in seqs if s.ttft is not None]
+    lat = {k: [getattr(s, k) for s in seqs if getattr(s, k) is not None] for k in ("ttft", "tpot", "e2e")}
     for rid, _, _ in reqs:
         eng.release(f"{tag}-{rid}")
-    return out_tokens, ttft, eng.total_steps - steps0
+    return out_tokens, lat, eng.total_steps - steps0
+
+
+def merge_latency(lats):
+    """Per-request latency lists (ttft / tpot / e2e, seconds) of several runs, joined."""
+    return {k: [x for lat in lats for x in lat[k]] for k in ("ttft", "tpot", "e2e")}
+
+
+def latency_summary(lat, digits: int = 2):
+    """p50 / p99 in ms of time to first token, time per output token after the
+    first, and request latency, with the reference bench's percentile
+    (numpy's, bench/bench.py:30-32, :61-66)."""
+    out = {}
+    for k in ("ttft", "tpot", "e2e"):
+        for q in (50, 99):
+            out[f"{k}_p{q}_ms"] = round(1e3 * float(np.percentile(lat[k], q)), digits) if lat[k] else None
+    return out
 
 
 class Clocks:
@@ -295,10 +313,10 @@ def main_ours(args):
 
         l0 = launched()
         e0.record()
-        toks, ttft, steps = run_workload(engine, reqs, tag, nvtx_window)
+        toks, lat, steps = run_workload(engine, reqs, tag, nvtx_window)
         e1.record()
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / 1e3, toks, ttft, steps, launched() - l0
+        return e0.elapsed_time(e1) / 1e3, toks, lat, steps, launched() - l0
 
     res = []
     torch.cuda.nvtx.range_push("vllt_timed")  # ncu --nvtx --nvtx-include vllt_timed/
@@ -340,7 +358,7 @@ def main_ours(args):
         dist.all_reduce(n, op=dist.ReduceOp.SUM)
         t_ours, t_e2e = float(v[0]), float(v[1])
         toks, toks_e2e = float(n[0]), float(n[1])
-    ttft_all = [x for r in res for x in r[2]]
+    lat_all = merge_latency([r[2] for r in res])
     decode_s, _, decode_t = decode_bench(torch, dev, 10, 3)
     hbm, peak_kind = peaks()
     achieved = decode_s["attn_bytes"] / decode_t / 1e9  # attention bytes / attention-call time
@@ -372,7 +390,7 @@ def main_ours(args):
                    "model": "TinyLlama-style 6L/384d (vllm-lite bench model)", "global_batch": 48 * world,
                    "seq_len": 768 if wl == "shared" else 512, "parallelism": f"replicas x{world}",
                    "forward_passes_per_step": steps_per_run, "l2": "flushed (256 MB write) before each timed step"},
-        "ttft_p50_ms": round(1e3 * statistics.median(ttft_all), 2) if ttft_all else None,
+        **latency_summary(lat_all),
         "e2e": {"value": round(toks_e2e / t_e2e, 1), "unit": "tok/s",
                 "api": "vllmlite LLMEngine + vllt.CudaRunner (host logits)",
                 "h2d_bytes_per_step": int(rr.h2d_bytes / max(rr.steps, 1) * steps_per_run),
@@ -431,7 +449,7 @@ def main_spec(args, torch, dev, rank, world):
         eng.step()
     same = streams(base, "b") == streams(eng, "c")
     eng.spec.proposed = eng.spec.accepted = 0
-    ts, toks, ttft, launches = [], 0, [], 0
+    ts, toks, lats, launches = [], 0, [], 0
     run = eng.runner
     with Clocks(int(os.environ.get("LOCAL_RANK", 0))) as clk:
         for i in range(args.steps):
@@ -440,13 +458,13 @@ def main_spec(args, torch, dev, rank, world):
             l0 = L.vllt_kernel_launches() + run.replayed_kernels - run.captured_kernels
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            n, tt, _ = run_workload(eng, reqs, f"t{i}")
+            n, lat, _ = run_workload(eng, reqs, f"t{i}")
             e1.record()
             torch.cuda.synchronize()
             ts.append(e0.elapsed_time(e1) / 1e3)
             launches = L.vllt_kernel_launches() + run.replayed_kernels - run.captured_kernels - l0
             toks += n
-            ttft += tt
+            lats.append(lat)
     t = sum(ts)
     if world > 1:
         import torch.distributed as dist
@@ -470,7 +488,7 @@ def main_spec(args, torch, dev, rank, world):
                        "parallelism": f"replicas x{world}", "l2": "flushed before each timed step"},
             "token_identical_to_k0": bool(same),
             "acceptance": round(eng.spec.accepted / max(eng.spec.proposed, 1), 4),
-            "ttft_p50_ms": round(1e3 * statistics.median(ttft), 2) if ttft else None,
+            **latency_summary(merge_latency(lats)),
             "gpu_launches": int(launches), "e2e": None, "clocks": clk.summary()}
         if cpu is not None:
             line["cpu_baseline"] = cpu
@@ -790,7 +808,7 @@ def main_llama(args, torch, dev, rank, world):
     t_wall = time.perf_counter()
     window = tuple(int(x) for x in args.nvtx_passes.split(":")) if args.nvtx_passes else None
     with Clocks(int(os.environ.get("LOCAL_RANK", 0))) as clk:
-        toks, ttft, steps = run_workload(eng, reqs, "t", window)
+        toks, lat, steps = run_workload(eng, reqs, "t", window)
     e1.record()
     if world > 1:
         run.mark(1)
@@ -816,7 +834,7 @@ def main_llama(args, torch, dev, rank, world):
                    "parallelism": f"tp{world}", "forward_passes": steps, "num_blocks": args.llama_blocks,
                    "warmup": f"{args.warmup} short 16-request workloads and one {args.llama_requests}-request "
                              "short workload (every decode bucket)", "l2": "flushed before the timed workload"},
-        "ttft_p50_ms": round(1e3 * statistics.median(ttft), 1) if ttft else None,
+        **latency_summary(lat, 1),
         "wall_s": round(t_wall, 3),
         "gpu_launches": int(launches),
         "e2e": None,
@@ -850,8 +868,8 @@ def reference_run(workload: str, seed: int = 0):
     eng = LLMEngine(engine_config(workload))
     reqs = requests(workload, seed)
     t0 = time.perf_counter()
-    toks, ttft, steps = run_workload(eng, reqs, "r")
-    return toks, time.perf_counter() - t0, ttft, steps
+    toks, lat, steps = run_workload(eng, reqs, "r")
+    return toks, time.perf_counter() - t0, lat, steps
 
 
 def cpu_baseline(workload: str):
@@ -862,13 +880,13 @@ def cpu_baseline(workload: str):
     reference_run(workload)  # warm-up (BLAS threads, page faults), as bench/bench.py:178-182
     best = None
     for _ in range(2):
-        toks, t, ttft, steps = reference_run(workload)
+        toks, t, lat, steps = reference_run(workload)
         if best is None or t < best[1]:
-            best = (toks, t, ttft)
+            best = (toks, t, lat)
     return {"value": round(best[0] / best[1], 1), "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
             "sample": f"whole 48-request {workload} workload, best of 2 after 1 warm-up, vllm-lite NumpyRunner "
                       f"(OpenBLAS threads={os.environ.get('OPENBLAS_NUM_THREADS', 'all')})",
-            "ttft_p50_ms": round(1e3 * statistics.median(best[2]), 2)}
+            **latency_summary(best[2])}
 
 
 def main_reference(args):
@@ -892,12 +910,12 @@ def main_reference(args):
     for _ in range(args.warmup):
         reference_run(wl)
     toks = t = 0.0
-    ttft_all = []
+    lats = []
     for _ in range(args.steps):
-        n, dt, ttft, steps = reference_run(wl)
+        n, dt, lat, steps = reference_run(wl)
         toks += n
         t += dt
-        ttft_all += ttft
+        lats.append(lat)
     v = round(toks / t, 1)
     print(json.dumps({
         "metric": "engine output tok/s (48-request mixed-length greedy workload)" if wl == "mixed"
@@ -907,7 +925,7 @@ def main_reference(args):
         "vs_baseline": round(v / PUBLISHED[wl], 3), "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": {"workload": f"C1 {wl}", "model": "TinyLlama-style 6L/384d", "global_batch": 48,
                    "seq_len": 768 if wl == "shared" else 512, "parallelism": "none (host CPU)"},
-        "ttft_p50_ms": round(1e3 * statistics.median(ttft_all), 2),
+        **latency_summary(merge_latency(lats)),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
                          "sample": f"{args.steps} whole workloads, vllm-lite NumpyRunner"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -352,3 +352,18 @@ def test_allreduce_share_counts_two_bucket_reductions_per_layer():
     log = [(1, 1, None, None), (20, 20, None, None), (512, 512, None, None), (513, 10, None, None)]
     got = bench.allreduce_share(log, ar_us, n_layers=32, max_tokens=8192)
     assert abs(got - 2 * 32 * (10 + 12 + 40 + 50) / 1e6) < 1e-12
+
+
+def test_latency_summary_uses_the_reference_percentiles():
+    """bench.py reports p50 / p99 of TTFT, TPOT and request latency as the
+    reference bench does (numpy percentiles of per-request seconds, in ms)."""
+    import numpy as np
+
+    import bench
+
+    lat = bench.merge_latency([{"ttft": [0.1, 0.2], "tpot": [0.01], "e2e": [1.0, 2.0]},
+                               {"ttft": [0.3], "tpot": [], "e2e": [3.0]}])
+    got = bench.latency_summary(lat)
+    assert got["ttft_p50_ms"] == 200.0 and got["ttft_p99_ms"] == round(1e3 * np.percentile([0.1, 0.2, 0.3], 99), 2)
+    assert got["tpot_p50_ms"] == 10.0 and got["e2e_p99_ms"] == round(1e3 * np.percentile([1, 2, 3], 99), 2)
+    assert bench.latency_summary({"ttft": [], "tpot": [], "e2e": []})["ttft_p50_ms"] is None
