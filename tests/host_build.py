@@ -25,15 +25,16 @@ def build_harness(name: str, out_dir: str):
     out = os.path.join(out_dir, f"lib{name}.so")
     # no FMA contraction: the device code rounds every product and quotient (__fmul_rn, __fdiv_rn);
     # -march=native: the harness runs where it is built, and fmaf becomes one instruction
-    subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-shared", "-fPIC", "-I",
-                    os.path.join(ROOT, "vllm-lite_b200", "csrc"), "-I", os.path.join(ROOT, "tests"),
+    subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-DVLLT_SIMT_HOST=1", "-shared",
+                    "-fPIC", "-I", os.path.join(ROOT, "tests", "simt_include"),
+                    "-I", os.path.join(ROOT, "vllm-lite_b200", "csrc"), "-I", os.path.join(ROOT, "tests"),
                     os.path.join(ROOT, "tests", f"{name}.cpp"), "-o", out], check=True)
     return ctypes.CDLL(out)
 
 
 # the fp32 path of libvllt: the C ABI, its launchers and their kernels
 LIBRARY_SOURCES = ("capi.cu", "norm.cu", "cache_ops.cu", "sampling.cu", "batch_meta.cu", "attention.cu",
-                   "attention_static.cu", "prefix_hash.cu", "attention_decode.cu")
+                   "attention_static.cu", "prefix_hash.cu", "attention_decode.cu", "forward_bf16.cu")
 
 
 def build_library_host(out_dir: str):
@@ -47,8 +48,8 @@ def build_library_host(out_dir: str):
         return None
     csrc = os.path.join(ROOT, "vllm-lite_b200", "csrc")
     out = os.path.join(out_dir, "libvllt_host.so")
-    subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-shared", "-fPIC",
-                    "-I", os.path.join(ROOT, "tests", "simt_include"), "-I", os.path.join(ROOT, "tests"), "-I", csrc,
+    subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-DVLLT_SIMT_HOST=1", "-shared",
+                    "-fPIC", "-I", os.path.join(ROOT, "tests", "simt_include"), "-I", os.path.join(ROOT, "tests"), "-I", csrc,
                     "-x", "c++", *[os.path.join(csrc, f) for f in LIBRARY_SOURCES],
                     "-x", "none", os.path.join(ROOT, "tests", "simt_stubs.cpp"), "-o", out], check=True)
     lib = ctypes.CDLL(out)

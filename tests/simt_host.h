@@ -26,7 +26,9 @@
 // makes the library's device helpers (device_common.cuh) use these shims.
 #pragma once
 
+#ifndef VLLT_SIMT_HOST
 #define VLLT_SIMT_HOST 1
+#endif
 
 #include <climits>
 #include <cmath>

@@ -1,7 +1,7 @@
-// Test infrastructure: the tensor-core paths of libvllt (bf16 forward,
-// tensor-core prefill attention) for the host build (tests/host_build.py
-// build_library_host). They report themselves unsupported; the fp32 forward
-// and the CUDA-core attention kernels never select them.
+// Test infrastructure: the parts of libvllt the host build leaves out
+// (tests/host_build.py build_library_host): the tensor-core prefill attention
+// (attention_pass then takes the CUDA-core kernel) and NCCL's all-reduce
+// (tensor parallelism). They report themselves unsupported.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -12,12 +12,10 @@ namespace vllt {
 
 void set_error(const char* fmt, ...);
 
-int forward_bf16(const vllt_model_desc*, const int32_t*, const vllt_caps*, const vllt_step_bounds*, void*, void*,
-                 int64_t, float*, cudaStream_t) {
-  set_error("bf16 forward: not in the host build");
+int tp_allreduce_bf16(void*, int64_t, void*, cudaStream_t) {
+  set_error("tensor-parallel all-reduce: not in the host build (NCCL)");
   return VLLT_ERR_UNSUPPORTED;
 }
-int64_t forward_bf16_ws_bytes(const vllt_model_desc*, const vllt_caps*) { return 0; }
 
 bool prefill_tc_supported(const AttnCall&) { return false; }
 int prefill_tc_positions(int n_rep) { return n_rep >= 16 ? 1 : 16 / n_rep; }

@@ -1,0 +1,108 @@
+"""CPU: libvllt's bf16 forward (the Llama-3-8B-shaped path) built for the host.
+
+tests/host_build.py builds forward_bf16.cu for the host with the rest of the
+library. Its orchestration, RMSNorm and embedding kernels, the bf16 GEMM
+epilogues (QKV with RoPE and the bf16 KV-cache write, SwiGLU, fp32 residual,
+stores) and the attention kernels (TMA decode for decode rows, the CUDA-core
+kernel for multi-token tiles) are the library's own code. The tensor-core
+GEMMs, which are not part of the host build, are stood in for by fp32
+accumulation over the same bf16 operands (tests/simt_include/vllt_gemm_bf16_host.h).
+
+As the GPU test does (tests/test_gpu_llama.py), the bf16 logits are compared
+with the fp32 parity forward (also built for the host) running the same
+weights widened to fp32, over the same three-pass schedule (chunked prefill,
+decode, a verify row set). The bar is the GPU test's: 2e-2 for both the max
+relative error and the per-row relative norm (three times the error that the
+CPU model of the bf16 rounding points measures). Every row whose fp32 top-1 /
+top-2 gap exceeds twice the pass's error picks the same token.
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from tests import fixtures as F
+from tests.conftest import needs_vllmlite
+
+torch = pytest.importorskip("torch")
+pytestmark = needs_vllmlite
+
+BAR = 2e-2
+
+
+@pytest.fixture
+def L(host_library):
+    return host_library
+
+
+class Forward:
+    """A runner's descriptor, caches and buffers in host memory."""
+
+    def __init__(self, L, shape, bf16, num_blocks=64, bs=16):
+        from types import SimpleNamespace
+
+        from vllt import _lib
+        from vllt.llama import LlamaRunner, LlamaWeights, fp32_reference_weights
+        from vllt.model import DeviceWeights
+        from vllt.runner import CudaRunner, StepPacker
+
+        self.L, self.shape = L, shape
+        D = shape.head_dim
+        dt = torch.bfloat16 if bf16 else torch.float32
+        kv = (shape.n_layers, num_blocks, shape.n_kv_heads, bs, D)
+        self.cache_k, self.cache_v = torch.zeros(kv, dtype=dt), torch.zeros(kv, dtype=dt)
+        if bf16:
+            w = LlamaWeights(shape, "cpu")
+            me = SimpleNamespace(model_cfg=shape, w=w, _ptrs=w.pointer_arrays(), tp_size=1, head_dim=D,
+                                 block_size=bs, num_blocks=num_blocks, tp_comm=None, cache_k=self.cache_k,
+                                 cache_v=self.cache_v)
+            self.desc = LlamaRunner._make_desc(me)
+        else:
+            w = DeviceWeights(shape, fp32_reference_weights(shape, "cpu"), device="cpu")
+            me = SimpleNamespace(model_cfg=shape, w=w, _ptrs=w.pointer_arrays(), block_size=bs,
+                                 num_blocks=num_blocks, head_dim=D, cache_k=self.cache_k, cache_v=self.cache_v)
+            self.desc = CudaRunner._make_desc(me)
+        self.keep = (w, me)
+        self.vocab_padded = w.vocab_padded
+        self.qp = L.vllt_query_tile_positions(C.byref(self.desc))
+        self.caps = _lib.Caps(8, 256, 32, -(-shape.max_seq_len // bs))
+        self.meta = np.zeros(L.vllt_meta_bytes(C.byref(self.caps)) // 4, np.int32)
+        self.ws = np.zeros(L.vllt_forward_workspace_bytes(C.byref(self.desc), C.byref(self.caps)), np.uint8)
+        self.logits = np.zeros((self.caps.max_rows, w.vocab_padded), np.float32)
+        self.packer = StepPacker(bs, num_blocks, shape.vocab_size, w.rope_len, self.qp)
+
+    def execute(self, out):
+        rec, bounds, rows, (S, T, R, W) = self.packer.pack(out)
+        rec = np.ascontiguousarray(rec, np.int32)
+        rc = self.L.vllt_forward(C.byref(self.desc), rec.ctypes.data, C.byref(self.caps), C.byref(bounds),
+                                 self.meta.ctypes.data, self.ws.ctypes.data, self.ws.size, self.logits.ctypes.data,
+                                 None)
+        assert rc == 0, self.L.vllt_last_error()
+        assert self.meta[7] == 0
+        return self.logits[:R, :self.shape.vocab_size].copy()
+
+
+def test_bf16_forward_matches_the_fp32_forward_on_the_same_weights(L):
+    from vllt.llama import LlamaShape
+
+    from tests.test_gpu_llama import schedule
+
+    shape = LlamaShape(n_layers=2, n_heads=8, n_kv_heads=2, d_model=1024, d_ff=2048, vocab_size=1000,
+                       max_seq_len=2048, seed=1)
+    bf, ref = Forward(L, shape, True), Forward(L, shape, False)
+    worst = worst_row = 0.0
+    decided = 0
+    for seqs in schedule(shape.vocab_size, np.random.default_rng(3)):
+        out = F.as_scheduler_output(seqs)
+        a, b = bf.execute(out), ref.execute(out)
+        assert a.shape == b.shape and np.isfinite(a).all()
+        err = np.abs(a - b).max()
+        worst = max(worst, float(err / np.abs(b).max()))
+        worst_row = max(worst_row, float((np.linalg.norm(a - b, axis=1) / np.linalg.norm(b, axis=1)).max()))
+        top2 = np.sort(b, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 2 * err
+        assert (a.argmax(1) == b.argmax(1))[clear].all()
+        decided += int(clear.sum())
+    assert worst <= BAR and worst_row <= BAR, (worst, worst_row)
+    assert decided > 0

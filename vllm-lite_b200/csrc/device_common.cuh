@@ -1,14 +1,13 @@
 // Device helpers shared by the kernels (sm_100a). Kernel headers include
 // this file only, so that their code also compiles for the host under a SIMT
-// emulation (VLLT_SIMT_HOST, defined by such an emulation before it includes
-// any kernel header; the product never defines it): the few helpers written
-// in inline PTX then have plain equivalents.
+// emulation (VLLT_SIMT_HOST, defined by the emulation's build, whose
+// cuda_runtime.h / cuda_bf16.h stand-ins come first on the include path; the
+// product never defines it): the few helpers written in inline PTX then have
+// plain equivalents.
 #pragma once
 
-#ifndef VLLT_SIMT_HOST
-#include <cuda_bf16.h>
+#include <cuda_bf16.h>  // under the host emulation: its stand-in headers
 #include <cuda_runtime.h>
-#endif
 #include <stdint.h>
 #include <string.h>
 
