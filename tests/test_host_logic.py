@@ -367,3 +367,41 @@ def test_latency_summary_uses_the_reference_percentiles():
     assert got["ttft_p50_ms"] == 200.0 and got["ttft_p99_ms"] == round(1e3 * np.percentile([0.1, 0.2, 0.3], 99), 2)
     assert got["tpot_p50_ms"] == 10.0 and got["e2e_p99_ms"] == round(1e3 * np.percentile([1, 2, 3], 99), 2)
     assert bench.latency_summary({"ttft": [], "tpot": [], "e2e": []})["ttft_p50_ms"] is None
+
+
+def test_build_fails_on_register_spills_outside_the_parity_gemm():
+    """vllt/build.py compiles with ptxas -warn-spills and refuses a spill in
+    any kernel but the fp32 parity GEMM: a spill in the decode, GEMM or
+    attention kernels costs time that only a GPU profile would show."""
+    from vllt import build as B
+
+    out = ("ptxas warning : Registers are spilled to local memory in function "
+           "'_ZN4vllt2dk13decode_kernelILi8EEEv14CUtensorMap_stS2_NS0_12DecodeParamsE', 8 bytes spill stores\n"
+           "ptxas warning : Registers are spilled to local memory in function "
+           "'_ZN4vllt12sgemm_kernelILi64ELi64ELi16ELi4ELi4ELi256ENS_8EpiStoreEEEvPKfiS3_iiPKiiiiPfPiT5_', 12 bytes\n"
+           "ptxas info    : Used 165 registers, used 1 barriers\n")
+    spilled = B.spilled_kernels(out)
+    assert len(spilled) == 2
+    bad = [k for k in spilled if not any(a in k for a in B.SPILL_ALLOWED)]
+    assert bad == ["_ZN4vllt2dk13decode_kernelILi8EEEv14CUtensorMap_stS2_NS0_12DecodeParamsE"]
+    assert "-warn-spills" in B.FLAGS
+
+
+def test_device_helpers_do_not_call_themselves():
+    """Helpers with a host alternative under the SIMT emulation have a device
+    body that the host build never compiles; none of them may call itself (a
+    refactor once turned an inline-PTX fence into a self-call)."""
+    import glob
+
+    n = 0
+    for f in glob.glob(os.path.join(ROOT, "vllm-lite_b200", "csrc", "*.cu*")):
+        src = open(f).read()
+        for m in re.finditer(r"__device__ __forceinline__ [\w:<>]+ (\w+)\([^)]*\) \{", src):
+            name, depth, i = m.group(1), 1, m.end()
+            while depth:  # the body, to its matching brace
+                depth += {"{": 1, "}": -1}.get(src[i], 0)
+                i += 1
+            body = src[m.end():i - 1]
+            n += 1
+            assert not re.search(r"\b%s\(" % name, body), f"{os.path.basename(f)}: {name} calls itself"
+    assert n > 30

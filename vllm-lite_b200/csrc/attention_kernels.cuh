@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(kWarps * 32) attention_kernel(AttnParams p) {
   constexpr int STR = Tile<T, D>::kStride;
   constexpr int VPR = D * (int)sizeof(T) / 16;  // 16-byte vectors per row
 
-  VLLT_DYNAMIC_SMEM(smem_raw);
+  VLLT_DYNAMIC_SMEM(smem_raw, 16);
   float* q_s = reinterpret_cast<float*>(smem_raw);                       // [ROWS][D]
   T* kv_s = reinterpret_cast<T*>(q_s + ROWS * D);                       // [kWarps][2][32][STR]
   float* p_s = reinterpret_cast<float*>(kv_s + kWarps * 2 * kKeys * STR);  // [kWarps][ROWS][32]

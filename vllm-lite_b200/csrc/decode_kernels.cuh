@@ -95,7 +95,7 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
 }
 // Makes the barrier initialisations visible before any other thread uses them.
 __device__ __forceinline__ void mbar_fence_init() {
-  mbar_fence_init();
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)), "r"(bytes) : "memory");
@@ -140,7 +140,7 @@ __device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (r & 7
 template <int NREP>
 __global__ void __launch_bounds__(kWarps * 32, 3)
 decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, DecodeParams p) {
-  VLLT_DYNAMIC_SMEM(smem_raw);
+  VLLT_DYNAMIC_SMEM(smem_raw, 1024);
   // 1024-align the stage ring (the swizzle pattern is defined on 1 KB atoms)
   unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
   unsigned char* ring = smem;                                            // [warps][stages][8 KB]

@@ -11,13 +11,15 @@
 #include <stdint.h>
 #include <string.h>
 
-// A kernel's dynamic shared memory: `VLLT_DYNAMIC_SMEM(name);` declares
-// `name` as the 16-byte aligned unsigned char array of the launch's dynamic
-// shared memory (under the host emulation, the emulation's buffer for it).
+// A kernel's dynamic shared memory: `VLLT_DYNAMIC_SMEM(name, align);`
+// declares `name` as the unsigned char array of the launch's dynamic shared
+// memory, `align`-byte aligned (under the host emulation, the emulation's
+// buffer for it). The alignment is a promise the compiler uses: with 1024,
+// the run-time rounding of the base to a 1 KB swizzle atom folds away.
 #ifdef VLLT_SIMT_HOST
-#define VLLT_DYNAMIC_SMEM(name) unsigned char* name = ::simt::dynamic_smem()
+#define VLLT_DYNAMIC_SMEM(name, align) unsigned char* name = ::simt::dynamic_smem()
 #else
-#define VLLT_DYNAMIC_SMEM(name) extern __shared__ __align__(16) unsigned char name[]
+#define VLLT_DYNAMIC_SMEM(name, align) extern __shared__ __align__(align) unsigned char name[]
 #endif
 
 // A kernel launch: `VLLT_LAUNCH(grid, block, smem, stream, kernel)(args...)`

@@ -26,6 +26,21 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxe
          "-Xptxas", "-warn-spills"]
 
 
+# Kernels allowed to spill registers: the fp32 parity GEMM (a few bytes, off
+# the bf16 serving path). Any other spill fails the build: a spill in a hot
+# kernel is a silent slowdown that only a GPU profile would show.
+SPILL_ALLOWED = ("sgemm_kernel",)
+
+
+def spilled_kernels(ptxas_output: str) -> list[str]:
+    """Mangled names of the kernels that ptxas (-warn-spills) reports spilling."""
+    out = []
+    for line in ptxas_output.splitlines():
+        if "Registers are spilled to local memory in function" in line:
+            out.append(line.split("'")[1] if "'" in line else line)
+    return out
+
+
 def nvcc() -> str:
     for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
         if cand and os.path.exists(cand):
@@ -58,6 +73,10 @@ def build(verbose: bool = False, jobs: int | None = None) -> str:
                 raise RuntimeError(f"nvcc failed on {src}:\n{r.stdout}\n{r.stderr}")
             if verbose and r.stderr.strip():
                 print(r.stderr, file=sys.stderr)
+            bad = [k for k in spilled_kernels(r.stdout + r.stderr) if not any(a in k for a in SPILL_ALLOWED)]
+            if bad:
+                os.remove(obj)
+                raise RuntimeError(f"register spills in {os.path.basename(src)}: {', '.join(bad)}")
         return obj
 
     with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
