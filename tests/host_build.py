@@ -25,33 +25,47 @@ def build_harness(name: str, out_dir: str):
     out = os.path.join(out_dir, f"lib{name}.so")
     # no FMA contraction: the device code rounds every product and quotient (__fmul_rn, __fdiv_rn);
     # -march=native: the harness runs where it is built, and fmaf becomes one instruction
-    subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-DVLLT_SIMT_HOST=1", "-shared",
+    subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-fno-gnu-unique", "-pthread", "-DVLLT_SIMT_HOST=1", "-shared",
                     "-fPIC", "-I", os.path.join(ROOT, "tests", "simt_include"),
                     "-I", os.path.join(ROOT, "vllm-lite_b200", "csrc"), "-I", os.path.join(ROOT, "tests"),
                     os.path.join(ROOT, "tests", f"{name}.cpp"), "-o", out], check=True)
     return ctypes.CDLL(out)
 
 
-# the fp32 path of libvllt: the C ABI, its launchers and their kernels
+# libvllt but NCCL: the C ABI, its launchers and their kernels (the tensor-core
+# ones on the emulation of tests/simt_include/simt_tc.h)
 LIBRARY_SOURCES = ("capi.cu", "norm.cu", "cache_ops.cu", "sampling.cu", "batch_meta.cu", "attention.cu",
-                   "attention_static.cu", "prefix_hash.cu", "attention_decode.cu", "forward_bf16.cu")
+                   "attention_static.cu", "prefix_hash.cu", "attention_decode.cu", "forward_bf16.cu", "gemm_bf16.cu",
+                   "attention_prefill_tc.cu")
 
 
 def build_library_host(out_dir: str):
-    """libvllt's fp32 path compiled for the host: the library's own sources
+    """libvllt compiled for the host: the library's own sources
     (LIBRARY_SOURCES, unchanged) against the stub CUDA headers of
     tests/simt_include, every launch running on the SIMT emulation of
-    tests/simt_host.h, plus tests/simt_stubs.cpp for the device-only paths.
-    Returns the CDLL with the C ABI's signatures set, or None without g++."""
+    tests/simt_host.h, plus tests/simt_stubs.cpp for NCCL and the emulation's
+    test hooks. The sources compile in parallel. Returns the CDLL with the C
+    ABI's signatures set, or None without g++."""
+    import concurrent.futures as cf
+
     gxx = shutil.which("g++")
     if gxx is None:
         return None
     csrc = os.path.join(ROOT, "vllm-lite_b200", "csrc")
+    flags = ["-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-fno-gnu-unique", "-pthread",
+             "-DVLLT_SIMT_HOST=1", "-fPIC", "-I", os.path.join(ROOT, "tests", "simt_include"),
+             "-I", os.path.join(ROOT, "tests"), "-I", csrc]
+    srcs = [os.path.join(csrc, f) for f in LIBRARY_SOURCES] + [os.path.join(ROOT, "tests", "simt_stubs.cpp")]
+
+    def compile_one(src):
+        obj = os.path.join(out_dir, os.path.basename(src) + ".o")
+        subprocess.run([gxx, *flags, "-x", "c++", "-c", src, "-o", obj], check=True)
+        return obj
+
+    with cf.ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
+        objs = list(ex.map(compile_one, srcs))
     out = os.path.join(out_dir, "libvllt_host.so")
-    subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-DVLLT_SIMT_HOST=1", "-shared",
-                    "-fPIC", "-I", os.path.join(ROOT, "tests", "simt_include"), "-I", os.path.join(ROOT, "tests"), "-I", csrc,
-                    "-x", "c++", *[os.path.join(csrc, f) for f in LIBRARY_SOURCES],
-                    "-x", "none", os.path.join(ROOT, "tests", "simt_stubs.cpp"), "-o", out], check=True)
+    subprocess.run([gxx, "-shared", "-pthread", *objs, "-o", out], check=True)
     lib = ctypes.CDLL(out)
     from vllt import _lib
 

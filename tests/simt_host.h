@@ -39,6 +39,10 @@
 #include <ctime>
 #include <functional>
 #include <type_traits>
+#include <atomic>
+#include <condition_variable>
+#include <mutex>
+#include <thread>
 #include <vector>
 
 #define __global__
@@ -47,7 +51,7 @@
 #define __forceinline__ inline
 #define __noinline__
 #define __launch_bounds__(...)
-#define __shared__ static
+#define __shared__ static thread_local
 #define __align__(n) __attribute__((aligned(n)))
 #define __grid_constant__
 
@@ -60,12 +64,13 @@ struct alignas(8) float2 { float x, y; };
 struct alignas(16) float4 { float x, y, z, w; };
 struct dim3 {
   unsigned x = 1, y = 1, z = 1;
-  dim3() = default;
-  dim3(unsigned a, unsigned b = 1, unsigned c = 1) : x(a), y(b), z(c) {}
+  constexpr dim3() = default;
+  constexpr dim3(unsigned a, unsigned b = 1, unsigned c = 1) : x(a), y(b), z(c) {}
 };
 inline int2 make_int2(int x, int y) { return {x, y}; }
 inline int4 make_int4(int x, int y, int z, int w) { return {x, y, z, w}; }
 inline uint2 make_uint2(unsigned x, unsigned y) { return {x, y}; }
+inline uint4 make_uint4(unsigned x, unsigned y, unsigned z, unsigned w) { return {x, y, z, w}; }
 inline float2 make_float2(float x, float y) { return {x, y}; }
 inline float4 make_float4(float x, float y, float z, float w) { return {x, y, z, w}; }
 
@@ -126,18 +131,28 @@ inline float2 __ffma2_rn(float2 a, float2 b, float2 c) { return {std::fmaf(a.x, 
 inline float2 __fmul2_rn(float2 a, float2 b) { return {a.x * b.x, a.y * b.y}; }
 inline float2 __fadd2_rn(float2 a, float2 b) { return {a.x + b.x, a.y + b.y}; }
 
-// ---- atomics (cooperative fibers: plain read-modify-write) ---------------------
-template <class T> inline T atomicAdd(T* p, T v) { T o = *p; *p = o + v; return o; }
-template <class T> inline T atomicSub(T* p, T v) { T o = *p; *p = o - v; return o; }
-template <class T> inline T atomicMax(T* p, T v) { T o = *p; if (v > o) *p = v; return o; }
-template <class T> inline T atomicMin(T* p, T v) { T o = *p; if (v < o) *p = v; return o; }
-template <class T> inline T atomicOr(T* p, T v) { T o = *p; *p = o | v; return o; }
-template <class T> inline T atomicAnd(T* p, T v) { T o = *p; *p = o & v; return o; }
-template <class T> inline T atomicExch(T* p, T v) { T o = *p; *p = v; return o; }
-template <class T> inline T atomicCAS(T* p, T c, T v) { T o = *p; if (o == c) *p = v; return o; }
+// ---- atomics: real read-modify-writes (the CTAs of a cluster run on separate OS threads) --
+template <class T, class F> inline T atomic_rmw(T* p, F f) {
+  T o;
+  __atomic_load(p, &o, __ATOMIC_SEQ_CST);
+  T n = f(o);
+  while (!__atomic_compare_exchange(p, &o, &n, false, __ATOMIC_SEQ_CST, __ATOMIC_SEQ_CST)) n = f(o);
+  return o;
+}
+template <class T> inline T atomicAdd(T* p, T v) { return atomic_rmw(p, [&](T o) { return (T)(o + v); }); }
+template <class T> inline T atomicSub(T* p, T v) { return atomic_rmw(p, [&](T o) { return (T)(o - v); }); }
+template <class T> inline T atomicMax(T* p, T v) { return atomic_rmw(p, [&](T o) { return v > o ? v : o; }); }
+template <class T> inline T atomicMin(T* p, T v) { return atomic_rmw(p, [&](T o) { return v < o ? v : o; }); }
+template <class T> inline T atomicOr(T* p, T v) { return atomic_rmw(p, [&](T o) { return (T)(o | v); }); }
+template <class T> inline T atomicAnd(T* p, T v) { return atomic_rmw(p, [&](T o) { return (T)(o & v); }); }
+template <class T> inline T atomicExch(T* p, T v) { return atomic_rmw(p, [&](T) { return v; }); }
+template <class T> inline T atomicCAS(T* p, T c, T v) { return atomic_rmw(p, [&](T o) { return o == c ? v : o; }); }
 
 // ---- built-in variables: set by the scheduler (threadIdx whenever a fiber resumes) --
-inline dim3 threadIdx, blockIdx, blockDim, gridDim;
+// Per OS thread: a launch runs its CTAs one after another on the calling
+// thread, except the CTAs of a thread-block cluster, which run at the same
+// time, one OS thread each.
+inline thread_local dim3 threadIdx, blockIdx, blockDim, gridDim;
 
 // ---- the CTA scheduler ---------------------------------------------------------
 namespace simt {
@@ -192,11 +207,12 @@ inline void* prepare_stack(char* base, size_t size, void (*entry)()) {
 
 constexpr int kMaxThreads = 1024;
 constexpr size_t kStack = 1 << 16;  // per fiber
+constexpr int kClusterGroup = -3;   // barrier group of barrier.cluster
 
 struct Fiber {
   void* sp = nullptr;
   dim3 tid;
-  int waiting = -2;  // -2 running / runnable, -1 CTA barrier, w >= 0 warp w's barrier
+  int waiting = -2;  // -2 running / runnable, -1 CTA barrier, -3 cluster barrier, w >= 0 warp w's barrier
   bool done = false;
 };
 
@@ -207,28 +223,59 @@ struct Cta {
   int cur = 0, n = 0, done = 0;
   int live_cta = 0;                  // threads not exited
   int live_warp[kMaxThreads / 32];   // lanes not exited per warp
-  int arrived_cta = 0;
+  int arrived_cta = 0, arrived_cluster = 0;
   int arrived_warp[kMaxThreads / 32];
   uint64_t slot[kMaxThreads / 32][32];  // shuffle exchange
   const std::function<void()>* body = nullptr;
   bool deadlock = false;
 };
 
+// The OS threads of one cluster's CTAs: barrier.cluster and the shared-memory
+// windows through which a CTA reads its peers' shared memory.
+struct Cluster {
+  int size = 1;
+  std::mutex mu;
+  std::condition_variable cv;
+  int arrived = 0, finished = 0;
+  uint64_t gen = 0;
+  bool broken = false;
+  std::vector<unsigned char*> dyn;  // per rank: dynamic shared memory
+  std::vector<size_t> dyn_bytes;
+  std::vector<const char*> anchor;  // per rank: a thread_local of this module (static __shared__ variables)
+};
+
+inline thread_local Cta* tls_cta = nullptr;
+inline thread_local std::vector<unsigned char>* tls_smem = nullptr;
+inline thread_local size_t tls_smem_bytes = 0;
+inline thread_local Cluster* tls_cluster = nullptr;
+inline thread_local int tls_rank = 0;
+
 inline Cta& cta() {
-  static Cta c;
-  return c;
+  if (!tls_cta) tls_cta = new Cta;
+  return *tls_cta;
 }
 inline uint64_t host_ns() {  // the device's %globaltimer
   timespec t;
   clock_gettime(CLOCK_MONOTONIC, &t);
   return (uint64_t)t.tv_sec * 1000000000ull + (uint64_t)t.tv_nsec;
 }
-inline std::vector<unsigned char>& dyn_smem() { static std::vector<unsigned char> m; return m; }
-inline const dim3& thread_idx() { return ::threadIdx; }
-inline unsigned char* dynamic_smem() {  // 16-byte aligned
-  auto& m = dyn_smem();
-  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(m.data()) + 15) & ~uintptr_t(15));
+inline std::vector<unsigned char>& dyn_smem() {
+  if (!tls_smem) tls_smem = new std::vector<unsigned char>;
+  return *tls_smem;
 }
+inline const dim3& thread_idx() { return ::threadIdx; }
+inline unsigned char* dynamic_smem() {  // 1024-byte aligned
+  auto& m = dyn_smem();
+  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(m.data()) + 1023) & ~uintptr_t(1023));
+}
+inline size_t dynamic_smem_bytes() { return tls_smem_bytes; }
+// A thread_local of this module: static __shared__ variables (thread_local
+// here) sit at the same offset from it in every OS thread's block of the
+// module's thread-local storage. (Host builds pass -fno-gnu-unique, so that a
+// module's inline and template statics stay its own when several modules
+// that compiled the same kernels are loaded.)
+__attribute__((visibility("hidden"))) inline thread_local char tls_anchor_byte;
+inline const char* tls_anchor() { return &tls_anchor_byte; }
 
 inline void switch_next() {
   Cta& c = cta();
@@ -248,12 +295,15 @@ inline void switch_next() {
   stack_switch(&c.f[from].sp, c.main_sp);
 }
 
+// Let the other runnable threads of the CTA run (a spin-wait's iteration).
+inline void yield() { switch_next(); }
+
 // Schedule variation: with a nonzero seed, a released barrier and the start
 // of a CTA hand over to a pseudo-random runnable thread instead of letting
 // the releasing one continue, so reads that race with another thread's writes
 // between two barriers see different orders from run to run of the seed.
 inline uint64_t& schedule_seed() {
-  static uint64_t s = 0;
+  static thread_local uint64_t s = 0;
   return s;
 }
 inline uint32_t next_random() {
@@ -270,7 +320,22 @@ inline void release(int group) {
   Cta& c = cta();
   for (auto& fb : c.f)
     if (!fb.done && fb.waiting == group) fb.waiting = -2;
-  if (group < 0) c.arrived_cta = 0; else c.arrived_warp[group] = 0;
+  if (group == -1) c.arrived_cta = 0;
+  else if (group == kClusterGroup) c.arrived_cluster = 0;
+  else c.arrived_warp[group] = 0;
+}
+
+inline void handover() {  // after a release: a random runnable thread continues
+  Cta& c = cta();
+  if (!schedule_seed()) return;
+  const int pick = (int)(next_random() % (uint32_t)c.n);
+  for (int k = 0; k < c.n; ++k) {
+    const int i = (pick + k) % c.n;
+    if (!c.f[i].done && c.f[i].waiting == -2) {
+      switch_to(i);
+      break;
+    }
+  }
 }
 
 inline void arrive(int group) {  // -1: the CTA; w: warp w
@@ -279,19 +344,55 @@ inline void arrive(int group) {  // -1: the CTA; w: warp w
   const int size = group < 0 ? c.live_cta : c.live_warp[group];
   if (++arrived >= size) {
     release(group);
-    if (schedule_seed()) {  // hand over to a random runnable thread (possibly this one)
-      const int pick = (int)(next_random() % (uint32_t)c.n);
-      for (int k = 0; k < c.n; ++k) {
-        const int i = (pick + k) % c.n;
-        if (!c.f[i].done && c.f[i].waiting == -2) {
-          switch_to(i);
-          break;
-        }
-      }
-    }
+    handover();
     return;
   }
   c.f[c.cur].waiting = group;
+  switch_next();
+}
+
+// The cluster-wide half of barrier.cluster, once every live thread of this
+// CTA has arrived: waits (blocking this OS thread) for the other CTAs of the
+// cluster. False if it can never complete (a peer CTA exited, or a peer's
+// threads deadlocked).
+inline bool cluster_os_barrier() {
+  Cluster* cl = tls_cluster;
+  if (!cl || cl->size == 1) return true;
+  std::unique_lock<std::mutex> lk(cl->mu);
+  if (cl->broken || cl->finished > 0) {
+    cl->broken = true;
+    cl->cv.notify_all();
+    return false;
+  }
+  const uint64_t g = cl->gen;
+  if (++cl->arrived == cl->size) {
+    cl->arrived = 0;
+    ++cl->gen;
+    cl->cv.notify_all();
+    return true;
+  }
+  cl->cv.wait(lk, [&] { return cl->gen != g || cl->broken; });
+  return cl->gen != g;
+}
+
+inline void complete_cluster_barrier() {
+  Cta& c = cta();
+  if (!cluster_os_barrier()) {  // the launch fails: back to the CTA's scheduler
+    c.deadlock = true;
+    stack_switch(&c.f[c.cur].sp, c.main_sp);
+  }
+  release(kClusterGroup);
+}
+
+// barrier.cluster.arrive + barrier.cluster.wait (a CTA barrier without a cluster).
+inline void cluster_arrive_wait() {
+  Cta& c = cta();
+  if (++c.arrived_cluster >= c.live_cta) {
+    complete_cluster_barrier();
+    handover();
+    return;
+  }
+  c.f[c.cur].waiting = kClusterGroup;
   switch_next();
 }
 
@@ -315,6 +416,7 @@ inline void exit_thread() {
   --c.live_warp[w];
   if (c.arrived_cta > 0 && c.arrived_cta >= c.live_cta) release(-1);
   if (c.arrived_warp[w] > 0 && c.arrived_warp[w] >= c.live_warp[w]) release(w);
+  if (c.arrived_cluster > 0 && c.arrived_cluster >= c.live_cta) complete_cluster_barrier();
   if (c.done == c.n) stack_switch(&me.sp, c.main_sp);  // the last thread: back to the launch
   switch_next();
   stack_switch(&me.sp, c.main_sp);  // not reached unless stopped
@@ -331,44 +433,130 @@ inline int flat_tid() {
   return (int)((t.z * ::blockDim.y + t.y) * ::blockDim.x + t.x);
 }
 
-// Runs body() as every thread of every CTA of the grid; returns false if a
-// CTA's threads waited on barriers that could never complete.
-inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<void()>& body) {
+// Checks a CTA's state when it has finished (tensor memory, ...): set by the
+// tensor-core emulation; false fails the launch.
+inline bool (*&cta_exit_check())() {
+  static bool (*f)() = nullptr;
+  return f;
+}
+inline void (*&cta_start_hook())() {
+  static void (*f)() = nullptr;
+  return f;
+}
+
+// Runs CTA `bid` (every thread of it) on this OS thread; false if its threads
+// waited on barriers that could never complete.
+inline bool run_cta(dim3 bid, dim3 block, const std::function<void()>& body) {
   const int n = (int)(block.x * block.y * block.z);
-  if (n < 1 || n > kMaxThreads) return false;
-  ::gridDim = grid;
-  ::blockDim = block;
-  dyn_smem().assign(smem + 16, 0);
+  ::blockIdx = bid;
   Cta& c = cta();
   if (c.stacks.size() < kStack * n) c.stacks.resize(kStack * n);
+  c.f.assign(n, Fiber{});
+  c.n = n;
+  c.cur = c.done = 0;
+  c.live_cta = n;
+  c.arrived_cta = c.arrived_cluster = 0;
+  for (int w = 0; w < kMaxThreads / 32; ++w) {
+    c.live_warp[w] = std::max(0, std::min(32, n - 32 * w));
+    c.arrived_warp[w] = 0;
+  }
+  c.body = &body;
+  c.deadlock = false;
+  for (int i = 0; i < n; ++i) {
+    c.f[i].tid = dim3(i % block.x, (i / block.x) % block.y, i / (block.x * block.y));
+    c.f[i].sp = prepare_stack(c.stacks.data() + kStack * i, kStack, trampoline);
+  }
+  if (cta_start_hook()) cta_start_hook()();
+  c.cur = schedule_seed() ? (int)(next_random() % (uint32_t)n) : 0;
+  stack_switch(&c.main_sp, c.f[c.cur].sp);
+  if (c.deadlock) {
+    std::fprintf(stderr, "simt: block (%u,%u,%u): threads wait on barriers that cannot complete\n", bid.x, bid.y,
+                 bid.z);
+    return false;
+  }
+  if (cta_exit_check() && !cta_exit_check()()) return false;
+  return true;
+}
+
+inline void set_smem(size_t smem) {
+  dyn_smem().assign(smem + 1024, 0);
+  tls_smem_bytes = smem;
+}
+
+// Runs body() as every thread of every CTA of the grid; returns false if a
+// CTA's threads waited on barriers that could never complete. With a cluster
+// of `cluster` CTAs along x, the CTAs of one cluster run at the same time,
+// each on its own OS thread, and clusters one after another.
+inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<void()>& body, unsigned cluster = 1) {
+  const int n = (int)(block.x * block.y * block.z);
+  if (n < 1 || n > kMaxThreads || cluster < 1 || grid.x % cluster) return false;
+  ::gridDim = grid;
+  ::blockDim = block;
+  if (cluster == 1) {
+    set_smem(smem);
+    for (unsigned bz = 0; bz < grid.z; ++bz)
+      for (unsigned by = 0; by < grid.y; ++by)
+        for (unsigned bx = 0; bx < grid.x; ++bx)
+          if (!run_cta(dim3(bx, by, bz), block, body)) return false;
+    return true;
+  }
+  const uint64_t seed = schedule_seed();
   for (unsigned bz = 0; bz < grid.z; ++bz)
     for (unsigned by = 0; by < grid.y; ++by)
-      for (unsigned bx = 0; bx < grid.x; ++bx) {
-        ::blockIdx = dim3(bx, by, bz);
-        c.f.assign(n, Fiber{});
-        c.n = n;
-        c.cur = c.done = 0;
-        c.live_cta = n;
-        c.arrived_cta = 0;
-        for (int w = 0; w < kMaxThreads / 32; ++w) {
-          c.live_warp[w] = std::max(0, std::min(32, n - 32 * w));
-          c.arrived_warp[w] = 0;
-        }
-        c.body = &body;
-        c.deadlock = false;
-        for (int i = 0; i < n; ++i) {
-          c.f[i].tid = dim3(i % block.x, (i / block.x) % block.y, i / (block.x * block.y));
-          c.f[i].sp = prepare_stack(c.stacks.data() + kStack * i, kStack, trampoline);
-        }
-        c.cur = schedule_seed() ? (int)(next_random() % (uint32_t)n) : 0;
-        stack_switch(&c.main_sp, c.f[c.cur].sp);
-        if (c.deadlock) {
-          std::fprintf(stderr, "simt: block (%u,%u,%u): threads wait on barriers that cannot complete\n", bx, by,
-                       bz);
-          return false;
-        }
+      for (unsigned cx = 0; cx < grid.x / cluster; ++cx) {
+        Cluster cl;
+        cl.size = (int)cluster;
+        cl.dyn.assign(cluster, nullptr);
+        cl.dyn_bytes.assign(cluster, 0);
+        cl.anchor.assign(cluster, nullptr);
+        std::vector<char> ok(cluster, 0);
+        std::vector<std::thread> th;
+        for (unsigned r = 0; r < cluster; ++r)
+          th.emplace_back([&, r] {
+            ::gridDim = grid;
+            ::blockDim = block;
+            tls_cluster = &cl;
+            tls_rank = (int)r;
+            schedule_seed() = seed ? seed ^ (0x9E3779B97F4A7C15ull * (r + 1)) : 0;
+            set_smem(smem);
+            {
+              std::lock_guard<std::mutex> lk(cl.mu);
+              cl.dyn[r] = dynamic_smem();
+              cl.dyn_bytes[r] = smem;
+              cl.anchor[r] = tls_anchor();
+            }
+            if (cluster_os_barrier()) ok[r] = run_cta(dim3(cx * cluster + r, by, bz), block, body);
+            {
+              std::lock_guard<std::mutex> lk(cl.mu);
+              ++cl.finished;
+              if (!ok[r] || cl.arrived > 0) cl.broken = true;
+              cl.cv.notify_all();
+            }
+            delete tls_cta;
+            tls_cta = nullptr;
+            delete tls_smem;
+            tls_smem = nullptr;
+            tls_cluster = nullptr;
+          });
+        for (auto& t : th) t.join();
+        for (unsigned r = 0; r < cluster; ++r)
+          if (!ok[r]) return false;
       }
   return true;
+}
+
+// The rank of this CTA in its cluster (%cluster_ctarank).
+inline int cluster_rank() { return tls_cluster ? tls_rank : 0; }
+
+// A pointer into this CTA's shared memory (dynamic, or a static __shared__
+// variable) as the same location in CTA `rank` of the cluster (mapa).
+inline void* map_shared(const void* p, int rank) {
+  Cluster* cl = tls_cluster;
+  if (!cl || rank == tls_rank) return const_cast<void*>(p);
+  const unsigned char* u = static_cast<const unsigned char*>(p);
+  unsigned char* base = dynamic_smem();
+  if (u >= base && u < base + tls_smem_bytes) return cl->dyn[rank] + (u - base);
+  return const_cast<char*>(cl->anchor[rank]) + (static_cast<const char*>(p) - tls_anchor());
 }
 
 template <class... KArgs, class... Args>
@@ -376,11 +564,17 @@ inline bool launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
   std::function<void()> body = [&] { kernel(args...); };
   return run_grid(grid, block, smem, body);
 }
+template <class... KArgs, class... Args>
+inline bool launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, unsigned cluster,
+                           Args... args) {
+  std::function<void()> body = [&] { kernel(args...); };
+  return run_grid(grid, block, smem, body, cluster);
+}
 
-// Sticky launch error (a barrier that could not complete), read and cleared
-// by the emulated cudaGetLastError.
-inline bool& launch_failed() {
-  static bool f = false;
+// Sticky launch error (a barrier that could not complete, a fault the
+// emulation detects), read and cleared by the emulated cudaGetLastError.
+inline std::atomic<bool>& launch_failed() {
+  static std::atomic<bool> f{false};
   return f;
 }
 
@@ -420,7 +614,7 @@ inline T shfl(T v, int src_lane, bool in_range) {
 
 inline void __syncthreads() { simt::arrive(-1); }
 inline int __syncthreads_or(int p) {
-  static int acc;
+  static thread_local int acc;
   simt::arrive(-1);
   acc = 0;
   simt::arrive(-1);

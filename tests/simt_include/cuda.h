@@ -38,6 +38,8 @@ struct HostTensorMap {  // what the host encoder records in CUtensorMap::opaque
   const unsigned char* base;
   uint64_t dim0, dim1, stride1;  // elements, rows, bytes per row
   uint32_t box0, box1, esize, swizzle;
+  uint64_t dim2, stride2;        // rank 3: planes, bytes per plane (rank 2: 1, 0)
+  uint32_t box2, rank;
 };
 static_assert(sizeof(HostTensorMap) <= sizeof(CUtensorMap), "map");
 
@@ -46,38 +48,54 @@ inline CUresult encode_tiled(CUtensorMap* m, CUtensorMapDataType dt, cuuint32_t 
                              const cuuint32_t* estr, CUtensorMapInterleave, CUtensorMapSwizzle sw,
                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill) {
   const uint32_t esize = dt == CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 ? 2 : dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 1;
-  if (rank != 2 || !m || !base || (reinterpret_cast<uintptr_t>(base) & 15) || strides[0] % 16 ||
+  if ((rank != 2 && rank != 3) || !m || !base || (reinterpret_cast<uintptr_t>(base) & 15) || strides[0] % 16 ||
       box[0] == 0 || box[1] == 0 || box[0] > 256 || box[1] > 256 || (box[0] * esize) % 16 || estr[0] != 1 ||
       estr[1] != 1 || (sw == CU_TENSOR_MAP_SWIZZLE_128B && box[0] * esize > 128))
     return CUDA_ERROR_INVALID_VALUE;
+  if (rank == 3 && (box[2] == 0 || box[2] > 256 || strides[1] % 16 || estr[2] != 1)) return CUDA_ERROR_INVALID_VALUE;
   HostTensorMap h{static_cast<const unsigned char*>(base), dims[0], dims[1], strides[0], box[0], box[1], esize,
-                  (uint32_t)sw};
+                  (uint32_t)sw, rank == 3 ? dims[2] : 1, rank == 3 ? strides[1] : 0, rank == 3 ? box[2] : 1, rank};
   memset(m, 0, sizeof(*m));
   memcpy(m->opaque, &h, sizeof(h));
   return CUDA_SUCCESS;
 }
 
-// One 2-D box load at (x, y); returns the box's bytes (the transaction count).
-inline uint32_t tma_load_2d_host(void* dst, const CUtensorMap* map, int x, int y) {
+// One box load at (x, y, z) (z = 0 for a 2-D map); returns the box's bytes
+// (the transaction count). The box lands as [box2][box1] rows of box0
+// elements; with the 128-byte swizzle, 16-byte chunk c of smem row r goes to
+// chunk c ^ (r % 8), which is the address-bit pattern of the device's swizzle
+// only for a destination 1024-byte aligned in the shared window: a 128-byte
+// swizzled copy into the dynamic shared memory at another offset is reported
+// as a launch failure.
+inline uint32_t tma_load_host(void* dst, const CUtensorMap* map, int x, int y, int z) {
   HostTensorMap h;
   memcpy(&h, map->opaque, sizeof(h));
-  const uint32_t row_bytes = h.box0 * h.esize;
-  if (((int64_t)x * h.esize) % 16 != 0) {  // faults on the device: report, copy nothing
-    launch_failed() = true;
-    return row_bytes * h.box1;
-  }
+  const uint32_t row_bytes = h.box0 * h.esize, rows = h.box1 * h.box2;
   unsigned char* d = static_cast<unsigned char*>(dst);
-  for (uint32_t r = 0; r < h.box1; ++r)
+  const unsigned char* win = dynamic_smem();
+  const bool in_window = d >= win && d < win + dynamic_smem_bytes();
+  if (((int64_t)x * h.esize) % 16 != 0 ||  // faults on the device: report, copy nothing
+      (h.swizzle == CU_TENSOR_MAP_SWIZZLE_128B && in_window && (d - win) % 1024 != 0) ||
+      (in_window && (size_t)(d - win) + (size_t)row_bytes * rows > dynamic_smem_bytes())) {
+    launch_failed() = true;
+    return row_bytes * rows;
+  }
+  for (uint32_t r = 0; r < rows; ++r)
     for (uint32_t c = 0; c < row_bytes / 16; ++c) {
       const uint32_t at = h.swizzle == CU_TENSOR_MAP_SWIZZLE_128B ? r * row_bytes + ((c ^ (r % 8)) * 16)
                                                                    : r * row_bytes + c * 16;
-      const int64_t row = (int64_t)y + r, col = (int64_t)x + (int64_t)c * 16 / h.esize;
-      if (row >= 0 && row < (int64_t)h.dim1 && col >= 0 && col < (int64_t)h.dim0)
-        memcpy(d + at, h.base + row * h.stride1 + col * h.esize, 16);
+      const int64_t plane = (int64_t)z + r / h.box1, row = (int64_t)y + r % h.box1;
+      const int64_t col = (int64_t)x + (int64_t)c * 16 / h.esize;
+      if (plane >= 0 && plane < (int64_t)h.dim2 && row >= 0 && row < (int64_t)h.dim1 && col >= 0 &&
+          col < (int64_t)h.dim0)
+        memcpy(d + at, h.base + plane * h.stride2 + row * h.stride1 + col * h.esize, 16);
       else
         memset(d + at, 0, 16);
     }
-  return row_bytes * h.box1;
+  return row_bytes * rows;
+}
+inline uint32_t tma_load_2d_host(void* dst, const CUtensorMap* map, int x, int y) {
+  return tma_load_host(dst, map, x, y, 0);
 }
 
 }  // namespace simt

@@ -50,9 +50,13 @@ inline cudaError_t cudaFuncSetAttribute(F, cudaFuncAttribute, int) {
   return cudaSuccess;
 }
 
-enum cudaLaunchAttributeID { cudaLaunchAttributeProgrammaticStreamSerialization = 1 };
+enum cudaLaunchAttributeID { cudaLaunchAttributeClusterDimension = 4,
+                             cudaLaunchAttributeProgrammaticStreamSerialization = 5 };
 struct cudaLaunchAttributeValue {
   int programmaticStreamSerializationAllowed;
+  struct {
+    unsigned x, y, z;
+  } clusterDim;
 };
 struct cudaLaunchAttribute {
   cudaLaunchAttributeID id;
@@ -65,11 +69,40 @@ struct cudaLaunchConfig_t {
   cudaLaunchAttribute* attrs;
   unsigned numAttrs;
 };
+// A cluster dimension attribute runs the CTAs of each cluster at the same
+// time (clusters along x only, as the library launches them); programmatic
+// stream serialization changes nothing here (launches run to completion).
+inline unsigned launch_cluster_x(const cudaLaunchConfig_t* c) {
+  for (unsigned i = 0; i < c->numAttrs; ++i)
+    if (c->attrs[i].id == cudaLaunchAttributeClusterDimension) {
+      const auto& d = c->attrs[i].val.clusterDim;
+      return d.y == 1 && d.z == 1 ? d.x : 0;
+    }
+  return 1;
+}
 template <class... KArgs, class... Args>
 inline cudaError_t cudaLaunchKernelEx(const cudaLaunchConfig_t* c, void (*kernel)(KArgs...), Args&&... args) {
-  return simt::launch(kernel, c->gridDim, c->blockDim, c->dynamicSmemBytes, static_cast<KArgs>(args)...)
+  const unsigned cx = launch_cluster_x(c);
+  if (cx == 0 || cx > 16 || c->gridDim.x % cx) return cudaErrorInvalidValue;
+  return simt::launch_cluster(kernel, c->gridDim, c->blockDim, c->dynamicSmemBytes, cx, static_cast<KArgs>(args)...)
              ? cudaSuccess
              : cudaErrorLaunchFailure;
+}
+
+// The device the emulation stands for: a B200's 148 SMs, one CTA of the
+// tensor-core kernels (about 200 KB of shared memory) per SM.
+enum cudaDeviceAttr { cudaDevAttrMultiProcessorCount = 16 };
+inline cudaError_t cudaDeviceGetAttribute(int* v, cudaDeviceAttr a, int) {
+  if (a != cudaDevAttrMultiProcessorCount) return cudaErrorInvalidValue;
+  *v = 148;
+  return cudaSuccess;
+}
+template <class F>
+inline cudaError_t cudaOccupancyMaxActiveClusters(int* n, F, const cudaLaunchConfig_t* c) {
+  const unsigned cx = launch_cluster_x(c);
+  if (cx == 0) return cudaErrorInvalidValue;
+  *n = 148 / (int)cx;
+  return cudaSuccess;
 }
 
 enum cudaStreamCaptureStatus { cudaStreamCaptureStatusNone = 0, cudaStreamCaptureStatusActive = 1 };

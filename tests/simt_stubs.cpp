@@ -1,12 +1,13 @@
-// Test infrastructure: the parts of libvllt the host build leaves out
-// (tests/host_build.py build_library_host): the tensor-core prefill attention
-// (attention_pass then takes the CUDA-core kernel) and NCCL's all-reduce
-// (tensor parallelism). They report themselves unsupported.
+// Test infrastructure: the part of libvllt the host build leaves out
+// (tests/host_build.py build_library_host): NCCL's all-reduce (tensor
+// parallelism), which reports itself unsupported; and the test hooks of the
+// emulation.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "../include/vllt.h"
 #include "ops.cuh"
+#include "simt_tc.h"
 
 namespace vllt {
 
@@ -17,16 +18,13 @@ int tp_allreduce_bf16(void*, int64_t, void*, cudaStream_t) {
   return VLLT_ERR_UNSUPPORTED;
 }
 
-bool prefill_tc_supported(const AttnCall&) { return false; }
-int prefill_tc_positions(int n_rep) { return n_rep >= 16 ? 1 : 16 / n_rep; }
-int prefill_tc_pass(const AttnCall&, int, const int32_t*, const int32_t*, const int32_t*, int, int, int, int*,
-                    cudaStream_t) {
-  set_error("tensor-core prefill: not in the host build");
-  return VLLT_ERR_UNSUPPORTED;
-}
-
 }  // namespace vllt
 
 // The emulation's schedule for every launch of the host build: 0 is the
 // default, any other value seeds the shuffled schedule (tests/simt_host.h).
 extern "C" void vllt_host_schedule_seed(uint64_t seed) { simt::schedule_seed() = seed; }
+// Drop the n-th tensor-map load of the tensor-core kernels from now on
+// (1: the next one; 0: none): its bytes never arrive, so a bounded wait expires.
+extern "C" void vllt_host_drop_tma(int64_t n) { simt::tensor::drop_countdown() = n; }
+// tcgen05.mma instructions the emulation has executed so far.
+extern "C" int64_t vllt_host_mma_count() { return simt::tensor::mma_count().load(); }

@@ -1,12 +1,13 @@
 """CPU: libvllt's bf16 forward (the Llama-3-8B-shaped path) built for the host.
 
 tests/host_build.py builds forward_bf16.cu for the host with the rest of the
-library. Its orchestration, RMSNorm and embedding kernels, the bf16 GEMM
-epilogues (QKV with RoPE and the bf16 KV-cache write, SwiGLU, fp32 residual,
-stores) and the attention kernels (TMA decode for decode rows, the CUDA-core
-kernel for multi-token tiles) are the library's own code. The tensor-core
-GEMMs, which are not part of the host build, are stood in for by fp32
-accumulation over the same bf16 operands (tests/simt_include/vllt_gemm_bf16_host.h).
+library, so the whole pass is the library's own code: its orchestration, the
+RMSNorm and embedding kernels, the tcgen05 GEMMs (the small-M cluster and
+stream-K forms a decode-sized pass takes, with their fused epilogues: QKV with
+RoPE and the bf16 KV-cache write, SwiGLU, fp32 residual, stores) and the
+attention kernels (TMA decode for decode rows, the tcgen05 prefill kernel for
+multi-token tiles), with the tensor-core, TMA and cluster instructions on the
+emulation of tests/simt_include/simt_tc.h.
 
 As the GPU test does (tests/test_gpu_llama.py), the bf16 logits are compared
 with the fp32 parity forward (also built for the host) running the same
@@ -90,7 +91,9 @@ def test_bf16_forward_matches_the_fp32_forward_on_the_same_weights(L):
 
     shape = LlamaShape(n_layers=2, n_heads=8, n_kv_heads=2, d_model=1024, d_ff=2048, vocab_size=1000,
                        max_seq_len=2048, seed=1)
+    L.vllt_host_mma_count.restype = C.c_int64
     bf, ref = Forward(L, shape, True), Forward(L, shape, False)
+    mma0 = L.vllt_host_mma_count()
     worst = worst_row = 0.0
     decided = 0
     for seqs in schedule(shape.vocab_size, np.random.default_rng(3)):
@@ -106,3 +109,4 @@ def test_bf16_forward_matches_the_fp32_forward_on_the_same_weights(L):
         decided += int(clear.sum())
     assert worst <= BAR and worst_row <= BAR, (worst, worst_row)
     assert decided > 0
+    assert L.vllt_host_mma_count() > mma0  # the tensor-core kernels ran

@@ -168,18 +168,23 @@ int attention_pass(const AttnCall& c0, const int32_t* item_seq, const int32_t* i
   }
   if (c0.err) flags = c0.err;
   const int n_rep = c.H / c.n_kv;
-  // standalone: (sequence, tile) items from the batch shape
+  // the tensor-core prefill kernel reports through the error word: without one
+  // the generic kernel takes the multi-token tiles
+  const bool tc_tiles = !single_query && prefill_tc_supported(c) && flags;
   int items_per_seq = 1;
-  if (!item_seq) {
-    const int qp = single_query ? 1 : query_tile_positions(c.dtype, c.D, c.bs, n_rep);
+  if (!item_seq) {  // standalone: (sequence, tile) items from the batch shape, tiles of the kernel that runs
+    const int qp = single_query ? 1 : tc_tiles ? prefill_tc_positions(n_rep) : tile_positions(n_rep);
     items_per_seq = single_query ? 1 : ceil_div(std::max(max_qlen, 1), qp);
     VLLT_REQUIRE((int64_t)items_per_seq * num_seqs < (1ll << 31), "attention: too many tiles");
     items_cap = items_per_seq * num_seqs;
+  } else {  // the metadata builder's tiles are query_tile_positions wide
+    VLLT_REQUIRE(single_query || tc_tiles || !prefill_tc_supported(c),
+                 "attention: tensor-core query tiles need the error word");
   }
   if (items_cap <= 0) return VLLT_OK;
   if (single_query && decode_supported(c) && flags)
     return decode_pass(c, item_seq, n_items, items_cap, num_seqs, max_ctx, flags, st, merge_decode_splits);
-  if (!single_query && prefill_tc_supported(c) && flags)
+  if (tc_tiles)
     return prefill_tc_pass(c, c.T_rows, item_seq, item_q0, n_items, items_cap, items_per_seq, num_seqs, flags, st);
 
   AttnParams p = params_of(c);

@@ -66,6 +66,25 @@ constexpr uint32_t idesc128() {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(128 >> 3) << 17) |
          ((uint32_t)(128 >> 4) << 24);
 }
+#ifdef VLLT_SIMT_HOST
+// the host emulation's equivalents (tests/simt_include/simt_tc.h)
+template <bool B_MN>
+inline void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
+  ::simt::tensor::mma_f16(tmem_d, a, b, idesc128<B_MN>(), acc);
+}
+inline void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  ::simt::tensor::tma_load(dst, map, bar, x, y, z);
+}
+inline void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  uint32_t r[32];
+  for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
+  ::simt::tensor::tmem_st32(taddr, r);
+}
+inline void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) { ::simt::tensor::tmem_ld32(taddr, r); }
+inline void tmem_wait_ld() {}
+inline void fence_proxy_async() {}
+inline float ex2(float x) { return ::simt::tensor::ex2_ftz(x); }
+#else
 template <bool B_MN>
 __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
   asm volatile(
@@ -79,6 +98,20 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       ::"r"(saddr(dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(saddr(bar))
       : "memory");
 }
+// 32 columns of this thread's TMEM lane into r[0..31]; complete after tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// generic-proxy writes to shared memory -> visible to the tensor core's reads
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -103,6 +136,7 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+#endif
 
 // The running max a row's probabilities are taken against moves only when a
 // tile's max exceeds it by more than 2^8 (log2 units): until then P <= 256,
@@ -115,7 +149,7 @@ __global__ void __launch_bounds__(192, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, PrefillParams p) {
   constexpr int QP = kRows / NREP;  // query positions per CTA
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  VLLT_DYNAMIC_SMEM(smem_raw, 1024);
   unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
   unsigned char* q_s = smem;                // 2 halves [128 rows][128 B]
   unsigned char* p_s = q_s + 2 * kHalf;     // 2 key halves [128 rows][128 B]
@@ -161,11 +195,11 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     mbar_init(&o_done, 1);
     mbar_init(&drain, 1);
     abort_s = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_fence_init();
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_s)), "r"(512));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    tmem_alloc(&tmem_s, 512);
+    tmem_relinquish();
   }
   fence_before();
   __syncthreads();
@@ -291,19 +325,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         const uint32_t ta = tmem + (j & 1) * 128 + lane_base;
         uint32_t r[kKeys];
 #pragma unroll
-        for (int c = 0; c < kKeys; c += 32) {
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-              "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-              : "=r"(r[c + 0]), "=r"(r[c + 1]), "=r"(r[c + 2]), "=r"(r[c + 3]), "=r"(r[c + 4]), "=r"(r[c + 5]),
-                "=r"(r[c + 6]), "=r"(r[c + 7]), "=r"(r[c + 8]), "=r"(r[c + 9]), "=r"(r[c + 10]), "=r"(r[c + 11]),
-                "=r"(r[c + 12]), "=r"(r[c + 13]), "=r"(r[c + 14]), "=r"(r[c + 15]), "=r"(r[c + 16]),
-                "=r"(r[c + 17]), "=r"(r[c + 18]), "=r"(r[c + 19]), "=r"(r[c + 20]), "=r"(r[c + 21]),
-                "=r"(r[c + 22]), "=r"(r[c + 23]), "=r"(r[c + 24]), "=r"(r[c + 25]), "=r"(r[c + 26]),
-                "=r"(r[c + 27]), "=r"(r[c + 28]), "=r"(r[c + 29]), "=r"(r[c + 30]), "=r"(r[c + 31])
-              : "r"(ta + c));
-        }
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        for (int c = 0; c < kKeys; c += 32) tmem_ld32_nowait(ta + c, r + c);
+        tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < kKeys; ++i) v[i] = __uint_as_float(r[i]);
       }
@@ -356,7 +379,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) =
             make_uint4(pk[c / 2], pk[c / 2 + 1], pk[c / 2 + 2], pk[c / 2 + 3]);
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P: generic writes -> MMA reads
+      fence_proxy_async();  // P: generic writes -> MMA reads
       fence_before();
       mbar_arrive(&p_full);
     }
@@ -396,7 +419,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   __syncthreads();
   if (warp == 0) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -429,7 +452,7 @@ int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
   smem_opt_in.run([&] {
     cudaFuncSetAttribute(prefill_tc_kernel<NREP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   });
-  prefill_tc_kernel<NREP><<<dim3(p.n_kv, items), 192, kSmemBytes, st>>>(tq, tk, tv, p);
+  VLLT_LAUNCH(dim3(p.n_kv, items), 192, kSmemBytes, st, prefill_tc_kernel<NREP>)(tq, tk, tv, p);
   return check_launch("prefill attention (tcgen05)");
 }
 

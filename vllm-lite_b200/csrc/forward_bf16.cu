@@ -14,13 +14,7 @@
 
 #include <algorithm>
 
-#ifdef VLLT_SIMT_HOST
-// the CPU tests' stand-in for the tensor-core GEMMs (SplitKScratch,
-// forward_splitk_scratch, gemm_bf16_launch over the same epilogues)
-#include <vllt_gemm_bf16_host.h>
-#else
 #include "gemm_bf16_tc.cuh"
-#endif
 #include "ops.cuh"
 
 namespace vllt {

@@ -25,6 +25,10 @@
 // shared memory only): the kernels are safe in multi-GPU processes.
 // Every mbarrier wait is bounded; on expiry the kernel sets an error bit, lets its
 // copies land (bounded), frees its tensor memory and returns.
+// Under the host emulation (VLLT_SIMT_HOST, tests/simt_host.h) the helpers
+// written in inline PTX are the emulation's tensor-core, TMA, mbarrier and
+// cluster operations (tests/simt_include/simt_tc.h), so the CPU tests run
+// these kernels' own code.
 #pragma once
 
 #include <cuda.h>
@@ -32,6 +36,9 @@
 #include <algorithm>
 
 #include "common.cuh"
+#ifdef VLLT_SIMT_HOST
+#include <simt_tc.h>
+#endif
 
 namespace vllt {
 namespace tc {
@@ -45,6 +52,29 @@ constexpr int TMEM_COLS = 256;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
 constexpr uint64_t kWaitNs = 1000000000ull;
 
+#ifdef VLLT_SIMT_HOST
+inline uint32_t saddr(const void* p) { return ::simt::tensor::saddr(p); }
+inline void mbar_init(uint64_t* bar, unsigned count) { ::simt::tensor::mbar_init(bar, count); }
+inline void mbar_expect_tx(uint64_t* bar, unsigned bytes) { ::simt::tensor::mbar_expect_tx(bar, bytes); }
+inline bool mbar_try_wait(uint64_t* bar, unsigned parity) { return ::simt::tensor::mbar_try_wait(bar, parity); }
+inline uint64_t global_ns() { return ::simt::tensor::global_ns(); }
+inline void mbar_arrive(uint64_t* bar) { ::simt::tensor::mbar_arrive(bar); }
+inline void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  ::simt::tensor::tma_load(dst, map, bar, x, y, 0);
+}
+inline void mma_commit(uint64_t* bar) { ::simt::tensor::mma_commit(bar); }
+inline void fence_before() {}
+inline void fence_after() {}
+inline void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  ::simt::tensor::tmem_ld32(taddr, r);
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+inline void mbar_fence_init() {}
+inline void tmem_alloc(uint32_t* dst, uint32_t ncols) { ::simt::tensor::tmem_alloc(dst, ncols); }
+inline void tmem_relinquish() { ::simt::tensor::tmem_relinquish(); }
+inline void tmem_dealloc(uint32_t taddr, uint32_t ncols) { ::simt::tensor::tmem_dealloc(taddr, ncols); }
+#else
 __device__ __forceinline__ uint32_t saddr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -66,23 +96,6 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity))
-    if (global_ns() - t0 > kWaitNs) return false;
-  return true;
-}
-// As mbar_wait, but also gives up as soon as another role of the CTA has set *abort.
-__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, unsigned parity, volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*abort) return false;
-    if (global_ns() - t0 > kWaitNs) return false;
-  }
-  return true;
-}
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
 }
@@ -93,22 +106,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B
-// apart (SBO), version 1 (sm_100), base offset 0.
-__device__ __forceinline__ uint64_t smem_desc(const void* p) {
-  const uint64_t a = (saddr(p) >> 4) & 0x3FFFu;
-  return a | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-// Instruction descriptor, kind::f16: fp32 D, bf16 A and B, both K-major, M128 N256.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
-
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
-}
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
                : "memory");
@@ -130,6 +127,59 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// The warp allocates `ncols` columns of tensor memory; their address goes to *dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(dst)), "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+#endif
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > kWaitNs) return false;
+  return true;
+}
+// As mbar_wait, but also gives up as soon as another role of the CTA has set *abort.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, unsigned parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (global_ns() - t0 > kWaitNs) return false;
+  }
+  return true;
+}
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B
+// apart (SBO), version 1 (sm_100), base offset 0.
+__device__ __forceinline__ uint64_t smem_desc(const void* p) {
+  const uint64_t a = (saddr(p) >> 4) & 0x3FFFu;
+  return a | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: fp32 D, bf16 A and B, both K-major, M128 N256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+#ifdef VLLT_SIMT_HOST
+inline void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  ::simt::tensor::mma_f16(tmem_d, adesc, bdesc, kIdesc, accumulate);
+}
+#else
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+#endif
 
 // Grouped raster order of output tiles (both kernels): consecutive tile ids
 // walk up to GROUP_M row tiles of one column tile, then the next column tile,
@@ -152,7 +202,7 @@ template <class Epi>
 __global__ void __launch_bounds__(128, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, int M_cap,
             const int* __restrict__ M_dev, int N, int K, Epi epi, int* __restrict__ err, SplitK sk) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  VLLT_DYNAMIC_SMEM(smem_raw, 1024);
   unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
   __shared__ uint64_t full[STAGES], empty[STAGES], accf;
   __shared__ uint32_t tmem_base_s;
@@ -175,12 +225,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
     }
     mbar_init(&accf, 1);
     failed_s = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_fence_init();
   }
   if (warp == 0) {  // whole warp: allocate the accumulator columns
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base_s)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    tmem_alloc(&tmem_base_s, TMEM_COLS);
+    tmem_relinquish();
   }
   fence_before();
   __syncthreads();
@@ -287,7 +336,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
   __syncthreads();
   if (warp == 0) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
@@ -303,7 +352,7 @@ template <class Epi>
 __global__ void __launch_bounds__(P_THREADS, 1)
 gemm_persistent_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, int M_cap,
                        const int* __restrict__ M_dev, int N, int K, Epi epi, int* __restrict__ err) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  VLLT_DYNAMIC_SMEM(smem_raw, 1024);
   unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
   __shared__ uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain;
   __shared__ uint32_t tmem_base_s;
@@ -325,12 +374,11 @@ gemm_persistent_kernel(const __grid_constant__ CUtensorMap ta, const __grid_cons
     }
     mbar_init(&drain, 1);
     abort_s = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_fence_init();
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base_s)),
-                 "r"(P_TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    tmem_alloc(&tmem_base_s, P_TMEM_COLS);
+    tmem_relinquish();
   }
   fence_before();
   __syncthreads();
@@ -434,7 +482,7 @@ gemm_persistent_kernel(const __grid_constant__ CUtensorMap ta, const __grid_cons
   __syncthreads();
   if (warp == 0) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P_TMEM_COLS));
+    tmem_dealloc(tmem, P_TMEM_COLS);
   }
 }
 
@@ -478,6 +526,11 @@ __device__ __forceinline__ int sk_slot(int c, int t, const SmallPlan& p) {
   return 2 * c + (t == (int)(sk_begin(c, p) / p.nk) ? 0 : 1);
 }
 
+#ifdef VLLT_SIMT_HOST
+inline void mma_bf16_n(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  ::simt::tensor::mma_f16(tmem_d, adesc, bdesc, idesc, accumulate);
+}
+#else
 __device__ __forceinline__ void mma_bf16_n(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
   asm volatile(
@@ -485,13 +538,14 @@ __device__ __forceinline__ void mma_bf16_n(uint32_t tmem_d, uint64_t adesc, uint
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+#endif
 
 template <class Epi>
 __global__ void __launch_bounds__(SK_THREADS, 1)
 gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, int M_cap,
                   const int* __restrict__ M_dev, int N, SmallPlan p, Epi epi, float* __restrict__ part,
                   int* __restrict__ err) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  VLLT_DYNAMIC_SMEM(smem_raw, 1024);
   unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
   __shared__ uint64_t full[SK_MAX_STAGES], empty[SK_MAX_STAGES], acc_full[2], acc_empty[2], drain;
   __shared__ uint32_t tmem_base_s;
@@ -518,12 +572,11 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant_
     }
     mbar_init(&drain, 1);
     abort_s = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_fence_init();
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base_s)),
-                 "r"(tmem_cols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    tmem_alloc(&tmem_base_s, tmem_cols);
+    tmem_relinquish();
   }
   fence_before();
   __syncthreads();
@@ -669,7 +722,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant_
   __syncthreads();
   if (warp == 0) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
+    tmem_dealloc(tmem, tmem_cols);
   }
 }
 
@@ -683,6 +736,27 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant_
 // rank order: deterministic) and applies the epilogue. No partials go through
 // global memory and no second kernel runs. The ring is reused for the staging
 // buffer once the last MMA has completed.
+// A location in another CTA's shared memory: its shared::cluster address on the
+// device, a pointer under the host emulation; `+ bytes` moves along it.
+#ifdef VLLT_SIMT_HOST
+typedef const unsigned char* PeerAddr;
+inline uint32_t cluster_rank() { return ::simt::tensor::cluster_rank(); }
+inline void cluster_sync() { ::simt::tensor::cluster_sync(); }
+inline PeerAddr peer_addr(const void* p, uint32_t rank) {
+  return static_cast<PeerAddr>(::simt::map_shared(p, (int)rank));
+}
+inline int ld_peer_s32(PeerAddr a) {
+  int v;
+  memcpy(&v, a, 4);
+  return v;
+}
+inline float4 ld_peer4(PeerAddr a) {
+  float4 v;
+  memcpy(&v, a, 16);
+  return v;
+}
+#else
+typedef uint32_t PeerAddr;
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -691,23 +765,24 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// shared::cta address -> the same offset in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+// p (this CTA's shared memory) -> the same offset in CTA `rank` of the cluster
+__device__ __forceinline__ PeerAddr peer_addr(const void* p, uint32_t rank) {
   uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr(p)), "r"(rank));
   return r;
 }
-__device__ __forceinline__ int ld_dsmem_s32(uint32_t addr) {
+__device__ __forceinline__ int ld_peer_s32(PeerAddr addr) {
   int v;
   asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
   return v;
 }
-__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
+__device__ __forceinline__ float4 ld_peer4(PeerAddr addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
   return v;
 }
+#endif
 
 struct ClusterPlan {
   int tiles;   // ceil(N / 128)
@@ -720,7 +795,7 @@ template <class Epi>
 __global__ void __launch_bounds__(SK_THREADS, 1)
 gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, int M_cap,
                     const int* __restrict__ M_dev, int N, ClusterPlan p, Epi epi, int* __restrict__ err) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  VLLT_DYNAMIC_SMEM(smem_raw, 1024);
   unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
   __shared__ uint64_t full[SK_MAX_STAGES], empty[SK_MAX_STAGES], acc_full, drain;
   __shared__ uint32_t tmem_base_s;
@@ -746,12 +821,11 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     mbar_init(&acc_full, 1);
     mbar_init(&drain, 1);
     abort_s = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_fence_init();
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base_s)),
-                 "r"(tmem_cols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    tmem_alloc(&tmem_base_s, tmem_cols);
+    tmem_relinquish();
   }
   fence_before();
   __syncthreads();
@@ -854,11 +928,10 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   bool cluster_ok = !abort_s;
   if (warp < 4)
     for (int src = 0; src < p.S && cluster_ok; ++src)
-      cluster_ok = ld_dsmem_s32(map_rank(saddr(const_cast<int*>(&abort_s)), src)) == 0;
+      cluster_ok = ld_peer_s32(peer_addr(const_cast<int*>(&abort_s), src)) == 0;
   if (warp < 4 && cluster_ok) {  // ---- reduction of token rows [r*n/S, (r+1)*n/S) ----
     const int n_tok = min(M, p.n_pad);
     const int r0 = rank * n_tok / p.S, r1 = (rank + 1) * n_tok / p.S;
-    const uint32_t base = saddr(stage_acc);
     for (int item = threadIdx.x; item < (r1 - r0) * 4; item += 128) {
       const int m = r0 + item / 4, q = item % 4;
       const int f = t * 128 + q * 32;
@@ -866,12 +939,11 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = 0.f;
-      const uint32_t off = (uint32_t)(m * 128 + q * 32) * 4;
       for (int src = 0; src < p.S; ++src) {
-        const uint32_t ra = map_rank(base + off, src);
+        const PeerAddr ra = peer_addr(stage_acc + m * 128 + q * 32, src);
         float4 r[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) r[j] = ld_dsmem4(ra + j * 16);
+        for (int j = 0; j < 8; ++j) r[j] = ld_peer4(ra + j * 16);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           v[4 * j] += r[j].x; v[4 * j + 1] += r[j].y; v[4 * j + 2] += r[j].z; v[4 * j + 3] += r[j].w;
@@ -886,7 +958,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   __syncthreads();
   if (warp == 0) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
+    tmem_dealloc(tmem, tmem_cols);
   }
 }
 
@@ -1232,8 +1304,8 @@ inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const vo
   VLLT_REQUIRE(tiles < (1ll << 31), "gemm_bf16: too many tiles");
   if (splits == 1) {  // persistent: one CTA per SM (at most one per tile)
     const unsigned ctas = (unsigned)std::min<int64_t>(tiles, sm_count());
-    tc::gemm_persistent_kernel<Epi><<<ctas, tc::P_THREADS, tc::SMEM_BYTES, st>>>(ta, tb, M_cap, M_dev, N, K, epi,
-                                                                                 err);
+    VLLT_LAUNCH(ctas, tc::P_THREADS, tc::SMEM_BYTES, st, tc::gemm_persistent_kernel<Epi>)(ta, tb, M_cap, M_dev, N, K,
+                                                                                         epi, err);
     return check_launch("gemm_bf16");
   }
   VLLT_REQUIRE(sk && sk->part && sk->counters && tiles <= sk->n_counters &&
@@ -1242,7 +1314,7 @@ inline int gemm_bf16_launch(const void* A, int M_cap, const int* M_dev, const vo
                splits, (long long)tiles);
   const tc::SplitK ks{sk->part, sk->counters};
   dim3 grid((unsigned)tiles, 1, splits);
-  tc::gemm_kernel<Epi><<<grid, 128, tc::SMEM_BYTES, st>>>(ta, tb, M_cap, M_dev, N, K, epi, err, ks);
+  VLLT_LAUNCH(grid, 128, tc::SMEM_BYTES, st, tc::gemm_kernel<Epi>)(ta, tb, M_cap, M_dev, N, K, epi, err, ks);
   return check_launch("gemm_bf16");
 }
 
