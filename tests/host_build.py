@@ -66,7 +66,14 @@ def build_library_host(out_dir: str):
         objs = list(ex.map(compile_one, srcs))
     out = os.path.join(out_dir, "libvllt_host.so")
     subprocess.run([gxx, "-shared", "-pthread", *objs, "-o", out], check=True)
-    lib = ctypes.CDLL(out)
+    return load_library_host(out)
+
+
+def load_library_host(path: str):
+    """The host build at `path` (from build_library_host) loaded with the C
+    ABI's signatures set: how a spawned test process opens the library its
+    parent built."""
+    lib = ctypes.CDLL(path)
     from vllt import _lib
 
     for name, (res, args) in _lib.SIGNATURES.items():

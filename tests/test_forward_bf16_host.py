@@ -38,9 +38,13 @@ def L(host_library):
 
 
 class Forward:
-    """A runner's descriptor, caches and buffers in host memory."""
+    """A runner's descriptor, caches and buffers in host memory. bf16 with
+    tp_size > 1: shard tp_rank of the model (vllt.llama.LlamaWeights), this
+    rank's KV heads in the caches, `tp_comm` passed through the descriptor as
+    TPLlamaRunner passes its NCCL communicator; the logits are this rank's
+    vocabulary slice."""
 
-    def __init__(self, L, shape, bf16, num_blocks=64, bs=16):
+    def __init__(self, L, shape, bf16, num_blocks=64, bs=16, tp_rank=0, tp_size=1, tp_comm=None):
         from types import SimpleNamespace
 
         from vllt import _lib
@@ -51,14 +55,16 @@ class Forward:
         self.L, self.shape = L, shape
         D = shape.head_dim
         dt = torch.bfloat16 if bf16 else torch.float32
-        kv = (shape.n_layers, num_blocks, shape.n_kv_heads, bs, D)
+        kv = (shape.n_layers, num_blocks, shape.n_kv_heads // tp_size, bs, D)
         self.cache_k, self.cache_v = torch.zeros(kv, dtype=dt), torch.zeros(kv, dtype=dt)
+        self.vocab = shape.vocab_size
         if bf16:
-            w = LlamaWeights(shape, "cpu")
-            me = SimpleNamespace(model_cfg=shape, w=w, _ptrs=w.pointer_arrays(), tp_size=1, head_dim=D,
-                                 block_size=bs, num_blocks=num_blocks, tp_comm=None, cache_k=self.cache_k,
+            w = LlamaWeights(shape, "cpu", tp_rank, tp_size)
+            me = SimpleNamespace(model_cfg=shape, w=w, _ptrs=w.pointer_arrays(), tp_size=tp_size, head_dim=D,
+                                 block_size=bs, num_blocks=num_blocks, tp_comm=tp_comm, cache_k=self.cache_k,
                                  cache_v=self.cache_v)
             self.desc = LlamaRunner._make_desc(me)
+            self.vocab = w.vocab_local
         else:
             w = DeviceWeights(shape, fp32_reference_weights(shape, "cpu"), device="cpu")
             me = SimpleNamespace(model_cfg=shape, w=w, _ptrs=w.pointer_arrays(), block_size=bs,
@@ -75,13 +81,14 @@ class Forward:
 
     def execute(self, out):
         rec, bounds, rows, (S, T, R, W) = self.packer.pack(out)
+        self.last_bounds = bounds
         rec = np.ascontiguousarray(rec, np.int32)
         rc = self.L.vllt_forward(C.byref(self.desc), rec.ctypes.data, C.byref(self.caps), C.byref(bounds),
                                  self.meta.ctypes.data, self.ws.ctypes.data, self.ws.size, self.logits.ctypes.data,
                                  None)
         assert rc == 0, self.L.vllt_last_error()
         assert self.meta[7] == 0
-        return self.logits[:R, :self.shape.vocab_size].copy()
+        return self.logits[:R, :self.vocab].copy()
 
 
 def test_bf16_forward_matches_the_fp32_forward_on_the_same_weights(L):
