@@ -15,9 +15,13 @@
 //     be reused;
 //   * a barrier that can never complete (threads waiting on different
 //     barriers) stops the launch with an error instead of hanging.
-// Fibers never preempt each other, so plain loads and stores are coherent
-// and atomics are ordinary read-modify-writes. __shared__ becomes a static
-// (one instance per CTA run; CTAs run one after another). Math intrinsics map
+// Fibers of one CTA never preempt each other, so their plain loads and stores
+// to shared memory are coherent. The CTAs of a launch run at the same time on
+// a pool of OS threads (one CTA at a time per thread), as on the GPU's SMs:
+// atomics are real read-modify-writes and __threadfence a real fence, and a
+// kernel whose CTAs depend on their order or on one another's plain stores
+// without them shows it here. __shared__ becomes a static thread_local (one
+// instance per OS thread, reused by the CTAs it runs). Math intrinsics map
 // to the host's IEEE operations (the _rn forms are exact; approximate ones
 // such as __expf or rsqrtf map to the host's expf / 1 / sqrtf, so results
 // agree with the device within their stated error, not bit for bit).
@@ -30,6 +34,7 @@
 #define VLLT_SIMT_HOST 1
 #endif
 
+#include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstdint>
@@ -122,8 +127,9 @@ inline int __ffs(int x) { return __builtin_ffs(x); }
 template <class T> inline T __ldg(const T* p) { return *p; }
 template <class T> inline T __ldcg(const T* p) { return *p; }
 template <class T> inline void __stcg(T* p, T v) { *p = v; }
-inline void __threadfence() {}
-inline void __threadfence_block() {}
+// CTAs run on several OS threads at once: the device-scope fence is a real one
+inline void __threadfence() { std::atomic_thread_fence(std::memory_order_seq_cst); }
+inline void __threadfence_block() { std::atomic_signal_fence(std::memory_order_seq_cst); }
 inline void __nanosleep(unsigned) {}
 
 // packed fp32 pairs (sm_100): element-wise, each rounded once
@@ -149,9 +155,8 @@ template <class T> inline T atomicExch(T* p, T v) { return atomic_rmw(p, [&](T) 
 template <class T> inline T atomicCAS(T* p, T c, T v) { return atomic_rmw(p, [&](T o) { return o == c ? v : o; }); }
 
 // ---- built-in variables: set by the scheduler (threadIdx whenever a fiber resumes) --
-// Per OS thread: a launch runs its CTAs one after another on the calling
-// thread, except the CTAs of a thread-block cluster, which run at the same
-// time, one OS thread each.
+// Per OS thread: each thread of the launch pool runs one CTA at a time; the
+// CTAs of a thread-block cluster run at the same time, one OS thread each.
 inline thread_local dim3 threadIdx, blockIdx, blockDim, gridDim;
 
 // ---- the CTA scheduler ---------------------------------------------------------
@@ -483,8 +488,56 @@ inline void set_smem(size_t smem) {
   tls_smem_bytes = smem;
 }
 
+// Worker OS threads that run the CTAs of a launch at the same time, as the
+// SMs do: each takes the next CTA index until the grid is done (one CTA at a
+// time per OS thread, its fibers cooperative). VLLT_SIMT_THREADS sets their
+// number (1: every CTA on the launching thread, in index order); by default
+// one per host core, at most 32. The pool lives until the process exits.
+struct GridPool {
+  std::mutex mu, launch_mu;
+  std::condition_variable go, idle;
+  const std::function<void()>* job = nullptr;
+  uint64_t gen = 0;
+  int busy = 0, workers = 0;
+};
+inline int pool_size() {
+  static const int n = [] {
+    const char* e = std::getenv("VLLT_SIMT_THREADS");
+    int v = e ? std::atoi(e) : (int)std::thread::hardware_concurrency();
+    return std::max(1, std::min(v, 32));
+  }();
+  return n;
+}
+inline GridPool& grid_pool() {
+  static GridPool* p = [] {
+    GridPool* g = new GridPool;  // never destroyed: the workers wait on it until exit
+    g->workers = pool_size() - 1;
+    for (int w = 0; w < g->workers; ++w)
+      std::thread([g] {
+        uint64_t seen = 0;
+        for (;;) {
+          const std::function<void()>* job;
+          {
+            std::unique_lock<std::mutex> lk(g->mu);
+            g->go.wait(lk, [&] { return g->gen != seen; });
+            seen = g->gen;
+            job = g->job;
+          }
+          (*job)();
+          std::lock_guard<std::mutex> lk(g->mu);
+          if (--g->busy == 0) g->idle.notify_all();
+        }
+      }).detach();
+    return g;
+  }();
+  return *p;
+}
+
 // Runs body() as every thread of every CTA of the grid; returns false if a
-// CTA's threads waited on barriers that could never complete. With a cluster
+// CTA's threads waited on barriers that could never complete. Without a
+// cluster, the grid's CTAs are spread over the pool's OS threads; each CTA's
+// shuffled schedule (a nonzero seed) is seeded from the launch's seed and the
+// CTA's index, so it does not depend on which thread runs it. With a cluster
 // of `cluster` CTAs along x, the CTAs of one cluster run at the same time,
 // each on its own OS thread, and clusters one after another.
 inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<void()>& body, unsigned cluster = 1) {
@@ -492,15 +545,41 @@ inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<voi
   if (n < 1 || n > kMaxThreads || cluster < 1 || grid.x % cluster) return false;
   ::gridDim = grid;
   ::blockDim = block;
-  if (cluster == 1) {
-    set_smem(smem);
-    for (unsigned bz = 0; bz < grid.z; ++bz)
-      for (unsigned by = 0; by < grid.y; ++by)
-        for (unsigned bx = 0; bx < grid.x; ++bx)
-          if (!run_cta(dim3(bx, by, bz), block, body)) return false;
-    return true;
-  }
   const uint64_t seed = schedule_seed();
+  if (cluster == 1) {
+    const int64_t n_cta = (int64_t)grid.x * grid.y * grid.z;
+    std::atomic<int64_t> next{0};
+    std::atomic<bool> ok{true};
+    const std::function<void()> job = [&] {
+      ::gridDim = grid;
+      ::blockDim = block;
+      set_smem(smem);
+      for (int64_t i; ok.load() && (i = next.fetch_add(1)) < n_cta;) {
+        const dim3 bid((unsigned)(i % grid.x), (unsigned)(i / grid.x % grid.y), (unsigned)(i / grid.x / grid.y));
+        schedule_seed() = seed ? seed ^ (0x9E3779B97F4A7C15ull * (uint64_t)(i + 1)) : 0;
+        if (!run_cta(bid, block, body)) ok = false;
+      }
+    };
+    GridPool& g = grid_pool();
+    const int helpers = (int)std::min<int64_t>(g.workers, n_cta - 1);
+    if (helpers <= 0) {
+      job();
+    } else {
+      std::lock_guard<std::mutex> one_launch(g.launch_mu);
+      {
+        std::lock_guard<std::mutex> lk(g.mu);
+        g.job = &job;
+        g.busy = g.workers;
+        ++g.gen;
+      }
+      g.go.notify_all();
+      job();
+      std::unique_lock<std::mutex> lk(g.mu);
+      g.idle.wait(lk, [&] { return g.busy == 0; });
+    }
+    schedule_seed() = seed;
+    return ok.load();
+  }
   for (unsigned bz = 0; bz < grid.z; ++bz)
     for (unsigned by = 0; by < grid.y; ++by)
       for (unsigned cx = 0; cx < grid.x / cluster; ++cx) {

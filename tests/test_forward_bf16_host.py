@@ -34,6 +34,7 @@ BAR = 2e-2
 
 @pytest.fixture
 def L(host_library):
+    host_library.vllt_host_mma_count.restype = C.c_int64
     return host_library
 
 
@@ -44,7 +45,8 @@ class Forward:
     TPLlamaRunner passes its NCCL communicator; the logits are this rank's
     vocabulary slice."""
 
-    def __init__(self, L, shape, bf16, num_blocks=64, bs=16, tp_rank=0, tp_size=1, tp_comm=None):
+    def __init__(self, L, shape, bf16, num_blocks=64, bs=16, tp_rank=0, tp_size=1, tp_comm=None, max_tokens=256,
+                 max_seqs=8):
         from types import SimpleNamespace
 
         from vllt import _lib
@@ -73,7 +75,7 @@ class Forward:
         self.keep = (w, me)
         self.vocab_padded = w.vocab_padded
         self.qp = L.vllt_query_tile_positions(C.byref(self.desc))
-        self.caps = _lib.Caps(8, 256, 32, -(-shape.max_seq_len // bs))
+        self.caps = _lib.Caps(max_seqs, max_tokens, 32, -(-shape.max_seq_len // bs))
         self.meta = np.zeros(L.vllt_meta_bytes(C.byref(self.caps)) // 4, np.int32)
         self.ws = np.zeros(L.vllt_forward_workspace_bytes(C.byref(self.desc), C.byref(self.caps)), np.uint8)
         self.logits = np.zeros((self.caps.max_rows, w.vocab_padded), np.float32)
@@ -98,7 +100,6 @@ def test_bf16_forward_matches_the_fp32_forward_on_the_same_weights(L):
 
     shape = LlamaShape(n_layers=2, n_heads=8, n_kv_heads=2, d_model=1024, d_ff=2048, vocab_size=1000,
                        max_seq_len=2048, seed=1)
-    L.vllt_host_mma_count.restype = C.c_int64
     bf, ref = Forward(L, shape, True), Forward(L, shape, False)
     mma0 = L.vllt_host_mma_count()
     worst = worst_row = 0.0
@@ -117,3 +118,59 @@ def test_bf16_forward_matches_the_fp32_forward_on_the_same_weights(L):
     assert worst <= BAR and worst_row <= BAR, (worst, worst_row)
     assert decided > 0
     assert L.vllt_host_mma_count() > mma0  # the tensor-core kernels ran
+
+
+def oracle_weights(w, shape):
+    """The product's unsharded bf16 weights (vllt.llama.LlamaWeights) in the
+    oracle's naming (oracle/llama_bf16.py), as float32 values: wqkv split into
+    wq / wk / wv, the interleaved gate/up rows taken apart."""
+    D, H, KV = shape.head_dim, shape.n_heads, shape.n_kv_heads
+    out = {"tok_emb": w.tok_emb.float(), "lm_head": w.lm_head.float()}
+    for i, l in enumerate(w.layers):
+        qkv = l["wqkv"].float()
+        out[f"{i}.wq"], out[f"{i}.wk"], out[f"{i}.wv"] = qkv[:H * D], qkv[H * D:(H + KV) * D], qkv[(H + KV) * D:]
+        out[f"{i}.wo"], out[f"{i}.w_down"] = l["wo"].float(), l["w_down"].float()
+        out[f"{i}.w_gate"], out[f"{i}.w_up"] = l["w_gu"][0::2].float(), l["w_gu"][1::2].float()
+    return out
+
+
+# Three times the worst error of the host build against the oracle measured on
+# this schedule (the two follow the same bf16 rounding points and differ only in
+# the order of fp32 accumulation, the prefill kernel's lazily moved running max
+# and exp2 against exp).
+LONG_BAR = 1e-2
+
+
+def test_bf16_forward_long_contexts_over_cached_prefixes(L):
+    """The GPU test's long-context schedule (tests/test_gpu_llama.py
+    long_schedule: prefill chunks of 2,400 and 4,100 tokens over cached
+    prefixes of 2,100 and 4,000, then a decode row at 4,501 keys and four
+    verify rows at 8,101-8,104, block tables from a shuffled pool of 800
+    blocks, the RoPE table at the C4 max_seq_len of 9216) on a narrow model of
+    the head size the kernels are built for. Reference: the bf16 forward's
+    rounding points restated on the CPU (oracle/llama_bf16.py) over the same
+    weights, each sequence whole with its chunking."""
+    from oracle.llama_bf16 import forward_sequence, schedule_sequences
+    from vllt.llama import LlamaShape
+
+    from tests.test_gpu_llama import long_schedule
+
+    shape = LlamaShape(n_layers=1, n_heads=2, n_kv_heads=1, d_model=256, d_ff=512, vocab_size=300,
+                       max_seq_len=9216, seed=4)
+    passes = long_schedule(shape.vocab_size, np.random.default_rng(8))
+    fw = Forward(L, shape, True, num_blocks=800, max_tokens=8192, max_seqs=2)
+    w = oracle_weights(fw.keep[0], shape)
+    seqs, rows = schedule_sequences(passes)
+    with torch.no_grad():
+        want = {k: forward_sequence(shape, w, toks, chunks, bf16=True).numpy() for k, (toks, chunks) in seqs.items()}
+    worst = 0.0
+    mma0 = L.vllt_host_mma_count()
+    for step, pass_rows in zip(passes, rows):
+        got = fw.execute(F.as_scheduler_output(step))
+        ref = np.concatenate([want[k][pos] for k, pos in pass_rows])
+        assert got.shape == ref.shape and np.isfinite(got).all()
+        worst = max(worst, float(np.abs(got - ref).max() / np.abs(ref).max()))
+        assert (got.argmax(1) == ref.argmax(1)).all()
+    print(f"long contexts: worst {worst:.3e} of max |logit|")
+    assert worst <= LONG_BAR
+    assert L.vllt_host_mma_count() > mma0
