@@ -37,7 +37,9 @@ needs_vllmlite = pytest.mark.skipif(not have_vllmlite(), reason="vllm-lite (the 
 
 @pytest.fixture(scope="session")
 def host_library(tmp_path_factory):
-    """libvllt's fp32 path built for the host (tests/host_build.py), once per session."""
+    """libvllt built for the host (tests/host_build.py), once per session;
+    instrumented for ThreadSanitizer when VLLT_HOST_TSAN=1 (the race check of
+    tests/test_race_check_host.py runs the host tests that way)."""
     from tests.host_build import build_library_host
 
     lib = build_library_host(str(tmp_path_factory.mktemp("libvllt_host")))

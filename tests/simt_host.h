@@ -50,6 +50,32 @@
 #include <thread>
 #include <vector>
 
+// ---- race checking: a build with -fsanitize=thread (tests/test_race_check_host.py) --
+// Every emulated GPU thread is a ThreadSanitizer fiber, and the emulation
+// states the happens-before edges the hardware gives: a barrier (CTA, warp,
+// cluster) orders each participant's accesses before it with every
+// participant's accesses after it, an mbarrier phase orders its arrivals and
+// completed copies before the waits that see it complete, and a CTA's start
+// and end order it against the CTAs an OS thread ran before and after it.
+// Shared- and global-memory accesses of the kernels' own code are then
+// checked: two threads touching the same bytes, one of them writing, with
+// neither ordered before the other, is reported. The emulation's own
+// bookkeeping (SIMT_INTERNAL) is not checked.
+#if defined(__SANITIZE_THREAD__)
+#include <sanitizer/tsan_interface.h>
+#define SIMT_INTERNAL __attribute__((no_sanitize("thread"), noinline))
+namespace simt {
+inline void hb_release(const void* key) { __tsan_release(const_cast<void*>(key)); }
+inline void hb_acquire(const void* key) { __tsan_acquire(const_cast<void*>(key)); }
+}  // namespace simt
+#else
+#define SIMT_INTERNAL
+namespace simt {
+inline void hb_release(const void*) {}
+inline void hb_acquire(const void*) {}
+}  // namespace simt
+#endif
+
 #define __global__
 #define __device__
 #define __host__
@@ -233,6 +259,11 @@ struct Cta {
   uint64_t slot[kMaxThreads / 32][32];  // shuffle exchange
   const std::function<void()>* body = nullptr;
   bool deadlock = false;
+  // happens-before keys: barrier groups by generation parity, CTA start / end
+  unsigned gen_cta = 0, gen_cluster = 0, gen_warp[kMaxThreads / 32] = {};
+  char hb_cta[2], hb_cluster[2], hb_warp[kMaxThreads / 32][2], hb_begin, hb_end;
+  std::vector<void*> tsan_fiber;  // the race checker's context per fiber (kept across CTAs)
+  void* tsan_main = nullptr;      // and the OS thread's own
 };
 
 // The OS threads of one cluster's CTAs: barrier.cluster and the shared-memory
@@ -247,6 +278,7 @@ struct Cluster {
   std::vector<unsigned char*> dyn;  // per rank: dynamic shared memory
   std::vector<size_t> dyn_bytes;
   std::vector<const char*> anchor;  // per rank: a thread_local of this module (static __shared__ variables)
+  char hb[2];                       // happens-before keys of barrier.cluster, by generation parity
 };
 
 inline thread_local Cta* tls_cta = nullptr;
@@ -255,7 +287,7 @@ inline thread_local size_t tls_smem_bytes = 0;
 inline thread_local Cluster* tls_cluster = nullptr;
 inline thread_local int tls_rank = 0;
 
-inline Cta& cta() {
+SIMT_INTERNAL inline Cta& cta() {
   if (!tls_cta) tls_cta = new Cta;
   return *tls_cta;
 }
@@ -264,7 +296,7 @@ inline uint64_t host_ns() {  // the device's %globaltimer
   clock_gettime(CLOCK_MONOTONIC, &t);
   return (uint64_t)t.tv_sec * 1000000000ull + (uint64_t)t.tv_nsec;
 }
-inline std::vector<unsigned char>& dyn_smem() {
+SIMT_INTERNAL inline std::vector<unsigned char>& dyn_smem() {
   if (!tls_smem) tls_smem = new std::vector<unsigned char>;
   return *tls_smem;
 }
@@ -282,7 +314,18 @@ inline size_t dynamic_smem_bytes() { return tls_smem_bytes; }
 __attribute__((visibility("hidden"))) inline thread_local char tls_anchor_byte;
 inline const char* tls_anchor() { return &tls_anchor_byte; }
 
-inline void switch_next() {
+// Tells the race checker which context runs next (fiber i, or -1: the OS
+// thread's CTA scheduler), right before the stack switch; no happens-before.
+SIMT_INTERNAL inline void to_context(Cta& c, int i) {
+#if defined(__SANITIZE_THREAD__)
+  __tsan_switch_to_fiber(i < 0 ? c.tsan_main : c.tsan_fiber[i], __tsan_switch_to_fiber_no_sync);
+#else
+  (void)c;
+  (void)i;
+#endif
+}
+
+SIMT_INTERNAL inline void switch_next() {
   Cta& c = cta();
   const int from = c.cur;
   for (int k = 1; k <= c.n; ++k) {
@@ -290,6 +333,7 @@ inline void switch_next() {
     if (!c.f[i].done && c.f[i].waiting == -2) {
       if (i == from) return;
       c.cur = i;
+      to_context(c, i);
       stack_switch(&c.f[from].sp, c.f[i].sp);
       ::threadIdx = c.f[c.cur].tid;  // resumed: this fiber's index again
       return;
@@ -297,6 +341,7 @@ inline void switch_next() {
   }
   // nobody can run: every live thread waits on a barrier that cannot complete
   c.deadlock = true;
+  to_context(c, -1);
   stack_switch(&c.f[from].sp, c.main_sp);
 }
 
@@ -311,7 +356,7 @@ inline uint64_t& schedule_seed() {
   static thread_local uint64_t s = 0;
   return s;
 }
-inline uint32_t next_random() {
+SIMT_INTERNAL inline uint32_t next_random() {
   uint64_t& x = schedule_seed();
   x ^= x << 13;
   x ^= x >> 7;
@@ -321,16 +366,23 @@ inline uint32_t next_random() {
 
 inline void switch_to(int i);
 
-inline void release(int group) {
+SIMT_INTERNAL inline void release(int group) {
   Cta& c = cta();
   for (auto& fb : c.f)
     if (!fb.done && fb.waiting == group) fb.waiting = -2;
-  if (group == -1) c.arrived_cta = 0;
-  else if (group == kClusterGroup) c.arrived_cluster = 0;
-  else c.arrived_warp[group] = 0;
+  if (group == -1) c.arrived_cta = 0, ++c.gen_cta;
+  else if (group == kClusterGroup) c.arrived_cluster = 0, ++c.gen_cluster;
+  else c.arrived_warp[group] = 0, ++c.gen_warp[group];
 }
 
-inline void handover() {  // after a release: a random runnable thread continues
+// The happens-before key of the current generation of a barrier group.
+SIMT_INTERNAL inline const char* hb_key(Cta& c, int group) {
+  if (group == -1) return &c.hb_cta[c.gen_cta & 1];
+  if (group == kClusterGroup) return &c.hb_cluster[c.gen_cluster & 1];
+  return &c.hb_warp[group][c.gen_warp[group] & 1];
+}
+
+SIMT_INTERNAL inline void handover() {  // after a release: a random runnable thread continues
   Cta& c = cta();
   if (!schedule_seed()) return;
   const int pick = (int)(next_random() % (uint32_t)c.n);
@@ -343,24 +395,28 @@ inline void handover() {  // after a release: a random runnable thread continues
   }
 }
 
-inline void arrive(int group) {  // -1: the CTA; w: warp w
+SIMT_INTERNAL inline void arrive(int group) {  // -1: the CTA; w: warp w
   Cta& c = cta();
+  const char* key = hb_key(c, group);
+  hb_release(key);
   int& arrived = group < 0 ? c.arrived_cta : c.arrived_warp[group];
   const int size = group < 0 ? c.live_cta : c.live_warp[group];
   if (++arrived >= size) {
     release(group);
     handover();
+    hb_acquire(key);
     return;
   }
   c.f[c.cur].waiting = group;
   switch_next();
+  hb_acquire(key);
 }
 
 // The cluster-wide half of barrier.cluster, once every live thread of this
 // CTA has arrived: waits (blocking this OS thread) for the other CTAs of the
 // cluster. False if it can never complete (a peer CTA exited, or a peer's
 // threads deadlocked).
-inline bool cluster_os_barrier() {
+SIMT_INTERNAL inline bool cluster_os_barrier() {
   Cluster* cl = tls_cluster;
   if (!cl || cl->size == 1) return true;
   std::unique_lock<std::mutex> lk(cl->mu);
@@ -380,39 +436,49 @@ inline bool cluster_os_barrier() {
   return cl->gen != g;
 }
 
-inline void complete_cluster_barrier() {
+SIMT_INTERNAL inline void complete_cluster_barrier() {
   Cta& c = cta();
   if (!cluster_os_barrier()) {  // the launch fails: back to the CTA's scheduler
     c.deadlock = true;
+    to_context(c, -1);
     stack_switch(&c.f[c.cur].sp, c.main_sp);
   }
   release(kClusterGroup);
 }
 
 // barrier.cluster.arrive + barrier.cluster.wait (a CTA barrier without a cluster).
-inline void cluster_arrive_wait() {
+SIMT_INTERNAL inline void cluster_arrive_wait() {
   Cta& c = cta();
+  // one key for every thread of the cluster: the OS-level barrier lets no
+  // thread past before all have arrived (and released)
+  const char* key = tls_cluster && tls_cluster->size > 1 ? &tls_cluster->hb[tls_cluster->gen & 1]
+                                                         : hb_key(c, kClusterGroup);
+  hb_release(key);
   if (++c.arrived_cluster >= c.live_cta) {
     complete_cluster_barrier();
     handover();
+    hb_acquire(key);
     return;
   }
   c.f[c.cur].waiting = kClusterGroup;
   switch_next();
+  hb_acquire(key);
 }
 
 // Run thread i now; the current thread stays runnable and resumes later.
-inline void switch_to(int i) {
+SIMT_INTERNAL inline void switch_to(int i) {
   Cta& c = cta();
   const int from = c.cur;
   if (i == from) return;
   c.cur = i;
+  to_context(c, i);
   stack_switch(&c.f[from].sp, c.f[i].sp);
   ::threadIdx = c.f[c.cur].tid;
 }
 
-inline void exit_thread() {
+SIMT_INTERNAL inline void exit_thread() {
   Cta& c = cta();
+  hb_release(&c.hb_end);
   Fiber& me = c.f[c.cur];
   me.done = true;
   ++c.done;
@@ -422,12 +488,17 @@ inline void exit_thread() {
   if (c.arrived_cta > 0 && c.arrived_cta >= c.live_cta) release(-1);
   if (c.arrived_warp[w] > 0 && c.arrived_warp[w] >= c.live_warp[w]) release(w);
   if (c.arrived_cluster > 0 && c.arrived_cluster >= c.live_cta) complete_cluster_barrier();
-  if (c.done == c.n) stack_switch(&me.sp, c.main_sp);  // the last thread: back to the launch
+  if (c.done == c.n) {  // the last thread: back to the launch
+    to_context(c, -1);
+    stack_switch(&me.sp, c.main_sp);
+  }
   switch_next();
+  to_context(c, -1);
   stack_switch(&me.sp, c.main_sp);  // not reached unless stopped
 }
 
-inline void trampoline() {
+SIMT_INTERNAL inline void trampoline() {
+  hb_acquire(&cta().hb_begin);
   ::threadIdx = cta().f[cta().cur].tid;
   (*cta().body)();
   exit_thread();
@@ -451,7 +522,7 @@ inline void (*&cta_start_hook())() {
 
 // Runs CTA `bid` (every thread of it) on this OS thread; false if its threads
 // waited on barriers that could never complete.
-inline bool run_cta(dim3 bid, dim3 block, const std::function<void()>& body) {
+SIMT_INTERNAL inline bool run_cta(dim3 bid, dim3 block, const std::function<void()>& body) {
   const int n = (int)(block.x * block.y * block.z);
   ::blockIdx = bid;
   Cta& c = cta();
@@ -471,9 +542,16 @@ inline bool run_cta(dim3 bid, dim3 block, const std::function<void()>& body) {
     c.f[i].tid = dim3(i % block.x, (i / block.x) % block.y, i / (block.x * block.y));
     c.f[i].sp = prepare_stack(c.stacks.data() + kStack * i, kStack, trampoline);
   }
+#if defined(__SANITIZE_THREAD__)
+  c.tsan_main = __tsan_get_current_fiber();
+  while ((int)c.tsan_fiber.size() < n) c.tsan_fiber.push_back(__tsan_create_fiber(0));
+#endif
   if (cta_start_hook()) cta_start_hook()();
+  hb_release(&c.hb_begin);
   c.cur = schedule_seed() ? (int)(next_random() % (uint32_t)n) : 0;
+  to_context(c, c.cur);
   stack_switch(&c.main_sp, c.f[c.cur].sp);
+  hb_acquire(&c.hb_end);
   if (c.deadlock) {
     std::fprintf(stderr, "simt: block (%u,%u,%u): threads wait on barriers that cannot complete\n", bid.x, bid.y,
                  bid.z);
@@ -674,7 +752,7 @@ inline Launcher<KArgs...> launcher(void (*kernel)(KArgs...), dim3 grid, dim3 blo
 }
 
 template <class T>
-inline T shfl(T v, int src_lane, bool in_range) {
+SIMT_INTERNAL inline T shfl(T v, int src_lane, bool in_range) {
   static_assert(sizeof(T) <= 8, "shuffle of more than 8 bytes");
   Cta& c = cta();
   const int t = flat_tid(), w = t / 32, lane = t % 32;
@@ -692,7 +770,7 @@ inline T shfl(T v, int src_lane, bool in_range) {
 
 
 inline void __syncthreads() { simt::arrive(-1); }
-inline int __syncthreads_or(int p) {
+SIMT_INTERNAL inline int __syncthreads_or(int p) {
   static thread_local int acc;
   simt::arrive(-1);
   acc = 0;
@@ -717,7 +795,7 @@ template <class T> inline T __shfl_up_sync(unsigned, T v, unsigned d, int = 32) 
   const int lane = simt::flat_tid() % 32;
   return simt::shfl(v, lane - (int)d, lane - (int)d >= 0);
 }
-inline unsigned __ballot_sync(unsigned, int p) {
+SIMT_INTERNAL inline unsigned __ballot_sync(unsigned, int p) {
   simt::Cta& c = simt::cta();
   const int t = simt::flat_tid(), w = t / 32, lane = t % 32;
   c.slot[w][lane] = p ? 1 : 0;

@@ -59,7 +59,7 @@ inline uint64_t& clock_state() {
   static thread_local uint64_t t = 0;
   return t;
 }
-inline uint64_t global_ns() { return clock_state() += 1000; }
+SIMT_INTERNAL inline uint64_t global_ns() { return clock_state() += 1000; }
 
 // ---- mbarrier ------------------------------------------------------------------------
 struct MbarWord {
@@ -70,30 +70,38 @@ struct MbarWord {
 };
 static_assert(sizeof(MbarWord) == 8, "an mbarrier is 8 bytes");
 inline MbarWord* word(uint64_t* bar) { return reinterpret_cast<MbarWord*>(bar); }
-inline void settle(MbarWord* m) {
+// The happens-before key of one phase of a barrier (race checking): its
+// arrivals and completed copies release it, a wait that sees the phase
+// complete acquires it.
+inline const char* phase_key(uint64_t* bar, unsigned phase) { return reinterpret_cast<const char*>(bar) + (phase & 1); }
+SIMT_INTERNAL inline void settle(MbarWord* m) {
   if (m->pending == 0 && m->tx == 0) {
     m->phase ^= 1;
     m->pending = m->expected;
   }
 }
-inline void mbar_init(uint64_t* bar, unsigned count) {
+SIMT_INTERNAL inline void mbar_init(uint64_t* bar, unsigned count) {
   if (count == 0 || count > 255) fail("mbarrier.init: arrival count out of the emulated range");
   *word(bar) = MbarWord{0, (uint16_t)count, (uint8_t)count, 0};
 }
-inline void mbar_arrive(uint64_t* bar) {
+SIMT_INTERNAL inline void mbar_arrive(uint64_t* bar) {
   MbarWord* m = word(bar);
+  hb_release(phase_key(bar, m->phase));
   if (m->pending == 0) fail("mbarrier.arrive: more arrivals than the count");
   --m->pending;
   settle(m);
 }
-inline void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+SIMT_INTERNAL inline void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
   word(bar)->tx += bytes;
   mbar_arrive(bar);
 }
-inline bool mbar_try_wait(uint64_t* bar, unsigned parity) {
-  if (word(bar)->phase != (parity & 1)) return true;
-  yield();  // the producer of this phase may be another thread of the CTA
-  return word(bar)->phase != (parity & 1);
+SIMT_INTERNAL inline bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  if (word(bar)->phase == (parity & 1)) {
+    yield();  // the producer of this phase may be another thread of the CTA
+    if (word(bar)->phase == (parity & 1)) return false;
+  }
+  hb_acquire(phase_key(bar, parity));
+  return true;
 }
 
 // ---- TMA -----------------------------------------------------------------------------
@@ -108,10 +116,16 @@ inline bool dropped() {
   if (c.load() <= 0) return false;
   return c.fetch_sub(1) == 1;
 }
+// The box lands in shared memory as the issuing thread's writes (checked for
+// races against the kernel's own accesses), then completes its bytes.
+inline void tma_complete(uint64_t* bar, uint32_t bytes);
 inline void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
   if (dropped()) return;
-  const uint32_t bytes = tma_load_host(dst, map, x, y, z);
+  tma_complete(bar, tma_load_host(dst, map, x, y, z));
+}
+SIMT_INTERNAL inline void tma_complete(uint64_t* bar, uint32_t bytes) {
   MbarWord* m = word(bar);
+  hb_release(phase_key(bar, m->phase));
   m->tx -= bytes;
   settle(m);
 }

@@ -446,11 +446,11 @@ def test_run_ahead_over_two_ranks(tmp_path):
 
     if not have_vllmlite():
         pytest.skip("vllm-lite (the host engine) is not importable")
-    lib = build_harness("meta_host", str(tmp_path))
-    if lib is None:
+    path = build_harness("meta_host", str(tmp_path), load=False)
+    if path is None:
         pytest.skip("g++ is not available")
     out = tmp_path / "out"
     out.mkdir()
-    mp.start_processes(_ahead_rank, args=(2, _free_port(), str(out), str(tmp_path / "libmeta_host.so")), nprocs=2,
-                       join=True, start_method="spawn")
+    mp.start_processes(_ahead_rank, args=(2, _free_port(), str(out), path), nprocs=2, join=True,
+                       start_method="spawn")
     assert sorted(os.listdir(out)) == ["ok0", "ok1"]

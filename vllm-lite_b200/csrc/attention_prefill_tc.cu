@@ -194,7 +194,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     mbar_init(&p_full, 128);
     mbar_init(&o_done, 1);
     mbar_init(&drain, 1);
-    abort_s = 0;
+    flag_write(&abort_s, 0);
     mbar_fence_init();
   }
   if (warp == 0) {
@@ -249,7 +249,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       }
       if (failed) {  // let the copies in flight land before the CTA can exit (bounded)
         atomicOr(p.err, 4);
-        abort_s = 1;
+        flag_write(&abort_s, 1);
         (void)mbar_wait(&bar_q, 0);
         for (int t = max(0, jk - 2); t < jk; ++t) (void)mbar_wait(&k_full[t & 1], (t >> 1) & 1);
         for (int t = max(0, jv - 2); t < jv; ++t) (void)mbar_wait(&v_full[t & 1], (t >> 1) & 1);
@@ -301,7 +301,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       }
       if (!ok) {
         atomicOr(p.err, 4);
-        abort_s = 1;
+        flag_write(&abort_s, 1);
       }
       if (issued > 0) {  // every MMA finished before the columns are freed
         mma_commit(&drain);
@@ -385,7 +385,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     }
     if (!ok) {
       if (lane == 0) atomicOr(p.err, 4);
-      abort_s = 1;
+      flag_write(&abort_s, 1);
     } else if (__all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, (n_tiles - 1) & 1, &abort_s))) {
       fence_after();  // epilogue: O / l -> bf16 rows
       const int pos = q0 + row / NREP;
@@ -412,7 +412,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       }
     } else {
       if (lane == 0) atomicOr(p.err, 4);
-      abort_s = 1;
+      flag_write(&abort_s, 1);
     }
   }
   fence_before();

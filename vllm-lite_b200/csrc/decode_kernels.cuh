@@ -11,6 +11,9 @@
 #include <cuda.h>
 
 #include "device_common.cuh"
+#ifdef VLLT_SIMT_HOST
+#include <simt_tc.h>
+#endif
 
 namespace vllt {
 namespace dk {
@@ -45,46 +48,21 @@ struct DecodeParams {
 };
 
 #ifdef VLLT_SIMT_HOST
-// The host emulation (tests/simt_host.h) of the mbarrier and TMA operations
-// below: an mbarrier word holds the pending transaction bytes, the pending
-// arrivals, the arrival count and the phase bit; a tensor-map load copies its
-// box at once (with the map's swizzle) and completes its bytes.
-struct MbarWord {
-  uint32_t tx;
-  uint16_t pending;
-  uint8_t expected;
-  uint8_t phase;
-};
-inline uint32_t saddr(const void* p) { return static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p)); }
-inline void mbar_settle(MbarWord* m) {
-  if (m->pending == 0 && m->tx == 0) {
-    m->phase ^= 1;
-    m->pending = m->expected;
-  }
-}
-inline void mbar_init(uint64_t* bar, unsigned count) {
-  *reinterpret_cast<MbarWord*>(bar) = MbarWord{0, (uint16_t)count, (uint8_t)count, 0};
-}
+// The host emulation's equivalents of the mbarrier and TMA operations below
+// (tests/simt_include/simt_tc.h, shared with the tensor-core kernels): an
+// mbarrier word holds the pending transaction bytes, the pending arrivals,
+// the arrival count and the phase bit; a tensor-map load copies its box at
+// once (with the map's swizzle) and completes its bytes; the clock that
+// bounds the waits is virtual.
+inline uint32_t saddr(const void* p) { return ::simt::tensor::saddr(p); }
+inline void mbar_init(uint64_t* bar, unsigned count) { ::simt::tensor::mbar_init(bar, count); }
 inline void mbar_fence_init() {}
-inline void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-  MbarWord* m = reinterpret_cast<MbarWord*>(bar);
-  m->tx += bytes;
-  --m->pending;
-  mbar_settle(m);
-}
-inline void mbar_arrive(uint64_t* bar) {
-  MbarWord* m = reinterpret_cast<MbarWord*>(bar);
-  --m->pending;
-  mbar_settle(m);
-}
-inline bool mbar_try_wait(uint64_t* bar, unsigned parity) {
-  return reinterpret_cast<MbarWord*>(bar)->phase != (parity & 1);
-}
-inline uint64_t global_ns() { return ::simt::host_ns(); }
+inline void mbar_expect_tx(uint64_t* bar, unsigned bytes) { ::simt::tensor::mbar_expect_tx(bar, bytes); }
+inline void mbar_arrive(uint64_t* bar) { ::simt::tensor::mbar_arrive(bar); }
+inline bool mbar_try_wait(uint64_t* bar, unsigned parity) { return ::simt::tensor::mbar_try_wait(bar, parity); }
+inline uint64_t global_ns() { return ::simt::tensor::global_ns(); }
 inline void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  MbarWord* m = reinterpret_cast<MbarWord*>(bar);
-  m->tx -= ::simt::tma_load_2d_host(dst, map, x, y);
-  mbar_settle(m);
+  ::simt::tensor::tma_load(dst, map, bar, x, y, 0);
 }
 #else
 __device__ __forceinline__ uint32_t saddr(const void* p) {

@@ -148,12 +148,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
     if (global_ns() - t0 > kWaitNs) return false;
   return true;
 }
+// The abort flag one role of a CTA raises and the other roles poll while they
+// wait: a volatile shared-memory word on the device (relaxed accesses in the
+// PTX memory model), a relaxed atomic under the host emulation, where the
+// roles run as concurrent threads that the race check watches.
+__device__ __forceinline__ int flag_read(const volatile int* f) {
+#ifdef VLLT_SIMT_HOST
+  return __atomic_load_n(const_cast<const int*>(f), __ATOMIC_RELAXED);
+#else
+  return *f;
+#endif
+}
+__device__ __forceinline__ void flag_write(volatile int* f, int v) {
+#ifdef VLLT_SIMT_HOST
+  __atomic_store_n(const_cast<int*>(f), v, __ATOMIC_RELAXED);
+#else
+  *f = v;
+#endif
+}
 // As mbar_wait, but also gives up as soon as another role of the CTA has set *abort.
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, unsigned parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (*abort) return false;
+    if (flag_read(abort)) return false;
     if (global_ns() - t0 > kWaitNs) return false;
   }
   return true;
@@ -206,7 +224,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
   unsigned char* smem = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
   __shared__ uint64_t full[STAGES], empty[STAGES], accf;
   __shared__ uint32_t tmem_base_s;
-  __shared__ int failed_s, last_s;
+  __shared__ int last_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = M_dev ? min(*M_dev, M_cap) : M_cap;
@@ -224,7 +242,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       mbar_init(&empty[s], 1);
     }
     mbar_init(&accf, 1);
-    failed_s = 0;
     mbar_fence_init();
   }
   if (warp == 0) {  // whole warp: allocate the accumulator columns
@@ -242,7 +259,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       const int s = kb % STAGES;
       if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) & 1) ^ 1)) {
         atomicOr(err, 4);
-        failed_s = 1;
         break;
       }
       unsigned char* a = smem + s * STAGE_BYTES;
@@ -250,16 +266,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       tma_load_2d(a, &ta, &full[s], (kb0 + kb) * BK, m0);
       tma_load_2d(a + A_BYTES, &tb, &full[s], (kb0 + kb) * BK, n0);
     }
-    if (failed_s) {  // let the copies already issued land before the CTA can exit
-      for (int j = max(0, kb - STAGES); j < kb; ++j) (void)mbar_wait(&full[j % STAGES], (j / STAGES) & 1);
-    }
+    // The copies issued last land before the CTA can exit, whichever role gave
+    // up (immediate when nothing failed: the epilogue waits for them anyway).
+    for (int j = max(0, kb - STAGES); j < kb; ++j) (void)mbar_wait(&full[j % STAGES], (j / STAGES) & 1);
   } else if (warp == 1 && lane == 0) {  // ---- MMA issuer ----
     bool ok = true;
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % STAGES;
       if (!mbar_wait(&full[s], (kb / STAGES) & 1)) {
         atomicOr(err, 4);
-        failed_s = 1;
         ok = false;
         break;
       }
@@ -373,7 +388,7 @@ gemm_persistent_kernel(const __grid_constant__ CUtensorMap ta, const __grid_cons
       mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
     }
     mbar_init(&drain, 1);
-    abort_s = 0;
+    flag_write(&abort_s, 0);
     mbar_fence_init();
   }
   if (warp == 0) {
@@ -406,7 +421,7 @@ gemm_persistent_kernel(const __grid_constant__ CUtensorMap ta, const __grid_cons
       }
       if (failed) {
         atomicOr(err, 4);
-        abort_s = 1;
+        flag_write(&abort_s, 1);
         // let the copies already issued land before the CTA can exit
         for (int j = max(0, g - STAGES); j < g; ++j) (void)mbar_wait(&full[j % STAGES], (j / STAGES) & 1);
       }
@@ -441,7 +456,7 @@ gemm_persistent_kernel(const __grid_constant__ CUtensorMap ta, const __grid_cons
       }
       if (failed) {
         atomicOr(err, 4);
-        abort_s = 1;
+        flag_write(&abort_s, 1);
       }
       if (g > 0) {  // every MMA this thread issued has finished before the columns are freed
         mma_commit(&drain);
@@ -457,7 +472,7 @@ gemm_persistent_kernel(const __grid_constant__ CUtensorMap ta, const __grid_cons
       if (!have) {
         if (lane == 0) {
           atomicOr(err, 4);
-          abort_s = 1;
+          flag_write(&abort_s, 1);
         }
         break;
       }
@@ -571,7 +586,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant_
       mbar_init(&acc_empty[a], 4);
     }
     mbar_init(&drain, 1);
-    abort_s = 0;
+    flag_write(&abort_s, 0);
     mbar_fence_init();
   }
   if (warp == 0) {
@@ -618,7 +633,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant_
       }
       if (failed) {
         atomicOr(err, 4);
-        abort_s = 1;
+        flag_write(&abort_s, 1);
         for (int j = max(0, g - stages); j < g; ++j) (void)mbar_wait(&full[j % stages], (j / stages) & 1);
       }
     }
@@ -661,7 +676,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant_
       }
       if (failed) {
         atomicOr(err, 4);
-        abort_s = 1;
+        flag_write(&abort_s, 1);
       }
       if (g > 0) {
         mma_commit(&drain);
@@ -682,7 +697,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant_
       if (!have) {
         if (lane == 0) {
           atomicOr(err, 4);
-          abort_s = 1;
+          flag_write(&abort_s, 1);
         }
         break;
       }
@@ -820,7 +835,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     }
     mbar_init(&acc_full, 1);
     mbar_init(&drain, 1);
-    abort_s = 0;
+    flag_write(&abort_s, 0);
     mbar_fence_init();
   }
   if (warp == 0) {
@@ -862,7 +877,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
       }
       if (failed) {
         atomicOr(err, 4);
-        abort_s = 1;
+        flag_write(&abort_s, 1);
         for (int j = max(0, g - stages); j < g; ++j) (void)mbar_wait(&full[j % stages], (j / stages) & 1);
       }
     }
@@ -890,7 +905,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
       if (!failed && n_it > 0) mma_commit(&acc_full);
       if (failed) {
         atomicOr(err, 4);
-        abort_s = 1;
+        flag_write(&abort_s, 1);
       }
       if (g > 0) {
         mma_commit(&drain);
@@ -902,7 +917,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     if (!have) {
       if (lane == 0) {
         atomicOr(err, 4);
-        abort_s = 1;
+        flag_write(&abort_s, 1);
       }
     } else {
       fence_after();
@@ -925,7 +940,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   // cluster reduces or runs the epilogue (which may write the KV cache). Each
   // CTA set its own abort_s before the barrier above (release / acquire), so
   // the peers' values read here are final.
-  bool cluster_ok = !abort_s;
+  bool cluster_ok = !flag_read(&abort_s);
   if (warp < 4)
     for (int src = 0; src < p.S && cluster_ok; ++src)
       cluster_ok = ld_peer_s32(peer_addr(const_cast<int*>(&abort_s), src)) == 0;
