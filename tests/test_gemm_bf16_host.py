@@ -153,3 +153,21 @@ def test_a_dropped_tma_load_reports_and_recovers(L, M, N, K, splits):
     got, flags, _ = run(L, A, W, splits, ws)
     assert flags == 0
     close(got, want, K)
+
+
+# The Llama-3-8B decode projections at the forward's own plan choices (the
+# emulated device has a B200's 148 SMs): qkv, o_proj and down (K = 14,336) in
+# the cluster form, gate/up (N = 28,672) in stream-K at 64 and 256 tokens, and
+# the split-K form past 256 tokens.
+@pytest.mark.parametrize("M,N,K,form", [(64, 6144, 4096, "cluster"), (64, 4096, 4096, "cluster"),
+                                        (64, 28672, 4096, "stream-k"), (64, 4096, 14336, "cluster"),
+                                        (256, 28672, 4096, "stream-k"), (512, 4096, 14336, "split-k")])
+def test_llama_decode_projection_shapes(L, M, N, K, form):
+    s = L.vllt_gemm_bf16_auto_splits(M, N, K)
+    assert {"cluster": s < 0, "stream-k": s == 0, "split-k": s > 1}[form], s
+    A, W, want = bf16_pair(M, N, K, N + K)
+    (got, flags, ws), n = mma_delta(L, lambda: run(L, A, W, 0))
+    assert flags == 0
+    close(got, want, K)
+    rows = -(-M // 128) if form == "split-k" else 1  # split-K tiles are 128 x 256, the swapped forms 128 features
+    assert n == (rows * -(-N // 256) if form == "split-k" else -(-N // 128)) * (K // 16)
