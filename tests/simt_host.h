@@ -35,6 +35,8 @@
 #endif
 
 #include <algorithm>
+#include <sys/mman.h>
+
 #include <climits>
 #include <cmath>
 #include <cstdint>
@@ -282,7 +284,37 @@ struct Cluster {
 };
 
 inline thread_local Cta* tls_cta = nullptr;
-inline thread_local std::vector<unsigned char>* tls_smem = nullptr;
+// A CTA's dynamic shared memory: a window that ends against a PROT_NONE page,
+// so a kernel's access past its dynamic shared memory stops the process as
+// the guard pages of the tests' global buffers do. Like the device's shared
+// memory it is not cleared between CTAs; each launch fills it with 0xFF bytes
+// (a NaN in every float, -1 in every int), so a kernel that reads shared
+// memory it never wrote sees it.
+struct SmemWindow {
+  unsigned char* map = nullptr;
+  size_t map_bytes = 0;
+  unsigned char* win = nullptr;
+  SmemWindow() = default;
+  SmemWindow(const SmemWindow&) = delete;
+  ~SmemWindow() {
+    if (map) munmap(map, map_bytes);
+  }
+  void prepare(size_t bytes) {
+    const size_t page = 4096, data = (bytes + 1023) / 1024 * 1024;
+    const size_t need = (data + page - 1) / page * page + page;
+    if (need > map_bytes) {
+      if (map) munmap(map, map_bytes);
+      void* m = mmap(nullptr, need, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
+      if (m == MAP_FAILED) std::abort();
+      map = static_cast<unsigned char*>(m);
+      map_bytes = need;
+      if (mprotect(map + map_bytes - page, page, PROT_NONE) != 0) std::abort();
+    }
+    win = map + map_bytes - page - data;  // 1024-byte aligned: the guard page is page aligned
+    std::memset(win, 0xFF, data);
+  }
+};
+inline thread_local SmemWindow* tls_smem = nullptr;
 inline thread_local size_t tls_smem_bytes = 0;
 inline thread_local Cluster* tls_cluster = nullptr;
 inline thread_local int tls_rank = 0;
@@ -296,15 +328,12 @@ inline uint64_t host_ns() {  // the device's %globaltimer
   clock_gettime(CLOCK_MONOTONIC, &t);
   return (uint64_t)t.tv_sec * 1000000000ull + (uint64_t)t.tv_nsec;
 }
-SIMT_INTERNAL inline std::vector<unsigned char>& dyn_smem() {
-  if (!tls_smem) tls_smem = new std::vector<unsigned char>;
+SIMT_INTERNAL inline SmemWindow& dyn_smem() {
+  if (!tls_smem) tls_smem = new SmemWindow;
   return *tls_smem;
 }
 inline const dim3& thread_idx() { return ::threadIdx; }
-inline unsigned char* dynamic_smem() {  // 1024-byte aligned
-  auto& m = dyn_smem();
-  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(m.data()) + 1023) & ~uintptr_t(1023));
-}
+inline unsigned char* dynamic_smem() { return dyn_smem().win; }  // 1024-byte aligned
 inline size_t dynamic_smem_bytes() { return tls_smem_bytes; }
 // A thread_local of this module: static __shared__ variables (thread_local
 // here) sit at the same offset from it in every OS thread's block of the
@@ -562,7 +591,7 @@ SIMT_INTERNAL inline bool run_cta(dim3 bid, dim3 block, const std::function<void
 }
 
 inline void set_smem(size_t smem) {
-  dyn_smem().assign(smem + 1024, 0);
+  dyn_smem().prepare(smem);
   tls_smem_bytes = smem;
 }
 
