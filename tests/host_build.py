@@ -24,6 +24,17 @@ def tsan_requested() -> bool:
     return os.environ.get("VLLT_HOST_TSAN") == "1"
 
 
+def sanitizer_flags(tsan: bool) -> list:
+    """Compiler flags of the instrumented builds: ThreadSanitizer (tsan), and
+    UndefinedBehaviorSanitizer when VLLT_HOST_UBSAN=1 (signed overflow,
+    shifts, misaligned or null accesses, out-of-range conversions: the
+    process stops at the first report)."""
+    f = ["-fsanitize=thread", "-g"] if tsan else []
+    if os.environ.get("VLLT_HOST_UBSAN") == "1":
+        f += ["-fsanitize=undefined", "-fno-sanitize-recover=all", "-g"]
+    return f
+
+
 _BUILT: dict = {}  # (harness, tsan) -> the library built earlier in this process
 
 
@@ -36,18 +47,19 @@ def build_harness(name: str, out_dir: str, tsan: bool | None = None, load: bool 
     gxx = shutil.which("g++")
     if gxx is None:
         return None
-    done = _BUILT.get((name, tsan))
+    key = (name, tsan, os.environ.get("VLLT_HOST_UBSAN") == "1")
+    done = _BUILT.get(key)
     if done is not None and os.path.exists(done):
         return ctypes.CDLL(done) if load else done
     out = os.path.join(out_dir, f"lib{name}.so")
     # no FMA contraction: the device code rounds every product and quotient (__fmul_rn, __fdiv_rn);
     # -march=native: the harness runs where it is built, and fmaf becomes one instruction
     subprocess.run([gxx, "-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-fno-gnu-unique", "-pthread",
-                    "-DVLLT_SIMT_HOST=1", "-shared", "-fPIC", *(["-fsanitize=thread", "-g"] if tsan else []),
+                    "-DVLLT_SIMT_HOST=1", "-shared", "-fPIC", *sanitizer_flags(tsan),
                     "-I", os.path.join(ROOT, "tests", "simt_include"),
                     "-I", os.path.join(ROOT, "vllm-lite_b200", "csrc"), "-I", os.path.join(ROOT, "tests"),
                     os.path.join(ROOT, "tests", f"{name}.cpp"), "-o", out], check=True)
-    _BUILT[(name, tsan)] = out
+    _BUILT[key] = out
     return ctypes.CDLL(out) if load else out
 
 
@@ -85,7 +97,7 @@ def build_library_host(out_dir: str, tsan: bool | None = None):
     csrc = os.path.join(ROOT, "vllm-lite_b200", "csrc")
     flags = ["-O2", "-march=native", "-std=c++20", "-ffp-contract=off", "-fno-gnu-unique", "-pthread",
              "-DVLLT_SIMT_HOST=1", "-fPIC", "-I", os.path.join(ROOT, "tests", "simt_include"),
-             "-I", os.path.join(ROOT, "tests"), "-I", csrc] + (["-fsanitize=thread", "-g"] if tsan else [])
+             "-I", os.path.join(ROOT, "tests"), "-I", csrc] + sanitizer_flags(tsan)
     srcs = [os.path.join(csrc, f) for f in LIBRARY_SOURCES] + [os.path.join(ROOT, "tests", "simt_stubs.cpp")]
 
     def compile_one(src):
@@ -96,8 +108,7 @@ def build_library_host(out_dir: str, tsan: bool | None = None):
     with cf.ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
         objs = list(ex.map(compile_one, srcs))
     out = os.path.join(out_dir, "libvllt_host.so")
-    subprocess.run([gxx, "-shared", "-pthread", *(["-fsanitize=thread"] if tsan else []), *objs, "-o", out],
-                   check=True)
+    subprocess.run([gxx, "-shared", "-pthread", *sanitizer_flags(tsan), *objs, "-o", out], check=True)
     return load_library_host(out)
 
 

@@ -1,0 +1,96 @@
+"""Test infrastructure: CudaRunner's state and launch in host memory, over
+the host build of libvllt (tests/host_build.py).
+
+HostRunner keeps the runner's device buffers as CPU tensors and uses
+CudaRunner's own pieces: packer, descriptor, graph-bucket bounds, pick buffer
+and error check. Every pass then goes through the library's compiled code on
+the SIMT emulation. Set `HostRunner.lib` to the host library before building
+an engine with it. This module imports nothing from the tests package, so a
+pytest plugin that runs the reference's own test files can load it by path.
+"""
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+
+class HostRunner:
+    """CudaRunner's state and launch in host memory, over the host library."""
+
+    tp_size = 1
+    lib = None
+
+    def __init__(self, model_cfg, cache_cfg, sched_cfg=None, device=None):
+        from types import SimpleNamespace
+
+        from vllt import _lib
+        from vllt.model import DeviceWeights, initial_weights
+        from vllt.runner import CudaRunner, StepPacker
+
+        L = self.L = self.lib
+        self.model_cfg, self.dev = model_cfg, torch.device("cpu")
+        self.block_size, self.num_blocks = cache_cfg.block_size, cache_cfg.num_blocks
+        self.check_step_flags = CudaRunner.check_step_flags.__get__(self)
+        self.pick_buffer = CudaRunner.pick_buffer.__get__(self)
+        self.bucket = CudaRunner.bucket.__get__(self)
+        self.w = DeviceWeights(model_cfg, initial_weights(model_cfg), device="cpu")
+        self.head_dim = model_cfg.d_model // model_cfg.n_heads
+        shape = (model_cfg.n_layers, self.num_blocks, model_cfg.n_kv_heads, self.block_size, self.head_dim)
+        self.cache_k = torch.zeros(shape, dtype=torch.float32)
+        self.cache_v = torch.zeros(shape, dtype=torch.float32)
+        me = SimpleNamespace(model_cfg=model_cfg, w=self.w, _ptrs=self.w.pointer_arrays(), block_size=self.block_size,
+                             num_blocks=self.num_blocks, head_dim=self.head_dim, cache_k=self.cache_k,
+                             cache_v=self.cache_v)
+        self._ptrs = me._ptrs
+        self.desc = CudaRunner._make_desc(me)
+        self.qp = L.vllt_query_tile_positions(C.byref(self.desc))
+        seqs, toks = sched_cfg.max_seqs, sched_cfg.max_batched_tokens
+        self.caps = _lib.Caps(seqs, toks, min(toks, 4 * seqs), -(-model_cfg.max_seq_len // self.block_size))
+        self.meta = torch.zeros(L.vllt_meta_bytes(C.byref(self.caps)) // 4, dtype=torch.int32)
+        self.ws = torch.zeros(L.vllt_forward_workspace_bytes(C.byref(self.desc), C.byref(self.caps)), dtype=torch.uint8)
+        self.logits_dev = torch.zeros((self.caps.max_rows, self.w.vocab_padded), dtype=torch.float32)
+        self.picks_dev = torch.zeros(2 * (self.caps.max_rows + self.caps.max_seqs) + 1, dtype=torch.int32)
+        self.desc.token_source, self.desc.token_source_len = self.picks_dev.data_ptr(), self.picks_dev.numel()
+        slots = 2 * seqs
+        self.table_pool = torch.full((slots, self.caps.max_table_width), -1, dtype=torch.int32)
+        self.desc.table_pool, self.desc.table_pool_slots = self.table_pool.data_ptr(), slots
+        self.packer = StepPacker(self.block_size, self.num_blocks, model_cfg.vocab_size, self.w.rope_len, self.qp,
+                                 pool_slots=slots, pool_width=self.caps.max_table_width,
+                                 token_refs=self.picks_dev.numel())
+        self.passes = self.stand_ins = 0
+
+    @property
+    def vocab_size(self):
+        return self.model_cfg.vocab_size
+
+    def launch(self, out):
+        from vllt import _lib
+
+        if out.cow:
+            pairs = np.ascontiguousarray(np.asarray(out.cow, np.int32).reshape(-1, 2))
+            cfg = self.model_cfg
+            assert self.L.vllt_copy_blocks(self.cache_k.data_ptr(), self.cache_v.data_ptr(), pairs.ctypes.data,
+                                           len(pairs), cfg.n_layers, self.num_blocks, cfg.n_kv_heads,
+                                           self.block_size, self.head_dim, _lib.VLLT_F32, None) == 0
+        rec, bounds, rows, (S, T, R, W) = self.packer.pack(out)
+        self.stand_ins += int((rec[5 + 3 * S:5 + 3 * S + T] < 0).sum())
+        rec = np.ascontiguousarray(rec, np.int32)
+        gb = self.bucket(bounds)  # the bounds of the CUDA graph that would serve this pass
+        rc = self.L.vllt_forward(C.byref(self.desc), rec.ctypes.data, C.byref(self.caps), C.byref(gb),
+                                 self.meta.data_ptr(), self.ws.data_ptr(), self.ws.numel(), self.logits_dev.data_ptr(),
+                                 None)
+        assert rc == 0, self.L.vllt_last_error()
+        self.passes += 1
+        return rows, R
+
+    def execute(self, out):
+        """(logits float32 [n_rows, vocab], rows), as CudaRunner.execute returns
+        them to an unmodified LLMEngine (vllmlite/runner.py:62-100)."""
+        rows, R = self.launch(out)
+        self.check_step_flags(int(self.meta[7]))
+        return self.logits_dev[:R, :self.model_cfg.vocab_size].numpy().copy(), rows
+
+    @property
+    def cache_bytes(self) -> int:
+        return 2 * self.cache_k.numel() * self.cache_k.element_size()

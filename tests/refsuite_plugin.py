@@ -1,0 +1,51 @@
+"""Test infrastructure: a pytest plugin that puts libvllt's runner behind the
+reference's own engine tests (tests/test_reference_suite_host.py loads it into
+a pytest run over the reference's test files).
+
+At configure time it builds libvllt for the host (host_build.py) and makes
+`vllmlite.engine.NumpyRunner`, the runner `LLMEngine.__init__` constructs
+(vllmlite/engine.py:46), build a HostRunner (host_runner.py): CudaRunner's
+packer, descriptor and flag checks over the library's compiled forward. That
+is the one-line backend switch a maintainer would add, so every LLMEngine the
+reference's tests build runs its passes through libvllt's code. Imported as a
+top-level module (this directory on sys.path), since the reference's tests
+own the package name `tests`.
+"""
+
+import os
+import tempfile
+
+_STATE = {}
+
+
+def pytest_configure(config):
+    import host_build
+    import host_runner
+
+    lib = host_build.build_library_host(os.environ.get("VLLT_REFSUITE_BUILD") or tempfile.mkdtemp())
+    if lib is None:
+        raise RuntimeError("g++ is not available")
+    host_runner.HostRunner.lib = lib
+    import vllt._lib as _lib
+    import vllmlite.engine as E
+    from types import SimpleNamespace
+
+    _lib.stream_handle = lambda stream=None: 0  # the host build has no streams
+    # LLMEngine passes only the model and cache configs (engine.py:46); the
+    # capacities cover the reference tests' scheduler settings
+    sched = SimpleNamespace(max_seqs=64, max_batched_tokens=4096)
+
+    def runner(model_cfg, cache_cfg):
+        r = host_runner.HostRunner(model_cfg, cache_cfg, sched)
+        _STATE["passes"] = _STATE.get("passes", 0)
+        _STATE.setdefault("runners", []).append(r)
+        return r
+
+    _STATE["orig"] = E.NumpyRunner
+    E.NumpyRunner = runner
+
+
+def pytest_terminal_summary(terminalreporter):
+    runners = _STATE.get("runners", [])
+    passes = sum(r.passes for r in runners)
+    terminalreporter.write_line(f"VLLT_REFSUITE runners={len(runners)} forward_passes={passes}")

@@ -362,16 +362,19 @@ SIMT_INTERNAL inline void switch_next() {
     if (!c.f[i].done && c.f[i].waiting == -2) {
       if (i == from) return;
       c.cur = i;
+      void** save = &c.f[from].sp;  // no access of the CTA's state between the
+      void* to = c.f[i].sp;         // race checker's context switch and the stack's
       to_context(c, i);
-      stack_switch(&c.f[from].sp, c.f[i].sp);
+      stack_switch(save, to);
       ::threadIdx = c.f[c.cur].tid;  // resumed: this fiber's index again
       return;
     }
   }
   // nobody can run: every live thread waits on a barrier that cannot complete
   c.deadlock = true;
+  void** save = &c.f[from].sp;
   to_context(c, -1);
-  stack_switch(&c.f[from].sp, c.main_sp);
+  stack_switch(save, c.main_sp);
 }
 
 // Let the other runnable threads of the CTA run (a spin-wait's iteration).
@@ -469,8 +472,9 @@ SIMT_INTERNAL inline void complete_cluster_barrier() {
   Cta& c = cta();
   if (!cluster_os_barrier()) {  // the launch fails: back to the CTA's scheduler
     c.deadlock = true;
+    void** save = &c.f[c.cur].sp;
     to_context(c, -1);
-    stack_switch(&c.f[c.cur].sp, c.main_sp);
+    stack_switch(save, c.main_sp);
   }
   release(kClusterGroup);
 }
@@ -500,15 +504,17 @@ SIMT_INTERNAL inline void switch_to(int i) {
   const int from = c.cur;
   if (i == from) return;
   c.cur = i;
+  void** save = &c.f[from].sp;
+  void* to = c.f[i].sp;
   to_context(c, i);
-  stack_switch(&c.f[from].sp, c.f[i].sp);
+  stack_switch(save, to);
   ::threadIdx = c.f[c.cur].tid;
 }
 
 SIMT_INTERNAL inline void exit_thread() {
   Cta& c = cta();
-  hb_release(&c.hb_end);
-  Fiber& me = c.f[c.cur];
+  Fiber* f = c.f.data();
+  Fiber& me = f[c.cur];
   me.done = true;
   ++c.done;
   const int w = (int)((me.tid.z * ::blockDim.y + me.tid.y) * ::blockDim.x + me.tid.x) / 32;
@@ -517,13 +523,27 @@ SIMT_INTERNAL inline void exit_thread() {
   if (c.arrived_cta > 0 && c.arrived_cta >= c.live_cta) release(-1);
   if (c.arrived_warp[w] > 0 && c.arrived_warp[w] >= c.live_warp[w]) release(w);
   if (c.arrived_cluster > 0 && c.arrived_cluster >= c.live_cta) complete_cluster_barrier();
-  if (c.done == c.n) {  // the last thread: back to the launch
-    to_context(c, -1);
-    stack_switch(&me.sp, c.main_sp);
+  // next: another runnable thread, else (the last thread, or every thread left
+  // waits on a barrier that cannot complete) the CTA's scheduler
+  int next = -1;
+  for (int k = 1; c.done < c.n && k <= c.n && next < 0; ++k) {
+    const int i = (c.cur + k) % c.n;
+    if (!f[i].done && f[i].waiting == -2) next = i;
   }
-  switch_next();
-  to_context(c, -1);
-  stack_switch(&me.sp, c.main_sp);  // not reached unless stopped
+  if (next < 0 && c.done < c.n) c.deadlock = true;
+  void** save = &me.sp;
+  void* to = next < 0 ? c.main_sp : f[next].sp;
+#if defined(__SANITIZE_THREAD__)
+  void* ctx = next < 0 ? c.tsan_main : c.tsan_fiber.data()[next];
+#endif
+  if (next >= 0) c.cur = next;
+  // This thread's last access of the CTA's state: the scheduler's acquire of
+  // hb_end at the CTA's end then orders all of them before what follows.
+  hb_release(&c.hb_end);
+#if defined(__SANITIZE_THREAD__)
+  __tsan_switch_to_fiber(ctx, __tsan_switch_to_fiber_no_sync);
+#endif
+  stack_switch(save, to);  // never resumed
 }
 
 SIMT_INTERNAL inline void trampoline() {
@@ -578,8 +598,9 @@ SIMT_INTERNAL inline bool run_cta(dim3 bid, dim3 block, const std::function<void
   if (cta_start_hook()) cta_start_hook()();
   hb_release(&c.hb_begin);
   c.cur = schedule_seed() ? (int)(next_random() % (uint32_t)n) : 0;
+  void* first = c.f[c.cur].sp;
   to_context(c, c.cur);
-  stack_switch(&c.main_sp, c.f[c.cur].sp);
+  stack_switch(&c.main_sp, first);
   hb_acquire(&c.hb_end);
   if (c.deadlock) {
     std::fprintf(stderr, "simt: block (%u,%u,%u): threads wait on barriers that cannot complete\n", bid.x, bid.y,

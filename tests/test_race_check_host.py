@@ -23,7 +23,10 @@ such ordering puts one after the other, are reported.
     reduction) including a dropped TMA load's error path, the tensor-core
     prefill attention, the TMA decode kernel and its stall injection, the
     generic attention kernel with split-K, and the sampling, metadata, norm
-    and cache kernels: no report.
+    and cache kernels: no report. The same builds carry
+    UndefinedBehaviorSanitizer (VLLT_HOST_UBSAN=1: signed overflow in index
+    arithmetic, shifts, misaligned or null accesses, out-of-range
+    conversions stop the process); the whole host suite also passes with it.
 
 Found this way: the split-K GEMM's TMA producer read a failure flag that
 the MMA issuer could be writing, to decide whether to wait for its copies
@@ -47,13 +50,24 @@ TSAN = tsan_runtime()
 pytestmark = pytest.mark.skipif(TSAN is None, reason="g++ has no ThreadSanitizer runtime")
 
 
-def tsan_env(log_path=None):
-    env = dict(os.environ, LD_PRELOAD=TSAN, VLLT_HOST_TSAN="1", VLLT_SIMT_THREADS="4",
+# The two sanitizer runtimes see each other: UBSan's runtime probes memory
+# through a pipe when a thread exits, and ThreadSanitizer's pipe interceptor
+# reports those probes of two exiting threads as a race.
+SUPPRESSIONS = "race:__sanitizer::IsAccessibleMemoryRange\n"
+
+
+def tsan_env(log_path=None, tmp=None):
+    opts = "exitcode=66:history_size=3:report_signal_unsafe=0" + (f":log_path={log_path}" if log_path else "")
+    if tmp is not None:
+        sup = os.path.join(str(tmp), "tsan.supp")
+        with open(sup, "w") as f:
+            f.write(SUPPRESSIONS)
+        opts += f":suppressions={sup}"
+    env = dict(os.environ, LD_PRELOAD=TSAN, VLLT_HOST_TSAN="1", VLLT_HOST_UBSAN="1", VLLT_SIMT_THREADS="4",
                # no BLAS worker threads: the builds fork, and the sanitizer's
                # fork handling trips over BLAS's pthread_join at fork
                OPENBLAS_NUM_THREADS="1", OMP_NUM_THREADS="1", MKL_NUM_THREADS="1",
-               TSAN_OPTIONS="exitcode=66:history_size=3:report_signal_unsafe=0"
-               + (f":log_path={log_path}" if log_path else ""),
+               TSAN_OPTIONS=opts,
                PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "vllm-lite_b200"),
                                            os.path.join(ROOT, "baseline", "_ref")]))
     return env
@@ -74,7 +88,7 @@ sys.exit(0 if rc else 3)
 def test_planted_races_are_reported_and_ordered_kernels_are_not(tmp_path, case, line):
     lib = build_harness("race_host", str(tmp_path), tsan=True, load=False)
     for ordered in (1, 0):
-        r = subprocess.run([sys.executable, "-c", RUN_CASE, lib, case, str(ordered)], env=tsan_env(),
+        r = subprocess.run([sys.executable, "-c", RUN_CASE, lib, case, str(ordered)], env=tsan_env(tmp=tmp_path),
                            capture_output=True, text=True, timeout=300)
         if ordered:
             assert r.returncode == 0 and "ThreadSanitizer" not in r.stderr, r.stderr[-3000:]
@@ -118,10 +132,10 @@ CASES = [
 def test_library_kernels_have_no_data_race(tmp_path):
     log = str(tmp_path / "tsan")
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", *CASES],
-                       cwd=ROOT, env=tsan_env(log), capture_output=True, text=True, timeout=1800)
+                       cwd=ROOT, env=tsan_env(log, tmp_path), capture_output=True, text=True, timeout=1800)
     reports = ""
     for f in sorted(os.listdir(tmp_path)):
-        if f.startswith("tsan"):
+        if f.startswith("tsan") and not f.endswith(".supp"):
             reports += open(tmp_path / f, errors="replace").read()
-    assert r.returncode == 0, (r.stdout[-3000:], reports[:6000])
+    assert r.returncode == 0, (r.stdout[-3000:], r.stderr[-3000:], reports[:6000])
     assert "ThreadSanitizer" not in reports, reports[:6000]
