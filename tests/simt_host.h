@@ -668,9 +668,18 @@ inline GridPool& grid_pool() {
 // CTA's index, so it does not depend on which thread runs it. With a cluster
 // of `cluster` CTAs along x, the CTAs of one cluster run at the same time,
 // each on its own OS thread, and clusters one after another.
+// A B200 CTA can have at most 227 KB of dynamic shared memory (opted in),
+// grids at most 2^31 - 1 CTAs along x and 65,535 along y and z.
+constexpr size_t kMaxDynamicSmem = 227 * 1024;
+
 inline bool run_grid(dim3 grid, dim3 block, size_t smem, const std::function<void()>& body, unsigned cluster = 1) {
   const int n = (int)(block.x * block.y * block.z);
   if (n < 1 || n > kMaxThreads || cluster < 1 || grid.x % cluster) return false;
+  if (smem > kMaxDynamicSmem || grid.y > 65535 || grid.z > 65535 || grid.x > 2147483647u) {
+    std::fprintf(stderr, "simt: launch of %u x %u x %u CTAs with %zu bytes of dynamic shared memory exceeds the "
+                 "device's limits\n", grid.x, grid.y, grid.z, smem);
+    return false;
+  }
   ::gridDim = grid;
   ::blockDim = block;
   const uint64_t seed = schedule_seed();
