@@ -63,7 +63,8 @@ def tsan_env(log_path=None, tmp=None):
         with open(sup, "w") as f:
             f.write(SUPPRESSIONS)
         opts += f":suppressions={sup}"
-    env = dict(os.environ, LD_PRELOAD=TSAN, VLLT_HOST_TSAN="1", VLLT_HOST_UBSAN="1", VLLT_SIMT_THREADS="4",
+    env = dict(os.environ, LD_PRELOAD=TSAN, VLLT_HOST_TSAN="1", VLLT_HOST_UBSAN="1",
+               VLLT_SIMT_THREADS=str(os.cpu_count() or 4),
                # no BLAS worker threads: the builds fork, and the sanitizer's
                # fork handling trips over BLAS's pthread_join at fork
                OPENBLAS_NUM_THREADS="1", OMP_NUM_THREADS="1", MKL_NUM_THREADS="1",
