@@ -405,3 +405,72 @@ def test_device_helpers_do_not_call_themselves():
             n += 1
             assert not re.search(r"\b%s\(" % name, body), f"{os.path.basename(f)}: {name} calls itself"
     assert n > 30
+
+
+# The PTX instructions the library's inline assembly uses. The host build runs
+# each helper's host branch, so the device branches' bodies are checked only
+# on a GPU; this list holds what ran on the B200 (plus ld.shared::cluster.s32,
+# the cluster's abort-flag read), and a new instruction has to be added here
+# on purpose.
+PTX_VOCABULARY = {
+    "barrier.cluster.arrive.release.aligned", "barrier.cluster.wait.acquire.aligned",
+    "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes",
+    "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes",
+    "cp.async.cg.shared.global", "cp.async.commit_group", "cp.async.wait_group", "ex2.approx.ftz.f32",
+    "fence.mbarrier_init.release.cluster", "fence.proxy.async.shared::cta", "griddepcontrol.launch_dependents",
+    "griddepcontrol.wait", "ld.shared::cluster.s32", "ld.shared::cluster.v4.f32", "mapa.shared::cluster.u32",
+    "mbarrier.arrive.expect_tx.shared::cta.b64", "mbarrier.arrive.shared::cta.b64", "mbarrier.init.shared::cta.b64",
+    "mbarrier.try_wait.parity.shared::cta.b64", "mov.u32", "mov.u64", "selp.u32", "setp.ne.b32",
+    "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32",
+    "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64",
+    "tcgen05.dealloc.cta_group::1.sync.aligned.b32", "tcgen05.fence::after_thread_sync",
+    "tcgen05.fence::before_thread_sync", "tcgen05.ld.sync.aligned.32x32b.x32.b32", "tcgen05.mma.cta_group::1.kind::f16",
+    "tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned", "tcgen05.st.sync.aligned.32x32b.x32.b32",
+    "tcgen05.wait::ld.sync.aligned", "tcgen05.wait::st.sync.aligned",
+}
+
+
+def _asm_templates(src):
+    """The instruction templates of every asm statement: the string literals
+    before the statement's first operand colon."""
+    import re
+
+    out = []
+    for m in re.finditer(r"\basm\s*(?:volatile)?\s*\(", src):
+        i, depth, in_str, tpl = m.end(), 1, False, []
+        while depth:
+            c = src[i]
+            if in_str:
+                if c == "\\":
+                    tpl.append(src[i:i + 2])
+                    i += 1
+                elif c == '"':
+                    in_str = False
+                else:
+                    tpl.append(c)
+            elif c == '"':
+                in_str = True
+            elif c == "(":
+                depth += 1
+            elif c == ")":
+                depth -= 1
+            elif c == ":":
+                break
+            i += 1
+        out.append("".join(tpl))
+    return out
+
+
+def test_inline_ptx_uses_only_the_instructions_that_ran_on_the_b200():
+    import glob
+    import re
+
+    used = set()
+    for f in glob.glob(os.path.join(ROOT, "vllm-lite_b200", "csrc", "*")):
+        for tpl in _asm_templates(open(f).read()):
+            for stmt in re.split(r";|\\n", tpl):  # statements; a "{ ... }" scope opens one
+                stmt = stmt.strip().lstrip("{").strip()
+                if stmt and stmt != "}" and not stmt.startswith("."):  # .reg declarations
+                    used.add(stmt.split()[0])
+    assert used, "no inline assembly found"
+    assert used <= PTX_VOCABULARY, sorted(used - PTX_VOCABULARY)
