@@ -16,9 +16,15 @@ import torch
 
 
 class HostRunner:
-    """CudaRunner's state and launch in host memory, over the host library."""
+    """CudaRunner's state and launch in host memory, over the host library;
+    with `bf16` (HostLlamaRunner) LlamaRunner's: the Llama-shaped model's bf16
+    weights and caches and its descriptor, so the forward takes the bf16
+    path (tcgen05 GEMMs, TMA decode, tensor-core prefill)."""
 
     tp_size = 1
+    tp_rank = 0
+    tp_comm = None
+    bf16 = False
     lib = None
 
     def __init__(self, model_cfg, cache_cfg, sched_cfg=None, device=None):
@@ -34,16 +40,24 @@ class HostRunner:
         self.check_step_flags = CudaRunner.check_step_flags.__get__(self)
         self.pick_buffer = CudaRunner.pick_buffer.__get__(self)
         self.bucket = CudaRunner.bucket.__get__(self)
-        self.w = DeviceWeights(model_cfg, initial_weights(model_cfg), device="cpu")
         self.head_dim = model_cfg.d_model // model_cfg.n_heads
         shape = (model_cfg.n_layers, self.num_blocks, model_cfg.n_kv_heads, self.block_size, self.head_dim)
-        self.cache_k = torch.zeros(shape, dtype=torch.float32)
-        self.cache_v = torch.zeros(shape, dtype=torch.float32)
-        me = SimpleNamespace(model_cfg=model_cfg, w=self.w, _ptrs=self.w.pointer_arrays(), block_size=self.block_size,
-                             num_blocks=self.num_blocks, head_dim=self.head_dim, cache_k=self.cache_k,
-                             cache_v=self.cache_v)
-        self._ptrs = me._ptrs
-        self.desc = CudaRunner._make_desc(me)
+        dt = torch.bfloat16 if self.bf16 else torch.float32
+        self.cache_k = torch.zeros(shape, dtype=dt)
+        self.cache_v = torch.zeros(shape, dtype=dt)
+        if self.bf16:
+            from vllt.llama import LlamaRunner, LlamaWeights
+
+            self.w = LlamaWeights(model_cfg, "cpu")
+            self._ptrs = self.w.pointer_arrays()
+            self.desc = LlamaRunner._make_desc(self)
+        else:
+            self.w = DeviceWeights(model_cfg, initial_weights(model_cfg), device="cpu")
+            me = SimpleNamespace(model_cfg=model_cfg, w=self.w, _ptrs=self.w.pointer_arrays(),
+                                 block_size=self.block_size, num_blocks=self.num_blocks, head_dim=self.head_dim,
+                                 cache_k=self.cache_k, cache_v=self.cache_v)
+            self._ptrs = me._ptrs
+            self.desc = CudaRunner._make_desc(me)
         self.qp = L.vllt_query_tile_positions(C.byref(self.desc))
         seqs, toks = sched_cfg.max_seqs, sched_cfg.max_batched_tokens
         self.caps = _lib.Caps(seqs, toks, min(toks, 4 * seqs), -(-model_cfg.max_seq_len // self.block_size))
@@ -72,7 +86,8 @@ class HostRunner:
             cfg = self.model_cfg
             assert self.L.vllt_copy_blocks(self.cache_k.data_ptr(), self.cache_v.data_ptr(), pairs.ctypes.data,
                                            len(pairs), cfg.n_layers, self.num_blocks, cfg.n_kv_heads,
-                                           self.block_size, self.head_dim, _lib.VLLT_F32, None) == 0
+                                           self.block_size, self.head_dim,
+                                           _lib.VLLT_BF16 if self.bf16 else _lib.VLLT_F32, None) == 0
         rec, bounds, rows, (S, T, R, W) = self.packer.pack(out)
         self.stand_ins += int((rec[5 + 3 * S:5 + 3 * S + T] < 0).sum())
         rec = np.ascontiguousarray(rec, np.int32)
@@ -94,3 +109,9 @@ class HostRunner:
     @property
     def cache_bytes(self) -> int:
         return 2 * self.cache_k.numel() * self.cache_k.element_size()
+
+
+class HostLlamaRunner(HostRunner):
+    """LlamaRunner (the bf16 path, one rank) over the host library."""
+
+    bf16 = True

@@ -18,6 +18,10 @@ prefix with the prefix cache, so copy-on-write runs through the compiled
 copy kernel) and C5 (periodic prompts with speculative k = 4, verified by
 the compiled accept kernel against the k = 0 streams). Greedy streams do not
 depend on which requests share a batch, so a subset of each is run.
+
+The C4 serving path (HostLlamaRunner: LlamaRunner's bf16 weights, caches and
+descriptor) runs the same way on a narrow Llama-shaped model, against the
+reference's LLMEngine over the same runner.
 """
 
 import pytest
@@ -85,3 +89,45 @@ def test_engine_streams_through_the_compiled_device_path(host_lib, workload, pic
         assert eng.passes_ahead >= eng.total_steps // 2 and eng.runner.stand_ins > 0
     if prefix:
         assert eng.scheduler.blocks.allocator.hits > 0
+
+
+def test_llama_engine_through_the_compiled_bf16_path(host_lib):
+    """The C4 serving path (the bench's gpu_engine with LlamaRunner) on a
+    narrow Llama-shaped model: GpuLLMEngine over the bf16 host runner (device
+    greedy and temperature picks, run-ahead) gives the token streams of the
+    reference's unmodified LLMEngine over the same runner, whose host
+    sample() reads the logits the same compiled forward produced. Chunked
+    prefill (budget 96) and a prompt past 256 tokens put tensor-core prefill
+    tiles over cached prefixes in the passes; decode rows take the TMA decode
+    kernel and every projection a tcgen05 GEMM."""
+    import numpy as np
+    from vllmlite.config import CacheConfig, EngineConfig, ModelConfig, SchedulerConfig
+    from vllmlite.sequence import SamplingParams
+
+    from tests.host_runner import HostLlamaRunner
+    from vllt.engine import GpuLLMEngine, cuda_engine
+
+    HostLlamaRunner.lib = host_lib
+    host_lib.vllt_host_mma_count.restype = __import__("ctypes").c_int64
+    mc = ModelConfig(n_layers=2, n_heads=2, n_kv_heads=1, d_model=256, d_ff=512, vocab_size=300, max_seq_len=1024,
+                     seed=3)
+    cfg = EngineConfig(model=mc, cache=CacheConfig(block_size=16, num_blocks=96),
+                       scheduler=SchedulerConfig(max_seqs=4, max_batched_tokens=96))
+    rng = np.random.default_rng(5)
+    prompts = [[int(t) for t in rng.integers(1, 300, size=n)] for n in (40, 300, 7, 120)]
+    params = [SamplingParams(max_tokens=10, temperature=0.0, ignore_eos=True) for _ in range(3)]
+    params.append(SamplingParams(max_tokens=10, temperature=0.8, top_p=0.9, seed=11, ignore_eos=True))
+
+    def streams(eng):
+        ids = [eng.add_request(params=p, prompt_token_ids=t) for t, p in zip(prompts, params)]
+        while eng.has_work:
+            eng.step()
+        return [eng.seqs[i].output_token_ids for i in ids]
+
+    mma0 = host_lib.vllt_host_mma_count()
+    want = streams(cuda_engine(cfg, runner_cls=HostLlamaRunner))
+    eng = cuda_engine(cfg, engine_cls=GpuLLMEngine.resolve(), runner_cls=HostLlamaRunner)
+    assert streams(eng) == want
+    assert all(len(s) == 10 for s in want)
+    assert eng.passes_ahead > 0
+    assert host_lib.vllt_host_mma_count() > mma0
