@@ -7,7 +7,10 @@ At configure time it builds libvllt for the host (host_build.py) and makes
 (vllmlite/engine.py:46), build a HostRunner (host_runner.py): CudaRunner's
 packer, descriptor and flag checks over the library's compiled forward. That
 is the one-line backend switch a maintainer would add, so every LLMEngine the
-reference's tests build runs its passes through libvllt's code. Imported as a
+reference's tests build runs its passes through libvllt's code. With
+VLLT_REFSUITE_ENGINE=gpu (or gpu-run-ahead) `vllmlite.engine.LLMEngine`
+itself becomes the product's GpuLLMEngine (device token picks; run-ahead on or
+off), which the tests then construct in its place. Imported as a
 top-level module (this directory on sys.path), since the reference's tests
 own the package name `tests`.
 """
@@ -43,6 +46,13 @@ def pytest_configure(config):
 
     _STATE["orig"] = E.NumpyRunner
     E.NumpyRunner = runner
+    mode = os.environ.get("VLLT_REFSUITE_ENGINE", "reference")
+    if mode != "reference":  # the product's engine in LLMEngine's place: device picks
+        from vllt.engine import GpuLLMEngine
+
+        cls = GpuLLMEngine.resolve()
+        cls.run_ahead = mode == "gpu-run-ahead"
+        E.LLMEngine = cls
 
 
 def pytest_terminal_summary(terminalreporter):

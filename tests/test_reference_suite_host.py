@@ -1,11 +1,14 @@
 """CPU: the reference's own engine, speculative-decoding and HTTP API tests,
-run unmodified with libvllt's runner behind LLMEngine.
+run unmodified with libvllt behind them.
 
 tests/refsuite_plugin.py makes `vllmlite.engine.NumpyRunner` (what
 LLMEngine.__init__ constructs, vllmlite/engine.py:46) build a HostRunner over
 the host build of libvllt: the backend switch a maintainer would add. The
 reference's test files then run as they are, read from the reference's source
-tree (this test is skipped where that tree is absent):
+tree (this test is skipped where that tree is absent), twice: with the
+reference's LLMEngine over that runner (its host sample() on the logits), and
+with the product's GpuLLMEngine in LLMEngine's place (device token picks and
+run-ahead, as `vllt.engine.gpu_engine` serves):
   * tests/test_engine.py: its invariance grid (block sizes 1-64, prefix
     caching, chunk budgets, no chunking, batch composition, preemption with
     and without the prefix cache), block accounting, prefix-cache hits, stop
@@ -33,8 +36,10 @@ FILES = ("test_engine.py", "test_speculative.py", "test_api.py")
 
 @pytest.mark.skipif(not all(os.path.exists(os.path.join(REFERENCE, "tests", f)) for f in FILES),
                     reason="the reference's source tree is not here")
-def test_reference_engine_tests_pass_with_libvllt_behind_the_engine(tmp_path):
+@pytest.mark.parametrize("engine", ["reference", "gpu-run-ahead"])
+def test_reference_engine_tests_pass_with_libvllt_behind_the_engine(tmp_path, engine):
     env = dict(os.environ, PYTHONDONTWRITEBYTECODE="1", VLLT_REFSUITE_BUILD=str(tmp_path),
+               VLLT_REFSUITE_ENGINE=engine,
                PYTHONPATH=os.pathsep.join([os.path.join(ROOT, "tests"), os.path.join(ROOT, "vllm-lite_b200"),
                                            REFERENCE]))
     files = [os.path.join(REFERENCE, "tests", f) for f in FILES]

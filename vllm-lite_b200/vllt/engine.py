@@ -360,7 +360,17 @@ def _make_gpu_engine(Base):
 
         @property
         def has_work(self) -> bool:
-            return self.scheduler.has_work or self._next is not None
+            """The reference's answer (vllmlite/engine.py:96), plus a pass
+            launched ahead that still has a live sequence or undelivered
+            reports: one whose sequences were all aborted since is no work,
+            so an abort of the last request leaves the engine idle at once,
+            as in the reference (the next step() still collects that pass)."""
+            if self.scheduler.has_work:
+                return True
+            if self._next is None:
+                return False
+            sched, dropped, _ = self._next
+            return bool(dropped) or any(not item.seq.status.finished for item in sched.scheduled)
 
         def can_run_ahead(self, sched, pend) -> bool:
             """Whether the pass after `sched` can be scheduled before this
