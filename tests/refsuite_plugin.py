@@ -10,7 +10,11 @@ is the one-line backend switch a maintainer would add, so every LLMEngine the
 reference's tests build runs its passes through libvllt's code. With
 VLLT_REFSUITE_ENGINE=gpu (or gpu-run-ahead) `vllmlite.engine.LLMEngine`
 itself becomes the product's GpuLLMEngine (device token picks; run-ahead on or
-off), which the tests then construct in its place. Imported as a
+off), which the tests then construct in its place. The reference's
+hash_block (vllmlite/block.py:34), which the BlockManager's prefix cache and
+the block tests call, becomes the device prefix hash's own code
+(csrc/prefix_hash.cuh, the function vllt_prefix_hash_chains runs per block)
+compiled for the host. Imported as a
 top-level module (this directory on sys.path), since the reference's tests
 own the package name `tests`.
 """
@@ -46,6 +50,7 @@ def pytest_configure(config):
 
     _STATE["orig"] = E.NumpyRunner
     E.NumpyRunner = runner
+    _patch_hash_block(host_build)
     mode = os.environ.get("VLLT_REFSUITE_ENGINE", "reference")
     if mode != "reference":  # the product's engine in LLMEngine's place: device picks
         from vllt.engine import GpuLLMEngine
@@ -55,7 +60,30 @@ def pytest_configure(config):
         E.LLMEngine = cls
 
 
+def _patch_hash_block(host_build):
+    import ctypes
+
+    import vllmlite.block as B
+    import vllmlite.block_manager as BM
+    import numpy as np
+
+    lib = host_build.build_harness("prefix_hash_host", os.environ.get("VLLT_REFSUITE_BUILD") or tempfile.mkdtemp())
+    lib.hash_chain_host.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+
+    def hash_block(prev_hash, token_ids):
+        toks = np.ascontiguousarray(np.asarray(token_ids, np.int64).astype(np.int32))
+        out = ctypes.create_string_buffer(32)
+        prev = ctypes.create_string_buffer(prev_hash.encode(), 32) if prev_hash else None
+        lib.hash_chain_host(ctypes.cast(prev, ctypes.c_void_p) if prev else None, toks.ctypes.data if toks.size else None,
+                            1, int(toks.size), out)
+        _STATE["hashes"] = _STATE.get("hashes", 0) + 1
+        return out.raw.decode()
+
+    B.hash_block = BM.hash_block = hash_block
+
+
 def pytest_terminal_summary(terminalreporter):
     runners = _STATE.get("runners", [])
     passes = sum(r.passes for r in runners)
-    terminalreporter.write_line(f"VLLT_REFSUITE runners={len(runners)} forward_passes={passes}")
+    terminalreporter.write_line(f"VLLT_REFSUITE runners={len(runners)} forward_passes={passes} "
+                                f"block_hashes={_STATE.get('hashes', 0)}")
