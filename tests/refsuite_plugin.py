@@ -14,7 +14,10 @@ off), which the tests then construct in its place. The reference's
 hash_block (vllmlite/block.py:34), which the BlockManager's prefix cache and
 the block tests call, becomes the device prefix hash's own code
 (csrc/prefix_hash.cuh, the function vllt_prefix_hash_chains runs per block)
-compiled for the host. Imported as a
+compiled for the host. And the reference's paged_attention
+(vllmlite/attention.py:59), which its attention tests call, becomes
+vllt.ops.paged_attention, the NumPy-signature drop-in, over the host build's
+C ABI. Imported as a
 top-level module (this directory on sys.path), since the reference's tests
 own the package name `tests`.
 """
@@ -51,6 +54,7 @@ def pytest_configure(config):
     _STATE["orig"] = E.NumpyRunner
     E.NumpyRunner = runner
     _patch_hash_block(host_build)
+    _patch_paged_attention(lib)
     mode = os.environ.get("VLLT_REFSUITE_ENGINE", "reference")
     if mode != "reference":  # the product's engine in LLMEngine's place: device picks
         from vllt.engine import GpuLLMEngine
@@ -82,8 +86,24 @@ def _patch_hash_block(host_build):
     B.hash_block = BM.hash_block = hash_block
 
 
+def _patch_paged_attention(lib):
+    import vllmlite.attention as A
+    import vllt._lib as _lib
+    import vllt.ops as ops
+
+    _lib._lib = lib  # vllt's ops load the host build of the library
+    ops.stream_handle = lambda stream=None: 0
+
+    def paged_attention(q, cache_k, cache_v, read_slots, n_kv_heads, scale):
+        _STATE["attention_calls"] = _STATE.get("attention_calls", 0) + 1
+        return ops.paged_attention(q, cache_k, cache_v, read_slots, n_kv_heads, scale, device="cpu")
+
+    A.paged_attention = paged_attention
+
+
 def pytest_terminal_summary(terminalreporter):
     runners = _STATE.get("runners", [])
     passes = sum(r.passes for r in runners)
     terminalreporter.write_line(f"VLLT_REFSUITE runners={len(runners)} forward_passes={passes} "
-                                f"block_hashes={_STATE.get('hashes', 0)}")
+                                f"block_hashes={_STATE.get('hashes', 0)} "
+                                f"attention_calls={_STATE.get('attention_calls', 0)}")

@@ -1,5 +1,5 @@
-"""CPU: the reference's own engine, speculative-decoding, HTTP API and block
-tests, run unmodified with libvllt behind them.
+"""CPU: the reference's own engine, speculative-decoding, HTTP API, block and
+attention tests, run unmodified with libvllt behind them.
 
 tests/refsuite_plugin.py makes `vllmlite.engine.NumpyRunner` (what
 LLMEngine.__init__ constructs, vllmlite/engine.py:46) build a HostRunner over
@@ -20,7 +20,10 @@ run-ahead, as `vllt.engine.gpu_engine` serves):
     metrics and concurrent requests sharing one engine;
   * tests/test_block.py: the block allocator and hash_block's chaining, with
     hash_block itself (and so every prefix-cache lookup of the runs above)
-    replaced by the device prefix hash's code compiled for the host.
+    replaced by the device prefix hash's code compiled for the host;
+  * tests/test_attention.py: paged attention against its dense restatement
+    (rtol 1e-4) on the reference's grid, with paged_attention replaced by
+    vllt.ops.paged_attention, the NumPy-signature drop-in, over the C ABI.
 Every one must pass, and the plugin's count shows the passes ran through
 libvllt (one runner per engine the tests built).
 """
@@ -34,7 +37,7 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REFERENCE = os.environ.get("VLLT_REFERENCE_TREE", "/root/reference")
-FILES = ("test_engine.py", "test_speculative.py", "test_api.py", "test_block.py")
+FILES = ("test_engine.py", "test_speculative.py", "test_api.py", "test_block.py", "test_attention.py")
 
 
 @pytest.mark.skipif(not all(os.path.exists(os.path.join(REFERENCE, "tests", f)) for f in FILES),
@@ -50,7 +53,9 @@ def test_reference_engine_tests_pass_with_libvllt_behind_the_engine(tmp_path, en
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "refsuite_plugin", "-p", "no:cacheprovider",
                         *files], cwd=str(tmp_path), env=env, capture_output=True, text=True, timeout=1800)
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
-    m = re.search(r"VLLT_REFSUITE runners=(\d+) forward_passes=(\d+) block_hashes=(\d+)", r.stdout)
-    assert m and int(m.group(1)) > 40 and int(m.group(2)) > 1000 and int(m.group(3)) > 100, r.stdout[-2000:]
+    m = re.search(r"runners=(\d+) forward_passes=(\d+) block_hashes=(\d+) attention_calls=(\d+)", r.stdout)
+    assert m, r.stdout[-2000:]
+    runners, passes, hashes, attention = (int(x) for x in m.groups())
+    assert runners > 40 and passes > 1000 and hashes > 100 and attention >= 27, r.stdout[-2000:]
     done = re.search(r"(\d+) passed", r.stdout)
-    assert done and "failed" not in r.stdout.splitlines()[-1] and int(done.group(1)) >= 60, r.stdout[-2000:]
+    assert done and "failed" not in r.stdout.splitlines()[-1] and int(done.group(1)) >= 90, r.stdout[-2000:]

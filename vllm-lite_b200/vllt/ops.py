@@ -98,17 +98,18 @@ def attention_flags(workspace) -> int:
     return int(workspace[:4].view(__import__("torch").int32).item())
 
 
-def paged_attention(q, cache_k, cache_v, read_slots, n_kv_heads, scale):
+def paged_attention(q, cache_k, cache_v, read_slots, n_kv_heads, scale, *, device=None):
     """NumPy drop-in for vllmlite.attention.paged_attention (one sequence).
 
-    q [q_len, H, D]; cache_* [slots, n_kv, D]; read_slots [ctx]. Runs on the
-    current CUDA device and returns float32 [q_len, H, D].
+    q [q_len, H, D]; cache_* [slots, n_kv, D]; read_slots [ctx]. Runs on
+    `device` (default: the current CUDA device) and returns float32
+    [q_len, H, D].
     """
     import torch
 
     q = np.asarray(q, np.float32)
     q_len, H, D = q.shape
-    dev = torch.device("cuda", torch.cuda.current_device())
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     ck = torch.from_numpy(np.ascontiguousarray(cache_k, np.float32)).to(dev)
     cv = torch.from_numpy(np.ascontiguousarray(cache_v, np.float32)).to(dev)
     slots_n, n_kv, _ = ck.shape
