@@ -32,7 +32,9 @@ def pytest_configure(config):
     import host_build
     import host_runner
 
-    lib = host_build.build_library_host(os.environ.get("VLLT_REFSUITE_BUILD") or tempfile.mkdtemp())
+    prebuilt = os.environ.get("VLLT_REFSUITE_LIB")  # a host build made by the calling test session
+    lib = (host_build.load_library_host(prebuilt) if prebuilt else
+           host_build.build_library_host(os.environ.get("VLLT_REFSUITE_BUILD") or tempfile.mkdtemp()))
     if lib is None:
         raise RuntimeError("g++ is not available")
     host_runner.HostRunner.lib = lib

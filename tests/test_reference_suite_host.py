@@ -43,9 +43,9 @@ FILES = ("test_engine.py", "test_speculative.py", "test_api.py", "test_block.py"
 @pytest.mark.skipif(not all(os.path.exists(os.path.join(REFERENCE, "tests", f)) for f in FILES),
                     reason="the reference's source tree is not here")
 @pytest.mark.parametrize("engine", ["reference", "gpu-run-ahead"])
-def test_reference_engine_tests_pass_with_libvllt_behind_the_engine(tmp_path, engine):
+def test_reference_engine_tests_pass_with_libvllt_behind_the_engine(host_library, tmp_path, engine):
     env = dict(os.environ, PYTHONDONTWRITEBYTECODE="1", VLLT_REFSUITE_BUILD=str(tmp_path),
-               VLLT_REFSUITE_ENGINE=engine,
+               VLLT_REFSUITE_LIB=host_library._name, VLLT_REFSUITE_ENGINE=engine,
                PYTHONPATH=os.pathsep.join([os.path.join(ROOT, "tests"), os.path.join(ROOT, "vllm-lite_b200"),
                                            REFERENCE]))
     files = [os.path.join(REFERENCE, "tests", f) for f in FILES]
