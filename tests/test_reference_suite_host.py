@@ -36,7 +36,9 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REFERENCE = os.environ.get("VLLT_REFERENCE_TREE", "/root/reference")
+# the reference's source checkout: VLLT_REFERENCE_TREE, else a "reference"
+# directory beside this repository
+REFERENCE = os.environ.get("VLLT_REFERENCE_TREE", os.path.join(os.path.dirname(ROOT), "reference"))
 FILES = ("test_engine.py", "test_speculative.py", "test_api.py", "test_block.py", "test_attention.py")
 
 
