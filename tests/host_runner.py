@@ -40,15 +40,18 @@ class HostRunner:
         self.check_step_flags = CudaRunner.check_step_flags.__get__(self)
         self.pick_buffer = CudaRunner.pick_buffer.__get__(self)
         self.bucket = CudaRunner.bucket.__get__(self)
+        self.copy_blocks_on_device = CudaRunner.copy_blocks_on_device.__get__(self)
+        self.torch = torch
         self.head_dim = model_cfg.d_model // model_cfg.n_heads
-        shape = (model_cfg.n_layers, self.num_blocks, model_cfg.n_kv_heads, self.block_size, self.head_dim)
+        shape = (model_cfg.n_layers, self.num_blocks, model_cfg.n_kv_heads // self.tp_size, self.block_size,
+                 self.head_dim)
         dt = torch.bfloat16 if self.bf16 else torch.float32
         self.cache_k = torch.zeros(shape, dtype=dt)
         self.cache_v = torch.zeros(shape, dtype=dt)
         if self.bf16:
             from vllt.llama import LlamaRunner, LlamaWeights
 
-            self.w = LlamaWeights(model_cfg, "cpu")
+            self.w = LlamaWeights(model_cfg, "cpu", self.tp_rank, self.tp_size)
             self._ptrs = self.w.pointer_arrays()
             self.desc = LlamaRunner._make_desc(self)
         else:
@@ -83,11 +86,8 @@ class HostRunner:
 
         if out.cow:
             pairs = np.ascontiguousarray(np.asarray(out.cow, np.int32).reshape(-1, 2))
-            cfg = self.model_cfg
-            assert self.L.vllt_copy_blocks(self.cache_k.data_ptr(), self.cache_v.data_ptr(), pairs.ctypes.data,
-                                           len(pairs), cfg.n_layers, self.num_blocks, cfg.n_kv_heads,
-                                           self.block_size, self.head_dim,
-                                           _lib.VLLT_BF16 if self.bf16 else _lib.VLLT_F32, None) == 0
+            self.copy_blocks_on_device(pairs.ctypes.data, len(pairs))
+            self._cow_pairs = pairs
         rec, bounds, rows, (S, T, R, W) = self.packer.pack(out)
         self.stand_ins += int((rec[5 + 3 * S:5 + 3 * S + T] < 0).sum())
         rec = np.ascontiguousarray(rec, np.int32)

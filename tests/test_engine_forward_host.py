@@ -131,3 +131,36 @@ def test_llama_engine_through_the_compiled_bf16_path(host_lib):
     assert all(len(s) == 10 for s in want)
     assert eng.passes_ahead > 0
     assert host_lib.vllt_host_mma_count() > mma0
+
+
+@pytest.mark.parametrize("tp_size", [1, 2])
+def test_copy_on_write_copies_the_runners_own_cache_layout(host_lib, tp_size):
+    """CudaRunner.copy_blocks_on_device (the copy-on-write of a forked block,
+    runner.py:54-60) on the bf16 Llama runner's caches: the element type and
+    the KV heads of this rank come from the caches themselves (a rank under
+    tensor parallelism holds n_kv / tp_size heads), every layer copied, no
+    other block touched."""
+    import numpy as np
+    from vllmlite.config import CacheConfig, ModelConfig
+
+    from tests.host_runner import HostLlamaRunner
+
+    class Shard(HostLlamaRunner):
+        pass
+
+    Shard.lib, Shard.tp_size, Shard.tp_rank, Shard.tp_comm = host_lib, tp_size, tp_size - 1, 0x7C
+    from types import SimpleNamespace
+
+    mc = ModelConfig(n_layers=2, n_heads=4, n_kv_heads=2, d_model=512, d_ff=512, vocab_size=300, max_seq_len=256,
+                     seed=3)
+    run = Shard(mc, CacheConfig(block_size=16, num_blocks=12), SimpleNamespace(max_seqs=2, max_batched_tokens=32))
+    assert run.cache_k.shape == (2, 12, 2 // tp_size, 16, 128) and run.cache_k.dtype == torch.bfloat16
+    g = torch.Generator().manual_seed(tp_size)
+    run.cache_k.copy_(torch.randn(run.cache_k.shape, generator=g).to(torch.bfloat16))
+    run.cache_v.copy_(torch.randn(run.cache_v.shape, generator=g).to(torch.bfloat16))
+    want_k, want_v = run.cache_k.clone(), run.cache_v.clone()
+    pairs = np.asarray([[3, 7], [0, 11]], np.int32)
+    for s, d in pairs:
+        want_k[:, d], want_v[:, d] = want_k[:, s], want_v[:, s]
+    run.copy_blocks_on_device(pairs.ctypes.data, len(pairs))
+    assert torch.equal(run.cache_k, want_k) and torch.equal(run.cache_v, want_v)

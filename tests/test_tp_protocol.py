@@ -54,6 +54,7 @@ def _messages():
 
 
 GATHER_ROWS = np.asarray([5, 0, 3], np.int32)
+COW_PAIRS = np.asarray([7, 12, 3, 40], np.int32)  # (src, dst) block pairs, flat
 
 
 def _logits(R, V):
@@ -71,8 +72,8 @@ def _rank(rank, world, port, result_dir):
     sys.path[:0] = [ROOT, os.path.join(ROOT, "vllm-lite_b200")]
     import torch.distributed as dist
 
-    from vllt.tp import (CTRL_WORDS, OP_FORWARD, OP_GATHER, OP_MARK, OP_STOP, ControlPlane, gather_vocab_rows,
-                         merge_argmax, serve)
+    from vllt.tp import (CTRL_WORDS, OP_COW, OP_FORWARD, OP_GATHER, OP_MARK, OP_STOP, ControlPlane,
+                         gather_vocab_rows, merge_argmax, serve)
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -84,13 +85,15 @@ def _rank(rank, world, port, result_dir):
                 plane.send(OP_FORWARD, np.zeros(65, np.int32))
             plane.send(OP_MARK)
             for j, (rec, b, g) in enumerate(msgs):
+                if j == 4:  # a pass with copy-on-write pairs: the copy message goes first
+                    plane.send(OP_COW, COW_PAIRS)
                 plane.send(OP_FORWARD, rec, b, g)
                 if j == 2:
                     plane.send(OP_GATHER, GATHER_ROWS)
             plane.send(OP_MARK)
             plane.send(OP_STOP)
         else:
-            seen, marks, gathers = [], [], []
+            seen, marks, gathers, cows = [], [], [], []
 
             def forward(bounds, greedy):
                 n = int(plane.ctrl[7])
@@ -99,13 +102,18 @@ def _rank(rank, world, port, result_dir):
             def gather(n):
                 gathers.append((len(seen), plane.buf[:n].numpy().copy()))
 
-            assert serve(plane, forward, marks.append, gather) == len(msgs)
+            def cow(n):
+                cows.append((len(seen), plane.buf[:n].numpy().copy()))
+
+            assert serve(plane, forward, marks.append, gather, cow) == len(msgs)
             assert marks == [0, 0]
             for (rec, b, g), (got, gb, gg) in zip(msgs, seen):
                 np.testing.assert_array_equal(got, rec)
                 assert [getattr(gb, f) for f in FIELDS] == [getattr(b, f) for f in FIELDS] and gg == g
             assert len(gathers) == 1 and gathers[0][0] == 3
             np.testing.assert_array_equal(gathers[0][1], GATHER_ROWS)
+            assert len(cows) == 1 and cows[0][0] == 4  # before the pass it belongs to
+            np.testing.assert_array_equal(cows[0][1], COW_PAIRS)
 
         # vocab-parallel greedy: rank r owns columns [r*V/2, (r+1)*V/2)
         R, V = 8, 40

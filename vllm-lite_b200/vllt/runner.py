@@ -495,11 +495,16 @@ class CudaRunner(_Base):
             raise IndexError("copy-on-write block id out of range")
         p = torch.from_numpy(a.astype(np.int32)).pin_memory().to(self.dev, non_blocking=True)  # no wait on the stream
         self._cow_pairs = p  # referenced until the copy kernel has been enqueued
-        cfg = self.model_cfg
-        check(self.L.vllt_copy_blocks(self.cache_k.data_ptr(), self.cache_v.data_ptr(), p.data_ptr(),
-                                      len(pairs), cfg.n_layers, self.num_blocks, cfg.n_kv_heads,
-                                      self.block_size, self.head_dim, _lib.VLLT_F32,
-                                      _lib.stream_handle()))
+        self.copy_blocks_on_device(p.data_ptr(), len(pairs))
+
+    def copy_blocks_on_device(self, pairs_ptr: int, n_pairs: int) -> None:
+        """Enqueue the block copies of n_pairs (src, dst) int32 pairs at a
+        device address, in this runner's caches: every layer, this rank's KV
+        heads ([L][blocks][n_kv][block][D]), the caches' element type."""
+        L, nb, n_kv, bs, D = self.cache_k.shape
+        dtype = _lib.VLLT_BF16 if self.cache_k.dtype == self.torch.bfloat16 else _lib.VLLT_F32
+        check(self.L.vllt_copy_blocks(self.cache_k.data_ptr(), self.cache_v.data_ptr(), pairs_ptr, n_pairs, L, nb,
+                                      n_kv, bs, D, dtype, _lib.stream_handle()))
 
     def _on_reserve(self, caps) -> None:
         """Hook for subclasses that size extra buffers by the capacities."""

@@ -13,7 +13,11 @@ forward pass:
      global index among the maxima wins (np.argmax semantics); every rank
      keeps the merged picks in its pick buffer, so a record that refers to
      them (rank 0's engine running ahead) resolves the same on every rank;
-  4. rows whose pick needs the whole vocabulary at once (a min_tokens EOS mask,
+  4. a pass with copy-on-write pairs (a shared, partly filled block the
+     scheduler forks: block_manager.py:77-93) is preceded by one copy
+     message carrying the pairs; every rank copies the blocks of its own KV
+     heads before the forward (runner.py:63-64 applies them first too);
+  5. rows whose pick needs the whole vocabulary at once (a min_tokens EOS mask,
      a repetition penalty, or a temperature draw: sampling.py:41-64) are named
      in a gather message; every rank contributes its slice of those rows and
      rank 0 runs the single-GPU sampling kernels on the full rows.
@@ -32,7 +36,7 @@ from ._lib import StepBounds, check, lib
 from .llama import LlamaRunner
 from .runner import CudaRunner
 
-OP_FORWARD, OP_STOP, OP_MARK, OP_GATHER = 1, 2, 3, 4
+OP_FORWARD, OP_STOP, OP_MARK, OP_GATHER, OP_COW = 1, 2, 3, 4, 5
 CTRL_WORDS = 8  # [op, tokens, rows, decode_seqs, tiles, max_ctx, greedy, record words]
 
 
@@ -120,10 +124,11 @@ class ControlPlane:
         return c[0], StepBounds(*c[1:6]), c[6], c[7]
 
 
-def serve(plane: ControlPlane, forward, mark, gather=None) -> int:
+def serve(plane: ControlPlane, forward, mark, gather=None, cow=None) -> int:
     """Worker dispatch loop: forward(bounds, greedy) for each OP_FORWARD,
     mark(tag) for each OP_MARK, gather(n) for each OP_GATHER (the n row
-    indices sit in the broadcast buffer), return the number of passes at
+    indices sit in the broadcast buffer), cow(n) for each OP_COW (n / 2
+    (src, dst) block pairs in the buffer), return the number of passes at
     OP_STOP. An unknown op is a protocol error (rank 0 never sends one)."""
     passes = 0
     while True:
@@ -137,6 +142,8 @@ def serve(plane: ControlPlane, forward, mark, gather=None) -> int:
             passes += 1
         elif op == OP_GATHER and gather is not None:
             gather(n)
+        elif op == OP_COW and cow is not None:
+            cow(n)
         else:
             raise RuntimeError(f"tensor-parallel control: unknown op {op}")
 
@@ -204,6 +211,12 @@ class TPLlamaRunner(LlamaRunner):
 
     # ---- rank 0 -------------------------------------------------------------------
     def launch(self, out):  # replaces LlamaRunner.launch (which is CudaRunner's plus the roofline)
+        if out.cow:  # every rank forks the blocks of its KV heads before the forward
+            pairs = np.asarray(out.cow, np.int64).reshape(-1, 2)
+            if int(pairs.min()) < 0 or int(pairs.max()) >= self.num_blocks:  # before any collective
+                raise IndexError("copy-on-write block id out of range")
+            self._broadcast(OP_COW, pairs.astype(np.int32).reshape(-1))
+            self.copy_on_write(out.cow)
         rec, bounds, rows, (S, T, R, W) = self.pack(out)  # every rank applies the record's table updates
         self._broadcast(OP_FORWARD, rec, bounds, greedy=1)
         self._last_n = rec.size
@@ -303,4 +316,8 @@ class TPLlamaRunner(LlamaRunner):
             self._gather(n)
             torch.cuda.current_stream(self.dev).synchronize()
 
-        return serve(self.plane, forward, self._record_mark, gather)
+        def cow(n):  # the pairs sit at the head of the broadcast buffer, on this device
+            self.copy_blocks_on_device(self.rec_dev.data_ptr(), n // 2)
+            torch.cuda.current_stream(self.dev).synchronize()
+
+        return serve(self.plane, forward, self._record_mark, gather, cow)
