@@ -17,7 +17,11 @@ the block tests call, becomes the device prefix hash's own code
 compiled for the host. And the reference's paged_attention
 (vllmlite/attention.py:59), which its attention tests call, becomes
 vllt.ops.paged_attention, the NumPy-signature drop-in, over the host build's
-C ABI. Imported as a
+C ABI. Requests without a seed draw from a generator seeded with a fixed
+value instead of fresh entropy (LLMEngine.add_request, engine.py:81): the HTTP
+tests sample at temperature 1.0 without a seed and count the tokens they get
+back, so with entropy a sampled EOS would end one early now and then, whatever
+the runner. Imported as a
 top-level module (this directory on sys.path), since the reference's tests
 own the package name `tests`.
 """
@@ -57,6 +61,7 @@ def pytest_configure(config):
     E.NumpyRunner = runner
     _patch_hash_block(host_build)
     _patch_paged_attention(lib)
+    _seed_unseeded_requests(E)
     mode = os.environ.get("VLLT_REFSUITE_ENGINE", "reference")
     if mode != "reference":  # the product's engine in LLMEngine's place: device picks
         from vllt.engine import GpuLLMEngine
@@ -101,6 +106,28 @@ def _patch_paged_attention(lib):
         return ops.paged_attention(q, cache_k, cache_v, read_slots, n_kv_heads, scale, device="cpu")
 
     A.paged_attention = paged_attention
+
+
+UNSEEDED = 20240601
+
+
+def _seed_unseeded_requests(E):
+    import numpy as np
+
+    class _Random:
+        def __getattr__(self, name):
+            return getattr(np.random, name)
+
+        def default_rng(self, seed=None, *args):
+            return np.random.default_rng(UNSEEDED if seed is None else seed, *args)
+
+    class _NumPy:  # vllmlite.engine's numpy, but for default_rng's unseeded case
+        random = _Random()
+
+        def __getattr__(self, name):
+            return getattr(np, name)
+
+    E.np = _NumPy()
 
 
 def pytest_terminal_summary(terminalreporter):

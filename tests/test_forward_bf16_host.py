@@ -82,6 +82,15 @@ class Forward:
         self.packer = StepPacker(bs, num_blocks, shape.vocab_size, w.rope_len, self.qp)
 
     def execute(self, out):
+        if out.cow:  # the runner's copy-on-write before the forward (vllmlite/runner.py:63-64)
+            from vllt import _lib
+
+            pairs = np.ascontiguousarray(np.asarray(out.cow, np.int32).reshape(-1, 2))
+            L_, nb, n_kv, bs, D = self.cache_k.shape
+            dt = _lib.VLLT_BF16 if self.cache_k.dtype == torch.bfloat16 else _lib.VLLT_F32
+            rc = self.L.vllt_copy_blocks(self.cache_k.data_ptr(), self.cache_v.data_ptr(), pairs.ctypes.data,
+                                         len(pairs), L_, nb, n_kv, bs, D, dt, None)
+            assert rc == 0, self.L.vllt_last_error()
         rec, bounds, rows, (S, T, R, W) = self.packer.pack(out)
         self.last_bounds = bounds
         rec = np.ascontiguousarray(rec, np.int32)

@@ -14,7 +14,8 @@ vocab-parallel as in TPLlamaRunner.greedy_picks: vllt_argmax_rows over this
 rank's slice, the (max, index) pairs all-gathered, vllt.tp.merge_argmax.
 
 On the GPU test's schedule (tests/tp_parity.py: chunked prefill, decode, a
-verify row set), at 2 ranks (8 heads / 2 KV heads: 4 / 1 per rank) and 4 ranks
+verify row set, then a pass that forks a partly filled block by copy-on-write
+and continues a sequence from the copy), at 2 ranks (8 heads / 2 KV heads: 4 / 1 per rank) and 4 ranks
 (8 / 4: 2 / 1 per rank), against a 1-rank bf16 forward of the same weights:
   * the gathered logits (vllt.tp.gather_vocab_rows over every rank's slice)
     within TP_BAR of the largest |logit|, the bar of the GPU test
@@ -90,8 +91,11 @@ def _rank(rank, world, port, lib_path, shape_kw, result_dir):
         vl, off = shard.keep[0].vocab_local, shard.keep[0].vocab_offset
         one = Forward(L, shape, True) if rank == 0 else None
         worst, agree, rows, exact, want_sizes = 0.0, 0, 0, True, []
-        for seqs in schedule(shape.vocab_size, np.random.default_rng(3)):
-            out = F.as_scheduler_output(seqs)
+        # the GPU test's passes (tests/tp_parity.py), the fork through copy-on-write last
+        fork = [dict(start=46, n=1, count=1, tokens=[7], block_ids=[0, 1, 14], drafts=[])]
+        passes = [(p, ()) for p in schedule(shape.vocab_size, np.random.default_rng(3))] + [(fork, [(2, 14)])]
+        for seqs, cow in passes:
+            out = F.as_scheduler_output(seqs, cow)
             local = shard.execute(out)
             want_sizes += [shard.last_bounds.tokens * shape.d_model] * (2 * shape.n_layers)
             R = local.shape[0]
@@ -136,4 +140,4 @@ def test_tensor_parallel_forward_matches_one_rank(host_library, tmp_path, world,
     r0 = res[0]
     print(f"tensor parallel {world}: worst {r0['worst']:.3e} of max |logit|, picks {r0['agree']}/{r0['rows']}")
     assert r0["worst"] < TP_BAR
-    assert r0["agree"] >= r0["rows"] - 1
+    assert r0["agree"] >= r0["rows"] - 1 and r0["rows"] == 13

@@ -4,8 +4,10 @@ Every rank builds its shard of a full-width 2-layer slice of the Llama-3-8B
 shape; rank 0 drives a fixed three-pass schedule through TPLlamaRunner
 (record broadcast, NCCL all-reduces in the forward, vocab-parallel greedy) and
 compares logits and picks with a 1-GPU LlamaRunner on the same weights.
-Rows whose pick needs the whole vocabulary (EOS mask, repetition penalty,
-temperature draw) are gathered from every rank: the gathered rows must hold
+A last pass forks a partly filled block (copy-on-write on every rank before
+the forward) and continues a sequence from the copy. Rows whose pick needs
+the whole vocabulary (EOS mask, repetition penalty, temperature draw) are
+gathered from every rank: the gathered rows must hold
 rank 0's own slice bit for bit and match the 1-GPU logits like the slices do.
 Prints one line "TP_PARITY ok <max rel err> <agree>/<rows>" on success.
 """
@@ -53,8 +55,12 @@ def main():
     else:
         ref = LlamaRunner(shape, cache, sched, use_graphs=False)
         worst, agree, rows = 0.0, 0, 0
-        for seqs in schedule(shape.vocab_size, np.random.default_rng(3)):
-            out = F.as_scheduler_output(seqs)
+        # then a fork: sequence A's partly filled third block (tokens 32-45) is
+        # copied to block 14 (copy-on-write) and a sequence continues from it
+        fork = [dict(start=46, n=1, count=1, tokens=[7], block_ids=[0, 1, 14], drafts=[])]
+        passes = [(p, ()) for p in schedule(shape.vocab_size, np.random.default_rng(3))] + [(fork, [(2, 14)])]
+        for seqs, cow in passes:
+            out = F.as_scheduler_output(seqs, cow)
             _, R = run.launch(out)
             picks = run.greedy_picks(R).cpu().numpy()
             local_logits = run.logits_dev[:R, :run.w.vocab_local].cpu().numpy()
