@@ -115,3 +115,69 @@ class HostLlamaRunner(HostRunner):
     """LlamaRunner (the bf16 path, one rank) over the host library."""
 
     bf16 = True
+
+
+class HostTPRunner(HostLlamaRunner):
+    """TPLlamaRunner over the host library, its ranks gloo processes: the
+    shard's weights and KV heads, and TPLlamaRunner's own protocol code
+    (launch with its copy-on-write message, record broadcast, vocab-parallel
+    greedy, row gathers, stop) on CPU tensors. The forward's all-reduce goes
+    to the host collective the process registered (vllt_host_set_allreduce).
+    Set `group` (rank, world) and `lib` before building one."""
+
+    group = None
+    COMM = 0x7C  # the opaque communicator handle the host collective checks
+
+    def __init__(self, model_cfg, cache_cfg, sched_cfg=None, device=None):
+        from vllt.tp import CTRL_WORDS, ControlPlane
+
+        self.tp_rank, self.tp_size, self.tp_comm = self.group.rank, self.group.world, self.COMM
+        super().__init__(model_cfg, cache_cfg, sched_cfg, device)
+        c = self.caps
+        words = 5 + 4 * c.max_seqs + c.max_tokens + 3 * c.max_seqs * c.max_table_width
+        self.rec_dev = torch.zeros(words + CTRL_WORDS, dtype=torch.int32)
+        self.rec_host = self.rec_dev
+        self.plane = ControlPlane(self.rec_dev)
+        self._val = torch.empty(c.max_rows, dtype=torch.float32)
+        self._idx = torch.empty(c.max_rows, dtype=torch.int32)
+        self._vals = torch.empty(self.tp_size * c.max_rows, dtype=torch.float32)
+        self._idxs = torch.empty(self.tp_size * c.max_rows, dtype=torch.int32)
+        self._pending_rows = self.steps = self.h2d_bytes = self.cows = 0
+        self.pooled_tables, self.use_graphs, self.bucket_bounds, self._fixed = True, False, True, True
+
+    from vllt.runner import CudaRunner as _C
+    from vllt.tp import TPLlamaRunner as _T
+
+    launch, _broadcast, greedy_picks, gather_rows, _gather, stop_workers, _reserve = (
+        _T.launch, _T._broadcast, _T.greedy_picks, _T.gather_rows, _T._gather, _T.stop_workers, _T._reserve)
+    pack, _timed_forward, _dispatch, _forward = _C.pack, _C._timed_forward, _C._dispatch, _C._forward
+    del _C, _T
+
+    def copy_on_write(self, pairs) -> None:  # CudaRunner's, without the pinned staging copy
+        a = np.ascontiguousarray(np.asarray(pairs, np.int32).reshape(-1, 2))
+        self.copy_blocks_on_device(a.ctypes.data, len(a))
+        self.cows += len(a)
+
+    def execute(self, out):
+        """Rank 0 for an unmodified LLMEngine: the full-vocabulary logits of
+        the pass, gathered from every rank's slice (TPLlamaRunner.gather_rows)."""
+        rows, R = self.launch(out)
+        self.check_step_flags(int(self.meta[7]))
+        self.greedy_picks(R)  # launch's greedy flag: every worker takes this all-gather after the forward
+        return self.gather_rows(list(range(R))).numpy().copy(), rows
+
+    def worker_loop(self):
+        """TPLlamaRunner.worker_loop without the device synchronizations (the
+        host build runs each launch to completion)."""
+        from vllt.tp import serve
+
+        def forward(bounds, greedy):
+            self._dispatch(bounds)
+            if greedy:
+                self.picks_dev[:bounds.rows].copy_(self.greedy_picks(bounds.rows))
+
+        def cow(n):
+            self.copy_blocks_on_device(self.rec_dev.data_ptr(), n // 2)
+            self.cows += n // 2
+
+        return serve(self.plane, forward, lambda tag: None, self._gather, cow)
